@@ -1,0 +1,176 @@
+/*
+ * mask_loss_b200.h -- C ABI of the B200-native mask matching + loss path.
+ *
+ * Plain pointers and sizes only: every tensor is a raw device pointer to a
+ * contiguous buffer in the layout stated next to it, every launch goes on the
+ * caller's stream, and nothing here allocates device memory (callers pass a
+ * workspace sized by the *_workspace_size query).  Every entry returns an
+ * ml_status; none of them calls exit() or synchronises the device.
+ *
+ * Each entry cites the reference interface it replaces
+ * (AndyBarcia/mask_loss, path:line).
+ */
+#ifndef MASK_LOSS_B200_H
+#define MASK_LOSS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ml_stream_t; /* == cudaStream_t */
+
+typedef enum ml_status {
+    ML_OK = 0,
+    ML_EINVAL = 1,       /* an argument is out of its documented range */
+    ML_ESHAPE = 2,       /* inconsistent or unsupported tensor shapes */
+    ML_EWORKSPACE = 3,   /* workspace pointer null/misaligned or too small */
+    ML_ECUDA = 4,        /* a CUDA launch or attribute call failed */
+    ML_ESOLVER = 5,      /* the assignment solver reported failure (see dev_status) */
+    ML_EUNSUPPORTED = 6  /* a size beyond what this build supports */
+} ml_status;
+
+/* Shapes of one call.  mask_logits (L,B,Q,H,W) fp32, mask_targets (B,Ht,Wt)
+ * int64, cls_logits (L,B,Q,C) fp32, cls_targets (B,GT_total) int64 (-1 pad). */
+typedef struct ml_dims {
+    int64_t L, B, Q, H, W;
+    int64_t Ht, Wt;
+    int64_t C;
+    int64_t GT_total;
+} ml_dims;
+
+/* Scalar arguments of mask_loss.mask_matching (src/bindings.cpp:86-111), same
+ * names and meaning.  Booleans are 0/1. */
+typedef struct ml_params {
+    float smooth, sigmoid_scale, dice_scale, cls_scale;
+    int64_t background_index;          /* GT column dropped from the costs, or -1 */
+    float uncertainty_gamma, uncertainty_gamma_min;
+    double inf_thresh;                 /* costs >= this are treated as +inf */
+    double num_masks;                  /* <= 0: use the matched count */
+    int32_t force_unmatched_class_to_background;
+    int32_t force_unmatched_masks_to_empty;
+    int64_t topk_matches;              /* K >= 0 */
+    int64_t strategy_id;               /* 0 global, 1 round, 2 greedy, 3 pseudo-greedy */
+    float mask_gamma, mask_alpha, cls_gamma, cls_alpha; /* alpha < 0 disables */
+    int64_t void_class_index;          /* -1: none */
+    int32_t use_softmax_label_loss;
+    int32_t normalize_uncertainty;
+} ml_params;
+
+/* Human-readable text of a status code (static storage). */
+const char* ml_status_string(int status);
+
+/* Detail of the last failing call on this host thread ("" if none). */
+const char* ml_last_error(void);
+
+/* Library version as 10000*major + 100*minor + patch. */
+int ml_version(void);
+
+/* GT_out = GT_total minus the background column when it lies in range. */
+int64_t ml_gt_out(int64_t GT_total, int64_t background_index);
+
+/* ---------------------------------------------------------------------- */
+/* Workspace sizes (bytes, 256-byte aligned pointers expected).             */
+/* ---------------------------------------------------------------------- */
+size_t ml_mask_matching_workspace_size(const ml_dims* d, const ml_params* p);
+size_t ml_mask_matching_backward_workspace_size(const ml_dims* d, const ml_params* p);
+size_t ml_match_workspace_size(int64_t L, int64_t B, int64_t Q, int64_t GT_out);
+
+/* ---------------------------------------------------------------------- */
+/* Pairwise costs.  Replaces pairwise_mask_loss_forward                    */
+/* (src/bindings.cpp:64-82, src/cuda/pw_mask.cu:314-501).                   */
+/* out: (3,L,B,Q,GT_out) fp32 -- sigmoid-CE, dice, label cost; +inf where   */
+/* the GT id paints no pixel (mask slices) or its class is <0 or >=C.       */
+/* Uses the same workspace as ml_mask_matching.                            */
+/* ---------------------------------------------------------------------- */
+int ml_pairwise_mask_loss_forward(const ml_dims* d, const ml_params* p,
+                                  const float* mask_logits, const int64_t* mask_targets,
+                                  const float* cls_logits, const int64_t* cls_targets,
+                                  float* out, void* workspace, size_t workspace_bytes,
+                                  ml_stream_t stream);
+
+/* Pairwise label cost alone.  Replaces forward_pw_sigmoid_label_loss /     */
+/* forward_pw_softmax_label_loss (src/bindings.cpp:141-155,                 */
+/* src/cuda/pw_sigmoid_label_loss.cu:108-187, pw_softmax_label_loss.cu:105-174). */
+/* out: (L,B,Q,GT_out) fp32.                                                */
+int ml_pairwise_label_loss_forward(int64_t L, int64_t B, int64_t Q, int64_t C,
+                                   int64_t GT_total, int64_t background_index,
+                                   float scale, float gamma, float alpha, int32_t use_softmax,
+                                   const float* cls_logits, const int64_t* cls_targets,
+                                   float* out, ml_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Assignment solver alone, one thread-block per (l,b) slice.  Replaces    */
+/* the host loop of src/cpu/matching.cpp:690-722 around                    */
+/* assign_predictions_for_slice (:476-571).  costs: (L,B,Q,GT_out) fp32,    */
+/* evaluated in fp64 exactly as the reference's kDouble copy.              */
+/* pred_to_gt / pred_round: (L,B,Q) int64.  dev_status: one device int32    */
+/* that stays 0 on success (nonzero: slice failed, outputs set to -1).      */
+/* ---------------------------------------------------------------------- */
+int ml_match(const float* costs, int64_t L, int64_t B, int64_t Q, int64_t GT_out,
+             double inf_thresh, int64_t topk, int64_t strategy_id,
+             int64_t* pred_to_gt, int64_t* pred_round, int32_t* dev_status,
+             void* workspace, size_t workspace_bytes, ml_stream_t stream);
+
+/* Same solver fed fp64 cost slices directly (for bit-exact checks against
+ * the reference solver on identical fp64 matrices). costs: (N,Q,GT_out). */
+int ml_match_f64(const double* costs, int64_t N, int64_t Q, int64_t GT_out,
+                 double inf_thresh, int64_t topk, int64_t strategy_id,
+                 int64_t* pred_to_gt, int64_t* pred_round, int32_t* dev_status,
+                 ml_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Fused forward: costs -> on-device matching -> matched-loss means.        */
+/* Replaces mask_loss.mask_matching (src/bindings.cpp:86-111,              */
+/* src/cpu/matching.cpp:592-752 + src/cuda/mask_matching_forward.cu:283-586). */
+/*   pred_to_gt, pred_round : (L,B,Q) int64                                */
+/*   layer_means            : (3,L) fp32 -- mask, dice, class means          */
+/*   sep_costs  (nullable)  : (3,L,B,Q,GT_out) fp32 copy of the costs        */
+/*   saved      (nullable)  : (L,B,Q,4) fp32 per-query statistics that let   */
+/*                            ml_mask_matching_backward skip its stats pass  */
+/*   num_masks_dev (nullable): device fp32 scalar overriding p->num_masks    */
+/*                            (used by data-parallel callers after an        */
+/*                            all-reduce, so no host sync is needed)         */
+/*   dev_status             : one device int32, 0 on success                */
+/* ---------------------------------------------------------------------- */
+int ml_mask_matching(const ml_dims* d, const ml_params* p,
+                     const float* mask_logits, const int64_t* mask_targets,
+                     const float* cls_logits, const int64_t* cls_targets,
+                     const float* num_masks_dev,
+                     int64_t* pred_to_gt, int64_t* pred_round, float* layer_means,
+                     float* sep_costs, float* saved, int32_t* dev_status,
+                     void* workspace, size_t workspace_bytes, ml_stream_t stream);
+
+/* Per-image GT count (present, non-background GT ids) summed over the batch,
+ * written as one fp32 to num_masks_out (device).  This is the num_masks a
+ * data-parallel caller all-reduces.  Needs the forward workspace. */
+int ml_count_masks(const ml_dims* d, const ml_params* p, const int64_t* mask_targets,
+                   float* num_masks_out, void* workspace, size_t workspace_bytes,
+                   ml_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Backward.  Replaces mask_loss.mask_matching_backward                     */
+/* (src/bindings.cpp:113-139, src/cuda/mask_matching_backward.cu:378-621).   */
+/*   grad_*_mean: (L,) fp32 device upstream gradients                       */
+/*   saved (nullable): the forward's per-query statistics; when null a      */
+/*                     statistics pass re-reads the logits (reference path) */
+/*   grad_mask_logits (L,B,Q,H,W), grad_cls_logits (L,B,Q,C): fp32, fully    */
+/*                     written (zeros where the loss does not reach).       */
+/* ---------------------------------------------------------------------- */
+int ml_mask_matching_backward(const ml_dims* d, const ml_params* p,
+                              const float* grad_mask_mean, const float* grad_dice_mean,
+                              const float* grad_cls_mean,
+                              const float* mask_logits, const int64_t* mask_targets,
+                              const float* cls_logits, const int64_t* cls_targets,
+                              const int64_t* pred_to_gt, const float* saved,
+                              const float* num_masks_dev,
+                              float* grad_mask_logits, float* grad_cls_logits,
+                              void* workspace, size_t workspace_bytes, ml_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MASK_LOSS_B200_H */

@@ -1,0 +1,562 @@
+// capi.cu -- extern "C" entry points declared in include/mask_loss_b200.h.
+//
+// Each entry validates its arguments with the reference's rules, carves the
+// caller's workspace, and launches on the caller's stream.  No device memory
+// is allocated here and nothing synchronises the device.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+using namespace mlb;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+    return fail(ML_ECUDA, "CUDA error in %s: %s", where, cudaGetErrorString(e));
+}
+
+#define ML_CHECK_LAUNCH(where)                                  \
+    do {                                                        \
+        cudaError_t e_ = cudaGetLastError();                    \
+        if (e_ != cudaSuccess) return cuda_fail(e_, where);     \
+    } while (0)
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+int sm_count() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+// ---------------------------------------------------------------------------
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// ---------------------------------------------------------------------------
+// Forward plan: tiling, workspace layout.
+// ---------------------------------------------------------------------------
+struct FwdPlan {
+    int L, B, Q, H, W, Ht, Wt, s, C, gt_total, gout, bg;
+    bool unc, foc, tma_ok;
+    int nacc, nrow;
+    int qrows, qrows_pad, nqt, gp, ngr, chunk_cells, nchunk, part_stride;
+    size_t cost_smem;
+    // workspace offsets
+    size_t off_totals, off_part, off_sep, off_total, off_rawI, off_rawT, off_qstat, bytes;
+};
+
+size_t cost_smem_bytes(int qrows_pad, int nacc, int gp, int s2) {
+    return 1024 + (size_t)kStages * qrows_pad * KC * 4 + (size_t)nacc * gp * qrows_pad * 4 +
+           2 * KC * 4 + 2 * KC * s2 * 2 + 16 + 8 * kStages;
+}
+
+int validate_dims(const ml_dims* d) {
+    if (!d) return fail(ML_EINVAL, "dims is null");
+    if (d->L < 0 || d->B < 0 || d->Q < 0 || d->C < 0 || d->GT_total < 0)
+        return fail(ML_ESHAPE, "negative dimension");
+    if (d->H <= 0 || d->W <= 0) return fail(ML_ESHAPE, "mask_logits must have positive spatial size");
+    if (d->Ht % d->H != 0 || d->Wt % d->W != 0)
+        return fail(ML_ESHAPE, "Target resolution must be an integer multiple of mask_logits resolution.");
+    if (d->Ht / d->H != d->Wt / d->W)
+        return fail(ML_ESHAPE, "Target downsample factors must be equal in both dimensions");
+    if (d->Ht / d->H > 16) return fail(ML_EUNSUPPORTED, "downsample factor above 16 is not supported");
+    const int64_t HW = d->H * d->W;
+    if (HW >= (int64_t(1) << 31) || d->L * d->B * d->Q >= (int64_t(1) << 31) ||
+        d->Ht * d->Wt >= (int64_t(1) << 31))
+        return fail(ML_EUNSUPPORTED, "dimension product exceeds 2^31");
+    if (d->GT_total >= 32767) return fail(ML_EUNSUPPORTED, "GT_total above 32766 is not supported");
+    return ML_OK;
+}
+
+int validate_params(const ml_params* p, int64_t C) {
+    if (!p) return fail(ML_EINVAL, "params is null");
+    if (p->mask_gamma < 0.0f) return fail(ML_EINVAL, "mask focal_gamma must be non-negative");
+    if (!(p->mask_alpha < 0.0f || p->mask_alpha <= 1.0f))
+        return fail(ML_EINVAL, "mask focal_alpha must be in [0, 1] or negative to disable");
+    if (p->cls_gamma < 0.0f) return fail(ML_EINVAL, "cls focal_gamma must be non-negative");
+    if (!(p->cls_alpha < 0.0f || p->cls_alpha <= 1.0f))
+        return fail(ML_EINVAL, "cls focal_alpha must be in [0, 1] or negative to disable");
+    if (p->uncertainty_gamma < 0.0f) return fail(ML_EINVAL, "uncertainty_gamma must be non-negative");
+    if (!(p->uncertainty_gamma_min >= 0.0f && p->uncertainty_gamma_min <= 1.0f))
+        return fail(ML_EINVAL, "uncertainty_gamma_min must be in [0,1]");
+    if (p->topk_matches < 0) return fail(ML_EINVAL, "K must be non-negative");
+    if (p->strategy_id < 0 || p->strategy_id > 3) return fail(ML_EINVAL, "Invalid matching strategy id");
+    const bool has_void = p->void_class_index >= 0 && p->void_class_index < C;
+    if (p->use_softmax_label_loss && p->force_unmatched_class_to_background && !has_void)
+        return fail(ML_EINVAL,
+                    "void_class_index must be provided when using softmax label loss and forcing "
+                    "unmatched class logits");
+    return ML_OK;
+}
+
+int make_plan(const ml_dims* d, const ml_params* p, FwdPlan* P) {
+    int rc = validate_dims(d);
+    if (rc) return rc;
+    P->L = (int)d->L; P->B = (int)d->B; P->Q = (int)d->Q; P->H = (int)d->H; P->W = (int)d->W;
+    P->Ht = (int)d->Ht; P->Wt = (int)d->Wt; P->s = P->Ht / P->H; P->C = (int)d->C;
+    P->gt_total = (int)d->GT_total;
+    const bool skip = p->background_index >= 0 && p->background_index < d->GT_total;
+    P->bg = skip ? (int)p->background_index : P->gt_total;
+    P->gout = P->gt_total - (skip ? 1 : 0);
+    P->unc = p->uncertainty_gamma != 0.0f;
+    P->foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
+    P->nacc = P->unc ? 3 : 2;
+    P->nrow = P->unc ? 5 : 2;
+    const int HW = P->H * P->W;
+    P->tma_ok = (HW % 4) == 0;
+    const int Q = P->Q > 0 ? P->Q : 1;
+    P->nqt = (Q + 127) / 128;
+    P->qrows = (Q + P->nqt - 1) / P->nqt;
+    P->qrows_pad = (P->qrows + 31) / 32 * 32;
+    const int s2 = P->s * P->s;
+    const int G = P->gout > 0 ? P->gout : 1;
+    const size_t fixed = cost_smem_bytes(P->qrows_pad, P->nacc, 0, s2);
+    const size_t per_col = (size_t)P->nacc * P->qrows_pad * 4;
+    const size_t small_budget = 110 * 1024, big_budget = 220 * 1024;
+    int gp_small = (int)((small_budget - fixed) / per_col);
+    int gp_big = (int)((big_budget - fixed) / per_col);
+    if (gp_big < 1) return fail(ML_EUNSUPPORTED, "query tile does not fit shared memory");
+    if (G <= gp_small || G <= gp_big) {
+        P->gp = G; P->ngr = 1;
+    } else {
+        P->ngr = (G + gp_big - 1) / gp_big;
+        P->gp = (G + P->ngr - 1) / P->ngr;
+    }
+    P->cost_smem = cost_smem_bytes(P->qrows_pad, P->nacc, P->gp, s2);
+    const int threads = P->qrows_pad;
+    int per_sm = (int)std::min<size_t>(228 * 1024 / (P->cost_smem + 1024), 2048 / threads);
+    if (per_sm < 1) per_sm = 1;
+    const int64_t base = (int64_t)P->L * P->B * P->nqt * P->ngr;
+    const int64_t target = (int64_t)sm_count() * per_sm;
+    int64_t nch = base > 0 ? (target + base - 1) / base : 1;
+    const int64_t max_ch = (HW + KC - 1) / KC;
+    if (nch > max_ch) nch = max_ch;
+    if (nch < 1) nch = 1;
+    P->chunk_cells = (int)(((HW + nch - 1) / nch + KC - 1) / KC * KC);
+    P->nchunk = (HW + P->chunk_cells - 1) / P->chunk_cells;
+    P->part_stride = (P->nacc * P->gp + P->nrow) * P->qrows_pad;
+    // workspace
+    const size_t LBQ = (size_t)P->L * P->B * P->Q;
+    const size_t LBQG = LBQ * P->gout;
+    size_t off = 0;
+    P->off_totals = off; off += align256(sizeof(int32_t) * (size_t)P->B * P->gt_total);
+    P->off_part = off;
+    off += align256(sizeof(float) * (size_t)base * P->nchunk * P->part_stride);
+    P->off_sep = off; off += align256(sizeof(float) * 3 * LBQG);
+    P->off_total = off; off += align256(sizeof(float) * LBQG);
+    P->off_rawI = off; off += align256(sizeof(float) * LBQG);
+    P->off_rawT = off; off += align256(sizeof(float) * LBQG);
+    P->off_qstat = off; off += align256(sizeof(float) * kQStat * LBQ);
+    P->bytes = off + 256;
+    return ML_OK;
+}
+
+unsigned char* ws_base(void* ws) {
+    return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
+}
+
+CostArgs cost_args(const FwdPlan& P, const ml_params* p, const float* ml, const int64_t* mt,
+                   const float* cl, const int64_t* ct, unsigned char* ws, int32_t* status) {
+    CostArgs a{};
+    a.logits = ml; a.targets = mt; a.cls_logits = cl; a.cls_targets = ct;
+    a.totals = reinterpret_cast<int32_t*>(ws + P.off_totals);
+    a.part = reinterpret_cast<float*>(ws + P.off_part);
+    a.sep = reinterpret_cast<float*>(ws + P.off_sep);
+    a.total = reinterpret_cast<float*>(ws + P.off_total);
+    a.rawI = reinterpret_cast<float*>(ws + P.off_rawI);
+    a.rawT = reinterpret_cast<float*>(ws + P.off_rawT);
+    a.qstat = reinterpret_cast<float*>(ws + P.off_qstat);
+    a.status = status;
+    a.L = P.L; a.B = P.B; a.Q = P.Q; a.H = P.H; a.W = P.W; a.Ht = P.Ht; a.Wt = P.Wt; a.s = P.s;
+    a.C = P.C; a.gt_total = P.gt_total; a.gout = P.gout; a.bg = P.bg;
+    a.qrows = P.qrows; a.qrows_pad = P.qrows_pad; a.nqt = P.nqt; a.gp = P.gp; a.ngr = P.ngr;
+    a.chunk_cells = P.chunk_cells; a.nchunk = P.nchunk; a.part_stride = P.part_stride;
+    a.smooth = p->smooth; a.sigmoid_scale = p->sigmoid_scale; a.dice_scale = p->dice_scale;
+    a.cls_scale = p->cls_scale; a.ug = p->uncertainty_gamma; a.ugmin = p->uncertainty_gamma_min;
+    a.mask_gamma = p->mask_gamma; a.mask_alpha = p->mask_alpha;
+    a.cls_gamma = p->cls_gamma; a.cls_alpha = p->cls_alpha;
+    a.area_scale = (float)(P.s * P.s);
+    a.normalize_uncertainty = p->normalize_uncertainty;
+    a.use_softmax = p->use_softmax_label_loss;
+    a.force_cls = p->force_unmatched_class_to_background;
+    a.has_void = (p->void_class_index >= 0 && p->void_class_index < P.C) ? 1 : 0;
+    a.void_index = a.has_void ? (int)p->void_class_index : -1;
+    return a;
+}
+
+template <bool UNC, bool FOC, bool TMA>
+int launch_cost_t(const FwdPlan& P, const CUtensorMap& tm, const CostArgs& a, cudaStream_t st) {
+    auto k = cost_partial_kernel<UNC, FOC, TMA>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.cost_smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cost_partial_kernel attributes");
+    dim3 grid(P.nchunk, P.nqt * P.ngr, P.L * P.B);
+    k<<<grid, P.qrows_pad, P.cost_smem, st>>>(tm, a);
+    ML_CHECK_LAUNCH("cost_partial_kernel");
+    return ML_OK;
+}
+
+// totals + chunk partials + finalize.  `a` decides which outputs are written.
+int run_costs(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStream_t st) {
+    const int64_t npix = (int64_t)P.Ht * P.Wt;
+    cudaError_t e = cudaMemsetAsync(const_cast<int32_t*>(a.totals), 0,
+                                    sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
+    if (e != cudaSuccess) return cuda_fail(e, "memset totals");
+    if (P.B > 0 && npix > 0 && P.gt_total > 0) {
+        const int bx = (int)std::min<int64_t>((npix + 255) / 256, std::max(1, 2 * sm_count() / std::max(1, P.B)));
+        const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
+        label_hist_kernel<<<dim3(bx, P.B), 256, hs, st>>>(a.targets, npix, P.gt_total,
+                                                          const_cast<int32_t*>(a.totals));
+        ML_CHECK_LAUNCH("label_hist_kernel");
+    }
+    if ((int64_t)P.L * P.B * P.Q == 0) return ML_OK;
+    CUtensorMap tm;
+    memset(&tm, 0, sizeof(tm));
+    bool tma = P.tma_ok && (reinterpret_cast<uintptr_t>(mask_logits) % 16 == 0);
+    if (tma) {
+        EncodeTiledFn enc = encode_fn();
+        if (!enc) {
+            tma = false;
+        } else {
+            const cuuint64_t dims[2] = {(cuuint64_t)P.H * P.W, (cuuint64_t)P.L * P.B * P.Q};
+            const cuuint64_t strides[1] = {(cuuint64_t)P.H * P.W * sizeof(float)};
+            const cuuint32_t box[2] = {(cuuint32_t)KC, (cuuint32_t)P.qrows};
+            const cuuint32_t es[2] = {1, 1};
+            CUresult r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(mask_logits),
+                             dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) tma = false;
+        }
+    }
+    int rc;
+    if (P.unc) {
+        if (P.foc) rc = tma ? launch_cost_t<true, true, true>(P, tm, a, st) : launch_cost_t<true, true, false>(P, tm, a, st);
+        else rc = tma ? launch_cost_t<true, false, true>(P, tm, a, st) : launch_cost_t<true, false, false>(P, tm, a, st);
+    } else {
+        if (P.foc) rc = tma ? launch_cost_t<false, true, true>(P, tm, a, st) : launch_cost_t<false, true, false>(P, tm, a, st);
+        else rc = tma ? launch_cost_t<false, false, true>(P, tm, a, st) : launch_cost_t<false, false, false>(P, tm, a, st);
+    }
+    if (rc) return rc;
+    const size_t fs = sizeof(float) * 4 * P.qrows;
+    if (P.unc) cost_finalize_kernel<true><<<dim3(P.nqt, P.L * P.B), 256, fs, st>>>(a);
+    else cost_finalize_kernel<false><<<dim3(P.nqt, P.L * P.B), 256, fs, st>>>(a);
+    ML_CHECK_LAUNCH("cost_finalize_kernel");
+    return ML_OK;
+}
+
+int check_ws(void* ws, size_t have, size_t need) {
+    if (need == 0) return ML_OK;
+    if (!ws) return fail(ML_EWORKSPACE, "workspace is null (need %zu bytes)", need);
+    if (have < need) return fail(ML_EWORKSPACE, "workspace too small: %zu < %zu bytes", have, need);
+    return ML_OK;
+}
+
+template <typename CT>
+int launch_match(const CT* costs, int64_t N, int64_t Q, int64_t G, double thr, int64_t K, int64_t strat,
+                 int64_t* p2g, int64_t* prnd, int32_t* status, cudaStream_t st) {
+    if (N == 0 || Q == 0) return ML_OK;
+    if (Q > 3000 || G > 32766) return fail(ML_EUNSUPPORTED, "solver supports Q <= 3000 and GT_out <= 32766");
+    if (!status) return fail(ML_EINVAL, "dev_status is null");
+    MatchArgs<CT> a;
+    a.costs = costs; a.pred_to_gt = p2g; a.pred_round = prnd; a.status = status;
+    a.Q = (int)Q; a.G = (int)G; a.inf_thresh = thr; a.topk = K; a.strategy = (int)strat;
+    const size_t limit = 200 * 1024;
+    size_t smem = match_smem_bytes((int)Q, (int)G, sizeof(CT), true);
+    a.stage_cost = smem <= limit;
+    if (!a.stage_cost) smem = match_smem_bytes((int)Q, (int)G, sizeof(CT), false);
+    if (smem > 227 * 1024) return fail(ML_EUNSUPPORTED, "solver state does not fit shared memory");
+    auto k = match_kernel<CT>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "match_kernel attributes");
+    k<<<(unsigned)N, 32, smem, st>>>(a);
+    ML_CHECK_LAUNCH("match_kernel");
+    return ML_OK;
+}
+
+LossArgs loss_args(const FwdPlan& P, const ml_params* p) {
+    LossArgs a{};
+    a.L = P.L; a.B = P.B; a.Q = P.Q; a.H = P.H; a.W = P.W; a.Ht = P.Ht; a.Wt = P.Wt; a.s = P.s;
+    a.C = P.C; a.G = P.gout; a.gt_total = P.gt_total; a.bg = P.bg;
+    a.num_masks = (float)p->num_masks;
+    a.smooth = p->smooth; a.sigmoid_scale = p->sigmoid_scale; a.dice_scale = p->dice_scale;
+    a.cls_scale = p->cls_scale; a.ug = p->uncertainty_gamma; a.ugmin = p->uncertainty_gamma_min;
+    a.mask_gamma = p->mask_gamma; a.mask_alpha = p->mask_alpha;
+    a.cls_gamma = p->cls_gamma; a.cls_alpha = p->cls_alpha;
+    a.force_masks = p->force_unmatched_masks_to_empty;
+    a.force_cls = p->force_unmatched_class_to_background;
+    a.has_void = (p->void_class_index >= 0 && p->void_class_index < P.C) ? 1 : 0;
+    a.void_index = a.has_void ? (int)p->void_class_index : -1;
+    a.use_softmax = p->use_softmax_label_loss;
+    a.normalize_uncertainty = p->normalize_uncertainty;
+    return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ml_status_string(int status) {
+    switch (status) {
+        case ML_OK: return "ok";
+        case ML_EINVAL: return "invalid argument";
+        case ML_ESHAPE: return "invalid shape";
+        case ML_EWORKSPACE: return "workspace missing or too small";
+        case ML_ECUDA: return "CUDA error";
+        case ML_ESOLVER: return "assignment solver failed";
+        case ML_EUNSUPPORTED: return "unsupported size";
+        default: return "unknown status";
+    }
+}
+
+const char* ml_last_error(void) { return g_last_error.c_str(); }
+
+int ml_version(void) { return 100; }
+
+int64_t ml_gt_out(int64_t GT_total, int64_t bg) {
+    return GT_total - ((bg >= 0 && bg < GT_total) ? 1 : 0);
+}
+
+size_t ml_mask_matching_workspace_size(const ml_dims* d, const ml_params* p) {
+    FwdPlan P;
+    if (!p || make_plan(d, p, &P)) return 0;
+    return P.bytes;
+}
+
+size_t ml_match_workspace_size(int64_t, int64_t, int64_t, int64_t) { return 0; }
+
+size_t ml_mask_matching_backward_workspace_size(const ml_dims* d, const ml_params*) {
+    if (!d) return 0;
+    const size_t LBQ = (size_t)d->L * d->B * d->Q;
+    return align256(sizeof(float) * 3 * (size_t)d->L) + align256(sizeof(float) * kSaved * LBQ) + 256;
+}
+
+int ml_pairwise_mask_loss_forward(const ml_dims* d, const ml_params* p, const float* mask_logits,
+                                  const int64_t* mask_targets, const float* cls_logits,
+                                  const int64_t* cls_targets, float* out, void* workspace,
+                                  size_t workspace_bytes, ml_stream_t stream) {
+    FwdPlan P;
+    int rc = validate_params(p, d ? d->C : 0);
+    if (rc) return rc;
+    if ((rc = make_plan(d, p, &P))) return rc;
+    if ((rc = check_ws(workspace, workspace_bytes, P.bytes))) return rc;
+    if (P.gout == 0) return ML_OK;
+    unsigned char* ws = ws_base(workspace);
+    CostArgs a = cost_args(P, p, mask_logits, mask_targets, cls_logits, cls_targets, ws, nullptr);
+    a.sep = out; a.total = nullptr; a.rawI = nullptr; a.rawT = nullptr;
+    return run_costs(P, a, mask_logits, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ml_pairwise_label_loss_forward(int64_t L, int64_t B, int64_t Q, int64_t C, int64_t GT_total,
+                                   int64_t bg, float scale, float gamma, float alpha,
+                                   int32_t use_softmax, const float* cls_logits,
+                                   const int64_t* cls_targets, float* out, ml_stream_t stream) {
+    if (L < 0 || B < 0 || Q < 0 || C <= 0 || GT_total < 0)
+        return fail(ML_ESHAPE, "class dimension must be positive");
+    if (gamma < 0.0f) return fail(ML_EINVAL, "focal_gamma must be non-negative");
+    if (!(alpha < 0.0f || alpha <= 1.0f)) return fail(ML_EINVAL, "focal_alpha must be in [0,1] or negative to disable");
+    const bool skip = bg >= 0 && bg < GT_total;
+    const int ibg = skip ? (int)bg : (int)GT_total;
+    const int gout = (int)(GT_total - (skip ? 1 : 0));
+    const int64_t rows = L * B * Q;
+    if (gout == 0 || rows == 0) return ML_OK;
+    const int64_t blocks = (rows * 32 + 255) / 256;
+    label_cost_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        cls_logits, cls_targets, out, (int)L, (int)B, (int)Q, (int)C, (int)GT_total, ibg, gout, scale,
+        gamma, alpha, use_softmax);
+    ML_CHECK_LAUNCH("label_cost_kernel");
+    return ML_OK;
+}
+
+int ml_match(const float* costs, int64_t L, int64_t B, int64_t Q, int64_t GT_out, double inf_thresh,
+             int64_t topk, int64_t strategy_id, int64_t* pred_to_gt, int64_t* pred_round,
+             int32_t* dev_status, void*, size_t, ml_stream_t stream) {
+    if (topk < 0) return fail(ML_EINVAL, "K must be non-negative");
+    if (strategy_id < 0 || strategy_id > 3) return fail(ML_EINVAL, "Invalid matching strategy id");
+    return launch_match<float>(costs, L * B, Q, GT_out, inf_thresh, topk, strategy_id, pred_to_gt,
+                               pred_round, dev_status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ml_match_f64(const double* costs, int64_t N, int64_t Q, int64_t GT_out, double inf_thresh,
+                 int64_t topk, int64_t strategy_id, int64_t* pred_to_gt, int64_t* pred_round,
+                 int32_t* dev_status, ml_stream_t stream) {
+    if (topk < 0) return fail(ML_EINVAL, "K must be non-negative");
+    if (strategy_id < 0 || strategy_id > 3) return fail(ML_EINVAL, "Invalid matching strategy id");
+    return launch_match<double>(costs, N, Q, GT_out, inf_thresh, topk, strategy_id, pred_to_gt,
+                                pred_round, dev_status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ml_mask_matching(const ml_dims* d, const ml_params* p, const float* mask_logits,
+                     const int64_t* mask_targets, const float* cls_logits, const int64_t* cls_targets,
+                     const float* num_masks_dev, int64_t* pred_to_gt, int64_t* pred_round,
+                     float* layer_means, float* sep_costs, float* saved, int32_t* dev_status,
+                     void* workspace, size_t workspace_bytes, ml_stream_t stream) {
+    FwdPlan P;
+    int rc = validate_params(p, d ? d->C : 0);
+    if (rc) return rc;
+    if ((rc = make_plan(d, p, &P))) return rc;
+    if (P.gout == 0)
+        return fail(ML_ESHAPE, "pairwise_sigmoid_dice_loss_forward must return {3,L,B,Q,GT_out}");
+    if ((rc = check_ws(workspace, workspace_bytes, P.bytes))) return rc;
+    if (!dev_status) return fail(ML_EINVAL, "dev_status is null");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char* ws = ws_base(workspace);
+    CostArgs a = cost_args(P, p, mask_logits, mask_targets, cls_logits, cls_targets, ws, dev_status);
+    if (sep_costs) a.sep = sep_costs;
+    if ((rc = run_costs(P, a, mask_logits, st))) return rc;
+    if ((rc = launch_match<float>(a.total, (int64_t)P.L * P.B, P.Q, P.gout, p->inf_thresh,
+                                  p->topk_matches, p->strategy_id, pred_to_gt, pred_round,
+                                  dev_status, st)))
+        return rc;
+    if (P.L == 0) return ML_OK;
+    LossArgs la = loss_args(P, p);
+    la.pred_to_gt = pred_to_gt; la.sep = a.sep; la.qstat = a.qstat; la.rawI = a.rawI; la.rawT = a.rawT;
+    la.num_masks_dev = num_masks_dev; la.saved = saved; la.layer_means = layer_means;
+    loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
+    ML_CHECK_LAUNCH("loss_fwd_kernel");
+    return ML_OK;
+}
+
+int ml_count_masks(const ml_dims* d, const ml_params* p, const int64_t* mask_targets,
+                   float* num_masks_out, void* workspace, size_t workspace_bytes, ml_stream_t stream) {
+    FwdPlan P;
+    int rc;
+    if (!p) return fail(ML_EINVAL, "params is null");
+    if ((rc = make_plan(d, p, &P))) return rc;
+    if ((rc = check_ws(workspace, workspace_bytes, P.bytes))) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char* ws = ws_base(workspace);
+    int32_t* totals = reinterpret_cast<int32_t*>(ws + P.off_totals);
+    cudaError_t e = cudaMemsetAsync(totals, 0, sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
+    if (e != cudaSuccess) return cuda_fail(e, "memset totals");
+    const int64_t npix = (int64_t)P.Ht * P.Wt;
+    if (P.B > 0 && npix > 0 && P.gt_total > 0) {
+        const int bx = (int)std::min<int64_t>((npix + 255) / 256, std::max(1, 2 * sm_count() / std::max(1, P.B)));
+        const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
+        label_hist_kernel<<<dim3(bx, P.B), 256, hs, st>>>(mask_targets, npix, P.gt_total, totals);
+        ML_CHECK_LAUNCH("label_hist_kernel");
+    }
+    count_masks_kernel<<<1, 256, 0, st>>>(totals, P.B, P.gt_total, P.bg, num_masks_out);
+    ML_CHECK_LAUNCH("count_masks_kernel");
+    return ML_OK;
+}
+
+int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float* grad_mask_mean,
+                              const float* grad_dice_mean, const float* grad_cls_mean,
+                              const float* mask_logits, const int64_t* mask_targets,
+                              const float* cls_logits, const int64_t* cls_targets,
+                              const int64_t* pred_to_gt, const float* saved,
+                              const float* num_masks_dev, float* grad_mask_logits,
+                              float* grad_cls_logits, void* workspace, size_t workspace_bytes,
+                              ml_stream_t stream) {
+    int rc = validate_params(p, d ? d->C : 0);
+    if (rc) return rc;
+    if ((rc = validate_dims(d))) return rc;
+    const size_t need = ml_mask_matching_backward_workspace_size(d, p);
+    if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
+    FwdPlan P{};
+    P.L = (int)d->L; P.B = (int)d->B; P.Q = (int)d->Q; P.H = (int)d->H; P.W = (int)d->W;
+    P.Ht = (int)d->Ht; P.Wt = (int)d->Wt; P.s = P.Ht / P.H; P.C = (int)d->C;
+    P.gt_total = (int)d->GT_total;
+    const bool skip = p->background_index >= 0 && p->background_index < d->GT_total;
+    // the backward maps pred_to_gt back through background_index only when it is >= 0
+    P.bg = p->background_index >= 0 ? (int)std::min<int64_t>(p->background_index, 1 << 30) : P.gt_total;
+    P.gout = P.gt_total - (skip ? 1 : 0);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char* ws = ws_base(workspace);
+    float* coef = reinterpret_cast<float*>(ws);
+    float* stats = reinterpret_cast<float*>(ws + align256(sizeof(float) * 3 * (size_t)P.L));
+    const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
+    if (LBQ == 0) return ML_OK;
+    LossArgs la = loss_args(P, p);
+    la.mask_logits = mask_logits; la.targets = mask_targets; la.cls_logits = cls_logits;
+    la.cls_targets = cls_targets; la.pred_to_gt = pred_to_gt; la.num_masks_dev = num_masks_dev;
+    la.grad_mask = grad_mask_mean; la.grad_dice = grad_dice_mean; la.grad_cls = grad_cls_mean;
+    la.coef = coef; la.grad_mask_logits = grad_mask_logits; la.grad_cls_logits = grad_cls_logits;
+    bwd_coef_kernel<<<P.L, 256, 0, st>>>(la);
+    ML_CHECK_LAUNCH("bwd_coef_kernel");
+    const bool unc = p->uncertainty_gamma != 0.0f;
+    const bool foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
+    if (saved) {
+        la.stats_in = saved;
+    } else {
+        la.stats_out = stats;
+        la.stats_in = stats;
+        dim3 g(P.Q, P.L * P.B);
+        if (unc) bwd_stats_kernel<true><<<g, 256, 0, st>>>(la);
+        else bwd_stats_kernel<false><<<g, 256, 0, st>>>(la);
+        ML_CHECK_LAUNCH("bwd_stats_kernel");
+    }
+    const int HW = P.H * P.W;
+    const bool vec = (HW % 4 == 0) && (reinterpret_cast<uintptr_t>(mask_logits) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(grad_mask_logits) % 16 == 0);
+    const int64_t target = (int64_t)sm_count() * 8;
+    int64_t nch = (target + P.L * P.B - 1) / std::max<int64_t>(1, P.L * P.B);
+    int64_t ck = (HW + nch - 1) / nch;
+    ck = (ck + 127) / 128 * 128;
+    ck = std::max<int64_t>(256, std::min<int64_t>(ck, 8192));
+    la.chunk_cells = (int)ck;
+    const int nchunk = (int)((HW + ck - 1) / ck);
+    dim3 gg(nchunk, P.L * P.B);
+    const size_t gs = sizeof(int) * ck;
+#define ML_MG(U, F, V) mask_grad_kernel<U, F, V><<<gg, 256, gs, st>>>(la)
+    if (unc) {
+        if (foc) { if (vec) ML_MG(true, true, true); else ML_MG(true, true, false); }
+        else { if (vec) ML_MG(true, false, true); else ML_MG(true, false, false); }
+    } else {
+        if (foc) { if (vec) ML_MG(false, true, true); else ML_MG(false, true, false); }
+        else { if (vec) ML_MG(false, false, true); else ML_MG(false, false, false); }
+    }
+#undef ML_MG
+    ML_CHECK_LAUNCH("mask_grad_kernel");
+    if (P.C > 0) {
+        const int64_t blocks = (LBQ * 32 + 255) / 256;
+        cls_grad_kernel<<<(unsigned)blocks, 256, 0, st>>>(la);
+        ML_CHECK_LAUNCH("cls_grad_kernel");
+    }
+    return ML_OK;
+}
+
+}  // extern "C"

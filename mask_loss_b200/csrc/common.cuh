@@ -1,0 +1,151 @@
+// common.cuh -- shared device helpers for the mask_loss_b200 kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mask_loss_b200.h"
+
+#define ML_INLINE __device__ __forceinline__
+
+namespace mlb {
+
+constexpr int kNone = -1;   // cell/pixel carries no output column
+constexpr int kMixed = -2;  // cell holds more than one label (s > 1 only)
+
+// ----------------------------------------------------------------------------
+// Label -> output column (GT_out index).  The background column is dropped
+// and later columns shift down by one (src/cuda/utils.cuh:38-40 inverted);
+// labels outside [0, GT_total) belong to no column (src/cuda/utils.cuh:27).
+// `bg` is GT_total when no column is dropped.
+// ----------------------------------------------------------------------------
+ML_INLINE int label_to_col(int64_t lab, int gt_total, int bg) {
+    if (lab < 0 || lab >= gt_total || lab == bg) return kNone;
+    int l = static_cast<int>(lab);
+    return l > bg ? l - 1 : l;
+}
+
+// ----------------------------------------------------------------------------
+// Element math.  Logit x -> e = exp(-|x|), log1p(e), sigmoid p.
+// MUFU forms (__expf, __logf, __fdividef); accuracy is far inside the 1e-4
+// relative tolerance for the sums they feed.
+// ----------------------------------------------------------------------------
+struct Elem {
+    float p;      // sigmoid(x)
+    float sp;     // log1p(exp(-|x|))
+    float neg;    // softplus(x)  = BCE against 0
+    float pos;    // softplus(-x) = BCE against 1
+};
+
+ML_INLINE Elem elem(float x) {
+    Elem r;
+    const float ax = fabsf(x);
+    const float e = __expf(-ax);
+    const float d = 1.0f + e;
+    r.sp = __logf(d);
+    const float inv = __fdividef(1.0f, d);
+    r.p = x >= 0.0f ? inv : e * inv;
+    r.neg = r.sp + fmaxf(x, 0.0f);
+    r.pos = r.sp + fmaxf(-x, 0.0f);
+    return r;
+}
+
+// Entropy weight clamp(H(p)^gamma, gmin, 1).  Mirrors
+// src/cuda/pw_mask.cu:131-136 including its fp32 saturation: where the
+// clamped p rounds to 1.0f the entropy is NaN and fmaxf(NaN, gmin) = gmin.
+ML_INLINE float unc_weight(float p, float ug, float ugmin) {
+    const float pc = fminf(fmaxf(p, 1e-12f), 1.0f - 1e-12f);
+    if (pc >= 1.0f) return fminf(1.0f, ugmin);
+    float h = -(pc * __logf(pc) + (1.0f - pc) * __logf(1.0f - pc)) * 1.4426950408889634f;
+    float w = __powf(h, ug);
+    w = fmaxf(w, ugmin);
+    return fminf(1.0f, w);
+}
+
+// Focal/alpha modulation of the BCE pieces (src/cuda/pw_mask.cu:242-247).
+struct Focal {
+    float alpha_pos, alpha_neg, gamma;
+    bool use_gamma;
+};
+
+ML_INLINE Focal make_focal(float gamma, float alpha) {
+    Focal f;
+    f.alpha_pos = alpha >= 0.0f ? alpha : 1.0f;
+    f.alpha_neg = alpha >= 0.0f ? 1.0f - alpha : 1.0f;
+    f.gamma = gamma;
+    f.use_gamma = gamma > 0.0f;
+    return f;
+}
+
+ML_INLINE float focal_neg(const Focal& f, const Elem& t) {
+    const float m = f.use_gamma ? __powf(t.p, f.gamma) : 1.0f;
+    return f.alpha_neg * m * t.neg;
+}
+
+ML_INLINE float focal_pos(const Focal& f, const Elem& t) {
+    const float m = f.use_gamma ? __powf(1.0f - t.p, f.gamma) : 1.0f;
+    return f.alpha_pos * m * t.pos;
+}
+
+// ----------------------------------------------------------------------------
+// Warp / block reductions (fixed order -> deterministic).
+// ----------------------------------------------------------------------------
+ML_INLINE float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+ML_INLINE float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ----------------------------------------------------------------------------
+// mbarrier + 1-D bulk copy (TMA engine, no tensor map): global -> shared.
+// ----------------------------------------------------------------------------
+ML_INLINE uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+ML_INLINE void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+ML_INLINE void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+ML_INLINE void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+ML_INLINE void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded wait on phase `parity`.  Returns false when the bound is hit.
+ML_INLINE bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t max_iters = 1u << 26) {
+    const uint32_t a = smem_u32(bar);
+    for (uint32_t it = 0; it < max_iters; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n"
+            " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// cp.async.bulk global->shared, completion signalled on `bar` (tx bytes).
+ML_INLINE void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+}  // namespace mlb

@@ -1,0 +1,125 @@
+// kernels.cuh -- kernel argument blocks and declarations shared by the
+// launchers in capi.cu.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace mlb {
+
+constexpr int KC = 32;            // cells per pipeline tile (128-byte TMA rows)
+constexpr int kStages = 4;        // TMA pipeline depth
+constexpr int kHistSmemMax = 8192;
+constexpr int kQStat = 5;         // per-query: P, Wtot, um_mask, um_dice, um_cls
+constexpr int kSaved = 4;         // saved for backward: P, T, I, Wtot
+
+struct CostArgs {
+    const float* logits;
+    const int64_t* targets;
+    const float* cls_logits;
+    const int64_t* cls_targets;
+    const int32_t* totals;   // (B, GT_total)
+    float* part;             // chunk partials
+    float* sep;              // (3,L,B,Q,G) or null
+    float* total;            // (L,B,Q,G) or null
+    float* rawI;             // (L,B,Q,G) or null
+    float* rawT;             // (L,B,Q,G) or null
+    float* qstat;            // (L,B,Q,kQStat)
+    int32_t* status;
+    int L, B, Q, H, W, Ht, Wt, s, C;
+    int gt_total, gout, bg;  // bg == gt_total when no column is dropped
+    int qrows, qrows_pad, nqt;
+    int gp, ngr;             // column-range width and count
+    int chunk_cells, nchunk;
+    int part_stride;         // floats per CTA partial
+    float smooth, sigmoid_scale, dice_scale, cls_scale;
+    float ug, ugmin;
+    float mask_gamma, mask_alpha, cls_gamma, cls_alpha;
+    float area_scale;
+    int normalize_uncertainty;
+    int use_softmax, force_cls, has_void, void_index;
+};
+
+__global__ void label_hist_kernel(const int64_t* __restrict__ targets, int64_t npix, int gt_total,
+                                  int32_t* __restrict__ totals);
+
+template <bool UNC, bool FOC, bool TMA>
+__global__ void cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a);
+
+template <bool UNC>
+__global__ void cost_finalize_kernel(CostArgs a);
+
+}  // namespace mlb
+
+namespace mlb {
+
+template <typename CT>
+struct MatchArgs {
+    const CT* costs;       // (N, Q, G)
+    int64_t* pred_to_gt;   // (N, Q)
+    int64_t* pred_round;   // (N, Q)
+    int32_t* status;
+    int Q, G;
+    double inf_thresh;
+    int64_t topk;
+    int strategy;
+    int stage_cost;
+};
+
+template <typename CT>
+__global__ void match_kernel(MatchArgs<CT> a);
+
+size_t match_smem_bytes(int Q, int G, size_t cost_elem, bool stage);
+
+}  // namespace mlb
+
+namespace mlb {
+
+struct LossArgs {
+    // shapes
+    int L, B, Q, H, W, Ht, Wt, s, C, G, gt_total, bg;
+    int chunk_cells;
+    // inputs
+    const float* mask_logits;
+    const int64_t* targets;
+    const float* cls_logits;
+    const int64_t* cls_targets;
+    const int64_t* pred_to_gt;
+    const float* sep;        // (3,L,B,Q,G)
+    const float* qstat;      // (L,B,Q,kQStat)
+    const float* rawI;
+    const float* rawT;
+    const float* num_masks_dev;
+    const float* grad_mask;  // (L,)
+    const float* grad_dice;
+    const float* grad_cls;
+    const float* stats_in;   // (L,B,Q,kSaved)
+    // outputs
+    float* saved;            // (L,B,Q,kSaved) or null
+    float* layer_means;      // (3,L)
+    float* coef;             // (L,3)
+    float* stats_out;        // (L,B,Q,kSaved)
+    float* grad_mask_logits;
+    float* grad_cls_logits;
+    // scalars
+    float num_masks;
+    float smooth, sigmoid_scale, dice_scale, cls_scale;
+    float ug, ugmin, mask_gamma, mask_alpha, cls_gamma, cls_alpha;
+    int force_masks, force_cls, has_void, void_index, use_softmax, normalize_uncertainty;
+};
+
+__global__ void loss_fwd_kernel(LossArgs a);
+__global__ void count_masks_kernel(const int32_t* totals, int B, int gt_total, int bg, float* out);
+__global__ void bwd_coef_kernel(LossArgs a);
+template <bool UNC> __global__ void bwd_stats_kernel(LossArgs a);
+template <bool UNC, bool FOC, bool VEC> __global__ void mask_grad_kernel(LossArgs a);
+__global__ void cls_grad_kernel(LossArgs a);
+
+}  // namespace mlb
+
+namespace mlb {
+__global__ void label_cost_kernel(const float* z_all, const int64_t* y_all, float* out, int L, int B,
+                                  int Q, int C, int gt_total, int bg, int gout, float scale,
+                                  float gamma, float alpha, int use_softmax);
+}  // namespace mlb

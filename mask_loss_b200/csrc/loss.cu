@@ -1,0 +1,361 @@
+// loss.cu -- matched-loss forward and the backward of the matching loss.
+//
+// Forward: replaces mask_matching_forward (src/cuda/mask_matching_forward.cu:
+// 21-586).  The matched terms are gathered from the cost slices (the
+// reference does the same with float atomics, :63-71); the unmatched terms
+// were already reduced per query by cost_finalize_kernel, so this kernel
+// touches only O(L*B*Q) numbers.  Sums use a fixed-order block reduction, so
+// the layer means are deterministic.
+//
+// Backward: replaces mask_matching_backward (src/cuda/mask_matching_backward.cu:
+// 21-621).  With the forward's saved per-query statistics the mask gradient is
+// a single streaming pass: read logits once (128-bit loads), write the
+// gradient once, label codes staged in shared memory per cell chunk and
+// reused by every query of the image.  Without them (the standalone binding
+// call) a statistics pass re-reads the logits first, like the reference.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mlb {
+
+// ---------------------------------------------------------------------------
+// Block-wide fixed-order sum of NV values per thread (blockDim.x <= 1024).
+// ---------------------------------------------------------------------------
+template <int NV>
+ML_INLINE void block_sum(float (&v)[NV], float* sh /* [32*NV] */) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = warp_sum(v[i]);
+    __syncthreads();
+    if (lane == 0)
+#pragma unroll
+        for (int i = 0; i < NV; ++i) sh[warp * NV + i] = v[i];
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            float x = lane < nw ? sh[lane * NV + i] : 0.0f;
+            v[i] = warp_sum(x);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+#pragma unroll
+        for (int i = 0; i < NV; ++i) sh[i] = v[i];
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = sh[i];
+    __syncthreads();
+}
+
+// Denominators (src/cuda/mask_matching_forward.cu:549-578 and
+// src/cuda/mask_matching_backward.cu:483-508).
+ML_INLINE void denominators(const LossArgs& a, float matched, float* md, float* cd) {
+    const float tot = (float)a.B * (float)a.Q;
+    float nm = a.num_masks_dev ? *a.num_masks_dev : a.num_masks;
+    const bool has_nm = nm > 0.0f;
+    float m = a.force_masks ? tot : (has_nm ? nm : matched);
+    float c = (a.force_cls || a.has_void) ? tot : (has_nm ? nm : matched);
+    *md = fmaxf(m, 1.0f);
+    *cd = fmaxf(c, 1.0f);
+}
+
+// ---------------------------------------------------------------------------
+// Forward: grid = L, block = 512.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) loss_fwd_kernel(LossArgs a) {
+    __shared__ float sh[32 * 4];
+    const int l = blockIdx.x;
+    const int n = a.B * a.Q;
+    const int64_t G = a.G;
+    const int64_t slice = (int64_t)a.L * a.B * a.Q * G;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // mask, dice, cls, matched
+    const bool need_cls = a.force_cls || a.has_void;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int64_t qi = (int64_t)l * n + i;
+        const int64_t g = a.pred_to_gt[qi];
+        const float* qs = a.qstat + qi * kQStat;
+        float sv[kSaved] = {qs[0], 0.0f, 0.0f, qs[1]};
+        if (g >= 0) {
+            const int64_t o = qi * G + g;
+            acc[0] += a.sep[o];
+            acc[1] += a.sep[slice + o];
+            acc[2] += a.sep[2 * slice + o];
+            acc[3] += 1.0f;
+            sv[1] = a.rawT[o];
+            sv[2] = a.rawI[o];
+        } else {
+            if (a.force_masks) { acc[0] += qs[2]; acc[1] += qs[3]; }
+            if (need_cls) acc[2] += qs[4];
+        }
+        if (a.saved)
+#pragma unroll
+            for (int k = 0; k < kSaved; ++k) a.saved[qi * kSaved + k] = sv[k];
+    }
+    block_sum<4>(acc, sh);
+    if (threadIdx.x == 0) {
+        float md, cd;
+        denominators(a, acc[3], &md, &cd);
+        a.layer_means[l] = acc[0] / md;
+        a.layer_means[a.L + l] = acc[1] / md;
+        a.layer_means[2 * a.L + l] = acc[2] / cd;
+    }
+}
+
+// Sum of present, non-background GT columns over the batch (num_masks).
+__global__ void count_masks_kernel(const int32_t* totals, int B, int gt_total, int bg, float* out) {
+    __shared__ float sh[32];
+    float v[1] = {0.0f};
+    for (int i = threadIdx.x; i < B * gt_total; i += blockDim.x) {
+        const int g = i % gt_total;
+        if (g != bg && totals[i] > 0) v[0] += 1.0f;
+    }
+    block_sum<1>(v, sh);
+    if (threadIdx.x == 0) *out = v[0];
+}
+
+// ---------------------------------------------------------------------------
+// Backward coefficients per layer: grid = L, block = 256.
+// coef[l] = {g_mask/md, g_dice/md, g_cls*cls_scale/cd}
+// ---------------------------------------------------------------------------
+__global__ void bwd_coef_kernel(LossArgs a) {
+    __shared__ float sh[32];
+    const int l = blockIdx.x;
+    const int n = a.B * a.Q;
+    float v[1] = {0.0f};
+    for (int i = threadIdx.x; i < n; i += blockDim.x) v[0] += a.pred_to_gt[(int64_t)l * n + i] >= 0;
+    block_sum<1>(v, sh);
+    if (threadIdx.x == 0) {
+        float md, cd;
+        denominators(a, v[0], &md, &cd);
+        const float im = 1.0f / md, ic = 1.0f / cd;
+        a.coef[l * 3 + 0] = a.grad_mask[l] * im;
+        a.coef[l * 3 + 1] = a.grad_dice[l] * im;
+        a.coef[l * 3 + 2] = a.grad_cls[l] * (ic * a.cls_scale);
+    }
+}
+
+// Count of pixels labelled `ga` in low-res cell `cell` (s x s block).
+ML_INLINE float cell_count(const int64_t* tb, int cell, int W, int Wt, int s, int64_t ga) {
+    const int ci = cell / W, cj = cell - ci * W;
+    const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
+    int c = 0;
+    for (int dy = 0; dy < s; ++dy)
+        for (int dx = 0; dx < s; ++dx) c += r0[(int64_t)dy * Wt + dx] == ga;
+    return (float)c;
+}
+
+// ---------------------------------------------------------------------------
+// Statistics pass for the standalone backward (no saved statistics):
+// grid = (Q, L*B), block = 256.  Mirrors the first loop of
+// src/cuda/mask_matching_backward.cu:110-138 with a fixed-order reduction.
+// ---------------------------------------------------------------------------
+template <bool UNC>
+__global__ void __launch_bounds__(256) bwd_stats_kernel(LossArgs a) {
+    __shared__ float sh[32 * 4];
+    const int q = blockIdx.x, lb = blockIdx.y, b = lb % a.B;
+    const int64_t qi = (int64_t)lb * a.Q + q;
+    const int64_t og = a.pred_to_gt[qi];
+    const int64_t ga = og + (og >= a.bg ? 1 : 0);
+    const bool matched = og >= 0 && ga < a.gt_total;
+    if (!matched && !a.force_masks) return;
+    const int HW = a.H * a.W;
+    const float N2 = (float)(a.s * a.s);
+    const float* x = a.mask_logits + qi * HW;
+    const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};  // sum w p, sum w t, sum w p t, sum w
+    for (int j = threadIdx.x; j < HW; j += blockDim.x) {
+        const Elem e = elem(x[j]);
+        const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
+        const float t = matched ? cell_count(tb, j, a.W, a.Wt, a.s, ga) : 0.0f;
+        v[0] += w * e.p; v[1] += w * t; v[2] += w * e.p * t; v[3] += w;
+    }
+    block_sum<4>(v, sh);
+    if (threadIdx.x == 0) {
+        float wt = a.normalize_uncertainty ? v[3] * N2 : N2 * (float)HW;
+        wt = fmaxf(wt, 1e-12f);
+        float* o = a.stats_out + qi * kSaved;
+        o[0] = v[0] * N2; o[1] = v[1]; o[2] = v[2]; o[3] = wt;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Mask-logit gradient: grid = (nchunk, L*B), block = 256.  One pass over the
+// logits of every query of image b in the block's cell chunk.  Formula of
+// src/cuda/mask_matching_backward.cu:169-215.
+// ---------------------------------------------------------------------------
+template <bool UNC, bool FOC, bool VEC>
+__global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
+    extern __shared__ int gcode[];  // [chunk] pure column / kNone / kMixed
+    const int lb = blockIdx.y, l = lb / a.B, b = lb % a.B;
+    const int HW = a.H * a.W;
+    const int c0 = blockIdx.x * a.chunk_cells;
+    const int nc = min(a.chunk_cells, HW - c0);
+    const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
+    const int s = a.s, s2 = s * s;
+    for (int k = threadIdx.x; k < nc; k += blockDim.x) {
+        const int cell = c0 + k;
+        int c;
+        if (s == 1) {
+            c = label_to_col(tb[cell], a.gt_total, a.bg);
+        } else {
+            const int ci = cell / a.W, cj = cell - ci * a.W;
+            const int64_t* r0 = tb + (int64_t)(ci * s) * a.Wt + (int64_t)cj * s;
+            c = label_to_col(r0[0], a.gt_total, a.bg);
+            for (int pp = 1; pp < s2 && c != kMixed; ++pp) {
+                const int cc = label_to_col(r0[(int64_t)(pp / s) * a.Wt + (pp % s)], a.gt_total, a.bg);
+                if (cc != c) c = kMixed;
+            }
+        }
+        gcode[k] = c;
+    }
+    __syncthreads();
+    const float N2 = (float)s2;
+    const Focal f = make_focal(a.mask_gamma, a.mask_alpha);
+    const float mcoef = a.coef[l * 3 + 0], dcoef = a.coef[l * 3 + 1];
+    for (int q = 0; q < a.Q; ++q) {
+        const int64_t qi = (int64_t)lb * a.Q + q;
+        const int64_t og = a.pred_to_gt[qi];
+        const int64_t ga = og + (og >= a.bg ? 1 : 0);
+        const bool matched = og >= 0 && ga < a.gt_total;
+        const int gcol = matched ? (int)og : -100;
+        float* gout = a.grad_mask_logits + qi * HW + c0;
+        const float* xin = a.mask_logits + qi * HW + c0;
+        const bool active = (matched || a.force_masks) && !(mcoef == 0.0f && dcoef == 0.0f);
+        if (!active) {
+            if (VEC) {
+                for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4)
+                    *reinterpret_cast<float4*>(gout + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+                for (int k = threadIdx.x; k < nc; k += blockDim.x) gout[k] = 0.0f;
+            }
+            continue;
+        }
+        const float* sv = a.stats_in + qi * kSaved;
+        const float P = sv[0], T = matched ? sv[1] : 0.0f, I = matched ? sv[2] : 0.0f, Wt = sv[3];
+        const float sf = a.sigmoid_scale / Wt;
+        const float den = P + T + a.smooth;
+        const float num = 2.0f * I + a.smooth;
+        const float inv_d2 = 1.0f / fmaxf(den * den, 1e-20f);
+        const float two_den = 2.0f * den;
+        auto g1 = [&](float x, int k) -> float {
+            const Elem e = elem(x);
+            const float om = 1.0f - e.p, pp = e.p * om;
+            const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
+            const int cc = gcode[k];
+            float t = 0.0f;
+            if (cc == gcol) t = N2;
+            else if (cc == kMixed && matched) t = cell_count(tb, c0 + k, a.W, a.Wt, s, ga);
+            const float ncnt = fmaxf(N2 - t, 0.0f);
+            float gs;
+            if (FOC) {
+                const float mp = f.use_gamma ? __powf(om, f.gamma) : 1.0f;
+                const float mn = f.use_gamma ? __powf(e.p, f.gamma) : 1.0f;
+                const float gpos = -w * f.alpha_pos * t * mp * (f.gamma * e.p * e.pos + om);
+                const float gneg = w * f.alpha_neg * ncnt * mn * (f.gamma * om * e.neg + e.p);
+                gs = (gpos + gneg) * sf;
+            } else {
+                gs = (w * (ncnt * e.p - t * om)) * sf;
+            }
+            const float gd = (num * (w * pp * N2) - two_den * (w * pp * t)) * inv_d2 * a.dice_scale;
+            return mcoef * gs + dcoef * gd;
+        };
+        if (VEC) {
+            for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4) {
+                const float4 xv = *reinterpret_cast<const float4*>(xin + k);
+                float4 r;
+                r.x = g1(xv.x, k); r.y = g1(xv.y, k + 1); r.z = g1(xv.z, k + 2); r.w = g1(xv.w, k + 3);
+                *reinterpret_cast<float4*>(gout + k) = r;
+            }
+        } else {
+            for (int k = threadIdx.x; k < nc; k += blockDim.x) gout[k] = g1(xin[k], k);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Class-logit gradient: one warp per (l,b,q) row, block = 256.
+// src/cuda/mask_matching_backward.cu:218-376.  Every element is written.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) cls_grad_kernel(LossArgs a) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t rows = (int64_t)a.L * a.B * a.Q;
+    if (warp >= rows) return;
+    const int64_t qi = warp;
+    const int l = (int)(qi / ((int64_t)a.B * a.Q));
+    const int b = (int)((qi / a.Q) % a.B);
+    const int C = a.C;
+    const float* z = a.cls_logits + qi * C;
+    float* gz = a.grad_cls_logits + qi * C;
+    const int64_t og = a.pred_to_gt[qi];
+    const int64_t ga = og + (og >= a.bg ? 1 : 0);
+    const bool matched = og >= 0 && ga < a.gt_total;
+    const bool need = a.force_cls || a.has_void;
+    const float base = a.coef[l * 3 + 2];
+    int y = -1;
+    bool zero = !(matched || need) || base == 0.0f;
+    if (!zero && matched) {
+        const int64_t y64 = a.cls_targets[(int64_t)b * a.gt_total + ga];
+        if (y64 < 0 || y64 >= C) zero = true;
+        else y = (int)y64;
+    }
+    if (zero) {
+        for (int c = lane; c < C; c += 32) gz[c] = 0.0f;
+        return;
+    }
+    const float invC = 1.0f / (float)C;
+    if (a.use_softmax) {
+        if (matched || (a.force_cls && a.has_void)) {
+            const int ti = matched ? y : a.void_index;
+            float m = -INFINITY;
+            for (int c = lane; c < C; c += 32) m = fmaxf(m, z[c]);
+            m = warp_max(m);
+            float se = 0.0f;
+            for (int c = lane; c < C; c += 32) se += __expf(z[c] - m);
+            se = warp_sum(se);
+            const float inv = se > 0.0f ? 1.0f / se : 0.0f;
+            for (int c = lane; c < C; c += 32) {
+                float g = __expf(z[c] - m) * inv;
+                if (c == ti) g -= 1.0f;
+                gz[c] = base * g;
+            }
+        } else {  // void present, not forced: sigmoid pull on the void logit
+            for (int c = lane; c < C; c += 32) {
+                float g = 0.0f;
+                if (c == a.void_index) g = base * (elem(z[c]).p - 1.0f);
+                gz[c] = g;
+            }
+        }
+        return;
+    }
+    const Focal f = make_focal(a.cls_gamma, a.cls_alpha);
+    for (int c = lane; c < C; c += 32) {
+        const Elem e = elem(z[c]);
+        const float om = 1.0f - e.p;
+        const float mp = f.use_gamma ? __powf(om, f.gamma) : 1.0f;
+        const float mn = f.use_gamma ? __powf(e.p, f.gamma) : 1.0f;
+        const float gpos = -f.alpha_pos * mp * (f.gamma * e.p * e.pos + om);
+        const float gneg = f.alpha_neg * mn * (f.gamma * om * e.neg + e.p);
+        const bool is_void = a.has_void && c == a.void_index;
+        float g;
+        if (matched) g = base * invC * (c == y ? gpos : gneg);
+        else if (a.force_cls) g = base * invC * (is_void ? gpos : gneg);
+        else if (is_void) g = base * gpos;
+        else g = 0.0f;
+        gz[c] = g;
+    }
+}
+
+template __global__ void bwd_stats_kernel<false>(LossArgs);
+template __global__ void bwd_stats_kernel<true>(LossArgs);
+template __global__ void mask_grad_kernel<false, false, false>(LossArgs);
+template __global__ void mask_grad_kernel<false, false, true>(LossArgs);
+template __global__ void mask_grad_kernel<false, true, false>(LossArgs);
+template __global__ void mask_grad_kernel<false, true, true>(LossArgs);
+template __global__ void mask_grad_kernel<true, false, false>(LossArgs);
+template __global__ void mask_grad_kernel<true, false, true>(LossArgs);
+template __global__ void mask_grad_kernel<true, true, false>(LossArgs);
+template __global__ void mask_grad_kernel<true, true, true>(LossArgs);
+
+}  // namespace mlb

@@ -1,0 +1,429 @@
+"""The op surface of the reference extension module ``mask_loss``.
+
+Same op names, positional argument order, meaning and return values as the
+``PYBIND11_MODULE`` in src/bindings.cpp:157-169 of AndyBarcia/mask_loss, so
+``sys.modules["mask_loss"] = mask_loss_b200.ops`` makes the reference's own
+``functions/`` wrappers run on this implementation.  Argument checks raise
+``RuntimeError`` with the reference's TORCH_CHECK messages.
+
+Every op runs on ``torch.cuda.current_stream()`` through the C ABI of
+``libmask_loss_b200.so``; there is no CPU path.  Nothing here synchronises the
+device: the assignment solver's failure flag is checked without blocking (the
+next op call, or :func:`check_status`, raises if an earlier solve failed), and
+``MASK_LOSS_B200_SYNC_CHECK=1`` makes every call check it synchronously.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import List, Optional
+
+import torch
+
+from . import _lib
+
+_SYNC = os.environ.get("MASK_LOSS_B200_SYNC_CHECK", "0") == "1"
+_pending: list = []  # (event, pinned int32 flag, message) of earlier device checks
+
+
+def _lib_handle():
+    return _lib.load()
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _check_input(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def _check_dtype(t: torch.Tensor, dtype, name: str) -> None:
+    if t.dtype != dtype:
+        raise RuntimeError(f"{name} must be {str(dtype).replace('torch.', '')}")
+
+
+def check_status(block: bool = False) -> None:
+    """Raise if an earlier on-device assignment solve reported failure."""
+    keep = []
+    err = None
+    for ev, host, msg in _pending:
+        if block:
+            ev.synchronize()
+        if ev.query():
+            if int(host.item()) != 0 and err is None:
+                err = RuntimeError(msg)
+            _pinned.append(host)
+        else:
+            keep.append((ev, host, msg))
+    _pending[:] = keep
+    if err is not None:
+        raise err
+
+
+_pinned = []  # pool of 1-element pinned int32 buffers, reused once their event completed
+
+
+def _pinned_slot() -> torch.Tensor:
+    if _pinned:
+        return _pinned.pop()
+    return torch.empty(1, dtype=torch.int32, pin_memory=True)
+
+
+def _defer(flag_i32: torch.Tensor, message: str) -> None:
+    if len(_pending) > 64:
+        check_status()
+    host = _pinned_slot()
+    host.copy_(flag_i32, non_blocking=True)
+    ev = torch.cuda.Event()
+    ev.record(torch.cuda.current_stream(flag_i32.device))
+    _pending.append((ev, host, message))
+    if _SYNC:
+        check_status(block=True)
+
+
+def defer_check(flag: torch.Tensor, message: str) -> None:
+    """Raise ``message`` from a later op call (or check_status) if the device
+    boolean ``flag`` is true -- argument checks without a host sync."""
+    _defer(flag.reshape(1).to(torch.int32), message)
+
+
+def _track_status(status: torch.Tensor) -> None:
+    _defer(status, "Hungarian: no augmenting path found; check costs/inf_thresh.")
+
+
+def _params(smooth=1.0, sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0, background_index=-1,
+            uncertainty_gamma=1.0, uncertainty_gamma_min=0.05, inf_thresh=1e30, num_masks=-1.0,
+            force_unmatched_class_to_background=False, force_unmatched_masks_to_empty=False,
+            topk_matches=1, strategy_id=0, mask_gamma=0.0, mask_alpha=-1.0, cls_gamma=0.0,
+            cls_alpha=-1.0, void_class_index=-1, use_softmax_label_loss=False,
+            normalize_uncertainty=True) -> _lib.Params:
+    return _lib.Params(float(smooth), float(sigmoid_scale), float(dice_scale), float(cls_scale),
+                       int(background_index), float(uncertainty_gamma),
+                       float(uncertainty_gamma_min), float(inf_thresh), float(num_masks),
+                       int(bool(force_unmatched_class_to_background)),
+                       int(bool(force_unmatched_masks_to_empty)), int(topk_matches),
+                       int(strategy_id), float(mask_gamma), float(mask_alpha), float(cls_gamma),
+                       float(cls_alpha), int(void_class_index), int(bool(use_softmax_label_loss)),
+                       int(bool(normalize_uncertainty)))
+
+
+def _dims(mask_logits, mask_targets, cls_logits, cls_targets) -> _lib.Dims:
+    L, B, Q, H, W = mask_logits.shape
+    _, Ht, Wt = mask_targets.shape
+    return _lib.Dims(L, B, Q, H, W, Ht, Wt, cls_logits.shape[3], cls_targets.shape[1])
+
+
+def _check_quad(mask_logits, mask_targets, cls_logits, cls_targets):
+    for t, n in ((mask_logits, "mask_logits"), (mask_targets, "mask_targets"),
+                 (cls_logits, "cls_logits"), (cls_targets, "cls_targets")):
+        _check_input(t, n)
+    if mask_logits.dim() != 5:
+        raise RuntimeError("mask_logits must be (L,B,Q,H,W)")
+    if mask_targets.dim() != 3:
+        raise RuntimeError("mask_targets must be (B,H_t,W_t)")
+    if cls_logits.dim() != 4:
+        raise RuntimeError("cls_logits must be (L,B,Q,C)")
+    if cls_targets.dim() != 2:
+        raise RuntimeError("cls_targets must be (B,GT)")
+    _check_dtype(mask_logits, torch.float32, "mask_logits")
+    _check_dtype(cls_logits, torch.float32, "cls_logits")
+    _check_dtype(mask_targets, torch.int64, "mask_targets")
+    _check_dtype(cls_targets, torch.int64, "cls_targets")
+    L, B, Q = mask_logits.shape[:3]
+    if mask_targets.shape[0] != B or cls_targets.shape[0] != B:
+        raise RuntimeError("batch size mismatch between logits and targets")
+    if tuple(cls_logits.shape[:3]) != (L, B, Q):
+        raise RuntimeError("cls_logits must match mask logits dimensions")
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+# ---------------------------------------------------------------------------
+# pairwise_mask_loss_forward (src/bindings.cpp:64-82)
+# ---------------------------------------------------------------------------
+def pairwise_mask_loss_forward(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
+                               sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0,
+                               background_index=-1, uncertainty_gamma=1.0,
+                               uncertainty_gamma_min=0.05, mask_gamma=0.0, mask_alpha=-1.0,
+                               cls_gamma=0.0, cls_alpha=-1.0, use_softmax_label_loss=False,
+                               normalize_uncertainty=True) -> torch.Tensor:
+    """(3,L,B,Q,GT_out) sigmoid-CE, dice and label costs; (L,B,Q,0) when no
+    column is left (src/cuda/pw_mask.cu:396-398)."""
+    _check_quad(mask_logits, mask_targets, cls_logits, cls_targets)
+    lib = _lib_handle()
+    d = _dims(mask_logits, mask_targets, cls_logits, cls_targets)
+    p = _params(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, uncertainty_gamma,
+                uncertainty_gamma_min, mask_gamma=mask_gamma, mask_alpha=mask_alpha,
+                cls_gamma=cls_gamma, cls_alpha=cls_alpha,
+                use_softmax_label_loss=use_softmax_label_loss,
+                normalize_uncertainty=normalize_uncertainty)
+    L, B, Q = mask_logits.shape[:3]
+    G = lib.ml_gt_out(d.GT_total, p.background_index)
+    if G == 0:
+        return torch.zeros((L, B, Q, 0), dtype=torch.float32, device=mask_logits.device)
+    out = torch.empty((3, L, B, Q, G), dtype=torch.float32, device=mask_logits.device)
+    nbytes = lib.ml_mask_matching_workspace_size(ctypes.byref(d), ctypes.byref(p))
+    if nbytes == 0:
+        raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
+    ws = _workspace(nbytes, mask_logits.device)
+    _lib.check(lib.ml_pairwise_mask_loss_forward(
+        ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits),
+        _ptr(cls_targets), _ptr(out), _ptr(ws), ws.numel(), _stream(mask_logits.device)))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# mask_matching (src/bindings.cpp:86-111) and its extended form
+# ---------------------------------------------------------------------------
+def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
+                     sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0, background_index=-1,
+                     uncertainty_gamma=1.0, uncertainty_gamma_min=0.05, inf_thresh=1e30,
+                     num_masks=-1.0, force_unmatched_class_to_background=False,
+                     force_unmatched_masks_to_empty=False, topk_matches=1, strategy_id=0,
+                     mask_gamma=0.0, mask_alpha=-1.0, cls_gamma=0.0, cls_alpha=-1.0,
+                     void_class_index=-1, use_softmax_label_loss=False, normalize_uncertainty=True,
+                     *, num_masks_dev: Optional[torch.Tensor] = None, want_saved: bool = False,
+                     want_costs: bool = False):
+    """``mask_matching`` plus the extras this implementation offers: a device
+    ``num_masks_dev`` (fp32 scalar, e.g. after an all-reduce), the per-query
+    statistics the backward can reuse (``saved``) and the cost slices.
+
+    Returns (pred_to_gt, pred_round, layer_means(3,L), saved or None, costs or None)."""
+    check_status()
+    _check_quad(mask_logits, mask_targets, cls_logits, cls_targets)
+    if topk_matches < 0:
+        raise RuntimeError("K must be non-negative")
+    if not 0 <= strategy_id <= 3:
+        raise RuntimeError("Invalid matching strategy id")
+    lib = _lib_handle()
+    dev = mask_logits.device
+    d = _dims(mask_logits, mask_targets, cls_logits, cls_targets)
+    p = _params(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, uncertainty_gamma,
+                uncertainty_gamma_min, inf_thresh, num_masks, force_unmatched_class_to_background,
+                force_unmatched_masks_to_empty, topk_matches, strategy_id, mask_gamma, mask_alpha,
+                cls_gamma, cls_alpha, void_class_index, use_softmax_label_loss,
+                normalize_uncertainty)
+    L, B, Q = mask_logits.shape[:3]
+    G = lib.ml_gt_out(d.GT_total, p.background_index)
+    p2g = torch.empty((L, B, Q), dtype=torch.int64, device=dev)
+    prd = torch.empty((L, B, Q), dtype=torch.int64, device=dev)
+    means = torch.empty((3, L), dtype=torch.float32, device=dev)
+    saved = torch.empty((L, B, Q, 4), dtype=torch.float32, device=dev) if want_saved else None
+    costs = (torch.empty((3, L, B, Q, G), dtype=torch.float32, device=dev)
+             if want_costs and G > 0 else None)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    nbytes = lib.ml_mask_matching_workspace_size(ctypes.byref(d), ctypes.byref(p))
+    if nbytes == 0:
+        raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
+    ws = _workspace(nbytes, dev)
+    if num_masks_dev is not None:
+        _check_input(num_masks_dev, "num_masks_dev")
+        _check_dtype(num_masks_dev, torch.float32, "num_masks_dev")
+    _lib.check(lib.ml_mask_matching(
+        ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits),
+        _ptr(cls_targets), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd), _ptr(means), _ptr(costs),
+        _ptr(saved), _ptr(status), _ptr(ws), ws.numel(), _stream(dev)))
+    _track_status(status)
+    return p2g, prd, means, saved, costs
+
+
+def mask_matching(mask_logits, mask_targets, cls_logits, cls_targets, smooth, sigmoid_scale=1.0,
+                  dice_scale=1.0, cls_scale=1.0, background_index=-1, uncertainty_gamma=1.0,
+                  uncertainty_gamma_min=0.05, inf_thresh=1e30, num_masks=-1.0,
+                  force_unmatched_class_to_background=False, force_unmatched_masks_to_empty=False,
+                  topk_matches=1, strategy_id=0, mask_gamma=0.0, mask_alpha=-1.0, cls_gamma=0.0,
+                  cls_alpha=-1.0, void_class_index=-1, use_softmax_label_loss=False,
+                  normalize_uncertainty=True) -> List[torch.Tensor]:
+    """[pred_to_gt, pred_round, layer_mask_mean, layer_dice_mean, layer_cls_mean]
+    (src/cpu/matching.cpp:592-752)."""
+    p2g, prd, means, _, _ = mask_matching_ex(
+        mask_logits, mask_targets, cls_logits, cls_targets, smooth, sigmoid_scale, dice_scale,
+        cls_scale, background_index, uncertainty_gamma, uncertainty_gamma_min, inf_thresh,
+        num_masks, force_unmatched_class_to_background, force_unmatched_masks_to_empty,
+        topk_matches, strategy_id, mask_gamma, mask_alpha, cls_gamma, cls_alpha, void_class_index,
+        use_softmax_label_loss, normalize_uncertainty)
+    return [p2g, prd, means[0], means[1], means[2]]
+
+
+# ---------------------------------------------------------------------------
+# mask_matching_backward (src/bindings.cpp:113-139)
+# ---------------------------------------------------------------------------
+def mask_matching_backward(grad_layer_mask_mean, grad_layer_dice_mean, grad_layer_cls_mean,
+                           mask_logits, mask_targets, cls_logits, cls_targets, pred_to_gt,
+                           smooth, sigmoid_scale, dice_scale, cls_scale, background_index,
+                           uncertainty_gamma, uncertainty_gamma_min, num_masks,
+                           force_unmatched_class_to_background, force_unmatched_masks_to_empty,
+                           mask_gamma, mask_alpha, cls_gamma, cls_alpha, void_class_index,
+                           use_softmax_label_loss=False, normalize_uncertainty=True, *,
+                           saved: Optional[torch.Tensor] = None,
+                           num_masks_dev: Optional[torch.Tensor] = None) -> List[torch.Tensor]:
+    """[grad_mask_logits, grad_cls_logits] (src/cuda/mask_matching_backward.cu:378-621)."""
+    check_status()
+    for t, n in ((grad_layer_mask_mean, "grad_layer_mask_mean"),
+                 (grad_layer_dice_mean, "grad_layer_dice_mean"),
+                 (grad_layer_cls_mean, "grad_layer_cls_mean"), (pred_to_gt, "pred_to_gt")):
+        _check_input(t, n)
+    _check_quad(mask_logits, mask_targets, cls_logits, cls_targets)
+    _check_dtype(grad_layer_mask_mean, torch.float32, "grad_layer_mask_mean")
+    _check_dtype(grad_layer_dice_mean, torch.float32, "grad_layer_dice_mean")
+    _check_dtype(grad_layer_cls_mean, torch.float32, "grad_layer_cls_mean")
+    _check_dtype(pred_to_gt, torch.int64, "pred_to_gt")
+    lib = _lib_handle()
+    dev = mask_logits.device
+    d = _dims(mask_logits, mask_targets, cls_logits, cls_targets)
+    p = _params(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, uncertainty_gamma,
+                uncertainty_gamma_min, 1e30, num_masks, force_unmatched_class_to_background,
+                force_unmatched_masks_to_empty, 1, 0, mask_gamma, mask_alpha, cls_gamma, cls_alpha,
+                void_class_index, use_softmax_label_loss, normalize_uncertainty)
+    gm = torch.empty_like(mask_logits)
+    gc = torch.empty_like(cls_logits)
+    nbytes = lib.ml_mask_matching_backward_workspace_size(ctypes.byref(d), ctypes.byref(p))
+    ws = _workspace(nbytes, dev)
+    if saved is not None:
+        _check_input(saved, "saved")
+    _lib.check(lib.ml_mask_matching_backward(
+        ctypes.byref(d), ctypes.byref(p), _ptr(grad_layer_mask_mean), _ptr(grad_layer_dice_mean),
+        _ptr(grad_layer_cls_mean), _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits),
+        _ptr(cls_targets), _ptr(pred_to_gt), _ptr(saved), _ptr(num_masks_dev), _ptr(gm), _ptr(gc),
+        _ptr(ws), ws.numel(), _stream(dev)))
+    return [gm, gc]
+
+
+# ---------------------------------------------------------------------------
+# Standalone pairwise ops (src/bindings.cpp:22-31, 51-62, 141-155)
+# ---------------------------------------------------------------------------
+def _pairwise_mask_only(logits, targets, background_index, which, smooth=1.0, scale=1.0, gamma=0.0,
+                        alpha=-1.0, ug=1.0, ugmin=0.05, normalize=True):
+    _check_input(logits, "logits")
+    _check_input(targets, "targets")
+    if logits.dim() != 5:
+        raise RuntimeError("logits must be (L,B,C,H,W)")
+    # GT_total = targets.max() + 1 (src/cuda/pw_sigmoid_ce.cu:221-224): a host read, as in the reference
+    gt_total = int(targets.max().item()) + 1 if targets.numel() else 0
+    L, B, Q = logits.shape[:3]
+    dev = logits.device
+    cls_logits = torch.zeros((L, B, Q, 1), dtype=torch.float32, device=dev)
+    cls_targets = torch.full((B, max(gt_total, 0)), -1, dtype=torch.int64, device=dev)
+    out = pairwise_mask_loss_forward(logits, targets, cls_logits, cls_targets, smooth, scale, scale,
+                                     1.0, background_index, ug, ugmin, gamma, alpha, 0.0, -1.0,
+                                     False, normalize)
+    if out.dim() == 4:
+        return out
+    return out[which].contiguous()
+
+
+def forward_pw_sigmoid_ce_loss(logits, targets, background_index=-1, scale=1.0, gamma=0.0,
+                               alpha=-1.0, uncertainty_gamma=1.0, uncertainty_gamma_min=0.05,
+                               normalize_uncertainty=True):
+    """(L,B,C,GT_out) pairwise sigmoid-CE (src/cuda/pw_sigmoid_ce.cu:199-316)."""
+    return _pairwise_mask_only(logits, targets, background_index, 0, 1.0, scale, gamma, alpha,
+                               uncertainty_gamma, uncertainty_gamma_min, normalize_uncertainty)
+
+
+def forward_pw_dice_loss(logits, targets, smooth, background_index=-1, scale=1.0,
+                         uncertainty_gamma=1.0, uncertainty_gamma_min=0.05):
+    """(L,B,C,GT_out) pairwise dice (src/cuda/pw_dice_loss.cu:111-220)."""
+    return _pairwise_mask_only(logits, targets, background_index, 1, smooth, scale, 0.0, -1.0,
+                               uncertainty_gamma, uncertainty_gamma_min, True)
+
+
+def _label_cost(logits, targets, background_index, scale, gamma, alpha, softmax, name):
+    _check_input(logits, "logits")
+    _check_input(targets, "targets")
+    if logits.dim() != 4:
+        raise RuntimeError(f"{name}: logits must be (L,B,Q,C)")
+    if targets.dim() != 2:
+        raise RuntimeError(f"{name}: targets must be (B,GT)")
+    L, B, Q, C = logits.shape
+    if targets.shape[0] != B:
+        raise RuntimeError(f"{name}: batch size mismatch between logits and targets")
+    lib = _lib_handle()
+    G = lib.ml_gt_out(targets.shape[1], int(background_index))
+    if G == 0:
+        return torch.zeros((L, B, Q, 0), dtype=torch.float32, device=logits.device)
+    z = logits.contiguous().float()
+    out = torch.empty((L, B, Q, G), dtype=torch.float32, device=logits.device)
+    _lib.check(lib.ml_pairwise_label_loss_forward(
+        L, B, Q, C, targets.shape[1], int(background_index), float(scale), float(gamma),
+        float(alpha), int(softmax), _ptr(z), _ptr(targets.contiguous()), _ptr(out),
+        _stream(logits.device)))
+    return out
+
+
+def forward_pw_sigmoid_label_loss(logits, targets, background_index=-1, scale=1.0, gamma=0.0,
+                                  alpha=-1.0):
+    """(L,B,Q,GT_out) pairwise sigmoid label cost (src/cuda/pw_sigmoid_label_loss.cu:108-187)."""
+    return _label_cost(logits, targets, background_index, scale, gamma, alpha, False,
+                       "pairwise_sigmoid_label_loss_forward")
+
+
+def forward_pw_softmax_label_loss(logits, targets, background_index=-1, scale=1.0):
+    """(L,B,Q,GT_out) pairwise softmax label cost (src/cuda/pw_softmax_label_loss.cu:105-174)."""
+    return _label_cost(logits, targets, background_index, scale, 0.0, -1.0, True,
+                       "pairwise_softmax_label_loss_forward")
+
+
+def _not_built(name):
+    def fn(*args, **kwargs):
+        raise NotImplementedError(
+            f"mask_loss_b200: {name} (standalone semantic loss, not on the matching path) "
+            "is not implemented in this build")
+    fn.__name__ = name
+    return fn
+
+
+forward_sigmoid_ce_loss = _not_built("forward_sigmoid_ce_loss")
+backward_sigmoid_ce_loss = _not_built("backward_sigmoid_ce_loss")
+forward_dice_loss = _not_built("forward_dice_loss")
+backward_dice_loss = _not_built("backward_dice_loss")
+
+
+# ---------------------------------------------------------------------------
+# Solver alone (for bit-exact checks on identical fp64 cost matrices)
+# ---------------------------------------------------------------------------
+def match_costs(costs: torch.Tensor, inf_thresh=1e30, topk=1, strategy_id=0):
+    """Assign every slice of a (..., Q, GT_out) fp32 or fp64 cost tensor on
+    the GPU.  Returns (pred_to_gt, pred_round) shaped like costs[..., 0]."""
+    _check_input(costs, "costs")
+    lib = _lib_handle()
+    Q, G = costs.shape[-2:]
+    N = costs.numel() // max(Q * G, 1) if Q * G else 0
+    p2g = torch.empty(costs.shape[:-1], dtype=torch.int64, device=costs.device)
+    prd = torch.empty_like(p2g)
+    status = torch.zeros(1, dtype=torch.int32, device=costs.device)
+    if costs.dtype == torch.float64:
+        rc = lib.ml_match_f64(_ptr(costs), N, Q, G, float(inf_thresh), int(topk), int(strategy_id),
+                              _ptr(p2g), _ptr(prd), _ptr(status), _stream(costs.device))
+    elif costs.dtype == torch.float32:
+        rc = lib.ml_match(_ptr(costs), 1, N, Q, G, float(inf_thresh), int(topk), int(strategy_id),
+                          _ptr(p2g), _ptr(prd), _ptr(status), None, 0, _stream(costs.device))
+    else:
+        raise RuntimeError("costs must be float32 or float64")
+    _lib.check(rc)
+    _track_status(status)
+    return p2g, prd
+
+
+def count_masks(mask_targets, GT_total: int, background_index: int) -> torch.Tensor:
+    """Device fp32 scalar: present non-background GT ids summed over the batch."""
+    _check_input(mask_targets, "mask_targets")
+    lib = _lib_handle()
+    B, Ht, Wt = mask_targets.shape
+    d = _lib.Dims(1, B, 1, Ht, Wt, Ht, Wt, 1, GT_total)
+    p = _params(background_index=background_index)
+    out = torch.empty((), dtype=torch.float32, device=mask_targets.device)
+    nbytes = lib.ml_mask_matching_workspace_size(ctypes.byref(d), ctypes.byref(p))
+    ws = _workspace(nbytes, mask_targets.device)
+    _lib.check(lib.ml_count_masks(ctypes.byref(d), ctypes.byref(p), _ptr(mask_targets), _ptr(out),
+                                  _ptr(ws), ws.numel(), _stream(mask_targets.device)))
+    return out
