@@ -82,15 +82,14 @@ struct FwdPlan {
     int L, B, Q, H, W, Ht, Wt, s, C, gt_total, gout, bg;
     bool unc, foc, tma_ok;
     int nacc, nrow;
-    int qrows, qrows_pad, nqt, gp, ngr, chunk_cells, nchunk, part_stride;
+    int qrows, qrows_pad, nqt, chunk_cells, nchunk, part_stride;
     size_t cost_smem;
     // workspace offsets
-    size_t off_totals, off_part, off_sep, off_total, off_rawI, off_rawT, off_qstat, bytes;
+    size_t off_totals, off_codes, off_part, off_sep, off_total, off_rawI, off_rawT, off_qstat, bytes;
 };
 
-size_t cost_smem_bytes(int qrows_pad, int nacc, int gp, int s2) {
-    return 1024 + (size_t)kStages * qrows_pad * KC * 4 + (size_t)nacc * gp * qrows_pad * 4 +
-           2 * KC * 4 + 2 * KC * s2 * 2 + 16 + 8 * kStages;
+size_t cost_smem_bytes(int qrows_pad) {
+    return 1024 + (size_t)kStages * (2 * (size_t)qrows_pad * KBOX * 4 + KC * 4) + 8 * kStages;
 }
 
 int validate_dims(const ml_dims* d) {
@@ -144,47 +143,44 @@ int make_plan(const ml_dims* d, const ml_params* p, FwdPlan* P) {
     P->unc = p->uncertainty_gamma != 0.0f;
     P->foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
     P->nacc = P->unc ? 3 : 2;
-    P->nrow = P->unc ? 5 : 2;
+    P->nrow = P->unc ? 5 : 3;
     const int HW = P->H * P->W;
     P->tma_ok = (HW % 4) == 0;
     const int Q = P->Q > 0 ? P->Q : 1;
     P->nqt = (Q + 127) / 128;
     P->qrows = (Q + P->nqt - 1) / P->nqt;
     P->qrows_pad = (P->qrows + 31) / 32 * 32;
-    const int s2 = P->s * P->s;
-    const int G = P->gout > 0 ? P->gout : 1;
-    const size_t fixed = cost_smem_bytes(P->qrows_pad, P->nacc, 0, s2);
-    const size_t per_col = (size_t)P->nacc * P->qrows_pad * 4;
-    const size_t small_budget = 110 * 1024, big_budget = 220 * 1024;
-    int gp_small = (int)((small_budget - fixed) / per_col);
-    int gp_big = (int)((big_budget - fixed) / per_col);
-    if (gp_big < 1) return fail(ML_EUNSUPPORTED, "query tile does not fit shared memory");
-    if (G <= gp_small || G <= gp_big) {
-        P->gp = G; P->ngr = 1;
-    } else {
-        P->ngr = (G + gp_big - 1) / gp_big;
-        P->gp = (G + P->ngr - 1) / P->ngr;
-    }
-    P->cost_smem = cost_smem_bytes(P->qrows_pad, P->nacc, P->gp, s2);
-    const int threads = P->qrows_pad;
+    P->cost_smem = cost_smem_bytes(P->qrows_pad);
+    const int threads = 2 * P->qrows_pad;
     int per_sm = (int)std::min<size_t>(228 * 1024 / (P->cost_smem + 1024), 2048 / threads);
     if (per_sm < 1) per_sm = 1;
-    const int64_t base = (int64_t)P->L * P->B * P->nqt * P->ngr;
-    const int64_t target = (int64_t)sm_count() * per_sm;
-    int64_t nch = base > 0 ? (target + base - 1) / base : 1;
-    const int64_t max_ch = (HW + KC - 1) / KC;
-    if (nch > max_ch) nch = max_ch;
-    if (nch < 1) nch = 1;
-    P->chunk_cells = (int)(((HW + nch - 1) / nch + KC - 1) / KC * KC);
+    // chunks per (image, query tile): smallest count whose CTA total fills the
+    // SMs in whole waves to within 10% (or the best found)
+    const int64_t base = (int64_t)P->L * P->B * P->nqt;
+    const int64_t slots = (int64_t)sm_count() * per_sm;
+    const int64_t max_ch = std::max<int64_t>(1, (HW + KC - 1) / KC);
+    int64_t best = 1;
+    double best_eff = -1.0;
+    const int64_t lo = base > 0 ? std::max<int64_t>(1, (slots + base - 1) / base) : 1;
+    for (int64_t nch = lo; nch <= std::min<int64_t>(max_ch, 4 * lo); ++nch) {
+        const int64_t total = base * nch;
+        const int64_t waves = (total + slots - 1) / slots;
+        const double eff = (double)total / (double)(waves * slots);
+        if (eff > best_eff + 1e-9) { best_eff = eff; best = nch; }
+        if (eff >= 0.9) break;
+    }
+    if (best > max_ch) best = max_ch;
+    P->chunk_cells = (int)(((HW + best - 1) / best + KC - 1) / KC * KC);
     P->nchunk = (HW + P->chunk_cells - 1) / P->chunk_cells;
-    P->part_stride = (P->nacc * P->gp + P->nrow) * P->qrows_pad;
+    P->part_stride = (P->nacc * std::max(P->gout, 1) + P->nrow) * P->qrows_pad;
     // workspace
     const size_t LBQ = (size_t)P->L * P->B * P->Q;
     const size_t LBQG = LBQ * P->gout;
     size_t off = 0;
     P->off_totals = off; off += align256(sizeof(int32_t) * (size_t)P->B * P->gt_total);
+    P->off_codes = off; off += align256(sizeof(int32_t) * (size_t)P->B * HW);
     P->off_part = off;
-    off += align256(sizeof(float) * (size_t)base * P->nchunk * P->part_stride);
+    off += align256(sizeof(float) * (size_t)base * P->nchunk * 2 * P->part_stride);
     P->off_sep = off; off += align256(sizeof(float) * 3 * LBQG);
     P->off_total = off; off += align256(sizeof(float) * LBQG);
     P->off_rawI = off; off += align256(sizeof(float) * LBQG);
@@ -203,6 +199,7 @@ CostArgs cost_args(const FwdPlan& P, const ml_params* p, const float* ml, const 
     CostArgs a{};
     a.logits = ml; a.targets = mt; a.cls_logits = cl; a.cls_targets = ct;
     a.totals = reinterpret_cast<int32_t*>(ws + P.off_totals);
+    a.codes = reinterpret_cast<int32_t*>(ws + P.off_codes);
     a.part = reinterpret_cast<float*>(ws + P.off_part);
     a.sep = reinterpret_cast<float*>(ws + P.off_sep);
     a.total = reinterpret_cast<float*>(ws + P.off_total);
@@ -212,7 +209,7 @@ CostArgs cost_args(const FwdPlan& P, const ml_params* p, const float* ml, const 
     a.status = status;
     a.L = P.L; a.B = P.B; a.Q = P.Q; a.H = P.H; a.W = P.W; a.Ht = P.Ht; a.Wt = P.Wt; a.s = P.s;
     a.C = P.C; a.gt_total = P.gt_total; a.gout = P.gout; a.bg = P.bg;
-    a.qrows = P.qrows; a.qrows_pad = P.qrows_pad; a.nqt = P.nqt; a.gp = P.gp; a.ngr = P.ngr;
+    a.qrows = P.qrows; a.qrows_pad = P.qrows_pad; a.nqt = P.nqt;
     a.chunk_cells = P.chunk_cells; a.nchunk = P.nchunk; a.part_stride = P.part_stride;
     a.smooth = p->smooth; a.sigmoid_scale = p->sigmoid_scale; a.dice_scale = p->dice_scale;
     a.cls_scale = p->cls_scale; a.ug = p->uncertainty_gamma; a.ugmin = p->uncertainty_gamma_min;
@@ -232,26 +229,39 @@ int launch_cost_t(const FwdPlan& P, const CUtensorMap& tm, const CostArgs& a, cu
     auto k = cost_partial_kernel<UNC, FOC, TMA>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.cost_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cost_partial_kernel attributes");
-    dim3 grid(P.nchunk, P.nqt * P.ngr, P.L * P.B);
-    k<<<grid, P.qrows_pad, P.cost_smem, st>>>(tm, a);
+    dim3 grid(P.nchunk, P.nqt, P.L * P.B);
+    k<<<grid, 2 * P.qrows_pad, P.cost_smem, st>>>(tm, a);
     ML_CHECK_LAUNCH("cost_partial_kernel");
     return ML_OK;
 }
 
-// totals + chunk partials + finalize.  `a` decides which outputs are written.
-int run_costs(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStream_t st) {
-    const int64_t npix = (int64_t)P.Ht * P.Wt;
+// Label codes + histogram (always), and when `costs` the chunk partials and
+// both finalize kernels.  `a` decides which outputs are written.
+int run_prep(const FwdPlan& P, const CostArgs& a, cudaStream_t st) {
     cudaError_t e = cudaMemsetAsync(const_cast<int32_t*>(a.totals), 0,
                                     sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
     if (e != cudaSuccess) return cuda_fail(e, "memset totals");
-    if (P.B > 0 && npix > 0 && P.gt_total > 0) {
-        const int bx = (int)std::min<int64_t>((npix + 255) / 256, std::max(1, 2 * sm_count() / std::max(1, P.B)));
+    const int HW = P.H * P.W;
+    if (P.B > 0 && HW > 0) {
+        const int bx = std::max(1, std::min((HW + 255) / 256, (4 * sm_count() + P.B - 1) / std::max(1, P.B)));
         const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
-        label_hist_kernel<<<dim3(bx, P.B), 256, hs, st>>>(a.targets, npix, P.gt_total,
+        label_code_kernel<<<dim3(bx, P.B), 256, hs, st>>>(a.targets, P.B, P.H, P.W, P.Wt, P.s,
+                                                          P.gt_total, P.bg,
+                                                          const_cast<int32_t*>(a.codes),
                                                           const_cast<int32_t*>(a.totals));
-        ML_CHECK_LAUNCH("label_hist_kernel");
+        ML_CHECK_LAUNCH("label_code_kernel");
     }
-    if ((int64_t)P.L * P.B * P.Q == 0) return ML_OK;
+    return ML_OK;
+}
+
+int run_costs(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStream_t st) {
+    int rc = run_prep(P, a, st);
+    if (rc) return rc;
+    const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
+    if (LBQ == 0 || P.gout == 0) return ML_OK;
+    const size_t part_bytes = sizeof(float) * (size_t)P.L * P.B * P.nqt * P.nchunk * 2 * P.part_stride;
+    cudaError_t e = cudaMemsetAsync(a.part, 0, part_bytes, st);
+    if (e != cudaSuccess) return cuda_fail(e, "memset partials");
     CUtensorMap tm;
     memset(&tm, 0, sizeof(tm));
     bool tma = P.tma_ok && (reinterpret_cast<uintptr_t>(mask_logits) % 16 == 0);
@@ -260,18 +270,17 @@ int run_costs(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStrea
         if (!enc) {
             tma = false;
         } else {
-            const cuuint64_t dims[2] = {(cuuint64_t)P.H * P.W, (cuuint64_t)P.L * P.B * P.Q};
+            const cuuint64_t dims[2] = {(cuuint64_t)P.H * P.W, (cuuint64_t)LBQ};
             const cuuint64_t strides[1] = {(cuuint64_t)P.H * P.W * sizeof(float)};
-            const cuuint32_t box[2] = {(cuuint32_t)KC, (cuuint32_t)P.qrows};
+            const cuuint32_t box[2] = {(cuuint32_t)KBOX, (cuuint32_t)P.qrows};
             const cuuint32_t es[2] = {1, 1};
             CUresult r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(mask_logits),
                              dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             if (r != CUDA_SUCCESS) tma = false;
         }
     }
-    int rc;
     if (P.unc) {
         if (P.foc) rc = tma ? launch_cost_t<true, true, true>(P, tm, a, st) : launch_cost_t<true, true, false>(P, tm, a, st);
         else rc = tma ? launch_cost_t<true, false, true>(P, tm, a, st) : launch_cost_t<true, false, false>(P, tm, a, st);
@@ -280,10 +289,15 @@ int run_costs(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStrea
         else rc = tma ? launch_cost_t<false, false, true>(P, tm, a, st) : launch_cost_t<false, false, false>(P, tm, a, st);
     }
     if (rc) return rc;
-    const size_t fs = sizeof(float) * 4 * P.qrows;
-    if (P.unc) cost_finalize_kernel<true><<<dim3(P.nqt, P.L * P.B), 256, fs, st>>>(a);
-    else cost_finalize_kernel<false><<<dim3(P.nqt, P.L * P.B), 256, fs, st>>>(a);
-    ML_CHECK_LAUNCH("cost_finalize_kernel");
+    const unsigned rb = (unsigned)((LBQ * 32 + 255) / 256);
+    if (P.unc) cost_rows_kernel<true, false><<<rb, 256, 0, st>>>(a);
+    else if (P.foc) cost_rows_kernel<false, false><<<rb, 256, 0, st>>>(a);
+    else cost_rows_kernel<false, true><<<rb, 256, 0, st>>>(a);
+    ML_CHECK_LAUNCH("cost_rows_kernel");
+    dim3 pg((unsigned)((P.qrows * P.gout + 255) / 256), P.nqt, P.L * P.B);
+    if (P.unc) cost_pairs_kernel<true><<<pg, 256, 0, st>>>(a);
+    else cost_pairs_kernel<false><<<pg, 256, 0, st>>>(a);
+    ML_CHECK_LAUNCH("cost_pairs_kernel");
     return ML_OK;
 }
 
@@ -468,16 +482,9 @@ int ml_count_masks(const ml_dims* d, const ml_params* p, const int64_t* mask_tar
     if ((rc = check_ws(workspace, workspace_bytes, P.bytes))) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char* ws = ws_base(workspace);
-    int32_t* totals = reinterpret_cast<int32_t*>(ws + P.off_totals);
-    cudaError_t e = cudaMemsetAsync(totals, 0, sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
-    if (e != cudaSuccess) return cuda_fail(e, "memset totals");
-    const int64_t npix = (int64_t)P.Ht * P.Wt;
-    if (P.B > 0 && npix > 0 && P.gt_total > 0) {
-        const int bx = (int)std::min<int64_t>((npix + 255) / 256, std::max(1, 2 * sm_count() / std::max(1, P.B)));
-        const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
-        label_hist_kernel<<<dim3(bx, P.B), 256, hs, st>>>(mask_targets, npix, P.gt_total, totals);
-        ML_CHECK_LAUNCH("label_hist_kernel");
-    }
+    CostArgs a = cost_args(P, p, nullptr, mask_targets, nullptr, nullptr, ws, nullptr);
+    if ((rc = run_prep(P, a, st))) return rc;
+    const int32_t* totals = a.totals;
     count_masks_kernel<<<1, 256, 0, st>>>(totals, P.B, P.gt_total, P.bg, num_masks_out);
     ML_CHECK_LAUNCH("count_masks_kernel");
     return ML_OK;

@@ -30,6 +30,25 @@ ML_INLINE int label_to_col(int64_t lab, int gt_total, int bg) {
 // MUFU forms (__expf, __logf, __fdividef); accuracy is far inside the 1e-4
 // relative tolerance for the sums they feed.
 // ----------------------------------------------------------------------------
+// Single MUFU instructions (hardware approximations, flush-to-zero).
+ML_INLINE float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+ML_INLINE float lg2_approx(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+ML_INLINE float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 struct Elem {
     float p;      // sigmoid(x)
     float sp;     // log1p(exp(-|x|))
@@ -126,10 +145,19 @@ ML_INLINE void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Bounded wait on phase `parity`.  Returns false when the bound is hit.
-ML_INLINE bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t max_iters = 1u << 26) {
+ML_INLINE uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait on phase `parity` of an mbarrier, bounded in wall time (default 2 s):
+// returns false when the bound is hit so the caller can flag an error
+// instead of spinning forever.
+ML_INLINE bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t max_ns = 2000000000ull) {
     const uint32_t a = smem_u32(bar);
-    for (uint32_t it = 0; it < max_iters; ++it) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
         uint32_t done;
         asm volatile(
             "{\n .reg .pred p;\n"
@@ -137,8 +165,12 @@ ML_INLINE bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t max_iters = 1u
             " selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(done) : "r"(a), "r"(parity) : "memory");
         if (done) return true;
+        if ((it & 255) == 0) {
+            const uint64_t now = global_ns();
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > max_ns) return false;
+        }
     }
-    return false;
 }
 
 // cp.async.bulk global->shared, completion signalled on `bar` (tx bytes).

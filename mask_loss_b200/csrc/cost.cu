@@ -8,19 +8,27 @@
 // g, the contractions  D[q,g] = sum_j dlt(x_qj) k_jg,  I[q,g] = sum_j w p k_jg,
 // T[q,g] = sum_j w k_jg  over the low-res cells j, where k_jg counts the
 // high-res pixels of cell j that carry label g (src/cuda/utils.cuh:6-36), plus
-// per-query row sums.  With s = H_t/H = 1 (and for every "pure" cell when
-// s > 1) k is one-hot, so the contraction is a segmented sum over the cell
-// stream: every query of a CTA walks the SAME label sequence, so label runs
-// are uniform across the CTA and each thread (one query) accumulates a run in
-// registers and flushes it to a per-thread column of shared-memory bins only
-// when the label changes.  Mixed cells (s > 1 on a label boundary) add their
-// per-pixel counts directly.  Logits stream through a 4-stage TMA pipeline
-// (cp.async.bulk.tensor, 128-byte swizzle, conflict-free LDS.128), each read
-// from HBM exactly once.
+// per-query row sums.  k is one-hot for s = H_t/H = 1 and for every "pure"
+// cell when s > 1, so the contraction is a segmented sum over the cell
+// stream.  Every query of a CTA walks the SAME label sequence, so label runs
+// are uniform across the CTA: a thread (one query row, one half of each tile)
+// accumulates the current run in registers and flushes it only when the label
+// changes, with an ordered `red.add` into a CTA-private slice of a global
+// partial buffer (a thread's same-address reductions apply in program order,
+// so the sums are deterministic).  Tiles whose 32 cells carry one label --
+// most of an image -- take a branch-free path.  Mixed cells (s > 1 on a label
+// boundary) add their per-pixel counts directly.
 //
-// The HW axis is split into chunks across CTAs (grid.x) to fill the 148 SMs;
-// chunk partials are reduced in fixed order by cost_finalize_kernel, so the
-// costs are deterministic run to run.
+// Data movement: a prep kernel turns the int64 label map into one int32 code
+// per low-res cell (and the per-image histogram) once; the cost kernel then
+// streams logits tiles of (qrows x 64 cells) with two cp.async.bulk.tensor
+// boxes (128-byte swizzle, conflict-free LDS.128) plus the tile's 256 bytes of
+// codes with one cp.async.bulk, all on one mbarrier, through a 3-stage
+// pipeline.  Logits are read from HBM exactly once.
+//
+// The HW axis is split into chunks across CTAs (grid.x) sized to whole waves
+// of the 148 SMs; two finalize kernels reduce the chunk partials in fixed
+// order.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -29,129 +37,136 @@
 namespace mlb {
 
 // ---------------------------------------------------------------------------
-// Per-image label histogram: totals[b, lab] for lab in [0, GT_total).
-// Same counts as counts.sum({2,3}) in src/cuda/pw_mask.cu:391.
+// Prep: per-cell code (pure output column / kNone / kMixed) and the per-image
+// label histogram totals[b, lab], lab in [0, GT_total) (the counts.sum({2,3})
+// of src/cuda/pw_mask.cu:391).  grid = (cell blocks, B).
 // ---------------------------------------------------------------------------
-__global__ void label_hist_kernel(const int64_t* __restrict__ targets, int64_t npix,
-                                  int gt_total, int32_t* __restrict__ totals) {
-    extern __shared__ int32_t sh[];
+__global__ void __launch_bounds__(256)
+label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int Wt, int s,
+                  int gt_total, int bg, int32_t* __restrict__ codes, int32_t* __restrict__ totals) {
+    extern __shared__ int32_t hist[];
     const int b = blockIdx.y;
     const bool use_sh = gt_total <= kHistSmemMax;
     if (use_sh)
-        for (int i = threadIdx.x; i < gt_total; i += blockDim.x) sh[i] = 0;
+        for (int i = threadIdx.x; i < gt_total; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    const int64_t* t = targets + (int64_t)b * npix;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < npix;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t lab = t[i];
-        if (lab >= 0 && lab < gt_total) {
-            if (use_sh) atomicAdd(&sh[lab], 1);
-            else atomicAdd(&totals[(int64_t)b * gt_total + lab], 1);
-        }
+    const int HW = H * W;
+    const int64_t* tb = targets + (int64_t)b * HW * s * s;
+    int32_t* cb = codes ? codes + (int64_t)b * HW : nullptr;
+    int32_t* tot = totals + (int64_t)b * gt_total;
+    for (int cell = blockIdx.x * blockDim.x + threadIdx.x; cell < HW; cell += gridDim.x * blockDim.x) {
+        int c = -3;
+        const int ci = cell / W, cj = cell - ci * W;
+        const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
+        for (int dy = 0; dy < s; ++dy)
+            for (int dx = 0; dx < s; ++dx) {
+                const int64_t lab = r0[(int64_t)dy * Wt + dx];
+                if (lab >= 0 && lab < gt_total) {
+                    if (use_sh) atomicAdd(&hist[lab], 1);
+                    else atomicAdd(&tot[lab], 1);
+                }
+                const int col = label_to_col(lab, gt_total, bg);
+                c = (c == -3 || c == col) ? col : kMixed;
+            }
+        if (cb) cb[cell] = c;
     }
     __syncthreads();
     if (use_sh)
         for (int i = threadIdx.x; i < gt_total; i += blockDim.x)
-            if (sh[i]) atomicAdd(&totals[(int64_t)b * gt_total + i], sh[i]);
+            if (hist[i]) atomicAdd(&tot[i], hist[i]);
 }
 
 // ---------------------------------------------------------------------------
-// Cell codes for one tile of KC cells: pure column (>= 0, local to the
-// column range [g0, g0+gp)), kNone, or kMixed with the s*s per-pixel local
-// columns in `mix` (s > 1 only).
+// Element pieces for the default path (no entropy weight, no focal terms):
+// e = exp(-|x|), d = 1 + e (log1p(e) = log(d) is summed through a product of
+// eight d's and one log2), p = sigmoid(x).
 // ---------------------------------------------------------------------------
-ML_INLINE void tile_codes(const int64_t* __restrict__ tb, int cell0, int nvalid, int W, int Wt,
-                          int s, int gt_total, int bg, int g0, int gp, int* code, int16_t* mix,
-                          int tid, int nthreads) {
-    const int s2 = s * s;
-    for (int k = tid; k < KC; k += nthreads) {
-        int c = kNone;
-        if (k < nvalid) {
-            const int cell = cell0 + k;
-            const int ci = cell / W, cj = cell - ci * W;
-            if (s == 1) {
-                int col = label_to_col(tb[cell], gt_total, bg) - g0;
-                c = (col >= 0 && col < gp) ? col : kNone;
-            } else {
-                const int64_t* row0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
-                int first = -3;
-                bool pure = true;
-                for (int dy = 0; dy < s; ++dy)
-                    for (int dx = 0; dx < s; ++dx) {
-                        int col = label_to_col(row0[(int64_t)dy * Wt + dx], gt_total, bg) - g0;
-                        col = (col >= 0 && col < gp) ? col : kNone;
-                        mix[k * s2 + dy * s + dx] = (int16_t)col;
-                        if (first == -3) first = col;
-                        else if (col != first) pure = false;
-                    }
-                c = pure ? first : kMixed;
-            }
-        }
-        code[k] = c;
-    }
+struct Fast {
+    float d, p;
+};
+
+ML_INLINE Fast fast_elem(float x) {
+    const float e = ex2_approx(-fabsf(x) * 1.4426950408889634f);
+    const float d = 1.0f + e;
+    const float r = rcp_approx(d);
+    Fast f;
+    f.d = d;
+    f.p = x >= 0.0f ? r : e * r;
+    return f;
+}
+
+// red.add into the partial buffer (program order per address -> deterministic).
+ML_INLINE void red_add(float* p, float v) {
+    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 
 // ---------------------------------------------------------------------------
-// The streaming cost kernel.  grid = (nchunk, nqt * ngr, L*B); block = QT
-// threads, thread t <-> query row q = qt*qrows + t.  Template flags:
+// The streaming cost kernel.  grid = (nchunk, nqt, L*B); block = 2*qrows_pad
+// threads: thread (h, t) <-> query row qt*qrows + t, cells [h*32, h*32+32) of
+// every 64-cell tile.  Template flags:
 //   UNC   entropy weights on (uncertainty_gamma != 0)
 //   FOC   focal gamma/alpha on the mask BCE
-//   TMA   logits rows are 16-byte strided so the tensor-map path is legal
+//   TMA   logits rows are 16-byte strided so the bulk-tensor path is legal
 // ---------------------------------------------------------------------------
 template <bool UNC, bool FOC, bool TMA>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
 cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     constexpr int NACC = UNC ? 3 : 2;
-    constexpr int NROW = UNC ? 5 : 2;
+    constexpr int NROW = UNC ? 5 : 3;
+    constexpr bool FAST = !UNC && !FOC;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // layout: [stages][qrows_pad][32 floats] swizzled | bins | codes | mix | bars
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int QT = blockDim.x;
-    float* stage = reinterpret_cast<float*>(base);
-    const int stage_floats = a.qrows_pad * KC;
-    float* bins = stage + kStages * stage_floats;           // [NACC][gp][QT]
-    int* codes = reinterpret_cast<int*>(bins + NACC * a.gp * QT);  // [2][KC]
-    int16_t* mix = reinterpret_cast<int16_t*>(codes + 2 * KC);     // [2][KC*s2]
-    const int s2 = a.s * a.s;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(
-        (reinterpret_cast<uintptr_t>(mix + 2 * KC * s2) + 7) & ~uintptr_t(7));
+    const int QP = a.qrows_pad;
+    const int box_floats = QP * KBOX;                  // one 32-cell box
+    float* xs = reinterpret_cast<float*>(base);        // [stage][2][QP][32]
+    int32_t* cs = reinterpret_cast<int32_t*>(xs + kStages * 2 * box_floats);  // [stage][KC]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(cs + kStages * KC);
 
-    const int t = threadIdx.x;
+    const int tid = threadIdx.x;
+    const int h = tid / QP;
+    const int t = tid - h * QP;
+    const int lane = tid & 31;
     const int lb = blockIdx.z;
     const int b = lb % a.B;
-    const int qt = blockIdx.y % a.nqt;
-    const int gr = blockIdx.y / a.nqt;
-    const int g0 = gr * a.gp;
+    const int qt = blockIdx.y;
     const int q = qt * a.qrows + t;
     const bool qvalid = (t < a.qrows) && (q < a.Q);
     const int HW = a.H * a.W;
     const int cell_begin = blockIdx.x * a.chunk_cells;
     const int cell_end = min(HW, cell_begin + a.chunk_cells);
     const int ntiles = (cell_end - cell_begin + KC - 1) / KC;
-    const int64_t row0 = ((int64_t)lb * a.Q) + qt * a.qrows;  // first global logits row
-    const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
+    const int row0 = lb * a.Q + qt * a.qrows;          // first global logits row
+    const int32_t* codes_b = a.codes + (int64_t)b * HW;
+    const int G = a.gout;
+    float* part = a.part + ((((int64_t)lb * a.nqt + qt) * a.nchunk + blockIdx.x) * 2 + h) *
+                               (int64_t)a.part_stride;
+    const float N2 = (float)(a.s * a.s);
+    const Focal foc = make_focal(a.mask_gamma, a.mask_alpha);
 
-    for (int i = 0; i < NACC * a.gp; ++i) bins[i * QT + t] = 0.0f;
+    auto issue = [&](int it) {  // one thread: loads of tile `it` into stage it % S
+        const int st = it % kStages;
+        const int c0 = cell_begin + it * KC;
+        const uint32_t cbytes = (uint32_t)min(KC, HW - c0) * 4u;
+        mbar_arrive_expect_tx(&bars[st], 2u * a.qrows * KBOX * 4u + cbytes);
+#pragma unroll
+        for (int bx = 0; bx < 2; ++bx)
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+                " [%0], [%1, {%2, %3}], [%4];"
+                ::"r"(smem_u32(xs + (st * 2 + bx) * box_floats)), "l"(&tmap), "r"(c0 + bx * KBOX),
+                  "r"(row0), "r"(smem_u32(&bars[st])) : "memory");
+        bulk_g2s(cs + st * KC, codes_b + c0, cbytes, &bars[st]);
+    };
 
-    const uint32_t stage_bytes = (uint32_t)a.qrows * KC * 4u;
     if (TMA) {
-        if (t == 0) {
+        if (tid == 0) {
             for (int i = 0; i < kStages; ++i) mbar_init(&bars[i], 1);
             fence_mbar_init();
         }
         __syncthreads();
-        if (t == 0) {
-            for (int i = 0; i < kStages - 1 && i < ntiles; ++i) {
-                mbar_arrive_expect_tx(&bars[i], stage_bytes);
-                const int cx = cell_begin + i * KC;
-                asm volatile(
-                    "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
-                    " [%0], [%1, {%2, %3}], [%4];"
-                    ::"r"(smem_u32(stage + i * stage_floats)), "l"(&tmap), "r"(cx),
-                      "r"((int)row0), "r"(smem_u32(&bars[i])) : "memory");
-            }
-        }
+        if (tid == 0)
+            for (int i = 0; i < kStages - 1 && i < ntiles; ++i) issue(i);
     }
 
     float racc[NACC];
@@ -161,263 +176,314 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
 #pragma unroll
     for (int i = 0; i < NROW; ++i) rows[i] = 0.0f;
     int cur = kNone;
-    const float N2 = (float)s2;
-    const Focal foc = make_focal(a.mask_gamma, a.mask_alpha);
+    int run_tiles = 0;
     bool ok = true;
 
-    auto flush = [&](int col) {
-        if (col >= 0) {
-#pragma unroll
-            for (int i = 0; i < NACC; ++i) {
-                bins[(i * a.gp + col) * QT + t] += racc[i] * N2;
-                racc[i] = 0.0f;
-            }
+    auto flush = [&]() {
+        if (cur >= 0 && qvalid) {
+            float* pc = part + (int64_t)cur * QP + t;
+            red_add(pc, FAST ? -racc[0] * N2 : racc[0] * N2);
+            red_add(pc + (int64_t)G * QP, racc[1] * N2);
+            if (UNC) red_add(pc + 2 * (int64_t)G * QP, racc[2] * N2);
         }
+#pragma unroll
+        for (int i = 0; i < NACC; ++i) racc[i] = 0.0f;
+        run_tiles = 0;
     };
 
     for (int it = 0; it < ntiles; ++it) {
         const int st = it % kStages;
         const int cell0 = cell_begin + it * KC;
         const int nvalid = min(KC, cell_end - cell0);
-        float* sx = stage + st * stage_floats;
         if (TMA) {
             if (!mbar_wait(&bars[st], (uint32_t)((it / kStages) & 1))) ok = false;
+            __syncthreads();  // everyone is done with the stage refilled below
+            if (tid == 0 && it + kStages - 1 < ntiles) issue(it + kStages - 1);
         } else {
-            // plain loads into the same swizzled layout
-            if (qvalid) {
-                const float* src = a.logits + (row0 + t) * (int64_t)HW + cell0;
-                for (int c = 0; c < KC / 4; ++c) {
-                    float4 v;
-                    float* vv = reinterpret_cast<float*>(&v);
+            __syncthreads();
+            for (int i = tid; i < 2 * a.qrows * (KBOX / 4); i += blockDim.x) {
+                const int bx = i / (a.qrows * (KBOX / 4));
+                const int rem = i - bx * a.qrows * (KBOX / 4);
+                const int r = rem / (KBOX / 4), c = rem - r * (KBOX / 4);
+                const float* src = a.logits + (int64_t)(row0 + r) * HW + cell0 + bx * KBOX + c * 4;
+                float4 v;
+                float* vv = reinterpret_cast<float*>(&v);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int k = bx * KBOX + c * 4 + u;
+                    vv[u] = (k < nvalid) ? src[u] : 0.0f;
+                }
+                *reinterpret_cast<float4*>(xs + (st * 2 + bx) * box_floats + r * KBOX +
+                                           ((c ^ (r & 7)) << 2)) = v;
+            }
+            for (int k = tid; k < KC; k += blockDim.x)
+                cs[st * KC + k] = k < nvalid ? codes_b[cell0 + k] : kNone;
+            __syncthreads();
+        }
+        // this thread's 32 cells: box h of the stage
+        const int nv = min(KBOX, max(0, nvalid - h * KBOX));
+        const int32_t* code = cs + st * KC + h * KBOX;
+        const int my_code = lane < nv ? code[lane] : kNone;
+        const int c0 = __shfl_sync(0xffffffffu, my_code, 0);
+        const bool uni = __all_sync(0xffffffffu, my_code == c0) && nv == KBOX && c0 >= kNone;
+        const float* rowp = xs + (st * 2 + h) * box_floats + t * KBOX;
+        float trow[NROW];
+#pragma unroll
+        for (int i = 0; i < NROW; ++i) trow[i] = 0.0f;
+        if (uni) {
+            // ---------------- one label for the whole box -------------------
+            if (c0 != cur) { flush(); cur = c0; }
+            const bool acc = cur >= 0;
+            if (FAST) {
+                float prod = 1.0f;
+#pragma unroll
+                for (int c = 0; c < KBOX / 4; ++c) {
+                    const float4 v = *reinterpret_cast<const float4*>(rowp + ((c ^ (t & 7)) << 2));
+                    const float xv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int k = c * 4 + u;
-                        vv[u] = (k < nvalid) ? src[k] : 0.0f;
+                        const Fast f = fast_elem(xv[u]);
+                        prod *= f.d;
+                        trow[0] += fmaxf(xv[u], 0.0f);
+                        trow[1] += f.p;
+                        if (acc) { racc[0] += xv[u]; racc[1] += f.p; }
                     }
-                    *reinterpret_cast<float4*>(sx + t * KC + ((c ^ (t & 7)) << 2)) = v;
+                    if (c & 1) { trow[2] += lg2_approx(prod); prod = 1.0f; }
+                }
+            } else {
+#pragma unroll 2
+                for (int c = 0; c < KBOX / 4; ++c) {
+                    const float4 v = *reinterpret_cast<const float4*>(rowp + ((c ^ (t & 7)) << 2));
+                    const float xv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const Elem e = elem(xv[u]);
+                        const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
+                        const float nt = FOC ? focal_neg(foc, e) : e.neg;
+                        const float dl = FOC ? w * (focal_pos(foc, e) - nt) : -w * xv[u];
+                        if (UNC) {
+                            trow[0] += w * nt; trow[1] += w * e.p; trow[2] += w;
+                            trow[3] += nt; trow[4] += e.p;
+                        } else {
+                            trow[0] += nt; trow[1] += e.p;
+                        }
+                        if (acc) {
+                            racc[0] += dl; racc[1] += w * e.p;
+                            if (UNC) racc[2] += w;
+                        }
+                    }
                 }
             }
-        }
-        int* code = codes + (it & 1) * KC;
-        int16_t* mx = mix + (it & 1) * KC * s2;
-        tile_codes(tb, cell0, nvalid, a.W, a.Wt, a.s, a.gt_total, a.bg, g0, a.gp, code, mx, t, QT);
-        __syncthreads();
-        if (TMA && t == 0 && it + kStages - 1 < ntiles) {
-            const int nit = it + kStages - 1;
-            const int nst = nit % kStages;
-            mbar_arrive_expect_tx(&bars[nst], stage_bytes);
-            asm volatile(
-                "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
-                " [%0], [%1, {%2, %3}], [%4];"
-                ::"r"(smem_u32(stage + nst * stage_floats)), "l"(&tmap),
-                  "r"(cell_begin + nit * KC), "r"((int)row0), "r"(smem_u32(&bars[nst]))
-                : "memory");
-        }
-        if (t < a.qrows) {
-            float trow[NROW];
-#pragma unroll
-            for (int i = 0; i < NROW; ++i) trow[i] = 0.0f;
-            const float* rowp = sx + t * KC;
-#pragma unroll 2
-            for (int c = 0; c < KC / 4; ++c) {
+            if (++run_tiles >= kFlushTiles) flush();
+        } else {
+            // ---------------- label changes inside the box -------------------
+            for (int c = 0; c < KBOX / 4; ++c) {
                 const float4 v = *reinterpret_cast<const float4*>(rowp + ((c ^ (t & 7)) << 2));
-                const float xs[4] = {v.x, v.y, v.z, v.w};
+                const float xv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int k = c * 4 + u;
-                    if (k >= nvalid) break;
-                    const float x = xs[u];
-                    const Elem e = elem(x);
+                    const int cc = __shfl_sync(0xffffffffu, my_code, k);
+                    if (k >= nv) continue;
+                    const Elem e = elem(xv[u]);
                     const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
                     const float nt = FOC ? focal_neg(foc, e) : e.neg;
-                    float dlt;
-                    if (FOC) dlt = w * (focal_pos(foc, e) - nt);
-                    else if (UNC) dlt = -w * x;
-                    else dlt = -x;  // softplus(-x) - softplus(x) == -x exactly
-                    if (UNC) {
+                    const float dl = FOC ? w * (focal_pos(foc, e) - nt) : -w * xv[u];
+                    if (FAST) {
+                        trow[0] += fmaxf(xv[u], 0.0f); trow[1] += e.p;
+                        trow[2] += e.sp * 1.4426950408889634f;
+                    } else if (UNC) {
                         trow[0] += w * nt; trow[1] += w * e.p; trow[2] += w;
                         trow[3] += nt; trow[4] += e.p;
                     } else {
                         trow[0] += nt; trow[1] += e.p;
                     }
-                    const int cc = code[k];
                     if (cc >= kNone) {
-                        if (cc != cur) { flush(cur); cur = cc; }
+                        if (cc != cur) { flush(); cur = cc; }
                         if (cc >= 0) {
-                            racc[0] += dlt;
+                            racc[0] += FAST ? xv[u] : dl;
                             racc[1] += w * e.p;
                             if (UNC) racc[2] += w;
                         }
-                    } else {  // mixed cell: one count per pixel
-                        const int16_t* mc = mx + k * s2;
-                        for (int pp = 0; pp < s2; ++pp) {
-                            const int col = mc[pp];
+                    } else if (qvalid) {  // mixed cell: one count per pixel
+                        const int cell = cell0 + h * KBOX + k;
+                        const int ci = cell / a.W, cj = cell - ci * a.W;
+                        const int64_t* r0 = a.targets + ((int64_t)b * a.Ht + (int64_t)ci * a.s) * a.Wt +
+                                            (int64_t)cj * a.s;
+                        for (int pp = 0; pp < a.s * a.s; ++pp) {
+                            const int col = label_to_col(r0[(int64_t)(pp / a.s) * a.Wt + (pp % a.s)],
+                                                         a.gt_total, a.bg);
                             if (col >= 0) {
-                                bins[(0 * a.gp + col) * QT + t] += dlt;
-                                bins[(1 * a.gp + col) * QT + t] += w * e.p;
-                                if (UNC) bins[(2 * a.gp + col) * QT + t] += w;
+                                float* pc = part + (int64_t)col * QP + t;
+                                red_add(pc, dl);
+                                red_add(pc + (int64_t)G * QP, w * e.p);
+                                if (UNC) red_add(pc + 2 * (int64_t)G * QP, w);
                             }
                         }
                     }
                 }
             }
-            flush(cur);  // two-level summation: runs never span tiles
-#pragma unroll
-            for (int i = 0; i < NROW; ++i) rows[i] += trow[i];
+            flush();
         }
-    }
-
-    if (!ok && t == 0) atomicOr(a.status, 2);
-    if (!qvalid) return;
-    float* out = a.part + ((((int64_t)lb * a.nqt + qt) * a.ngr + gr) * a.nchunk + blockIdx.x) *
-                              (int64_t)a.part_stride;
-    for (int i = 0; i < NACC * a.gp; ++i) out[i * a.qrows_pad + t] = bins[i * QT + t];
 #pragma unroll
-    for (int i = 0; i < NROW; ++i) out[(NACC * a.gp + i) * a.qrows_pad + t] = rows[i];
+        for (int i = 0; i < NROW; ++i) rows[i] += trow[i];
+    }
+    flush();
+
+    if (!ok && tid == 0 && a.status) atomicOr(a.status, 2);
+    if (!qvalid) return;
+    float* pr = part + (int64_t)NACC * G * QP + t;
+#pragma unroll
+    for (int i = 0; i < NROW; ++i) pr[(int64_t)i * QP] = rows[i];
 }
 
 // ---------------------------------------------------------------------------
-// Finalize: fixed-order reduction of the chunk partials, cost formulas,
-// label cost, total cost, and the per-query terms the loss needs.
-// grid = (nqt, L*B); block = 256.
+// Finalize, per query: reduce the row partials, the per-query terms the loss
+// needs, and the class row statistics.  One warp per query row.
+// qstat layout: P, Wtot, um_mask, um_dice, um_cls, base, cls_row, -
 // ---------------------------------------------------------------------------
-template <bool UNC>
-__global__ void __launch_bounds__(256) cost_finalize_kernel(CostArgs a) {
+template <bool UNC, bool FAST>
+__global__ void __launch_bounds__(256) cost_rows_kernel(CostArgs a) {
     constexpr int NACC = UNC ? 3 : 2;
-    constexpr int NROW = UNC ? 5 : 2;
-    extern __shared__ float fsh[];
-    const int qt = blockIdx.x;
-    const int lb = blockIdx.y;
-    const int l = lb / a.B, b = lb % a.B;
-    const int nq = min(a.qrows, a.Q - qt * a.qrows);
-    if (nq <= 0) return;
-    float* rP = fsh;              // P = N2 * sum w p
-    float* rWt = rP + a.qrows;    // weight total (normalised)
-    float* rBase = rWt + a.qrows; // N2 * sum w neg
-    float* rLse = rBase + a.qrows;  // class: lse (softmax) or sum focal-neg (sigmoid)
+    constexpr int NROW = UNC ? 5 : 3;
+    const int64_t qi = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (qi >= (int64_t)a.L * a.B * a.Q) return;
+    const int lb = (int)(qi / a.Q);
+    const int q = (int)(qi - (int64_t)lb * a.Q);
+    const int qt = q / a.qrows, t = q - qt * a.qrows;
     const int HW = a.H * a.W;
     const float N2 = (float)(a.s * a.s);
-    const int tid = threadIdx.x;
-
-    // rows
-    for (int t = tid; t < nq; t += blockDim.x) {
-        float r[NROW];
+    // rows: lanes stride over the 2*nchunk partial slots, fixed-order warp sum
+    float r[NROW];
 #pragma unroll
-        for (int i = 0; i < NROW; ++i) r[i] = 0.0f;
-        for (int ch = 0; ch < a.nchunk; ++ch) {
-            const float* p = a.part + ((((int64_t)lb * a.nqt + qt) * a.ngr + 0) * a.nchunk + ch) *
-                                          (int64_t)a.part_stride;
+    for (int i = 0; i < NROW; ++i) r[i] = 0.0f;
+    const int nslot = 2 * a.nchunk;
+    const float* pbase = a.part + (((int64_t)lb * a.nqt + qt) * nslot) * (int64_t)a.part_stride +
+                         (int64_t)NACC * a.gout * a.qrows_pad + t;
+    for (int sl = lane; sl < nslot; sl += 32) {
+        const float* p = pbase + (int64_t)sl * a.part_stride;
 #pragma unroll
-            for (int i = 0; i < NROW; ++i) r[i] += p[(NACC * a.gp + i) * a.qrows_pad + t];
-        }
-        float base = r[0] * N2, P = r[1] * N2;
-        float wt = UNC ? r[2] * N2 : (float)a.Ht * (float)a.Wt;
-        if (!a.normalize_uncertainty) wt = (float)a.Ht * (float)a.Wt;
-        wt = fmaxf(wt, 1e-12f);
-        rP[t] = P; rWt[t] = wt; rBase[t] = base;
-        // unmatched-mask terms (src/cuda/mask_matching_forward.cu:122-143,224-235):
-        // unweighted BCE mean over HW and empty-mask dice.
-        const float su = UNC ? r[3] : r[0];
-        const float pu = UNC ? r[4] : r[1];
-        const int64_t qi = (int64_t)lb * a.Q + qt * a.qrows + t;
-        const float ps = pu * a.area_scale;
-        a.qstat[qi * kQStat + 2] = a.sigmoid_scale * (su / (float)HW);
-        a.qstat[qi * kQStat + 3] = a.dice_scale * (ps / (ps + a.smooth));
-        a.qstat[qi * kQStat + 0] = P;
-        a.qstat[qi * kQStat + 1] = wt;
+        for (int i = 0; i < NROW; ++i) r[i] += p[(int64_t)i * a.qrows_pad];
     }
-
-    // class rows: one warp per query
-    const int warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int i = 0; i < NROW; ++i) r[i] = warp_sum(r[i]);
+    // class row: lse (softmax) / sum of focal-neg terms (sigmoid), and the
+    // unmatched class term (src/cuda/mask_matching_forward.cu:150-276)
+    const float* z = a.cls_logits + qi * a.C;
     const Focal cf = make_focal(a.cls_gamma, a.cls_alpha);
-    const bool fwd_sig_focal = !a.use_softmax;  // forward kernel uses focal only for sigmoid
-    const Focal uf = make_focal(fwd_sig_focal ? a.cls_gamma : 0.0f, fwd_sig_focal ? a.cls_alpha : -1.0f);
-    for (int t = warp; t < nq; t += nw) {
-        const int64_t qi = (int64_t)lb * a.Q + qt * a.qrows + t;
-        const float* z = a.cls_logits + qi * a.C;
-        float m = -INFINITY;
-        for (int c = lane; c < a.C; c += 32) m = fmaxf(m, z[c]);
-        m = warp_max(m);
-        float se = 0.0f, sn = 0.0f, snu = 0.0f;
-        for (int c = lane; c < a.C; c += 32) {
-            const float zc = z[c];
-            se += __expf(zc - m);
-            const Elem e = elem(zc);
-            sn += focal_neg(cf, e);
-            snu += focal_neg(uf, e);
-        }
-        se = warp_sum(se); sn = warp_sum(sn); snu = warp_sum(snu);
-        const float lse = __logf(fmaxf(se, 1e-20f)) + m;
-        if (lane == 0) {
-            rLse[t] = a.use_softmax ? lse : sn;
-            // unmatched class loss (src/cuda/mask_matching_forward.cu:150-276)
-            float um = 0.0f;
-            if (a.has_void) {
-                const float zv = z[a.void_index];
-                if (a.use_softmax && a.force_cls) {
-                    um = lse - zv;
-                } else {
-                    const Elem ev = elem(zv);
-                    const float vp = focal_pos(uf, ev), vn = focal_neg(uf, ev);
-                    um = a.force_cls ? (snu / (float)a.C + (vp - vn) / (float)a.C) : vp;
-                }
-            } else if (a.force_cls) {
-                um = snu / (float)a.C;
-            }
-            a.qstat[qi * kQStat + 4] = um * a.cls_scale;
-        }
+    const Focal uf = make_focal(a.use_softmax ? 0.0f : a.cls_gamma, a.use_softmax ? -1.0f : a.cls_alpha);
+    float m = -INFINITY;
+    for (int c = lane; c < a.C; c += 32) m = fmaxf(m, z[c]);
+    m = warp_max(m);
+    float se = 0.0f, sn = 0.0f, snu = 0.0f;
+    for (int c = lane; c < a.C; c += 32) {
+        const float zc = z[c];
+        se += __expf(zc - m);
+        const Elem e = elem(zc);
+        sn += focal_neg(cf, e);
+        snu += focal_neg(uf, e);
     }
-    __syncthreads();
+    se = warp_sum(se); sn = warp_sum(sn); snu = warp_sum(snu);
+    if (lane != 0) return;
+    float base, P, wt, su, pu;
+    if (UNC) {
+        base = r[0] * N2; P = r[1] * N2; wt = r[2] * N2; su = r[3]; pu = r[4];
+    } else if (FAST) {
+        su = r[0] + r[2] * 0.6931471805599453f;  // sum softplus(x) = sum max(x,0) + ln2 * sum log2(1+e)
+        pu = r[1];
+        base = su * N2; P = pu * N2; wt = (float)a.Ht * (float)a.Wt;
+    } else {
+        su = r[0]; pu = r[1];
+        base = su * N2; P = pu * N2; wt = (float)a.Ht * (float)a.Wt;
+    }
+    if (!a.normalize_uncertainty) wt = (float)a.Ht * (float)a.Wt;
+    wt = fmaxf(wt, 1e-12f);
+    const float lse = __logf(fmaxf(se, 1e-20f)) + m;
+    float um = 0.0f;
+    if (a.has_void) {
+        const float zv = z[a.void_index];
+        if (a.use_softmax && a.force_cls) {
+            um = lse - zv;
+        } else {
+            const Elem ev = elem(zv);
+            const float vp = focal_pos(uf, ev), vn = focal_neg(uf, ev);
+            um = a.force_cls ? (snu / (float)a.C + (vp - vn) / (float)a.C) : vp;
+        }
+    } else if (a.force_cls) {
+        um = snu / (float)a.C;
+    }
+    const float ps = pu * a.area_scale;
+    float* o = a.qstat + qi * kQStat;
+    o[0] = P;
+    o[1] = wt;
+    o[2] = a.sigmoid_scale * (su / (float)HW);     // unmatched: BCE mean against empty
+    o[3] = a.dice_scale * (ps / (ps + a.smooth));  // unmatched: empty-mask dice
+    o[4] = um * a.cls_scale;
+    o[5] = base;
+    o[6] = a.use_softmax ? lse : sn;
+}
 
-    // pairs (q, g)
+// ---------------------------------------------------------------------------
+// Finalize, per (q, g) pair: fixed-order reduction of the run partials, cost
+// formulas (src/cuda/pw_mask.cu:290-304), label cost, total cost.
+// grid = (ceil(qrows*G / 256), nqt, L*B), q fastest within a block.
+// ---------------------------------------------------------------------------
+template <bool UNC>
+__global__ void __launch_bounds__(256) cost_pairs_kernel(CostArgs a) {
+    constexpr int NACC = UNC ? 3 : 2;
+    const int qt = blockIdx.y, lb = blockIdx.z, b = lb % a.B;
+    const int nq = min(a.qrows, a.Q - qt * a.qrows);
     const int G = a.gout;
-    const int64_t slice = (int64_t)a.L * a.B * a.Q * G;
-    for (int i = tid; i < nq * G; i += blockDim.x) {
-        const int g = i / nq, t = i - g * nq;
-        const int gr = g / a.gp, gl = g - gr * a.gp;
-        float acc[NACC];
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nq * G) return;
+    const int g = i / nq, t = i - g * nq;
+    const int nslot = 2 * a.nchunk;
+    const float* p = a.part + (((int64_t)lb * a.nqt + qt) * nslot) * (int64_t)a.part_stride +
+                     (int64_t)g * a.qrows_pad + t;
+    float acc[NACC];
 #pragma unroll
-        for (int k = 0; k < NACC; ++k) acc[k] = 0.0f;
-        for (int ch = 0; ch < a.nchunk; ++ch) {
-            const float* p = a.part + ((((int64_t)lb * a.nqt + qt) * a.ngr + gr) * a.nchunk + ch) *
-                                          (int64_t)a.part_stride;
+    for (int k = 0; k < NACC; ++k) acc[k] = 0.0f;
+    for (int sl = 0; sl < nslot; ++sl) {
+        const float* ps = p + (int64_t)sl * a.part_stride;
 #pragma unroll
-            for (int k = 0; k < NACC; ++k) acc[k] += p[(k * a.gp + gl) * a.qrows_pad + t];
-        }
-        const int ga = g + (g >= a.bg ? 1 : 0);
-        const int64_t qi = (int64_t)lb * a.Q + qt * a.qrows + t;
-        const int64_t o = qi * G + g;
-        const int32_t tc = a.totals[(int64_t)b * a.gt_total + ga];
-        const float T = UNC ? acc[2] : (float)tc;
-        float bce, dice;
-        if (tc == 0) {
-            bce = INFINITY; dice = INFINITY;
-        } else {
-            bce = (rBase[t] + acc[0]) / rWt[t] * a.sigmoid_scale;
-            dice = (1.0f - (2.0f * acc[1] + a.smooth) / (rP[t] + T + a.smooth)) * a.dice_scale;
-        }
-        // label cost
-        const int64_t y = a.cls_targets[(int64_t)b * a.gt_total + ga];
-        float cls;
-        if (y < 0 || y >= a.C) {
-            cls = INFINITY;
-        } else {
-            const float zy = a.cls_logits[qi * a.C + y];
-            if (a.use_softmax) {
-                cls = (rLse[t] - zy) * a.cls_scale;
-            } else {
-                const Elem e = elem(zy);
-                cls = (rLse[t] + focal_pos(cf, e) - focal_neg(cf, e)) / (float)a.C * a.cls_scale;
-            }
-        }
-        if (a.sep) {
-            a.sep[o] = bce;
-            a.sep[slice + o] = dice;
-            a.sep[2 * slice + o] = cls;
-        }
-        if (a.total) a.total[o] = (bce + dice) + cls;
-        if (a.rawI) { a.rawI[o] = acc[1]; a.rawT[o] = T; }
+        for (int k = 0; k < NACC; ++k) acc[k] += ps[(int64_t)k * G * a.qrows_pad];
     }
+    const int ga = g + (g >= a.bg ? 1 : 0);
+    const int64_t qi = (int64_t)lb * a.Q + qt * a.qrows + t;
+    const int64_t o = qi * G + g;
+    const float* qs = a.qstat + qi * kQStat;
+    const int32_t tc = a.totals[(int64_t)b * a.gt_total + ga];
+    const float T = UNC ? acc[2] : (float)tc;
+    float bce, dice;
+    if (tc == 0) {
+        bce = INFINITY; dice = INFINITY;
+    } else {
+        bce = (qs[5] + acc[0]) / qs[1] * a.sigmoid_scale;
+        dice = (1.0f - (2.0f * acc[1] + a.smooth) / (qs[0] + T + a.smooth)) * a.dice_scale;
+    }
+    const int64_t y = a.cls_targets[(int64_t)b * a.gt_total + ga];
+    float cls;
+    if (y < 0 || y >= a.C) {
+        cls = INFINITY;
+    } else {
+        const float zy = a.cls_logits[qi * a.C + y];
+        if (a.use_softmax) {
+            cls = (qs[6] - zy) * a.cls_scale;
+        } else {
+            const Focal cf = make_focal(a.cls_gamma, a.cls_alpha);
+            const Elem e = elem(zy);
+            cls = (qs[6] + focal_pos(cf, e) - focal_neg(cf, e)) / (float)a.C * a.cls_scale;
+        }
+    }
+    const int64_t slice = (int64_t)a.L * a.B * a.Q * G;
+    if (a.sep) {
+        a.sep[o] = bce;
+        a.sep[slice + o] = dice;
+        a.sep[2 * slice + o] = cls;
+    }
+    if (a.total) a.total[o] = (bce + dice) + cls;
+    if (a.rawI) { a.rawI[o] = acc[1]; a.rawT[o] = T; }
 }
 
 template __global__ void cost_partial_kernel<false, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
@@ -428,12 +494,11 @@ template __global__ void cost_partial_kernel<false, true, true>(const __grid_con
 template __global__ void cost_partial_kernel<false, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
 template __global__ void cost_partial_kernel<true, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
 template __global__ void cost_partial_kernel<true, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_finalize_kernel<false>(CostArgs);
-template __global__ void cost_finalize_kernel<true>(CostArgs);
-
-}  // namespace mlb
-
-namespace mlb {
+template __global__ void cost_rows_kernel<false, false>(CostArgs);
+template __global__ void cost_rows_kernel<false, true>(CostArgs);
+template __global__ void cost_rows_kernel<true, false>(CostArgs);
+template __global__ void cost_pairs_kernel<false>(CostArgs);
+template __global__ void cost_pairs_kernel<true>(CostArgs);
 
 // Standalone pairwise label cost, one warp per (l,b,q) row
 // (src/cuda/pw_softmax_label_loss.cu:12-103, src/cuda/pw_sigmoid_label_loss.cu:16-106).

@@ -8,10 +8,12 @@
 
 namespace mlb {
 
-constexpr int KC = 32;            // cells per pipeline tile (128-byte TMA rows)
-constexpr int kStages = 4;        // TMA pipeline depth
+constexpr int KBOX = 32;          // cells per TMA box row (128 bytes, one swizzle span)
+constexpr int KC = 2 * KBOX;      // cells per pipeline tile (two boxes)
+constexpr int kStages = 3;        // TMA pipeline depth
+constexpr int kFlushTiles = 8;    // longest register run (tiles) before a flush
 constexpr int kHistSmemMax = 8192;
-constexpr int kQStat = 5;         // per-query: P, Wtot, um_mask, um_dice, um_cls
+constexpr int kQStat = 8;         // per-query: P, Wtot, um_mask, um_dice, um_cls, base, cls_row, -
 constexpr int kSaved = 4;         // saved for backward: P, T, I, Wtot
 
 struct CostArgs {
@@ -20,6 +22,7 @@ struct CostArgs {
     const float* cls_logits;
     const int64_t* cls_targets;
     const int32_t* totals;   // (B, GT_total)
+    const int32_t* codes;    // (B, H*W) per-cell column code
     float* part;             // chunk partials
     float* sep;              // (3,L,B,Q,G) or null
     float* total;            // (L,B,Q,G) or null
@@ -30,7 +33,6 @@ struct CostArgs {
     int L, B, Q, H, W, Ht, Wt, s, C;
     int gt_total, gout, bg;  // bg == gt_total when no column is dropped
     int qrows, qrows_pad, nqt;
-    int gp, ngr;             // column-range width and count
     int chunk_cells, nchunk;
     int part_stride;         // floats per CTA partial
     float smooth, sigmoid_scale, dice_scale, cls_scale;
@@ -41,14 +43,18 @@ struct CostArgs {
     int use_softmax, force_cls, has_void, void_index;
 };
 
-__global__ void label_hist_kernel(const int64_t* __restrict__ targets, int64_t npix, int gt_total,
+__global__ void label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int Wt,
+                                  int s, int gt_total, int bg, int32_t* __restrict__ codes,
                                   int32_t* __restrict__ totals);
 
 template <bool UNC, bool FOC, bool TMA>
 __global__ void cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a);
 
+template <bool UNC, bool FAST>
+__global__ void cost_rows_kernel(CostArgs a);
+
 template <bool UNC>
-__global__ void cost_finalize_kernel(CostArgs a);
+__global__ void cost_pairs_kernel(CostArgs a);
 
 }  // namespace mlb
 
