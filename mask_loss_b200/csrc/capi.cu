@@ -89,7 +89,7 @@ struct FwdPlan {
 };
 
 size_t cost_smem_bytes(int qrows_pad) {
-    return 1024 + (size_t)kStages * (2 * (size_t)qrows_pad * KBOX * 4 + KC * 4) + 8 * kStages;
+    return 1024 + (size_t)kStages * (2 * (size_t)qrows_pad * KBOX * 4 + KC * 4) + 16 * kStages;
 }
 
 int validate_dims(const ml_dims* d) {
@@ -151,7 +151,7 @@ int make_plan(const ml_dims* d, const ml_params* p, FwdPlan* P) {
     P->qrows = (Q + P->nqt - 1) / P->nqt;
     P->qrows_pad = (P->qrows + 31) / 32 * 32;
     P->cost_smem = cost_smem_bytes(P->qrows_pad);
-    const int threads = 2 * P->qrows_pad;
+    const int threads = 2 * P->qrows_pad + 32;
     int per_sm = (int)std::min<size_t>(228 * 1024 / (P->cost_smem + 1024), 2048 / threads);
     if (per_sm < 1) per_sm = 1;
     // chunks per (image, query tile): smallest count whose CTA total fills the
@@ -230,7 +230,7 @@ int launch_cost_t(const FwdPlan& P, const CUtensorMap& tm, const CostArgs& a, cu
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.cost_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cost_partial_kernel attributes");
     dim3 grid(P.nchunk, P.nqt, P.L * P.B);
-    k<<<grid, 2 * P.qrows_pad, P.cost_smem, st>>>(tm, a);
+    k<<<grid, 2 * P.qrows_pad + 32, P.cost_smem, st>>>(tm, a);
     ML_CHECK_LAUNCH("cost_partial_kernel");
     return ML_OK;
 }

@@ -100,16 +100,38 @@ ML_INLINE void red_add(float* p, float v) {
     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 
+// Mixed cell (s > 1 on a label boundary): add the cell's per-pixel counts to
+// the columns they belong to, one red.add per pixel and accumulator.
+template <bool UNC>
+__device__ __noinline__ void mixed_cell(const int64_t* targets, int W, int Ht, int Wt, int s,
+                                        int gt_total, int bg, float* part, int b, int cell, int t,
+                                        int QP, int G, float dl, float wp, float w) {
+    const int ci = cell / W, cj = cell - ci * W;
+    const int64_t* r0 = targets + ((int64_t)b * Ht + (int64_t)ci * s) * Wt + (int64_t)cj * s;
+    for (int pp = 0; pp < s * s; ++pp) {
+        const int col = label_to_col(r0[(int64_t)(pp / s) * Wt + (pp % s)], gt_total, bg);
+        if (col >= 0) {
+            float* pc = part + (int64_t)col * QP + t;
+            red_add(pc, dl);
+            red_add(pc + (int64_t)G * QP, wp);
+            if (UNC) red_add(pc + 2 * (int64_t)G * QP, w);
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // The streaming cost kernel.  grid = (nchunk, nqt, L*B); block = 2*qrows_pad
-// threads: thread (h, t) <-> query row qt*qrows + t, cells [h*32, h*32+32) of
-// every 64-cell tile.  Template flags:
+// consumer threads plus one producer warp.  The producer fills a 3-stage ring
+// (full/empty mbarriers, no block-wide barrier in the loop); consumer thread
+// (h, t) <-> query row qt*qrows + t, cells [h*32, h*32+32) of every 64-cell
+// tile.  Inside a box the run starts are one ballot (bnd), so the element
+// loop only branches on 4-cell groups that contain a start.  Template flags:
 //   UNC   entropy weights on (uncertainty_gamma != 0)
 //   FOC   focal gamma/alpha on the mask BCE
 //   TMA   logits rows are 16-byte strided so the bulk-tensor path is legal
 // ---------------------------------------------------------------------------
 template <bool UNC, bool FOC, bool TMA>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(kCostThreads, 2)
 cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     constexpr int NACC = UNC ? 3 : 2;
     constexpr int NROW = UNC ? 5 : 3;
@@ -121,53 +143,92 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     const int box_floats = QP * KBOX;                  // one 32-cell box
     float* xs = reinterpret_cast<float*>(base);        // [stage][2][QP][32]
     int32_t* cs = reinterpret_cast<int32_t*>(xs + kStages * 2 * box_floats);  // [stage][KC]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(cs + kStages * KC);
+    uint64_t* full = reinterpret_cast<uint64_t*>(cs + kStages * KC);
+    uint64_t* empty = full + kStages;
 
     const int tid = threadIdx.x;
-    const int h = tid / QP;
-    const int t = tid - h * QP;
+    const int ncons = 2 * QP;                          // consumer threads
+    const int n_cwarps = ncons / 32;
     const int lane = tid & 31;
     const int lb = blockIdx.z;
     const int b = lb % a.B;
     const int qt = blockIdx.y;
-    const int q = qt * a.qrows + t;
-    const bool qvalid = (t < a.qrows) && (q < a.Q);
     const int HW = a.H * a.W;
     const int cell_begin = blockIdx.x * a.chunk_cells;
     const int cell_end = min(HW, cell_begin + a.chunk_cells);
     const int ntiles = (cell_end - cell_begin + KC - 1) / KC;
     const int row0 = lb * a.Q + qt * a.qrows;          // first global logits row
     const int32_t* codes_b = a.codes + (int64_t)b * HW;
+
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], n_cwarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (tid >= ncons) {
+        // ------------------------------ producer warp ------------------------------
+        bool ok = true;
+        for (int it = 0; it < ntiles && ok; ++it) {
+            const int st = it % kStages;
+            if (it >= kStages && !mbar_wait(&empty[st], (uint32_t)(((it / kStages) - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            const int c0 = cell_begin + it * KC;
+            const int nvalid = min(KC, cell_end - c0);
+            if (TMA) {
+                if (lane == 0) {
+                    const uint32_t cbytes = (uint32_t)min(KC, HW - c0) * 4u;
+                    mbar_arrive_expect_tx(&full[st], 2u * a.qrows * KBOX * 4u + cbytes);
+#pragma unroll
+                    for (int bx = 0; bx < 2; ++bx)
+                        asm volatile(
+                            "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+                            " [%0], [%1, {%2, %3}], [%4];"
+                            ::"r"(smem_u32(xs + (st * 2 + bx) * box_floats)), "l"(&tmap),
+                              "r"(c0 + bx * KBOX), "r"(row0), "r"(smem_u32(&full[st])) : "memory");
+                    bulk_g2s(cs + st * KC, codes_b + c0, cbytes, &full[st]);
+                }
+            } else {
+                // plain loads into the same swizzled layout, then one arrive
+                for (int i = lane; i < 2 * a.qrows * (KBOX / 4); i += 32) {
+                    const int bx = i / (a.qrows * (KBOX / 4));
+                    const int rem = i - bx * a.qrows * (KBOX / 4);
+                    const int r = rem / (KBOX / 4), c = rem - r * (KBOX / 4);
+                    const float* src = a.logits + (int64_t)(row0 + r) * HW + c0 + bx * KBOX + c * 4;
+                    float4 v;
+                    float* vv = reinterpret_cast<float*>(&v);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int k = bx * KBOX + c * 4 + u;
+                        vv[u] = (k < nvalid) ? src[u] : 0.0f;
+                    }
+                    *reinterpret_cast<float4*>(xs + (st * 2 + bx) * box_floats + r * KBOX +
+                                               ((c ^ (r & 7)) << 2)) = v;
+                }
+                for (int k = lane; k < KC; k += 32) cs[st * KC + k] = k < nvalid ? codes_b[c0 + k] : kNone;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[st]);
+            }
+        }
+        if (!ok && lane == 0 && a.status) atomicOr(a.status, 2);
+        return;
+    }
+
+    // ------------------------------- consumers -----------------------------------
+    const int h = tid / QP;
+    const int t = tid - h * QP;
+    const int q = qt * a.qrows + t;
+    const bool qvalid = (t < a.qrows) && (q < a.Q);
     const int G = a.gout;
     float* part = a.part + ((((int64_t)lb * a.nqt + qt) * a.nchunk + blockIdx.x) * 2 + h) *
                                (int64_t)a.part_stride;
     const float N2 = (float)(a.s * a.s);
     const Focal foc = make_focal(a.mask_gamma, a.mask_alpha);
-
-    auto issue = [&](int it) {  // one thread: loads of tile `it` into stage it % S
-        const int st = it % kStages;
-        const int c0 = cell_begin + it * KC;
-        const uint32_t cbytes = (uint32_t)min(KC, HW - c0) * 4u;
-        mbar_arrive_expect_tx(&bars[st], 2u * a.qrows * KBOX * 4u + cbytes);
-#pragma unroll
-        for (int bx = 0; bx < 2; ++bx)
-            asm volatile(
-                "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
-                " [%0], [%1, {%2, %3}], [%4];"
-                ::"r"(smem_u32(xs + (st * 2 + bx) * box_floats)), "l"(&tmap), "r"(c0 + bx * KBOX),
-                  "r"(row0), "r"(smem_u32(&bars[st])) : "memory");
-        bulk_g2s(cs + st * KC, codes_b + c0, cbytes, &bars[st]);
-    };
-
-    if (TMA) {
-        if (tid == 0) {
-            for (int i = 0; i < kStages; ++i) mbar_init(&bars[i], 1);
-            fence_mbar_init();
-        }
-        __syncthreads();
-        if (tid == 0)
-            for (int i = 0; i < kStages - 1 && i < ntiles; ++i) issue(i);
-    }
 
     float racc[NACC];
 #pragma unroll
@@ -175,7 +236,8 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     float rows[NROW];
 #pragma unroll
     for (int i = 0; i < NROW; ++i) rows[i] = 0.0f;
-    int cur = kNone;
+    int cur = kNone;     // code of the current run (uniform within a warp)
+    float m = 0.0f;      // 1 while the current run belongs to an output column
     int run_tiles = 0;
     bool ok = true;
 
@@ -191,146 +253,98 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
         run_tiles = 0;
     };
 
+    // per-element update of the row sums and the run accumulators
+    float trow[NROW] = {};
+    float prod = 1.0f;
+    auto element = [&](float x, int cell) {
+        if (FAST) {
+            const Fast f = fast_elem(x);
+            prod *= f.d;
+            trow[0] += fmaxf(x, 0.0f);
+            trow[1] += f.p;
+            racc[0] = fmaf(m, x, racc[0]);
+            racc[1] = fmaf(m, f.p, racc[1]);
+            if (cur == kMixed && qvalid)
+                mixed_cell<UNC>(a.targets, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, -x, f.p, 1.0f);
+        } else {
+            const Elem e = elem(x);
+            const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
+            const float nt = FOC ? focal_neg(foc, e) : e.neg;
+            const float dl = FOC ? w * (focal_pos(foc, e) - nt) : -w * x;
+            if (UNC) {
+                trow[0] += w * nt; trow[1] += w * e.p; trow[2] += w;
+                trow[3] += nt; trow[4] += e.p;
+            } else {
+                trow[0] += nt; trow[1] += e.p;
+            }
+            racc[0] = fmaf(m, dl, racc[0]);
+            racc[1] = fmaf(m, w * e.p, racc[1]);
+            if (UNC) racc[2] = fmaf(m, w, racc[2]);
+            if (cur == kMixed && qvalid)
+                mixed_cell<UNC>(a.targets, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, dl, w * e.p, w);
+        }
+    };
+
     for (int it = 0; it < ntiles; ++it) {
         const int st = it % kStages;
         const int cell0 = cell_begin + it * KC;
         const int nvalid = min(KC, cell_end - cell0);
-        if (TMA) {
-            if (!mbar_wait(&bars[st], (uint32_t)((it / kStages) & 1))) ok = false;
-            __syncthreads();  // everyone is done with the stage refilled below
-            if (tid == 0 && it + kStages - 1 < ntiles) issue(it + kStages - 1);
-        } else {
-            __syncthreads();
-            for (int i = tid; i < 2 * a.qrows * (KBOX / 4); i += blockDim.x) {
-                const int bx = i / (a.qrows * (KBOX / 4));
-                const int rem = i - bx * a.qrows * (KBOX / 4);
-                const int r = rem / (KBOX / 4), c = rem - r * (KBOX / 4);
-                const float* src = a.logits + (int64_t)(row0 + r) * HW + cell0 + bx * KBOX + c * 4;
-                float4 v;
-                float* vv = reinterpret_cast<float*>(&v);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int k = bx * KBOX + c * 4 + u;
-                    vv[u] = (k < nvalid) ? src[u] : 0.0f;
-                }
-                *reinterpret_cast<float4*>(xs + (st * 2 + bx) * box_floats + r * KBOX +
-                                           ((c ^ (r & 7)) << 2)) = v;
-            }
-            for (int k = tid; k < KC; k += blockDim.x)
-                cs[st * KC + k] = k < nvalid ? codes_b[cell0 + k] : kNone;
-            __syncthreads();
-        }
+        if (!mbar_wait(&full[st], (uint32_t)((it / kStages) & 1))) { ok = false; break; }
         // this thread's 32 cells: box h of the stage
         const int nv = min(KBOX, max(0, nvalid - h * KBOX));
         const int32_t* code = cs + st * KC + h * KBOX;
         const int my_code = lane < nv ? code[lane] : kNone;
-        const int c0 = __shfl_sync(0xffffffffu, my_code, 0);
-        const bool uni = __all_sync(0xffffffffu, my_code == c0) && nv == KBOX && c0 >= kNone;
+        const int prev = __shfl_up_sync(0xffffffffu, my_code, 1);
+        const bool starts = lane < nv && (my_code == kMixed || my_code != (lane == 0 ? cur : prev));
+        const uint32_t bnd = __ballot_sync(0xffffffffu, starts);
         const float* rowp = xs + (st * 2 + h) * box_floats + t * KBOX;
-        float trow[NROW];
 #pragma unroll
         for (int i = 0; i < NROW; ++i) trow[i] = 0.0f;
-        if (uni) {
-            // ---------------- one label for the whole box -------------------
-            if (c0 != cur) { flush(); cur = c0; }
-            const bool acc = cur >= 0;
-            if (FAST) {
-                float prod = 1.0f;
-#pragma unroll
-                for (int c = 0; c < KBOX / 4; ++c) {
-                    const float4 v = *reinterpret_cast<const float4*>(rowp + ((c ^ (t & 7)) << 2));
-                    const float xv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const Fast f = fast_elem(xv[u]);
-                        prod *= f.d;
-                        trow[0] += fmaxf(xv[u], 0.0f);
-                        trow[1] += f.p;
-                        if (acc) { racc[0] += xv[u]; racc[1] += f.p; }
-                    }
-                    if (c & 1) { trow[2] += lg2_approx(prod); prod = 1.0f; }
-                }
-            } else {
+        prod = 1.0f;
+        if (nv == KBOX) {
 #pragma unroll 2
-                for (int c = 0; c < KBOX / 4; ++c) {
-                    const float4 v = *reinterpret_cast<const float4*>(rowp + ((c ^ (t & 7)) << 2));
-                    const float xv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const Elem e = elem(xv[u]);
-                        const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
-                        const float nt = FOC ? focal_neg(foc, e) : e.neg;
-                        const float dl = FOC ? w * (focal_pos(foc, e) - nt) : -w * xv[u];
-                        if (UNC) {
-                            trow[0] += w * nt; trow[1] += w * e.p; trow[2] += w;
-                            trow[3] += nt; trow[4] += e.p;
-                        } else {
-                            trow[0] += nt; trow[1] += e.p;
-                        }
-                        if (acc) {
-                            racc[0] += dl; racc[1] += w * e.p;
-                            if (UNC) racc[2] += w;
-                        }
-                    }
-                }
-            }
-            if (++run_tiles >= kFlushTiles) flush();
-        } else {
-            // ---------------- label changes inside the box -------------------
             for (int c = 0; c < KBOX / 4; ++c) {
                 const float4 v = *reinterpret_cast<const float4*>(rowp + ((c ^ (t & 7)) << 2));
                 const float xv[4] = {v.x, v.y, v.z, v.w};
+                const uint32_t b4 = (bnd >> (4 * c)) & 0xFu;
+                if (b4 == 0u) {
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int k = c * 4 + u;
-                    const int cc = __shfl_sync(0xffffffffu, my_code, k);
-                    if (k >= nv) continue;
-                    const Elem e = elem(xv[u]);
-                    const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
-                    const float nt = FOC ? focal_neg(foc, e) : e.neg;
-                    const float dl = FOC ? w * (focal_pos(foc, e) - nt) : -w * xv[u];
-                    if (FAST) {
-                        trow[0] += fmaxf(xv[u], 0.0f); trow[1] += e.p;
-                        trow[2] += e.sp * 1.4426950408889634f;
-                    } else if (UNC) {
-                        trow[0] += w * nt; trow[1] += w * e.p; trow[2] += w;
-                        trow[3] += nt; trow[4] += e.p;
-                    } else {
-                        trow[0] += nt; trow[1] += e.p;
-                    }
-                    if (cc >= kNone) {
-                        if (cc != cur) { flush(); cur = cc; }
-                        if (cc >= 0) {
-                            racc[0] += FAST ? xv[u] : dl;
-                            racc[1] += w * e.p;
-                            if (UNC) racc[2] += w;
+                    for (int u = 0; u < 4; ++u) element(xv[u], cell0 + h * KBOX + 4 * c + u);
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        if ((b4 >> u) & 1u) {
+                            flush();
+                            cur = __shfl_sync(0xffffffffu, my_code, 4 * c + u);
+                            m = cur >= 0 ? 1.0f : 0.0f;
                         }
-                    } else if (qvalid) {  // mixed cell: one count per pixel
-                        const int cell = cell0 + h * KBOX + k;
-                        const int ci = cell / a.W, cj = cell - ci * a.W;
-                        const int64_t* r0 = a.targets + ((int64_t)b * a.Ht + (int64_t)ci * a.s) * a.Wt +
-                                            (int64_t)cj * a.s;
-                        for (int pp = 0; pp < a.s * a.s; ++pp) {
-                            const int col = label_to_col(r0[(int64_t)(pp / a.s) * a.Wt + (pp % a.s)],
-                                                         a.gt_total, a.bg);
-                            if (col >= 0) {
-                                float* pc = part + (int64_t)col * QP + t;
-                                red_add(pc, dl);
-                                red_add(pc + (int64_t)G * QP, w * e.p);
-                                if (UNC) red_add(pc + 2 * (int64_t)G * QP, w);
-                            }
-                        }
+                        element(xv[u], cell0 + h * KBOX + 4 * c + u);
                     }
                 }
+                if (FAST && (c & 1)) { trow[2] += lg2_approx(prod); prod = 1.0f; }
             }
-            flush();
+        } else {  // last, partial tile of the image
+            for (int k = 0; k < nv; ++k) {
+                const float x = rowp[((((k >> 2) ^ (t & 7)) << 2)) + (k & 3)];
+                if ((bnd >> k) & 1u) {
+                    flush();
+                    cur = __shfl_sync(0xffffffffu, my_code, k);
+                    m = cur >= 0 ? 1.0f : 0.0f;
+                }
+                element(x, cell0 + h * KBOX + k);
+                if (FAST) { trow[2] += lg2_approx(prod); prod = 1.0f; }
+            }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
 #pragma unroll
         for (int i = 0; i < NROW; ++i) rows[i] += trow[i];
+        if (bnd != 0u) run_tiles = 0;
+        if (++run_tiles >= kFlushTiles) flush();
     }
     flush();
 
-    if (!ok && tid == 0 && a.status) atomicOr(a.status, 2);
+    if (!ok && lane == 0 && a.status) atomicOr(a.status, 2);
     if (!qvalid) return;
     float* pr = part + (int64_t)NACC * G * QP + t;
 #pragma unroll

@@ -12,6 +12,7 @@ constexpr int KBOX = 32;          // cells per TMA box row (128 bytes, one swizz
 constexpr int KC = 2 * KBOX;      // cells per pipeline tile (two boxes)
 constexpr int kStages = 3;        // TMA pipeline depth
 constexpr int kFlushTiles = 8;    // longest register run (tiles) before a flush
+constexpr int kCostThreads = 288; // 256 consumers + 1 producer warp (upper bound)
 constexpr int kHistSmemMax = 8192;
 constexpr int kQStat = 8;         // per-query: P, Wtot, um_mask, um_dice, um_cls, base, cls_row, -
 constexpr int kSaved = 4;         // saved for backward: P, T, I, Wtot
