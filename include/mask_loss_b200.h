@@ -68,6 +68,18 @@ const char* ml_last_error(void);
 /* Library version as 10000*major + 100*minor + patch. */
 int ml_version(void);
 
+/* Number of kernels this library has launched in this process (monotonic). */
+int64_t ml_launch_count(void);
+
+/* Measurement hooks.  While enabled, the library records a CUDA event pair
+ * on the launching stream around every launch of its three hot kernels
+ * (kind 0: pairwise-cost streaming kernel, 1: mask-gradient kernel,
+ * 2: assignment solver).  ml_profile_read waits for the recorded events,
+ * returns the summed milliseconds and launch counts per kind (arrays of
+ * nkinds entries) and clears the record.  No counterpart in the reference. */
+void ml_profile_enable(int on);
+int ml_profile_read(float* ms, int64_t* launches, int nkinds);
+
 /* GT_out = GT_total minus the background column when it lies in range. */
 int64_t ml_gt_out(int64_t GT_total, int64_t background_index);
 

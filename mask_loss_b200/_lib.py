@@ -45,6 +45,9 @@ SIGNATURES = {
     "ml_last_error": (ctypes.c_char_p, []),
     "ml_version": (ctypes.c_int, []),
     "ml_gt_out": (c_i64, [c_i64, c_i64]),
+    "ml_launch_count": (c_i64, []),
+    "ml_profile_enable": (None, [ctypes.c_int]),
+    "ml_profile_read": (ctypes.c_int, [c_vp, c_vp, ctypes.c_int]),
     "ml_mask_matching_workspace_size": (c_sz, [ctypes.POINTER(Dims), ctypes.POINTER(Params)]),
     "ml_mask_matching_backward_workspace_size": (c_sz, [ctypes.POINTER(Dims), ctypes.POINTER(Params)]),
     "ml_match_workspace_size": (c_sz, [c_i64, c_i64, c_i64, c_i64]),

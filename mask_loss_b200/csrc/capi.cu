@@ -11,7 +11,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
+#include <vector>
 #include <string>
 
 #include "common.cuh"
@@ -38,11 +40,40 @@ int cuda_fail(cudaError_t e, const char* where) {
     return fail(ML_ECUDA, "CUDA error in %s: %s", where, cudaGetErrorString(e));
 }
 
+std::atomic<int64_t> g_launches{0};
+
 #define ML_CHECK_LAUNCH(where)                                  \
     do {                                                        \
+        g_launches.fetch_add(1, std::memory_order_relaxed);     \
         cudaError_t e_ = cudaGetLastError();                    \
         if (e_ != cudaSuccess) return cuda_fail(e_, where);     \
     } while (0)
+
+// Optional per-launch CUDA-event timing of the hot kernels (ml_profile_*).
+struct ProfRec {
+    cudaEvent_t a, b;
+    int kind;
+};
+std::mutex g_prof_mu;
+std::vector<ProfRec> g_prof;
+std::atomic<int> g_prof_on{0};
+
+struct ProfScope {
+    ProfRec r{nullptr, nullptr, -1};
+    cudaStream_t st;
+    ProfScope(int kind, cudaStream_t s) : st(s) {
+        if (!g_prof_on.load(std::memory_order_relaxed)) return;
+        if (cudaEventCreate(&r.a) != cudaSuccess || cudaEventCreate(&r.b) != cudaSuccess) return;
+        r.kind = kind;
+        cudaEventRecord(r.a, st);
+    }
+    ~ProfScope() {
+        if (r.kind < 0) return;
+        cudaEventRecord(r.b, st);
+        std::lock_guard<std::mutex> g(g_prof_mu);
+        g_prof.push_back(r);
+    }
+};
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -230,6 +261,7 @@ int launch_cost_t(const FwdPlan& P, const CUtensorMap& tm, const CostArgs& a, cu
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.cost_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cost_partial_kernel attributes");
     dim3 grid(P.nchunk, P.nqt, P.L * P.B);
+    ProfScope prof(0, st);
     k<<<grid, 2 * P.qrows_pad + 32, P.cost_smem, st>>>(tm, a);
     ML_CHECK_LAUNCH("cost_partial_kernel");
     return ML_OK;
@@ -325,7 +357,10 @@ int launch_match(const CT* costs, int64_t N, int64_t Q, int64_t G, double thr, i
     auto k = match_kernel<CT>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "match_kernel attributes");
-    k<<<(unsigned)N, 32, smem, st>>>(a);
+    {
+        ProfScope prof(2, st);
+        k<<<(unsigned)N, 32, smem, st>>>(a);
+    }
     ML_CHECK_LAUNCH("match_kernel");
     return ML_OK;
 }
@@ -368,6 +403,31 @@ const char* ml_status_string(int status) {
 const char* ml_last_error(void) { return g_last_error.c_str(); }
 
 int ml_version(void) { return 100; }
+
+int64_t ml_launch_count(void) { return g_launches.load(); }
+
+void ml_profile_enable(int on) { g_prof_on.store(on ? 1 : 0); }
+
+int ml_profile_read(float* ms, int64_t* launches, int nkinds) {
+    std::vector<ProfRec> recs;
+    {
+        std::lock_guard<std::mutex> g(g_prof_mu);
+        recs.swap(g_prof);
+    }
+    for (int k = 0; k < nkinds; ++k) { ms[k] = 0.0f; launches[k] = 0; }
+    int rc = ML_OK;
+    for (auto& r : recs) {
+        float t = 0.0f;
+        if (cudaEventSynchronize(r.b) == cudaSuccess && cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess) {
+            if (r.kind < nkinds) { ms[r.kind] += t; launches[r.kind] += 1; }
+        } else {
+            rc = fail(ML_ECUDA, "profile event read failed");
+        }
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    return rc;
+}
 
 int64_t ml_gt_out(int64_t GT_total, int64_t bg) {
     return GT_total - ((bg >= 0 && bg < GT_total) ? 1 : 0);
@@ -549,12 +609,15 @@ int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float*
     dim3 gg(nchunk, P.L * P.B);
     const size_t gs = sizeof(int) * ck;
 #define ML_MG(U, F, V) mask_grad_kernel<U, F, V><<<gg, 256, gs, st>>>(la)
+    {
+    ProfScope prof(1, st);
     if (unc) {
         if (foc) { if (vec) ML_MG(true, true, true); else ML_MG(true, true, false); }
         else { if (vec) ML_MG(true, false, true); else ML_MG(true, false, false); }
     } else {
         if (foc) { if (vec) ML_MG(false, true, true); else ML_MG(false, true, false); }
         else { if (vec) ML_MG(false, false, true); else ML_MG(false, false, false); }
+    }
     }
 #undef ML_MG
     ML_CHECK_LAUNCH("mask_grad_kernel");
