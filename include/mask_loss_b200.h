@@ -103,6 +103,29 @@ int ml_pairwise_mask_loss_forward(const ml_dims* d, const ml_params* p,
                                   float* out, void* workspace, size_t workspace_bytes,
                                   ml_stream_t stream);
 
+/* Same costs as ml_pairwise_mask_loss_forward, for callers that cannot
+ * allocate device memory (for example code that runs inside a host-side
+ * allocator, a memory pool or a callback that forbids cudaMalloc, or that
+ * runs where device memory is fully reserved up front).  No counterpart in
+ * the reference: it has no workspace argument, and its scratch lives in a
+ * file-scope device array of ml_noalloc_scratch_limit() bytes (64 MiB) that
+ * every GPU loading this library holds until the process exits.
+ *   - Calls larger than that limit fail with ML_EUNSUPPORTED and a message
+ *     (ml_last_error); use the workspace entry point for them.
+ *   - It calls no cudaMalloc/cudaFree and no allocating library routine.
+ *   - The first call on a device looks up the array's device address with
+ *     that device current; make that first call before any stream capture.
+ *   - Every call shares the one array: calls that can overlap on the GPU
+ *     (different streams, or different host threads on one device) race
+ *     and must be serialised by the caller. */
+int ml_pairwise_mask_loss_forward_noalloc(const ml_dims* d, const ml_params* p,
+                                          const float* mask_logits, const int64_t* mask_targets,
+                                          const float* cls_logits, const int64_t* cls_targets,
+                                          float* out, ml_stream_t stream);
+
+/* Scratch capacity (bytes) of ml_pairwise_mask_loss_forward_noalloc. */
+size_t ml_noalloc_scratch_limit(void);
+
 /* Pairwise label cost alone.  Replaces forward_pw_sigmoid_label_loss /     */
 /* forward_pw_softmax_label_loss (src/bindings.cpp:141-155,                 */
 /* src/cuda/pw_sigmoid_label_loss.cu:108-187, pw_softmax_label_loss.cu:105-174). */

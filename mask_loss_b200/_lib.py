@@ -53,6 +53,10 @@ SIGNATURES = {
     "ml_match_workspace_size": (c_sz, [c_i64, c_i64, c_i64, c_i64]),
     "ml_pairwise_mask_loss_forward": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params),
                                                      c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_sz, c_vp]),
+    "ml_pairwise_mask_loss_forward_noalloc": (ctypes.c_int, [ctypes.POINTER(Dims),
+                                                             ctypes.POINTER(Params), c_vp, c_vp,
+                                                             c_vp, c_vp, c_vp, c_vp]),
+    "ml_noalloc_scratch_limit": (c_sz, []),
     "ml_pairwise_label_loss_forward": (ctypes.c_int, [c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                                       c_f32, c_f32, c_f32, c_i32, c_vp, c_vp, c_vp,
                                                       c_vp]),

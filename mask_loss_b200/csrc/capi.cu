@@ -383,6 +383,38 @@ LossArgs loss_args(const FwdPlan& P, const ml_params* p) {
     return a;
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the pairwise-cost path.  Its scratch (label
+// codes, per-image histogram, chunk partials, per-query statistics) lives in
+// this fixed device array instead of a caller-provided workspace.  Every GPU
+// that loads the library reserves it until the process exits.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;  // 64 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  The host-side
+// symbol is only a stand-in; the real address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+int noalloc_scratch(unsigned char** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return fail(ML_EUNSUPPORTED, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+        g_noalloc_ptr[dev] = static_cast<unsigned char*>(ptr);
+    }
+    *out = g_noalloc_ptr[dev];
+    return ML_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -462,6 +494,44 @@ int ml_pairwise_mask_loss_forward(const ml_dims* d, const ml_params* p, const fl
     a.sep = out; a.total = nullptr; a.rawI = nullptr; a.rawT = nullptr;
     return run_costs(P, a, mask_logits, reinterpret_cast<cudaStream_t>(stream));
 }
+
+int ml_pairwise_mask_loss_forward_noalloc(const ml_dims* d, const ml_params* p,
+                                          const float* mask_logits, const int64_t* mask_targets,
+                                          const float* cls_logits, const int64_t* cls_targets,
+                                          float* out, ml_stream_t stream) {
+    FwdPlan P;
+    int rc = validate_params(p, d ? d->C : 0);
+    if (rc) return rc;
+    if ((rc = make_plan(d, p, &P))) return rc;
+    // scratch layout: totals | codes | chunk partials | per-query statistics
+    const size_t LBQ = (size_t)P.L * P.B * P.Q;
+    const size_t n_tot = align256(sizeof(int32_t) * (size_t)P.B * P.gt_total);
+    const size_t n_codes = align256(sizeof(int32_t) * (size_t)P.B * P.H * P.W);
+    const size_t n_part =
+        align256(sizeof(float) * (size_t)P.L * P.B * P.nqt * P.nchunk * 2 * P.part_stride);
+    const size_t n_qstat = align256(sizeof(float) * kQStat * LBQ);
+    const size_t need = n_tot + n_codes + n_part + n_qstat;
+    if (need > kNoAllocScratchBytes)
+        return fail(ML_EUNSUPPORTED,
+                    "ml_pairwise_mask_loss_forward_noalloc: this call needs %zu bytes of scratch, "
+                    "above the fixed %zu-byte limit; use ml_pairwise_mask_loss_forward with a "
+                    "workspace instead", need, kNoAllocScratchBytes);
+    if (P.gout == 0) return ML_OK;
+    unsigned char* scratch = nullptr;
+    if ((rc = noalloc_scratch(&scratch))) return rc;
+    CostArgs a = cost_args(P, p, mask_logits, mask_targets, cls_logits, cls_targets, scratch, nullptr);
+    a.totals = reinterpret_cast<int32_t*>(scratch);
+    a.codes = reinterpret_cast<int32_t*>(scratch + n_tot);
+    a.part = reinterpret_cast<float*>(scratch + n_tot + n_codes);
+    a.qstat = reinterpret_cast<float*>(scratch + n_tot + n_codes + n_part);
+    a.sep = out; a.total = nullptr; a.rawI = nullptr; a.rawT = nullptr;
+    // run_costs clears the histogram and the partials before use (the array
+    // keeps the previous call's contents); codes and statistics are fully
+    // rewritten.
+    return run_costs(P, a, mask_logits, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t ml_noalloc_scratch_limit(void) { return kNoAllocScratchBytes; }
 
 int ml_pairwise_label_loss_forward(int64_t L, int64_t B, int64_t Q, int64_t C, int64_t GT_total,
                                    int64_t bg, float scale, float gamma, float alpha,
