@@ -195,7 +195,7 @@ def read_traffic(cfg_name: str):
 def run_ours(args, cfg):
     import torch.distributed as dist
 
-    from mask_loss_b200 import _lib, ops, synthetic
+    from mask_loss_b200 import _lib, ops, parallel, synthetic
     from mask_loss_b200 import functions as F
 
     ws, rank, local = dist_info()
@@ -206,7 +206,7 @@ def run_ours(args, cfg):
     lib = _lib.load()
 
     # this rank's shard: images [rank*B, (rank+1)*B) of the global batch
-    imgs = list(range(rank * cfg.B, (rank + 1) * cfg.B))
+    imgs = list(parallel.shard_images(ws * cfg.B, rank, ws))
     batch = synthetic.make_batch(cfg, images=imgs, device="cpu", logits=False)
     mt = batch["mask_targets"].to(dev)
     ct = batch["cls_targets"].to(dev)
@@ -217,11 +217,8 @@ def run_ours(args, cfg):
     GT_total = ct.shape[1]
 
     def step(ml_in, mt_in, cl_in, ct_in):
-        nm = ops.count_masks(mt_in, ct_in.shape[1], kw["background_index"])
-        if ws > 1:
-            dist.all_reduce(nm)
-            nm = nm / ws
-        nm = nm.clamp(min=1.0)
+        nm = parallel.global_num_masks(ops.count_masks(mt_in, ct_in.shape[1],
+                                                       kw["background_index"]))
         x = ml_in.detach().requires_grad_(True)
         z = cl_in.detach().requires_grad_(True)
         p2g, prd, m, d, c = F.MaskMatchingFunction.apply(
@@ -231,9 +228,9 @@ def run_ours(args, cfg):
             0.0, None, None, None, kw["void_class_index"], "softmax")
         losses = torch.stack([m, d, c])
         losses.sum().backward()
-        if ws > 1:
-            dist.all_reduce(losses.detach(), async_op=True)
-        return losses.detach(), x.grad, z.grad
+        losses = losses.detach()
+        parallel.average_losses(losses, async_op=True)
+        return losses, x.grad, z.grad
 
     def barrier():
         torch.cuda.synchronize()

@@ -613,6 +613,7 @@ int ml_count_masks(const ml_dims* d, const ml_params* p, const int64_t* mask_tar
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char* ws = ws_base(workspace);
     CostArgs a = cost_args(P, p, nullptr, mask_targets, nullptr, nullptr, ws, nullptr);
+    a.codes = nullptr;  // histogram only
     if ((rc = run_prep(P, a, st))) return rc;
     const int32_t* totals = a.totals;
     count_masks_kernel<<<1, 256, 0, st>>>(totals, P.B, P.gt_total, P.bg, num_masks_out);

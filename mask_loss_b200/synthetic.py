@@ -168,13 +168,15 @@ def make_batch(cfg: Config, images=None, device="cpu", logits=True):
     cls_t = torch.from_numpy(cls).to(device)
     out = {"mask_targets": targets, "cls_targets": cls_t}
     if logits:
-        shape = (cfg.L, len(idx), cfg.Q, cfg.H, cfg.W)
-        if str(device).startswith("cuda"):
-            g = torch.Generator(device=device).manual_seed(1000 * cfg.cfg + 7)
-            out["mask_logits"] = torch.randn(shape, generator=g, device=device) * cfg.logit_std
-            out["cls_logits"] = torch.randn((cfg.L, len(idx), cfg.Q, cfg.C), generator=g, device=device)
-        else:
-            g = torch.Generator().manual_seed(1000 * cfg.cfg + 7)
-            out["mask_logits"] = torch.randn(shape, generator=g) * cfg.logit_std
-            out["cls_logits"] = torch.randn((cfg.L, len(idx), cfg.Q, cfg.C), generator=g)
+        # one generator per image, so any subset of images gets the same values
+        ml, cl = [], []
+        for b in idx:
+            if str(device).startswith("cuda"):
+                g = torch.Generator(device=device).manual_seed(1000 * cfg.cfg + 7 + 100003 * b)
+            else:
+                g = torch.Generator().manual_seed(1000 * cfg.cfg + 7 + 100003 * b)
+            ml.append(torch.randn((cfg.L, 1, cfg.Q, cfg.H, cfg.W), generator=g, device=device))
+            cl.append(torch.randn((cfg.L, 1, cfg.Q, cfg.C), generator=g, device=device))
+        out["mask_logits"] = torch.cat(ml, 1) * cfg.logit_std
+        out["cls_logits"] = torch.cat(cl, 1)
     return out
