@@ -256,18 +256,32 @@ def run_ours(args, cfg):
 
     for _ in range(args.warmup):
         step(ml, mt, cl, ct)
-    # ---- device-resident throughput (value) + per-kernel events + clocks ----
-    clocks = ClockSampler(local)
-    clocks.start()
+    # ---- eager steps with the library's per-kernel event hooks (stage times) ----
     lib.ml_profile_enable(1)
-    n0 = lib.ml_launch_count()
-    ms = timed(lambda: step(ml, mt, cl, ct), args.steps)
-    launches = lib.ml_launch_count() - n0
+    n_eager = max(3, min(args.steps, 50))
+    ms_eager = timed(lambda: step(ml, mt, cl, ct), n_eager) / n_eager
     lib.ml_profile_enable(0)
     kms = np.zeros(3, np.float32)
     kn = np.zeros(3, np.int64)
     lib.ml_profile_read(kms.ctypes.data, kn.ctypes.data, 3)
+
+    # ---- device-resident throughput (value): the whole step as one CUDA graph ----
+    from mask_loss_b200.graphs import MatchingLossStep
+    g_ml, g_mt, g_cl, g_ct = ml.clone(), mt.clone(), cl.clone(), ct.clone()
+    gstep = MatchingLossStep(
+        g_ml, g_mt, g_cl, g_ct, kw["smooth"], kw["sigmoid_scale"], kw["dice_scale"],
+        kw["cls_scale"], kw["background_index"], kw["uncertainty_gamma"],
+        kw["uncertainty_gamma_min"], True, kw["inf_thresh"], "allreduce", True, False, 1,
+        "global", 0.0, None, None, None, kw["void_class_index"], "softmax",
+        warmup=max(1, args.warmup))
+    for _ in range(args.warmup):
+        gstep.replay()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms = timed(gstep.replay, args.steps)
     clk = clocks.stop()
+    gstep.check()
+    launches = gstep.kernels_per_replay * args.steps
     ms_step = ms / args.steps
     value = ws * cfg.B * cfg.L / (ms_step / 1e3)
 
@@ -281,18 +295,19 @@ def run_ours(args, cfg):
     d2h = h_out.numel() * h_out.element_size()
 
     def e2e_step():
-        a = h_ml.to(dev, non_blocking=True)
-        b = h_mt.to(dev, non_blocking=True)
-        c = h_cl.to(dev, non_blocking=True)
-        d = h_ct.to(dev, non_blocking=True)
-        losses, _, _ = step(a, b, c, d)
-        h_out.copy_(losses, non_blocking=True)
+        g_ml.copy_(h_ml, non_blocking=True)
+        g_mt.copy_(h_mt, non_blocking=True)
+        g_cl.copy_(h_cl, non_blocking=True)
+        g_ct.copy_(h_ct, non_blocking=True)
+        gstep.replay()
+        h_out.copy_(gstep.losses, non_blocking=True)
 
     for _ in range(max(1, args.warmup // 2)):
         e2e_step()
-    e2e_steps = max(3, min(args.steps, 10))
+    e2e_steps = max(3, min(args.steps, 20))
     ms_e2e = timed(e2e_step, e2e_steps) / e2e_steps
     e2e = ws * cfg.B * cfg.L / (ms_e2e / 1e3)
+    gstep.check()
     ops.check_status(block=True)
 
     if rank != 0:
@@ -339,7 +354,9 @@ def run_ours(args, cfg):
                      "algorithmic_bytes_per_launch": cost_bytes, "avg_launch_ms": cost_ms,
                      "peak_source": peak_src},
         "stages_ms": {"cost_partial_kernel": cost_ms, "mask_grad_kernel": grad_ms,
-                      "match_kernel": match_ms},
+                      "match_kernel": match_ms, "eager_step": ms_eager},
+        "execution": "value and e2e replay the step as one CUDA graph "
+                     "(mask_loss_b200.graphs.MatchingLossStep); stage times from eager steps",
         "gpu_launches": int(launches),
         "clocks": clk,
         "cpu_baseline": cpu,

@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstring>
 #include <atomic>
+#include <map>
 #include <mutex>
 #include <vector>
 #include <string>
@@ -77,10 +78,35 @@ struct ProfScope {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device);
+// later calls with the same or a smaller size touch no CUDA API (so they are
+// safe inside stream capture).
+std::mutex g_smem_mu;
+std::map<std::pair<int, const void*>, int> g_smem_done;
+
+template <typename K>
+cudaError_t ensure_smem(K kernel, size_t bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const auto key = std::make_pair(dev, reinterpret_cast<const void*>(kernel));
+    std::lock_guard<std::mutex> g(g_smem_mu);
+    auto it = g_smem_done.find(key);
+    if (it != g_smem_done.end() && (int)bytes <= it->second) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) g_smem_done[key] = (int)bytes;
+    return e;
+}
+
 int sm_count() {
+    static int cached[64] = {};
     int dev = 0, n = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess)
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return n;
+    if (cached[dev]) return cached[dev];
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+        cached[dev] = n;
+    else
+        n = 148;
     return n > 0 ? n : 148;
 }
 
@@ -258,7 +284,7 @@ CostArgs cost_args(const FwdPlan& P, const ml_params* p, const float* ml, const 
 template <bool UNC, bool FOC, bool TMA>
 int launch_cost_t(const FwdPlan& P, const CUtensorMap& tm, const CostArgs& a, cudaStream_t st) {
     auto k = cost_partial_kernel<UNC, FOC, TMA>;
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.cost_smem);
+    cudaError_t e = ensure_smem(k, P.cost_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cost_partial_kernel attributes");
     dim3 grid(P.nchunk, P.nqt, P.L * P.B);
     ProfScope prof(0, st);
@@ -355,7 +381,7 @@ int launch_match(const CT* costs, int64_t N, int64_t Q, int64_t G, double thr, i
     if (!a.stage_cost) smem = match_smem_bytes((int)Q, (int)G, sizeof(CT), false);
     if (smem > 227 * 1024) return fail(ML_EUNSUPPORTED, "solver state does not fit shared memory");
     auto k = match_kernel<CT>;
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = ensure_smem(k, smem);
     if (e != cudaSuccess) return cuda_fail(e, "match_kernel attributes");
     {
         ProfScope prof(2, st);

@@ -1,0 +1,86 @@
+"""CUDA-graph capture of a whole matching + loss step.
+
+A training loop with fixed shapes (padded Q, fixed image size and GT slots)
+issues the same ~20 launches every step; from Python that costs more host
+time than the GPU work at the Mask2Former COCO shape.  ``MatchingLossStep``
+captures cost kernels, the on-device solver, the matched-loss forward, the
+backward and the optional num_masks all-reduce once, and replays them with one
+``cudaGraphLaunch`` per step.
+
+Usage::
+
+    step = MatchingLossStep(mask_logits, mask_targets, cls_logits, cls_targets,
+                            *matching_args)      # the 20 scalar args of MaskMatchingFunction
+    step.inputs["mask_logits"].copy_(new_logits)  # or write into them in place
+    step.replay()
+    step.losses          # (3, L): mask, dice, class means
+    step.grad_mask_logits, step.grad_cls_logits, step.pred_to_gt, step.pred_round
+    step.check()         # raises if a replay's solver reported failure
+
+The inputs are the caller's tensors (kept as static buffers).  ``num_masks``
+may be ``"allreduce"``: the per-image GT count is then all-reduced over the
+default process group inside the graph (NCCL supports capture).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops, parallel
+from .functions import MaskMatchingFunction
+
+
+class MatchingLossStep:
+    def __init__(self, mask_logits, mask_targets, cls_logits, cls_targets, *args,
+                 warmup: int = 2, loss_weights=(1.0, 1.0, 1.0)):
+        if len(args) != 20:
+            raise ValueError("expected the 20 scalar arguments of MaskMatchingFunction after the "
+                             "four tensors")
+        self.inputs = {"mask_logits": mask_logits, "mask_targets": mask_targets,
+                       "cls_logits": cls_logits, "cls_targets": cls_targets}
+        self.args = list(args)
+        self.allreduce_num_masks = isinstance(args[9], str) and args[9] == "allreduce"
+        self.w = loss_weights
+        self.graph = None
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):  # sets kernel attributes, resolves entry points
+                self._run()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = len(ops._captured)
+        from . import _lib
+        l0 = _lib.load().ml_launch_count()
+        with torch.cuda.graph(self.graph):
+            out = self._run()
+        self.kernels_per_replay = int(_lib.load().ml_launch_count() - l0)
+        self._flags = ops._captured[n0:]
+        del ops._captured[n0:]
+        (self.pred_to_gt, self.pred_round, self.losses, self.grad_mask_logits,
+         self.grad_cls_logits) = out
+
+    def _run(self):
+        ml = self.inputs["mask_logits"]
+        mt = self.inputs["mask_targets"]
+        cl = self.inputs["cls_logits"]
+        ct = self.inputs["cls_targets"]
+        a = list(self.args)
+        if self.allreduce_num_masks:
+            a[9] = parallel.global_num_masks(ops.count_masks(mt, ct.shape[1], int(a[4])))
+        x = ml.detach().requires_grad_(True)
+        z = cl.detach().requires_grad_(True)
+        p2g, prd, m, d, c = MaskMatchingFunction.apply(x, mt, z, ct, *a)
+        losses = torch.stack([m, d, c])
+        (self.w[0] * m + self.w[1] * d + self.w[2] * c).sum().backward()
+        return p2g, prd, losses.detach(), x.grad, z.grad
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def check(self) -> None:
+        """Raise if the last replay's solver (or argument check) reported
+        failure.  Synchronises."""
+        for flag, msg in self._flags:
+            if int(flag.reshape(-1)[0].item()) != 0:
+                raise RuntimeError(msg)

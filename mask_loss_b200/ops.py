@@ -68,6 +68,7 @@ def check_status(block: bool = False) -> None:
         raise err
 
 
+_captured: list = []  # (device int32 flag, message) recorded during stream capture
 _pinned = []  # pool of 1-element pinned int32 buffers, reused once their event completed
 
 
@@ -78,6 +79,11 @@ def _pinned_slot() -> torch.Tensor:
 
 
 def _defer(flag_i32: torch.Tensor, message: str) -> None:
+    if torch.cuda.is_current_stream_capturing():
+        # inside CUDA-graph capture: the flag stays on the device; the graph's
+        # owner (graphs.MatchingLossStep) checks it after replays
+        _captured.append((flag_i32, message))
+        return
     if len(_pending) > 64:
         check_status()
     host = _pinned_slot()
