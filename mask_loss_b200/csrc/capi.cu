@@ -211,20 +211,20 @@ int make_plan(const ml_dims* d, const ml_params* p, FwdPlan* P) {
     const int threads = 2 * P->qrows_pad + 32;
     int per_sm = (int)std::min<size_t>(228 * 1024 / (P->cost_smem + 1024), 2048 / threads);
     if (per_sm < 1) per_sm = 1;
-    // chunks per (image, query tile): smallest count whose CTA total fills the
-    // SMs in whole waves to within 10% (or the best found)
+    // chunks per (image, query tile): the smallest count whose CTAs fill the
+    // SMs in whole waves to >= 95 % (else the best found up to 4 waves)
     const int64_t base = (int64_t)P->L * P->B * P->nqt;
     const int64_t slots = (int64_t)sm_count() * per_sm;
     const int64_t max_ch = std::max<int64_t>(1, (HW + KC - 1) / KC);
     int64_t best = 1;
     double best_eff = -1.0;
-    const int64_t lo = base > 0 ? std::max<int64_t>(1, (slots + base - 1) / base) : 1;
-    for (int64_t nch = lo; nch <= std::min<int64_t>(max_ch, 4 * lo); ++nch) {
+    const int64_t hi = base > 0 ? std::max<int64_t>(1, 4 * ((slots + base - 1) / base)) : 1;
+    for (int64_t nch = 1; nch <= std::min<int64_t>(max_ch, hi); ++nch) {
         const int64_t total = base * nch;
         const int64_t waves = (total + slots - 1) / slots;
         const double eff = (double)total / (double)(waves * slots);
         if (eff > best_eff + 1e-9) { best_eff = eff; best = nch; }
-        if (eff >= 0.9) break;
+        if (eff >= 0.95) { best = nch; break; }
     }
     if (best > max_ch) best = max_ch;
     P->chunk_cells = (int)(((HW + best - 1) / best + KC - 1) / KC * KC);
@@ -385,7 +385,7 @@ int launch_match(const CT* costs, int64_t N, int64_t Q, int64_t G, double thr, i
     if (e != cudaSuccess) return cuda_fail(e, "match_kernel attributes");
     {
         ProfScope prof(2, st);
-        k<<<(unsigned)N, 32, smem, st>>>(a);
+        k<<<(unsigned)N, kMatchThreads, smem, st>>>(a);
     }
     ML_CHECK_LAUNCH("match_kernel");
     return ML_OK;

@@ -31,6 +31,8 @@
 // order.
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -84,6 +86,9 @@ label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int 
 struct Fast {
     float d, p;
 };
+
+constexpr std::integral_constant<bool, false> kNo{};
+constexpr std::integral_constant<bool, true> kYes{};
 
 ML_INLINE Fast fast_elem(float x) {
     const float e = ex2_approx(-fabsf(x) * 1.4426950408889634f);
@@ -256,7 +261,8 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     // per-element update of the row sums and the run accumulators
     float trow[NROW] = {};
     float prod = 1.0f;
-    auto element = [&](float x, int cell) {
+    auto element = [&](float x, int cell, auto mix_tag) {
+        constexpr bool MIX = decltype(mix_tag)::value;
         if (FAST) {
             const Fast f = fast_elem(x);
             prod *= f.d;
@@ -264,7 +270,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
             trow[1] += f.p;
             racc[0] = fmaf(m, x, racc[0]);
             racc[1] = fmaf(m, f.p, racc[1]);
-            if (cur == kMixed && qvalid)
+            if (MIX && qvalid)
                 mixed_cell<UNC>(a.targets, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, -x, f.p, 1.0f);
         } else {
             const Elem e = elem(x);
@@ -280,7 +286,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
             racc[0] = fmaf(m, dl, racc[0]);
             racc[1] = fmaf(m, w * e.p, racc[1]);
             if (UNC) racc[2] = fmaf(m, w, racc[2]);
-            if (cur == kMixed && qvalid)
+            if (MIX && qvalid)
                 mixed_cell<UNC>(a.targets, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, dl, w * e.p, w);
         }
     };
@@ -309,7 +315,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                 const uint32_t b4 = (bnd >> (4 * c)) & 0xFu;
                 if (b4 == 0u) {
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) element(xv[u], cell0 + h * KBOX + 4 * c + u);
+                    for (int u = 0; u < 4; ++u) element(xv[u], cell0 + h * KBOX + 4 * c + u, kNo);
                 } else {
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
@@ -318,7 +324,9 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                             cur = __shfl_sync(0xffffffffu, my_code, 4 * c + u);
                             m = cur >= 0 ? 1.0f : 0.0f;
                         }
-                        element(xv[u], cell0 + h * KBOX + 4 * c + u);
+                        // a mixed cell is always a one-cell run
+                        if (cur == kMixed) element(xv[u], cell0 + h * KBOX + 4 * c + u, kYes);
+                        else element(xv[u], cell0 + h * KBOX + 4 * c + u, kNo);
                     }
                 }
                 if (FAST && (c & 1)) { trow[2] += lg2_approx(prod); prod = 1.0f; }
@@ -331,7 +339,8 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                     cur = __shfl_sync(0xffffffffu, my_code, k);
                     m = cur >= 0 ? 1.0f : 0.0f;
                 }
-                element(x, cell0 + h * KBOX + k);
+                if (cur == kMixed) element(x, cell0 + h * KBOX + k, kYes);
+                else element(x, cell0 + h * KBOX + k, kNo);
                 if (FAST) { trow[2] += lg2_approx(prod); prod = 1.0f; }
             }
         }
@@ -455,14 +464,30 @@ __global__ void __launch_bounds__(256) cost_pairs_kernel(CostArgs a) {
     const int nslot = 2 * a.nchunk;
     const float* p = a.part + (((int64_t)lb * a.nqt + qt) * nslot) * (int64_t)a.part_stride +
                      (int64_t)g * a.qrows_pad + t;
-    float acc[NACC];
+    // four interleaved partial sums (fixed association -> deterministic),
+    // so the slot loads are independent and overlap
+    float acc4[4][NACC];
 #pragma unroll
-    for (int k = 0; k < NACC; ++k) acc[k] = 0.0f;
-    for (int sl = 0; sl < nslot; ++sl) {
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int k = 0; k < NACC; ++k) acc4[j][k] = 0.0f;
+    int sl = 0;
+    for (; sl + 4 <= nslot; sl += 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float* ps = p + (int64_t)(sl + j) * a.part_stride;
+#pragma unroll
+            for (int k = 0; k < NACC; ++k) acc4[j][k] += ps[(int64_t)k * G * a.qrows_pad];
+        }
+    }
+    for (; sl < nslot; ++sl) {
         const float* ps = p + (int64_t)sl * a.part_stride;
 #pragma unroll
-        for (int k = 0; k < NACC; ++k) acc[k] += ps[(int64_t)k * G * a.qrows_pad];
+        for (int k = 0; k < NACC; ++k) acc4[0][k] += ps[(int64_t)k * G * a.qrows_pad];
     }
+    float acc[NACC];
+#pragma unroll
+    for (int k = 0; k < NACC; ++k) acc[k] = (acc4[0][k] + acc4[1][k]) + (acc4[2][k] + acc4[3][k]);
     const int ga = g + (g >= a.bg ? 1 : 0);
     const int64_t qi = (int64_t)lb * a.Q + qt * a.qrows + t;
     const int64_t o = qi * G + g;

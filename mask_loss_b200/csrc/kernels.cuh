@@ -14,6 +14,7 @@ constexpr int kStages = 3;        // TMA pipeline depth
 constexpr int kFlushTiles = 8;    // longest register run (tiles) before a flush
 constexpr int kCostThreads = 288; // 256 consumers + 1 producer warp (upper bound)
 constexpr int kHistSmemMax = 8192;
+constexpr int kMatchThreads = 128; // warp 0 solves; all warps stage and rank
 constexpr int kQStat = 8;         // per-query: P, Wtot, um_mask, um_dice, um_cls, base, cls_row, -
 constexpr int kSaved = 4;         // saved for backward: P, T, I, Wtot
 

@@ -69,7 +69,7 @@ struct SolverMem {
 template <typename CT>
 __device__ bool hungarian(const CostView<CT>& C, const int* preds, int n, const int* cols, int M,
                           double thr, double BIG, int* asg, SolverMem& m) {
-    const int lane = threadIdx.x;
+    const int lane = threadIdx.x & 31;
     for (int k = lane; k < n; k += 32) asg[k] = -1;
     __syncwarp();
     if (M == 0 || n == 0 || n < M) return true;
@@ -132,11 +132,101 @@ __device__ bool hungarian(const CostView<CT>& C, const int* preds, int n, const 
     return true;
 }
 
+
+// Register-resident variant of `hungarian` for n <= 32*NJ - 1 columns: lane
+// `lane` owns columns j = lane + 32k (k < NJ) and keeps v, minv and the used
+// flags in registers; u, p and way stay in shared memory (random access).
+// Same operation order and tie rule as `hungarian`, so results are identical.
+template <int NJ, typename CT>
+__device__ bool hungarian_reg(const CostView<CT>& C, const int* preds, int n, const int* cols, int M,
+                              double thr, double BIG, int* asg, SolverMem& m) {
+    const int lane = threadIdx.x & 31;
+    for (int k = lane; k < n; k += 32) asg[k] = -1;
+    __syncwarp();
+    if (M == 0 || n == 0 || n < M) return true;
+    for (int i = lane; i <= M; i += 32) m.u[i] = 0.0;
+    for (int j = lane; j <= n; j += 32) { m.p[j] = 0; m.way[j] = 0; }
+    double v[NJ];
+#pragma unroll
+    for (int k = 0; k < NJ; ++k) v[k] = 0.0;
+    __syncwarp();
+    for (int i = 1; i <= M; ++i) {
+        if (lane == 0) m.p[0] = i;
+        double minv[NJ];
+#pragma unroll
+        for (int k = 0; k < NJ; ++k) minv[k] = kInf;
+        uint32_t used = 0;
+        __syncwarp();
+        int j0 = 0;
+        int steps = 0;
+        do {
+            if ((j0 & 31) == lane) used |= 1u << (j0 >> 5);
+            const int i0 = m.p[j0];
+            const int col = cols[i0 - 1];
+            const double ui0 = m.u[i0];
+            double best = kInf;
+            int bj = 0x7fffffff;
+#pragma unroll
+            for (int k = 0; k < NJ; ++k) {
+                const int j = lane + 32 * k;
+                if (j < 1 || j > n || ((used >> k) & 1u)) continue;
+                const double raw = C.at(preds[j - 1], col);
+                const double cij = ok_cost(raw, thr) ? raw : BIG;
+                const double cur = __dsub_rn(__dsub_rn(cij, ui0), v[k]);
+                if (cur < minv[k]) { minv[k] = cur; m.way[j] = j0; }
+                if (minv[k] < best) { best = minv[k]; bj = j; }
+            }
+            warp_argmin(best, bj);
+            if (!isfinite(best) || bj > n) return false;
+            const double delta = best;
+#pragma unroll
+            for (int k = 0; k < NJ; ++k) {
+                const int j = lane + 32 * k;
+                if (j > n) continue;
+                if ((used >> k) & 1u) {
+                    const int r = m.p[j];
+                    m.u[r] = __dadd_rn(m.u[r], delta);
+                    v[k] = __dsub_rn(v[k], delta);
+                } else {
+                    minv[k] = __dsub_rn(minv[k], delta);
+                }
+            }
+            __syncwarp();
+            j0 = bj;
+            if (++steps > n + 1) return false;
+        } while (m.p[j0] != 0);
+        if (lane == 0) {
+            int jj = j0;
+            int guard = 0;
+            do {
+                const int j1 = m.way[jj];
+                m.p[jj] = m.p[j1];
+                jj = j1;
+            } while (jj != 0 && ++guard <= n + 1);
+        }
+        __syncwarp();
+    }
+    for (int j = 1 + lane; j <= n; j += 32)
+        if (m.p[j] > 0) asg[j - 1] = m.p[j] - 1;
+    __syncwarp();
+    return true;
+}
+
+template <typename CT>
+__device__ bool solve(const CostView<CT>& C, const int* preds, int n, const int* cols, int M,
+                      double thr, double BIG, int* asg, SolverMem& m) {
+    if (n < 32) return hungarian_reg<1>(C, preds, n, cols, M, thr, BIG, asg, m);
+    if (n < 64) return hungarian_reg<2>(C, preds, n, cols, M, thr, BIG, asg, m);
+    if (n < 128) return hungarian_reg<4>(C, preds, n, cols, M, thr, BIG, asg, m);
+    if (n < 256) return hungarian_reg<8>(C, preds, n, cols, M, thr, BIG, asg, m);
+    return hungarian(C, preds, n, cols, M, thr, BIG, asg, m);
+}
+
 // Greedy fill with capacities, src/cpu/matching.cpp:193-229.
 template <typename CT>
 __device__ void greedy(const CostView<CT>& C, const int* preds, int np, const int* valid, int nv,
                        double thr, int* cap, int* p2g) {
-    const int lane = threadIdx.x;
+    const int lane = threadIdx.x & 31;
     for (int k = 0; k < np; ++k) {
         const int q = preds[k];
         if (p2g[q] >= 0) continue;
@@ -164,7 +254,7 @@ __device__ void greedy(const CostView<CT>& C, const int* preds, int np, const in
 // Order-preserving warp compaction: out[k] for flag(k) true, returns count.
 template <typename F>
 ML_INLINE int warp_compact(int n, F flag, int* out, const int* in) {
-    const int lane = threadIdx.x;
+    const int lane = threadIdx.x & 31;
     int total = 0;
     for (int base = 0; base < n; base += 32) {
         const int k = base + lane;
@@ -182,11 +272,12 @@ ML_INLINE int warp_compact(int n, F flag, int* out, const int* in) {
 // One warp per slice.  Dynamic shared memory holds the solver state and,
 // when `stage_cost`, the transposed cost slice.
 template <typename CT>
-__global__ void __launch_bounds__(32) match_kernel(MatchArgs<CT> a) {
+__global__ void __launch_bounds__(kMatchThreads) match_kernel(MatchArgs<CT> a) {
     extern __shared__ __align__(16) unsigned char msh[];
     const int slice = blockIdx.x;
     const int Q = a.Q, G = a.G;
-    const int lane = threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int tid = threadIdx.x, nthr = blockDim.x;
     const CT* cg = a.costs + (int64_t)slice * Q * G;
     int64_t* out_p = a.pred_to_gt + (int64_t)slice * Q;
     int64_t* out_r = a.pred_round + (int64_t)slice * Q;
@@ -214,17 +305,22 @@ __global__ void __launch_bounds__(32) match_kernel(MatchArgs<CT> a) {
     CT* cs = nullptr;
     if (a.stage_cost) {
         cs = reinterpret_cast<CT*>(take(sizeof(CT) * (size_t)Q * G));
-        for (int i = lane; i < Q * G; i += 32) {
+#pragma unroll 4
+        for (int i = tid; i < Q * G; i += nthr) {
             const int q = i / G, g = i - q * G;
             cs[g * Q + q] = cg[i];
         }
     }
     CostView<CT> C{cg, cs, Q, G};
-    for (int q = lane; q < Q; q += 32) p2g[q] = -1;
-    __syncwarp();
-
     const double thr = a.inf_thresh;
     const int64_t K = a.topk;
+    __shared__ int failed;
+    if (tid == 0) failed = 0;
+    for (int q = tid; q < Q; q += nthr) p2g[q] = -1;
+    __syncthreads();
+    if (threadIdx.x >= 32) goto rank;  // warp 0 runs the strategies
+    {
+
     bool good = true;
     if (Q > 0 && G > 0 && K > 0) {
         // valid columns: any finite cost below the threshold
@@ -246,7 +342,7 @@ __global__ void __launch_bounds__(32) match_kernel(MatchArgs<CT> a) {
                         ++M;
                     }
                 __syncwarp();
-                good = hungarian(C, preds, Q, cols, M, thr, BIG, asg, m);
+                good = solve(C, preds, Q, cols, M, thr, BIG, asg, m);
                 if (good)
                     for (int q = lane; q < Q; q += 32)
                         if (asg[q] >= 0) {
@@ -262,7 +358,7 @@ __global__ void __launch_bounds__(32) match_kernel(MatchArgs<CT> a) {
                     int M = warp_compact(nv, [&](int t) { return cap[valid[t]] > 0; }, cols, valid);
                     if (M == 0 || nrem == 0) break;
                     if (M > nrem) M = nrem;
-                    good = hungarian(C, pa, nrem, cols, M, thr, BIG, asg, m);
+                    good = solve(C, pa, nrem, cols, M, thr, BIG, asg, m);
                     if (!good) break;
                     // assignments (distinct columns within a round)
                     for (int k = lane; k < nrem; k += 32) {
@@ -286,7 +382,7 @@ __global__ void __launch_bounds__(32) match_kernel(MatchArgs<CT> a) {
                 const int M = nv < Q ? nv : Q;
                 for (int t = lane; t < M; t += 32) cols[t] = valid[t];
                 __syncwarp();
-                good = hungarian(C, preds, Q, cols, M, thr, BIG, asg, m);
+                good = solve(C, preds, Q, cols, M, thr, BIG, asg, m);
                 if (good) {
                     for (int q = lane; q < Q; q += 32)
                         if (asg[q] >= 0) {
@@ -304,13 +400,19 @@ __global__ void __launch_bounds__(32) match_kernel(MatchArgs<CT> a) {
         }
     }
     __syncwarp();
-    if (!good) {
-        if (lane == 0) atomicOr(a.status, 1);
-        for (int q = lane; q < Q; q += 32) { out_p[q] = -1; out_r[q] = -1; }
+    if (!good && lane == 0) {
+        atomicOr(a.status, 1);
+        failed = 1;
+    }
+    }
+rank:
+    __syncthreads();
+    if (failed) {
+        for (int q = tid; q < Q; q += nthr) { out_p[q] = -1; out_r[q] = -1; }
         return;
     }
     // rank per GT by (cost, q), src/cpu/matching.cpp:538-565
-    for (int q = lane; q < Q; q += 32) {
+    for (int q = tid; q < Q; q += nthr) {
         const int g = p2g[q];
         int64_t pr = -1;
         int64_t pg = -1;
