@@ -213,7 +213,10 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
     const float N2 = (float)s2;
     const Focal f = make_focal(a.mask_gamma, a.mask_alpha);
     const float mcoef = a.coef[l * 3 + 0], dcoef = a.coef[l * 3 + 1];
-    for (int q = 0; q < a.Q; ++q) {
+    // one warp per query: the per-query set-up is amortised over the whole
+    // cell chunk (128-bit accesses, 512 bytes per warp instruction)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int q = warp; q < a.Q; q += nw) {
         const int64_t qi = (int64_t)lb * a.Q + q;
         const int64_t og = a.pred_to_gt[qi];
         const int64_t ga = og + (og >= a.bg ? 1 : 0);
@@ -224,10 +227,11 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
         const bool active = (matched || a.force_masks) && !(mcoef == 0.0f && dcoef == 0.0f);
         if (!active) {
             if (VEC) {
-                for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4)
-                    *reinterpret_cast<float4*>(gout + k) = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+                for (int k = lane * 4; k < nc; k += 128)
+                    __stcs(reinterpret_cast<float4*>(gout + k), make_float4(0.f, 0.f, 0.f, 0.f));
             } else {
-                for (int k = threadIdx.x; k < nc; k += blockDim.x) gout[k] = 0.0f;
+                for (int k = lane; k < nc; k += 32) gout[k] = 0.0f;
             }
             continue;
         }
@@ -261,14 +265,15 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
             return mcoef * gs + dcoef * gd;
         };
         if (VEC) {
-            for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4) {
-                const float4 xv = *reinterpret_cast<const float4*>(xin + k);
+#pragma unroll 4
+            for (int k = lane * 4; k < nc; k += 128) {
+                const float4 xv = __ldcs(reinterpret_cast<const float4*>(xin + k));
                 float4 r;
                 r.x = g1(xv.x, k); r.y = g1(xv.y, k + 1); r.z = g1(xv.z, k + 2); r.w = g1(xv.w, k + 3);
-                *reinterpret_cast<float4*>(gout + k) = r;
+                __stcs(reinterpret_cast<float4*>(gout + k), r);
             }
         } else {
-            for (int k = threadIdx.x; k < nc; k += blockDim.x) gout[k] = g1(xin[k], k);
+            for (int k = lane; k < nc; k += 32) gout[k] = g1(xin[k], k);
         }
     }
 }
