@@ -204,6 +204,53 @@ int ml_mask_matching_backward(const ml_dims* d, const ml_params* p,
                               float* grad_mask_logits, float* grad_cls_logits,
                               void* workspace, size_t workspace_bytes, ml_stream_t stream);
 
+/* ---------------------------------------------------------------------- */
+/* Point-sampled costs and matching (config 3).  Replaces                    */
+/* pairwise_sigmoid_cross_entropy_loss_sampling_py                           */
+/* (functions/sigmoid/pw_sigmoid_ce.py:407-549) and                          */
+/* pairwise_dice_loss_sampling_py (functions/dice/pw_dice_loss.py:174-268):  */
+/* one shared set of num_points points per image, point_coords (B,P,2) fp32  */
+/* in [0,1] (x, y), logits sampled bilinearly with zero padding (grid_sample, */
+/* align_corners as given), labels read at floor(x*(W_t-1)), floor(y*(H_t-1)). */
+/* BCE = (<c+,t> + <c-,1-t>)/P, dice over the points, +inf for GT ids absent */
+/* from the whole label map; no entropy weights (uncertainty_gamma must be 0) */
+/* and no forced-empty unmatched masks.  logits_dtype: 0 fp32, 1 bf16.        */
+/* The matched losses and gradients of the sampled costs have no counterpart  */
+/* in the reference (it never wires sampling into matching,                   */
+/* functions/mask/matching.py:836).                                           */
+/* ---------------------------------------------------------------------- */
+size_t ml_sampled_workspace_size(const ml_dims* d, const ml_params* p, int64_t num_points);
+size_t ml_sampled_backward_workspace_size(const ml_dims* d, const ml_params* p,
+                                          int64_t num_points, int32_t logits_dtype);
+
+int ml_pairwise_mask_loss_sampled_forward(const ml_dims* d, const ml_params* p, int64_t num_points,
+                                          int32_t align_corners, int32_t logits_dtype,
+                                          const void* mask_logits, const int64_t* mask_targets,
+                                          const float* cls_logits, const int64_t* cls_targets,
+                                          const float* point_coords, float* out, void* workspace,
+                                          size_t workspace_bytes, ml_stream_t stream);
+
+int ml_mask_matching_sampled(const ml_dims* d, const ml_params* p, int64_t num_points,
+                             int32_t align_corners, int32_t logits_dtype, const void* mask_logits,
+                             const int64_t* mask_targets, const float* cls_logits,
+                             const int64_t* cls_targets, const float* point_coords,
+                             const float* num_masks_dev, int64_t* pred_to_gt, int64_t* pred_round,
+                             float* layer_means, float* sep_costs, float* saved, int32_t* dev_status,
+                             void* workspace, size_t workspace_bytes, ml_stream_t stream);
+
+/* grad_mask_logits has the logits' dtype; gradients are accumulated with
+ * atomics through the bilinear weights (order-dependent in the last ulp). */
+int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int64_t num_points,
+                                      int32_t align_corners, int32_t logits_dtype,
+                                      const float* grad_mask_mean, const float* grad_dice_mean,
+                                      const float* grad_cls_mean, const void* mask_logits,
+                                      const int64_t* mask_targets, const float* cls_logits,
+                                      const int64_t* cls_targets, const float* point_coords,
+                                      const int64_t* pred_to_gt, const float* saved,
+                                      const float* num_masks_dev, void* grad_mask_logits,
+                                      float* grad_cls_logits, void* workspace,
+                                      size_t workspace_bytes, ml_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -72,6 +72,22 @@ SIGNATURES = {
     "ml_mask_matching_backward": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params),
                                                  c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                                  c_vp, c_vp, c_vp, c_vp, c_vp, c_sz, c_vp]),
+    "ml_sampled_workspace_size": (c_sz, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_i64]),
+    "ml_sampled_backward_workspace_size": (c_sz, [ctypes.POINTER(Dims), ctypes.POINTER(Params),
+                                                  c_i64, c_i32]),
+    "ml_pairwise_mask_loss_sampled_forward": (ctypes.c_int, [ctypes.POINTER(Dims),
+                                                             ctypes.POINTER(Params), c_i64, c_i32,
+                                                             c_i32, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                             c_vp, c_vp, c_sz, c_vp]),
+    "ml_mask_matching_sampled": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_i64,
+                                                c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_sz,
+                                                c_vp]),
+    "ml_mask_matching_sampled_backward": (ctypes.c_int, [ctypes.POINTER(Dims),
+                                                         ctypes.POINTER(Params), c_i64, c_i32,
+                                                         c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                         c_vp, c_sz, c_vp]),
 }
 
 _LIB = None

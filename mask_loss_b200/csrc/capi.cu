@@ -312,9 +312,17 @@ int run_prep(const FwdPlan& P, const CostArgs& a, cudaStream_t st) {
     return ML_OK;
 }
 
+int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStream_t st);
+
 int run_costs(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStream_t st) {
     int rc = run_prep(P, a, st);
     if (rc) return rc;
+    return run_cost_core(P, a, mask_logits, st);
+}
+
+// Chunk partials + both finalize kernels (codes and totals already built).
+int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStream_t st) {
+    int rc = ML_OK;
     const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
     if (LBQ == 0 || P.gout == 0) return ML_OK;
     const size_t part_bytes = sizeof(float) * (size_t)P.L * P.B * P.nqt * P.nchunk * 2 * P.part_stride;
@@ -438,6 +446,74 @@ int noalloc_scratch(unsigned char** out) {
         g_noalloc_ptr[dev] = static_cast<unsigned char*>(ptr);
     }
     *out = g_noalloc_ptr[dev];
+    return ML_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Point-sampled path.  The cost stage runs on a (L,B,Q,1,P) view of the
+// sampled values: the plan is made for H=1, W=P, s=1.
+// ---------------------------------------------------------------------------
+struct SampledPlan {
+    FwdPlan cp;          // cost-stage plan over the sampled values
+    int H, W, Ht, Wt, P;
+    size_t off_present, off_perm, off_zs, bytes;
+};
+
+int make_sampled_plan(const ml_dims* d, const ml_params* p, int64_t P, SampledPlan* S) {
+    int rc = validate_dims(d);
+    if (rc) return rc;
+    if (P <= 0 || P >= (int64_t(1) << 24)) return fail(ML_ESHAPE, "num_points must be in [1, 2^24)");
+    if (p->force_unmatched_masks_to_empty)
+        return fail(ML_EUNSUPPORTED, "force_unmatched_masks_to_empty is not supported with point sampling");
+    if (p->uncertainty_gamma != 0.0f)
+        return fail(ML_EUNSUPPORTED, "uncertainty weights are not used by point-sampled costs: pass uncertainty_gamma=0");
+    ml_dims dv = *d;
+    dv.H = 1; dv.W = P; dv.Ht = 1; dv.Wt = P;
+    if ((rc = make_plan(&dv, p, &S->cp))) return rc;
+    S->H = (int)d->H; S->W = (int)d->W; S->Ht = (int)d->Ht; S->Wt = (int)d->Wt; S->P = (int)P;
+    const size_t LBQ = (size_t)d->L * d->B * d->Q;
+    size_t off = S->cp.bytes;
+    S->off_present = off; off += align256(sizeof(int32_t) * (size_t)d->B * d->GT_total);
+    S->off_perm = off; off += align256(sizeof(int32_t) * (size_t)d->B * P);
+    S->off_zs = off; off += align256(sizeof(float) * LBQ * P);
+    S->bytes = off + 256;
+    return ML_OK;
+}
+
+// present histogram, point sort (codes/totals of the cost plan), sampling.
+int run_sampled_prep(const SampledPlan& S, const ml_params* p, const void* mask_logits, int dtype,
+                     const int64_t* mask_targets, const float* coords, int align, unsigned char* ws,
+                     CostArgs& a, cudaStream_t st) {
+    const FwdPlan& P = S.cp;
+    int32_t* present = reinterpret_cast<int32_t*>(ws + S.off_present);
+    int32_t* perm = reinterpret_cast<int32_t*>(ws + S.off_perm);
+    float* zs = reinterpret_cast<float*>(ws + S.off_zs);
+    cudaError_t e = cudaMemsetAsync(present, 0, sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
+    if (e == cudaSuccess)
+        e = cudaMemsetAsync(const_cast<int32_t*>(a.totals), 0, sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
+    if (e != cudaSuccess) return cuda_fail(e, "memset histograms");
+    const int HW = S.H * S.W;
+    if (P.B > 0) {
+        const int bx = std::max(1, std::min((HW + 255) / 256, (4 * sm_count() + P.B - 1) / std::max(1, P.B)));
+        const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
+        label_code_kernel<<<dim3(bx, P.B), 256, hs, st>>>(mask_targets, P.B, S.H, S.W, S.Wt, S.Ht / S.H,
+                                                          P.gt_total, P.bg, nullptr, present);
+        ML_CHECK_LAUNCH("label_code_kernel");
+        point_sort_kernel<<<P.B, 256, sizeof(int32_t) * (P.gout + 2), st>>>(
+            mask_targets, coords, S.Ht, S.Wt, S.P, P.gt_total, P.bg, P.gout, perm,
+            const_cast<int32_t*>(a.codes), const_cast<int32_t*>(a.totals));
+        ML_CHECK_LAUNCH("point_sort_kernel");
+    }
+    const int64_t LB = (int64_t)P.L * P.B;
+    if (LB > 0 && P.Q > 0) {
+        cudaError_t le = launch_point_sample(dtype, mask_logits, coords, perm, P.B, P.L, P.Q, S.H, S.W,
+                                             S.P, align, zs, st);
+        if (le != cudaSuccess) return cuda_fail(le, "point_sample_kernel");
+        ML_CHECK_LAUNCH("point_sample_kernel");
+    }
+    a.present = present;
+    a.logits = zs;
+    (void)p;
     return ML_OK;
 }
 
@@ -724,6 +800,142 @@ int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float*
         ML_CHECK_LAUNCH("cls_grad_kernel");
     }
     return ML_OK;
+}
+
+
+size_t ml_sampled_workspace_size(const ml_dims* d, const ml_params* p, int64_t num_points) {
+    SampledPlan S;
+    if (!p || make_sampled_plan(d, p, num_points, &S)) return 0;
+    return S.bytes;
+}
+
+int ml_pairwise_mask_loss_sampled_forward(const ml_dims* d, const ml_params* p, int64_t num_points,
+                                          int32_t align_corners, int32_t logits_dtype,
+                                          const void* mask_logits, const int64_t* mask_targets,
+                                          const float* cls_logits, const int64_t* cls_targets,
+                                          const float* point_coords, float* out, void* workspace,
+                                          size_t workspace_bytes, ml_stream_t stream) {
+    SampledPlan S;
+    int rc = validate_params(p, d ? d->C : 0);
+    if (rc) return rc;
+    if ((rc = make_sampled_plan(d, p, num_points, &S))) return rc;
+    if ((rc = check_ws(workspace, workspace_bytes, S.bytes))) return rc;
+    if (S.cp.gout == 0) return ML_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char* ws = ws_base(workspace);
+    CostArgs a = cost_args(S.cp, p, nullptr, mask_targets, cls_logits, cls_targets, ws, nullptr);
+    if ((rc = run_sampled_prep(S, p, mask_logits, logits_dtype, mask_targets, point_coords,
+                               align_corners, ws, a, st)))
+        return rc;
+    a.sep = out; a.total = nullptr; a.rawI = nullptr; a.rawT = nullptr;
+    return run_cost_core(S.cp, a, a.logits, st);
+}
+
+int ml_mask_matching_sampled(const ml_dims* d, const ml_params* p, int64_t num_points,
+                             int32_t align_corners, int32_t logits_dtype, const void* mask_logits,
+                             const int64_t* mask_targets, const float* cls_logits,
+                             const int64_t* cls_targets, const float* point_coords,
+                             const float* num_masks_dev, int64_t* pred_to_gt, int64_t* pred_round,
+                             float* layer_means, float* sep_costs, float* saved, int32_t* dev_status,
+                             void* workspace, size_t workspace_bytes, ml_stream_t stream) {
+    SampledPlan S;
+    int rc = validate_params(p, d ? d->C : 0);
+    if (rc) return rc;
+    if ((rc = make_sampled_plan(d, p, num_points, &S))) return rc;
+    const FwdPlan& P = S.cp;
+    if (P.gout == 0)
+        return fail(ML_ESHAPE, "pairwise_sigmoid_dice_loss_forward must return {3,L,B,Q,GT_out}");
+    if ((rc = check_ws(workspace, workspace_bytes, S.bytes))) return rc;
+    if (!dev_status) return fail(ML_EINVAL, "dev_status is null");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char* ws = ws_base(workspace);
+    CostArgs a = cost_args(P, p, nullptr, mask_targets, cls_logits, cls_targets, ws, dev_status);
+    if (sep_costs) a.sep = sep_costs;
+    if ((rc = run_sampled_prep(S, p, mask_logits, logits_dtype, mask_targets, point_coords,
+                               align_corners, ws, a, st)))
+        return rc;
+    if ((rc = run_cost_core(P, a, a.logits, st))) return rc;
+    if ((rc = launch_match<float>(a.total, (int64_t)P.L * P.B, P.Q, P.gout, p->inf_thresh,
+                                  p->topk_matches, p->strategy_id, pred_to_gt, pred_round,
+                                  dev_status, st)))
+        return rc;
+    if (P.L == 0) return ML_OK;
+    LossArgs la = loss_args(P, p);
+    la.pred_to_gt = pred_to_gt; la.sep = a.sep; la.qstat = a.qstat; la.rawI = a.rawI; la.rawT = a.rawT;
+    la.num_masks_dev = num_masks_dev; la.saved = saved; la.layer_means = layer_means;
+    loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
+    ML_CHECK_LAUNCH("loss_fwd_kernel");
+    return ML_OK;
+}
+
+int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int64_t num_points,
+                                      int32_t align_corners, int32_t logits_dtype,
+                                      const float* grad_mask_mean, const float* grad_dice_mean,
+                                      const float* grad_cls_mean, const void* mask_logits,
+                                      const int64_t* mask_targets, const float* cls_logits,
+                                      const int64_t* cls_targets, const float* point_coords,
+                                      const int64_t* pred_to_gt, const float* saved,
+                                      const float* num_masks_dev, void* grad_mask_logits,
+                                      float* grad_cls_logits, void* workspace,
+                                      size_t workspace_bytes, ml_stream_t stream) {
+    SampledPlan S;
+    int rc = validate_params(p, d ? d->C : 0);
+    if (rc) return rc;
+    if ((rc = make_sampled_plan(d, p, num_points, &S))) return rc;
+    if (!saved) return fail(ML_EINVAL, "the sampled backward needs the forward's saved statistics");
+    const FwdPlan& P = S.cp;
+    const size_t LBQ = (size_t)P.L * P.B * P.Q;
+    const size_t HWl = (size_t)S.H * S.W;
+    const size_t off_coef = S.bytes;
+    const size_t off_gacc = off_coef + align256(sizeof(float) * 3 * (size_t)P.L);
+    const size_t need = off_gacc + (logits_dtype == 1 ? align256(sizeof(float) * LBQ * HWl) : 0) + 256;
+    if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned char* ws = ws_base(workspace);
+    CostArgs a = cost_args(P, p, nullptr, mask_targets, cls_logits, cls_targets, ws, nullptr);
+    if ((rc = run_sampled_prep(S, p, mask_logits, logits_dtype, mask_targets, point_coords,
+                               align_corners, ws, a, st)))
+        return rc;
+    LossArgs la = loss_args(P, p);
+    la.H = S.H; la.W = S.W; la.Ht = S.Ht; la.Wt = S.Wt;
+    la.bg = p->background_index >= 0 ? (int)std::min<int64_t>(p->background_index, 1 << 30) : P.gt_total;
+    la.cls_logits = cls_logits; la.cls_targets = cls_targets; la.pred_to_gt = pred_to_gt;
+    la.num_masks_dev = num_masks_dev; la.grad_mask = grad_mask_mean; la.grad_dice = grad_dice_mean;
+    la.grad_cls = grad_cls_mean; la.coef = reinterpret_cast<float*>(ws + off_coef);
+    la.stats_in = saved; la.grad_cls_logits = grad_cls_logits;
+    if (LBQ == 0) return ML_OK;
+    bwd_coef_kernel<<<P.L, 256, 0, st>>>(la);
+    ML_CHECK_LAUNCH("bwd_coef_kernel");
+    float* gacc = logits_dtype == 1 ? reinterpret_cast<float*>(ws + off_gacc)
+                                    : static_cast<float*>(grad_mask_logits);
+    cudaError_t e = cudaMemsetAsync(gacc, 0, sizeof(float) * LBQ * HWl, st);
+    if (e != cudaSuccess) return cuda_fail(e, "memset sampled gradient");
+    const bool foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
+    int32_t* perm = reinterpret_cast<int32_t*>(ws + S.off_perm);
+    e = launch_point_grad(foc, la, a.logits, point_coords, perm, a.codes, S.P, align_corners, gacc,
+                          (int64_t)LBQ, st);
+    if (e != cudaSuccess) return cuda_fail(e, "point_grad_kernel");
+    ML_CHECK_LAUNCH("point_grad_kernel");
+    if (logits_dtype == 1) {
+        e = launch_to_bf16(gacc, grad_mask_logits, (int64_t)(LBQ * HWl), st);
+        if (e != cudaSuccess) return cuda_fail(e, "f32_to_bf16_kernel");
+        ML_CHECK_LAUNCH("f32_to_bf16_kernel");
+    }
+    if (P.C > 0) {
+        const int64_t blocks = ((int64_t)LBQ * 32 + 255) / 256;
+        cls_grad_kernel<<<(unsigned)blocks, 256, 0, st>>>(la);
+        ML_CHECK_LAUNCH("cls_grad_kernel");
+    }
+    return ML_OK;
+}
+
+size_t ml_sampled_backward_workspace_size(const ml_dims* d, const ml_params* p, int64_t num_points,
+                                          int32_t logits_dtype) {
+    SampledPlan S;
+    if (!p || make_sampled_plan(d, p, num_points, &S)) return 0;
+    const size_t LBQ = (size_t)d->L * d->B * d->Q;
+    return S.bytes + align256(sizeof(float) * 3 * (size_t)d->L) +
+           (logits_dtype == 1 ? align256(sizeof(float) * LBQ * d->H * d->W) : 0) + 256;
 }
 
 }  // extern "C"

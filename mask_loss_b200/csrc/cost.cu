@@ -494,8 +494,11 @@ __global__ void __launch_bounds__(256) cost_pairs_kernel(CostArgs a) {
     const float* qs = a.qstat + qi * kQStat;
     const int32_t tc = a.totals[(int64_t)b * a.gt_total + ga];
     const float T = UNC ? acc[2] : (float)tc;
+    // +inf where the GT id paints no pixel of the image (with point sampling
+    // the presence comes from the full label map, T from the points)
+    const bool absent = a.present ? a.present[(int64_t)b * a.gt_total + ga] == 0 : tc == 0;
     float bce, dice;
-    if (tc == 0) {
+    if (absent) {
         bce = INFINITY; dice = INFINITY;
     } else {
         bce = (qs[5] + acc[0]) / qs[1] * a.sigmoid_scale;

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 
 #include "common.cuh"
 
@@ -16,7 +17,8 @@ constexpr int kCostThreads = 288; // 256 consumers + 1 producer warp (upper boun
 constexpr int kHistSmemMax = 8192;
 constexpr int kMatchThreads = 128; // warp 0 solves; all warps stage and rank
 constexpr int kQStat = 8;         // per-query: P, Wtot, um_mask, um_dice, um_cls, base, cls_row, -
-constexpr int kSaved = 4;         // saved for backward: P, T, I, Wtot
+constexpr int kSaved = 4;
+constexpr int kSampleQ = 8;        // queries per thread in point_sample_kernel         // saved for backward: P, T, I, Wtot
 
 struct CostArgs {
     const float* logits;
@@ -25,6 +27,7 @@ struct CostArgs {
     const int64_t* cls_targets;
     const int32_t* totals;   // (B, GT_total)
     const int32_t* codes;    // (B, H*W) per-cell column code
+    const int32_t* present;  // (B, GT_total) full-image label counts for the +inf mask, or null
     float* part;             // chunk partials
     float* sep;              // (3,L,B,Q,G) or null
     float* total;            // (L,B,Q,G) or null
@@ -130,4 +133,18 @@ namespace mlb {
 __global__ void label_cost_kernel(const float* z_all, const int64_t* y_all, float* out, int L, int B,
                                   int Q, int C, int gt_total, int bg, int gout, float scale,
                                   float gamma, float alpha, int use_softmax);
+}  // namespace mlb
+
+namespace mlb {
+__global__ void point_sort_kernel(const int64_t* targets, const float* coords, int Ht, int Wt, int P,
+                                  int gt_total, int bg, int gout, int32_t* perm, int32_t* scodes,
+                                  int32_t* ptotals);
+__global__ void f32_to_bf16_kernel(const float* src, __nv_bfloat16* dst, int64_t n);
+cudaError_t launch_point_sample(int dtype, const void* logits, const float* coords,
+                                const int32_t* perm, int B, int L, int Q, int H, int W, int P,
+                                int align, float* zs, cudaStream_t st);
+cudaError_t launch_point_grad(bool foc, const LossArgs& la, const float* zs, const float* coords,
+                              const int32_t* perm, const int32_t* scodes, int P, int align,
+                              float* gacc, int64_t rows, cudaStream_t st);
+cudaError_t launch_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t st);
 }  // namespace mlb

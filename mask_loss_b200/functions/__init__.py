@@ -15,3 +15,8 @@ from .pairwise import (  # noqa: F401
     pairwise_softmax_label_loss,
 )
 from .semantic import DiceLossFunction, SigmoidCELossFunction  # noqa: F401
+from .sampled import (  # noqa: F401
+    MaskMatchingSampledFunction,
+    pairwise_dice_loss_sampling,
+    pairwise_sigmoid_cross_entropy_loss_sampling,
+)

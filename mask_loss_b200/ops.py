@@ -433,3 +433,156 @@ def count_masks(mask_targets, GT_total: int, background_index: int) -> torch.Ten
     _lib.check(lib.ml_count_masks(ctypes.byref(d), ctypes.byref(p), _ptr(mask_targets), _ptr(out),
                                   _ptr(ws), ws.numel(), _stream(mask_targets.device)))
     return out
+
+
+# ---------------------------------------------------------------------------
+# Point-sampled costs and matching (config 3)
+# ---------------------------------------------------------------------------
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return 0
+    if t.dtype == torch.bfloat16:
+        return 1
+    raise RuntimeError("mask_logits must be float32 or bfloat16")
+
+
+def _check_sampled(mask_logits, mask_targets, cls_logits, cls_targets, point_coords):
+    for t, n in ((mask_logits, "mask_logits"), (mask_targets, "mask_targets"),
+                 (cls_logits, "cls_logits"), (cls_targets, "cls_targets"),
+                 (point_coords, "point_coords")):
+        _check_input(t, n)
+    _dtype_code(mask_logits)
+    _check_dtype(cls_logits, torch.float32, "cls_logits")
+    _check_dtype(mask_targets, torch.int64, "mask_targets")
+    _check_dtype(cls_targets, torch.int64, "cls_targets")
+    _check_dtype(point_coords, torch.float32, "point_coords")
+    B = mask_logits.shape[1]
+    if point_coords.dim() != 3 or point_coords.shape[0] != B or point_coords.shape[2] != 2:
+        raise RuntimeError("point_coords must be (B,P,2)")
+
+
+def reference_point_coords(mask_targets: torch.Tensor, num_points: int, background_index=-1,
+                           generator=None) -> torch.Tensor:
+    """(B,P,2) points drawn as the reference's *_sampling_py functions draw
+    them: torch.rand(1,P,2) on the targets' device, once per image that holds
+    a non-background GT id, in image order (rows of other images are zero).
+    Reads the per-image presence on the host, like the reference."""
+    B = mask_targets.shape[0]
+    dev = mask_targets.device
+    out = torch.zeros((B, num_points, 2), dtype=torch.float32, device=dev)
+    if background_index is not None and background_index >= 0:
+        has = (mask_targets != background_index).flatten(1).any(1).tolist()
+    else:
+        has = [True] * B
+    for b in range(B):
+        if has[b]:
+            out[b] = torch.rand((1, num_points, 2), device=dev, generator=generator)[0]
+    return out
+
+
+def pairwise_mask_loss_sampled_forward(mask_logits, mask_targets, cls_logits, cls_targets,
+                                       point_coords, smooth=1.0, sigmoid_scale=1.0,
+                                       dice_scale=1.0, cls_scale=1.0, background_index=-1,
+                                       mask_gamma=0.0, mask_alpha=-1.0, cls_gamma=0.0,
+                                       cls_alpha=-1.0, use_softmax_label_loss=False,
+                                       align_corners=False) -> torch.Tensor:
+    """(3,L,B,Q,GT_out) point-sampled sigmoid-CE, dice and label costs."""
+    _check_sampled(mask_logits, mask_targets, cls_logits, cls_targets, point_coords)
+    lib = _lib_handle()
+    d = _dims(mask_logits, mask_targets, cls_logits, cls_targets)
+    p = _params(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, 0.0, 0.05,
+                mask_gamma=mask_gamma, mask_alpha=mask_alpha, cls_gamma=cls_gamma,
+                cls_alpha=cls_alpha, use_softmax_label_loss=use_softmax_label_loss)
+    L, B, Q = mask_logits.shape[:3]
+    P = point_coords.shape[1]
+    G = lib.ml_gt_out(d.GT_total, p.background_index)
+    if G == 0:
+        return torch.zeros((L, B, Q, 0), dtype=torch.float32, device=mask_logits.device)
+    out = torch.empty((3, L, B, Q, G), dtype=torch.float32, device=mask_logits.device)
+    nbytes = lib.ml_sampled_workspace_size(ctypes.byref(d), ctypes.byref(p), P)
+    if nbytes == 0:
+        raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
+    ws = _workspace(nbytes, mask_logits.device)
+    _lib.check(lib.ml_pairwise_mask_loss_sampled_forward(
+        ctypes.byref(d), ctypes.byref(p), P, int(bool(align_corners)), _dtype_code(mask_logits),
+        _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits), _ptr(cls_targets),
+        _ptr(point_coords), _ptr(out), _ptr(ws), ws.numel(), _stream(mask_logits.device)))
+    return out
+
+
+def mask_matching_sampled_ex(mask_logits, mask_targets, cls_logits, cls_targets, point_coords,
+                             smooth=1.0, sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0,
+                             background_index=-1, inf_thresh=1e30, num_masks=-1.0,
+                             force_unmatched_class_to_background=False, topk_matches=1,
+                             strategy_id=0, mask_gamma=0.0, mask_alpha=-1.0, cls_gamma=0.0,
+                             cls_alpha=-1.0, void_class_index=-1, use_softmax_label_loss=False,
+                             align_corners=False, *, num_masks_dev=None, want_saved=False,
+                             want_costs=False):
+    """Point-sampled counterpart of mask_matching_ex: returns (pred_to_gt,
+    pred_round, layer_means(3,L), saved or None, costs or None)."""
+    check_status()
+    _check_sampled(mask_logits, mask_targets, cls_logits, cls_targets, point_coords)
+    lib = _lib_handle()
+    dev = mask_logits.device
+    d = _dims(mask_logits, mask_targets, cls_logits, cls_targets)
+    p = _params(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, 0.0, 0.05,
+                inf_thresh, num_masks, force_unmatched_class_to_background, False, topk_matches,
+                strategy_id, mask_gamma, mask_alpha, cls_gamma, cls_alpha, void_class_index,
+                use_softmax_label_loss, True)
+    L, B, Q = mask_logits.shape[:3]
+    P = point_coords.shape[1]
+    G = lib.ml_gt_out(d.GT_total, p.background_index)
+    p2g = torch.empty((L, B, Q), dtype=torch.int64, device=dev)
+    prd = torch.empty((L, B, Q), dtype=torch.int64, device=dev)
+    means = torch.empty((3, L), dtype=torch.float32, device=dev)
+    saved = torch.empty((L, B, Q, 4), dtype=torch.float32, device=dev) if want_saved else None
+    costs = (torch.empty((3, L, B, Q, G), dtype=torch.float32, device=dev)
+             if want_costs and G > 0 else None)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    nbytes = lib.ml_sampled_workspace_size(ctypes.byref(d), ctypes.byref(p), P)
+    if nbytes == 0:
+        raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
+    ws = _workspace(nbytes, dev)
+    _lib.check(lib.ml_mask_matching_sampled(
+        ctypes.byref(d), ctypes.byref(p), P, int(bool(align_corners)), _dtype_code(mask_logits),
+        _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits), _ptr(cls_targets),
+        _ptr(point_coords), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd), _ptr(means), _ptr(costs),
+        _ptr(saved), _ptr(status), _ptr(ws), ws.numel(), _stream(dev)))
+    _track_status(status)
+    return p2g, prd, means, saved, costs
+
+
+def mask_matching_sampled_backward(grad_layer_mask_mean, grad_layer_dice_mean,
+                                   grad_layer_cls_mean, mask_logits, mask_targets, cls_logits,
+                                   cls_targets, point_coords, pred_to_gt, saved, smooth=1.0,
+                                   sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0,
+                                   background_index=-1, num_masks=-1.0,
+                                   force_unmatched_class_to_background=False, mask_gamma=0.0,
+                                   mask_alpha=-1.0, cls_gamma=0.0, cls_alpha=-1.0,
+                                   void_class_index=-1, use_softmax_label_loss=False,
+                                   align_corners=False, *, num_masks_dev=None):
+    """[grad_mask_logits (logits dtype), grad_cls_logits] of the sampled op."""
+    check_status()
+    _check_sampled(mask_logits, mask_targets, cls_logits, cls_targets, point_coords)
+    _check_input(saved, "saved")
+    lib = _lib_handle()
+    dev = mask_logits.device
+    d = _dims(mask_logits, mask_targets, cls_logits, cls_targets)
+    p = _params(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, 0.0, 0.05, 1e30,
+                num_masks, force_unmatched_class_to_background, False, 1, 0, mask_gamma,
+                mask_alpha, cls_gamma, cls_alpha, void_class_index, use_softmax_label_loss, True)
+    P = point_coords.shape[1]
+    dt = _dtype_code(mask_logits)
+    gm = torch.empty_like(mask_logits)
+    gc = torch.empty_like(cls_logits)
+    nbytes = lib.ml_sampled_backward_workspace_size(ctypes.byref(d), ctypes.byref(p), P, dt)
+    if nbytes == 0:
+        raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
+    ws = _workspace(nbytes, dev)
+    _lib.check(lib.ml_mask_matching_sampled_backward(
+        ctypes.byref(d), ctypes.byref(p), P, int(bool(align_corners)), dt,
+        _ptr(grad_layer_mask_mean), _ptr(grad_layer_dice_mean), _ptr(grad_layer_cls_mean),
+        _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits), _ptr(cls_targets),
+        _ptr(point_coords), _ptr(pred_to_gt), _ptr(saved), _ptr(num_masks_dev), _ptr(gm), _ptr(gc),
+        _ptr(ws), ws.numel(), _stream(dev)))
+    return [gm, gc]

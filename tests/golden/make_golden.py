@@ -194,6 +194,31 @@ def gen_solver(seed=7):
     print("solver cases:", len(costs))
 
 
+def gen_sampled(name, seed, L, B, Q, H, W, Ht, Wt, G, P, focal_gamma=0.0, focal_alpha=None,
+                bg=0, align_corners=False):
+    """Point-sampled costs of the reference's *_sampling_py functions
+    (functions/sigmoid/pw_sigmoid_ce.py:407-549, functions/dice/pw_dice_loss.py:174-268);
+    the coordinates are the ones those functions draw after torch.manual_seed(seed)."""
+    from oracle import sampled as S
+    g = torch.Generator().manual_seed(seed)
+    x32 = (torch.randn(L, B, Q, H, W, generator=g) * 3.0).float()
+    t, _ = make_targets(g, B, Ht, Wt, G, 3)
+    x = x32  # the reference samples with fp32 coordinates, so it runs in fp32
+    torch.manual_seed(seed)
+    sce = RF.pairwise_sigmoid_cross_entropy_loss_sampling_py(
+        x, t, background_index=bg, scale=2.0, num_points=P, align_corners=align_corners,
+        focal_gamma=focal_gamma, focal_alpha=focal_alpha)
+    torch.manual_seed(seed)
+    dice = RF.pairwise_dice_loss_sampling_py(x, t, smooth=1.0, background_index=bg, scale=3.0,
+                                             num_points=P, align_corners=align_corners)
+    coords = S.reference_coords(t, P, seed, background_index=bg)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), mask_logits=x32.numpy(),
+                        mask_targets=t.numpy(), coords=coords.numpy(), sce=sce.numpy(),
+                        dice=dice.numpy(), meta=np.array([P, bg, int(align_corners), focal_gamma,
+                                                          -1.0 if focal_alpha is None else focal_alpha]))
+    print(f"{name}: sce finite {np.isfinite(sce.numpy()).sum()}")
+
+
 if __name__ == "__main__":
     O.build()
     if O.ref_lib() is None:
@@ -201,3 +226,7 @@ if __name__ == "__main__":
     for i, (name, spec) in enumerate(CASES.items()):
         gen_case(name, spec, 100 + i)
     gen_solver()
+    gen_sampled("sampled_basic", 501, 1, 3, 8, 12, 12, 24, 24, 5, 500)
+    gen_sampled("sampled_focal_s4", 502, 2, 2, 6, 8, 10, 32, 40, 4, 777, focal_gamma=2.0,
+                focal_alpha=0.25)
+    gen_sampled("sampled_align_nobg", 503, 1, 2, 5, 9, 9, 9, 9, 3, 300, bg=-1, align_corners=True)

@@ -72,3 +72,19 @@ def test_solver_matches_compiled_reference():
             a2, r2 = O.assign_slice(c, 1e30, K, strat, use_ref=True)
             np.testing.assert_array_equal(a, a2)
             np.testing.assert_array_equal(r, r2)
+
+
+@pytest.mark.parametrize("name", ["sampled_basic", "sampled_focal_s4", "sampled_align_nobg"])
+def test_sampled_costs_against_reference_fixtures(name):
+    from oracle import sampled as S
+    d = np.load(GOLDEN + f"/{name}.npz")
+    Pn, bg, al, fg, fa = d["meta"]
+    P = O.Params(background_index=int(bg), sigmoid_scale=2.0, dice_scale=3.0, smooth=1.0,
+                 mask_gamma=float(fg), mask_alpha=float(fa))
+    gt = int(d["mask_targets"].max()) + 1
+    out = S.pairwise_costs_sampled(d["mask_logits"], d["mask_targets"], d["coords"], gt, P,
+                                   align_corners=bool(al)).numpy()
+    for got, ref in ((out[0], d["sce"]), (out[1], d["dice"])):
+        assert np.array_equal(np.isinf(got), np.isinf(ref))
+        f = np.isfinite(ref)
+        np.testing.assert_allclose(got[f], ref[f], rtol=1e-5, atol=1e-6)
