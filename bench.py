@@ -167,7 +167,7 @@ def run_reference(args, cfg):
         "steps": done, "steps_requested": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / done,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded, config-2 shapes)",
+        "data": f"synthetic (seeded, {cfg.name} shapes)",
         "config": {"workload": cfg.name, "images_per_step": per_step, "Q": cfg.Q,
                    "HW": f"{cfg.H}x{cfg.W}", "classes": cfg.C},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
@@ -215,17 +215,32 @@ def run_ours(args, cfg):
     cl = torch.randn((cfg.L, cfg.B, cfg.Q, cfg.C), generator=g, device=dev)
     kw = synthetic.parity_kwargs(cfg)
     GT_total = ct.shape[1]
+    sampled = cfg.name == "cfg3"
+    pc = None
+    if sampled:  # point-sampled configuration: bf16 logits, P points per image
+        ml = ml.to(torch.bfloat16)
+        gp = torch.Generator(device=dev).manual_seed(31 + rank)
+        pc = torch.rand((cfg.B, synthetic.CFG3_POINTS, 2), generator=gp, device=dev)
+
+    def sargs(nm):
+        return (kw["smooth"], kw["sigmoid_scale"], kw["dice_scale"], kw["cls_scale"],
+                kw["background_index"], kw["inf_thresh"], nm, True, 1, "global", 0.0, None, None,
+                None, kw["void_class_index"], "softmax", False)
 
     def step(ml_in, mt_in, cl_in, ct_in):
         nm = parallel.global_num_masks(ops.count_masks(mt_in, ct_in.shape[1],
                                                        kw["background_index"]))
         x = ml_in.detach().requires_grad_(True)
         z = cl_in.detach().requires_grad_(True)
-        p2g, prd, m, d, c = F.MaskMatchingFunction.apply(
-            x, mt_in, z, ct_in, kw["smooth"], kw["sigmoid_scale"], kw["dice_scale"],
-            kw["cls_scale"], kw["background_index"], kw["uncertainty_gamma"],
-            kw["uncertainty_gamma_min"], True, kw["inf_thresh"], nm, True, False, 1, "global",
-            0.0, None, None, None, kw["void_class_index"], "softmax")
+        if sampled:
+            p2g, prd, m, d, c = F.MaskMatchingSampledFunction.apply(x, mt_in, z, ct_in, pc,
+                                                                    *sargs(nm))
+        else:
+            p2g, prd, m, d, c = F.MaskMatchingFunction.apply(
+                x, mt_in, z, ct_in, kw["smooth"], kw["sigmoid_scale"], kw["dice_scale"],
+                kw["cls_scale"], kw["background_index"], kw["uncertainty_gamma"],
+                kw["uncertainty_gamma_min"], True, kw["inf_thresh"], nm, True, False, 1, "global",
+                0.0, None, None, None, kw["void_class_index"], "softmax")
         losses = torch.stack([m, d, c])
         losses.sum().backward()
         losses = losses.detach()
@@ -268,17 +283,34 @@ def run_ours(args, cfg):
     # ---- device-resident throughput (value): the whole step as one CUDA graph ----
     from mask_loss_b200.graphs import MatchingLossStep
     g_ml, g_mt, g_cl, g_ct = ml.clone(), mt.clone(), cl.clone(), ct.clone()
-    gstep = MatchingLossStep(
-        g_ml, g_mt, g_cl, g_ct, kw["smooth"], kw["sigmoid_scale"], kw["dice_scale"],
-        kw["cls_scale"], kw["background_index"], kw["uncertainty_gamma"],
-        kw["uncertainty_gamma_min"], True, kw["inf_thresh"], "allreduce", True, False, 1,
-        "global", 0.0, None, None, None, kw["void_class_index"], "softmax",
-        warmup=max(1, args.warmup))
+    if sampled:
+        gstep = MatchingLossStep(g_ml, g_mt, g_cl, g_ct, *sargs("allreduce"), point_coords=pc,
+                                 warmup=max(1, args.warmup))
+    else:
+        gstep = MatchingLossStep(
+            g_ml, g_mt, g_cl, g_ct, kw["smooth"], kw["sigmoid_scale"], kw["dice_scale"],
+            kw["cls_scale"], kw["background_index"], kw["uncertainty_gamma"],
+            kw["uncertainty_gamma_min"], True, kw["inf_thresh"], "allreduce", True, False, 1,
+            "global", 0.0, None, None, None, kw["void_class_index"], "softmax",
+            warmup=max(1, args.warmup))
     for _ in range(args.warmup):
         gstep.replay()
+    # inputs smaller than the 126 MB L2 (config 3): flush L2 between steps by
+    # writing a 256 MB buffer, and subtract the flush time measured alone
+    in_bytes = sum(t.numel() * t.element_size() for t in (g_ml, g_mt, g_cl, g_ct))
+    flush_ms = 0.0
+    step_fn = gstep.replay
+    if in_bytes < 160 << 20:
+        flush_buf = torch.empty(64 << 20, dtype=torch.float32, device=dev)
+
+        def step_fn():
+            flush_buf.zero_()
+            gstep.replay()
+
+        flush_ms = timed(flush_buf.zero_, args.steps) / args.steps
     clocks = ClockSampler(local)
     clocks.start()
-    ms = timed(gstep.replay, args.steps)
+    ms = timed(step_fn, args.steps) - flush_ms * args.steps
     clk = clocks.stop()
     gstep.check()
     launches = gstep.kernels_per_replay * args.steps
@@ -323,14 +355,15 @@ def run_ours(args, cfg):
     peak = peak or 6650.0
     # roofline of the dominant kernel: the streaming cost kernel reads every
     # logit once plus one int32 code per cell and image
-    cost_bytes = cfg.L * cfg.B * cfg.Q * cfg.H * cfg.W * 4 + cfg.B * cfg.H * cfg.W * 4
+    cells = synthetic.CFG3_POINTS if sampled else cfg.H * cfg.W  # sampled values are fp32
+    cost_bytes = cfg.L * cfg.B * cfg.Q * cells * 4 + cfg.B * cells * 4
     cost_ms = float(kms[0] / max(kn[0], 1))
     achieved = cost_bytes / (cost_ms / 1e3) / 1e9
     traffic = read_traffic(cfg.name)
     grad_ms = float(kms[1] / max(kn[1], 1))
     match_ms = float(kms[2] / max(kn[2], 1))
     cpu = None
-    if ws == 1:
+    if ws == 1 and not sampled:
         threads = max(1, os.cpu_count() or 1)
         n_img = min(threads, 2 * cfg.B)
         v, dt, solver = cpu_images_per_sec(cfg, n_img, threads)
@@ -341,12 +374,16 @@ def run_ours(args, cfg):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded, config-2 shapes); inputs > L2, no flush needed",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 logits, f32 math" if sampled else "f32",
+        "data": (f"synthetic (seeded, {cfg.name} shapes)" +
+                 (f"; {synthetic.CFG3_POINTS} uniform points per image" if sampled else
+                  "; inputs > L2, no flush needed")),
         "config": {"workload": cfg.name, "images_per_gpu": cfg.B, "global_batch": ws * cfg.B,
                    "Q": cfg.Q, "HW": f"{cfg.H}x{cfg.W}", "classes": cfg.C, "K": 1,
                    "strategy": "global", "label_loss": "softmax", "parallelism": f"dp{ws}",
-                   "l2": "inputs larger than L2"},
+                   "l2": ("inputs larger than L2" if not flush_ms else
+                          f"L2 flushed before every step (256 MB write, {flush_ms:.3f} ms, subtracted)")},
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": ms_e2e},
         "roofline": {"bound": "hbm", "kernel": "cost_partial_kernel", "achieved": achieved,

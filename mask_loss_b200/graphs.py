@@ -26,19 +26,28 @@ from __future__ import annotations
 import torch
 
 from . import ops, parallel
-from .functions import MaskMatchingFunction
+from .functions import MaskMatchingFunction, MaskMatchingSampledFunction
 
 
 class MatchingLossStep:
+    """With ``point_coords`` (B,P,2) the step runs the point-sampled op
+    (MaskMatchingSampledFunction) and ``args`` are its 17 scalar arguments;
+    otherwise MaskMatchingFunction's 20."""
+
     def __init__(self, mask_logits, mask_targets, cls_logits, cls_targets, *args,
-                 warmup: int = 2, loss_weights=(1.0, 1.0, 1.0)):
-        if len(args) != 20:
-            raise ValueError("expected the 20 scalar arguments of MaskMatchingFunction after the "
-                             "four tensors")
+                 point_coords=None, warmup: int = 2, loss_weights=(1.0, 1.0, 1.0)):
+        self.sampled = point_coords is not None
+        nargs = 17 if self.sampled else 20
+        if len(args) != nargs:
+            raise ValueError(f"expected {nargs} scalar arguments after the four tensors")
         self.inputs = {"mask_logits": mask_logits, "mask_targets": mask_targets,
                        "cls_logits": cls_logits, "cls_targets": cls_targets}
+        if self.sampled:
+            self.inputs["point_coords"] = point_coords
         self.args = list(args)
-        self.allreduce_num_masks = isinstance(args[9], str) and args[9] == "allreduce"
+        self.nm_slot = 6 if self.sampled else 9
+        self.allreduce_num_masks = (isinstance(args[self.nm_slot], str) and
+                                    args[self.nm_slot] == "allreduce")
         self.w = loss_weights
         self.graph = None
         side = torch.cuda.Stream()
@@ -67,10 +76,14 @@ class MatchingLossStep:
         ct = self.inputs["cls_targets"]
         a = list(self.args)
         if self.allreduce_num_masks:
-            a[9] = parallel.global_num_masks(ops.count_masks(mt, ct.shape[1], int(a[4])))
+            a[self.nm_slot] = parallel.global_num_masks(ops.count_masks(mt, ct.shape[1], int(a[4])))
         x = ml.detach().requires_grad_(True)
         z = cl.detach().requires_grad_(True)
-        p2g, prd, m, d, c = MaskMatchingFunction.apply(x, mt, z, ct, *a)
+        if self.sampled:
+            p2g, prd, m, d, c = MaskMatchingSampledFunction.apply(
+                x, mt, z, ct, self.inputs["point_coords"], *a)
+        else:
+            p2g, prd, m, d, c = MaskMatchingFunction.apply(x, mt, z, ct, *a)
         losses = torch.stack([m, d, c])
         (self.w[0] * m + self.w[1] * d + self.w[2] * c).sum().backward()
         return p2g, prd, losses.detach(), x.grad, z.grad

@@ -52,6 +52,8 @@ def _check_dtype(t: torch.Tensor, dtype, name: str) -> None:
 
 def check_status(block: bool = False) -> None:
     """Raise if an earlier on-device assignment solve reported failure."""
+    if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+        return  # no event queries inside stream capture
     keep = []
     err = None
     for ev, host, msg in _pending:

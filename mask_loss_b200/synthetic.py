@@ -47,9 +47,14 @@ CONFIGS = {
                    (0.0005, 0.20)),
     "cfg5": Config("cfg5", 5, 1, 8, 200, 640, 128, 1, 41, 3.0, "video", ("uniform", 1, 30),
                    (0.002, 0.10), frames=5),
+    "cfg3": Config("cfg3", 3, 1, 16, 100, 128, 128, 4, 134, 3.0, "ellipse_rect",
+                   ("poisson", 15, 1, 100), (0.001, 0.40)),
     "native": Config("native", 6, 1, 8, 128, 256, 256, 4, 128, 1.0, "ellipse", ("uniform", 10, 19),
                      (0.002, 0.05)),
 }
+
+CFG3_POINTS = 12544  # points per image of the point-sampled configuration (112 x 112)
+
 
 # Matching/loss arguments of the parity settings: softmax label loss over C'
 # classes with void = C'-1, unmatched queries pushed to void, K=1 global
