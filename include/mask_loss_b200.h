@@ -239,7 +239,10 @@ int ml_mask_matching_sampled(const ml_dims* d, const ml_params* p, int64_t num_p
                              void* workspace, size_t workspace_bytes, ml_stream_t stream);
 
 /* grad_mask_logits has the logits' dtype; gradients are accumulated with
- * atomics through the bilinear weights (order-dependent in the last ulp). */
+ * atomics through the bilinear weights (order-dependent in the last ulp).
+ * forward_workspace (nullable): the workspace of the ml_mask_matching_sampled
+ * call with the same arguments, still unmodified; its sorted points and
+ * samples are reused instead of being rebuilt. */
 int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int64_t num_points,
                                       int32_t align_corners, int32_t logits_dtype,
                                       const float* grad_mask_mean, const float* grad_dice_mean,
@@ -247,9 +250,9 @@ int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int6
                                       const int64_t* mask_targets, const float* cls_logits,
                                       const int64_t* cls_targets, const float* point_coords,
                                       const int64_t* pred_to_gt, const float* saved,
-                                      const float* num_masks_dev, void* grad_mask_logits,
-                                      float* grad_cls_logits, void* workspace,
-                                      size_t workspace_bytes, ml_stream_t stream);
+                                      const float* num_masks_dev, const void* forward_workspace,
+                                      void* grad_mask_logits, float* grad_cls_logits,
+                                      void* workspace, size_t workspace_bytes, ml_stream_t stream);
 
 #ifdef __cplusplus
 }

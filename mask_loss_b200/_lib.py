@@ -87,7 +87,7 @@ SIGNATURES = {
                                                          ctypes.POINTER(Params), c_i64, c_i32,
                                                          c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                                          c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
-                                                         c_vp, c_sz, c_vp]),
+                                                         c_vp, c_vp, c_sz, c_vp]),
 }
 
 _LIB = None

@@ -456,13 +456,14 @@ int noalloc_scratch(unsigned char** out) {
 struct SampledPlan {
     FwdPlan cp;          // cost-stage plan over the sampled values
     int H, W, Ht, Wt, P;
-    size_t off_present, off_perm, off_zs, bytes;
+    size_t off_present, off_perm, off_scoords, off_zs, bytes;
 };
 
 int make_sampled_plan(const ml_dims* d, const ml_params* p, int64_t P, SampledPlan* S) {
     int rc = validate_dims(d);
     if (rc) return rc;
-    if (P <= 0 || P >= (int64_t(1) << 24)) return fail(ML_ESHAPE, "num_points must be in [1, 2^24)");
+    if (P <= 0 || P > kMaxSortPoints)
+        return fail(ML_EUNSUPPORTED, "num_points must be in [1, %d]", kMaxSortPoints);
     if (p->force_unmatched_masks_to_empty)
         return fail(ML_EUNSUPPORTED, "force_unmatched_masks_to_empty is not supported with point sampling");
     if (p->uncertainty_gamma != 0.0f)
@@ -470,11 +471,14 @@ int make_sampled_plan(const ml_dims* d, const ml_params* p, int64_t P, SampledPl
     ml_dims dv = *d;
     dv.H = 1; dv.W = P; dv.Ht = 1; dv.Wt = P;
     if ((rc = make_plan(&dv, p, &S->cp))) return rc;
+    if (point_sort_smem((int)P, S->cp.gout) > 200 * 1024)
+        return fail(ML_EUNSUPPORTED, "too many points x GT columns for the point sort");
     S->H = (int)d->H; S->W = (int)d->W; S->Ht = (int)d->Ht; S->Wt = (int)d->Wt; S->P = (int)P;
     const size_t LBQ = (size_t)d->L * d->B * d->Q;
     size_t off = S->cp.bytes;
     S->off_present = off; off += align256(sizeof(int32_t) * (size_t)d->B * d->GT_total);
     S->off_perm = off; off += align256(sizeof(int32_t) * (size_t)d->B * P);
+    S->off_scoords = off; off += align256(sizeof(float) * 2 * (size_t)d->B * P);
     S->off_zs = off; off += align256(sizeof(float) * LBQ * P);
     S->bytes = off + 256;
     return ML_OK;
@@ -487,6 +491,7 @@ int run_sampled_prep(const SampledPlan& S, const ml_params* p, const void* mask_
     const FwdPlan& P = S.cp;
     int32_t* present = reinterpret_cast<int32_t*>(ws + S.off_present);
     int32_t* perm = reinterpret_cast<int32_t*>(ws + S.off_perm);
+    float* scoords = reinterpret_cast<float*>(ws + S.off_scoords);
     float* zs = reinterpret_cast<float*>(ws + S.off_zs);
     cudaError_t e = cudaMemsetAsync(present, 0, sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
     if (e == cudaSuccess)
@@ -499,15 +504,17 @@ int run_sampled_prep(const SampledPlan& S, const ml_params* p, const void* mask_
         label_code_kernel<<<dim3(bx, P.B), 256, hs, st>>>(mask_targets, P.B, S.H, S.W, S.Wt, S.Ht / S.H,
                                                           P.gt_total, P.bg, nullptr, present);
         ML_CHECK_LAUNCH("label_code_kernel");
-        point_sort_kernel<<<P.B, 256, sizeof(int32_t) * (P.gout + 2), st>>>(
-            mask_targets, coords, S.Ht, S.Wt, S.P, P.gt_total, P.bg, P.gout, perm,
-            const_cast<int32_t*>(a.codes), const_cast<int32_t*>(a.totals));
-        ML_CHECK_LAUNCH("point_sort_kernel");
+        cudaError_t le = launch_point_sort(mask_targets, coords, P.B, S.Ht, S.Wt, S.P, P.gt_total, P.bg,
+                                           P.gout, perm, const_cast<int32_t*>(a.codes), scoords,
+                                           const_cast<int32_t*>(a.totals), st);
+        g_launches.fetch_add(1);
+        if (le != cudaSuccess) return cuda_fail(le, "point_sort_kernel");
     }
     const int64_t LB = (int64_t)P.L * P.B;
     if (LB > 0 && P.Q > 0) {
-        cudaError_t le = launch_point_sample(dtype, mask_logits, coords, perm, P.B, P.L, P.Q, S.H, S.W,
+        cudaError_t le = launch_point_sample(dtype, mask_logits, scoords, P.B, P.L, P.Q, S.H, S.W,
                                              S.P, align, zs, st);
+        g_launches.fetch_add(1);
         if (le != cudaSuccess) return cuda_fail(le, "point_sample_kernel");
         ML_CHECK_LAUNCH("point_sample_kernel");
     }
@@ -875,9 +882,9 @@ int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int6
                                       const int64_t* mask_targets, const float* cls_logits,
                                       const int64_t* cls_targets, const float* point_coords,
                                       const int64_t* pred_to_gt, const float* saved,
-                                      const float* num_masks_dev, void* grad_mask_logits,
-                                      float* grad_cls_logits, void* workspace,
-                                      size_t workspace_bytes, ml_stream_t stream) {
+                                      const float* num_masks_dev, const void* forward_workspace,
+                                      void* grad_mask_logits, float* grad_cls_logits,
+                                      void* workspace, size_t workspace_bytes, ml_stream_t stream) {
     SampledPlan S;
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
@@ -886,16 +893,23 @@ int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int6
     const FwdPlan& P = S.cp;
     const size_t LBQ = (size_t)P.L * P.B * P.Q;
     const size_t HWl = (size_t)S.H * S.W;
-    const size_t off_coef = S.bytes;
-    const size_t off_gacc = off_coef + align256(sizeof(float) * 3 * (size_t)P.L);
-    const size_t need = off_gacc + (logits_dtype == 1 ? align256(sizeof(float) * LBQ * HWl) : 0) + 256;
+    const size_t need = ml_sampled_backward_workspace_size(d, p, num_points, logits_dtype);
     if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char* ws = ws_base(workspace);
-    CostArgs a = cost_args(P, p, nullptr, mask_targets, cls_logits, cls_targets, ws, nullptr);
-    if ((rc = run_sampled_prep(S, p, mask_logits, logits_dtype, mask_targets, point_coords,
-                               align_corners, ws, a, st)))
-        return rc;
+    // sorted points and samples: reuse the forward's when given, else rebuild
+    unsigned char* fw = forward_workspace ? ws_base(const_cast<void*>(forward_workspace)) : ws;
+    CostArgs a = cost_args(P, p, nullptr, mask_targets, cls_logits, cls_targets, fw, nullptr);
+    if (!forward_workspace) {
+        if ((rc = run_sampled_prep(S, p, mask_logits, logits_dtype, mask_targets, point_coords,
+                                   align_corners, ws, a, st)))
+            return rc;
+    } else {
+        a.logits = reinterpret_cast<float*>(fw + S.off_zs);
+    }
+    const float* scoords = reinterpret_cast<const float*>(fw + S.off_scoords);
+    const size_t off_coef = S.bytes;
+    const size_t off_gacc = off_coef + align256(sizeof(float) * 3 * (size_t)P.L);
     LossArgs la = loss_args(P, p);
     la.H = S.H; la.W = S.W; la.Ht = S.Ht; la.Wt = S.Wt;
     la.bg = p->background_index >= 0 ? (int)std::min<int64_t>(p->background_index, 1 << 30) : P.gt_total;
@@ -906,20 +920,24 @@ int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int6
     if (LBQ == 0) return ML_OK;
     bwd_coef_kernel<<<P.L, 256, 0, st>>>(la);
     ML_CHECK_LAUNCH("bwd_coef_kernel");
+    const bool foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
     float* gacc = logits_dtype == 1 ? reinterpret_cast<float*>(ws + off_gacc)
                                     : static_cast<float*>(grad_mask_logits);
-    cudaError_t e = cudaMemsetAsync(gacc, 0, sizeof(float) * LBQ * HWl, st);
-    if (e != cudaSuccess) return cuda_fail(e, "memset sampled gradient");
-    const bool foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
-    int32_t* perm = reinterpret_cast<int32_t*>(ws + S.off_perm);
-    e = launch_point_grad(foc, la, a.logits, point_coords, perm, a.codes, S.P, align_corners, gacc,
-                          (int64_t)LBQ, st);
+    const bool rows_fit = HWl * 4 <= kRowMapMaxBytes;
+    if (!rows_fit) {
+        cudaError_t e = cudaMemsetAsync(gacc, 0, sizeof(float) * LBQ * HWl, st);
+        if (e != cudaSuccess) return cuda_fail(e, "memset sampled gradient");
+    }
+    bool used_rows = false;
+    cudaError_t e = launch_point_grad(foc, logits_dtype, la, a.logits, scoords, a.codes, S.P,
+                                      align_corners, grad_mask_logits, gacc, (int64_t)LBQ,
+                                      &used_rows, st);
+    g_launches.fetch_add(1);
     if (e != cudaSuccess) return cuda_fail(e, "point_grad_kernel");
-    ML_CHECK_LAUNCH("point_grad_kernel");
-    if (logits_dtype == 1) {
+    if (!used_rows && logits_dtype == 1) {
         e = launch_to_bf16(gacc, grad_mask_logits, (int64_t)(LBQ * HWl), st);
+        g_launches.fetch_add(1);
         if (e != cudaSuccess) return cuda_fail(e, "f32_to_bf16_kernel");
-        ML_CHECK_LAUNCH("f32_to_bf16_kernel");
     }
     if (P.C > 0) {
         const int64_t blocks = ((int64_t)LBQ * 32 + 255) / 256;
@@ -934,8 +952,9 @@ size_t ml_sampled_backward_workspace_size(const ml_dims* d, const ml_params* p, 
     SampledPlan S;
     if (!p || make_sampled_plan(d, p, num_points, &S)) return 0;
     const size_t LBQ = (size_t)d->L * d->B * d->Q;
+    const bool rows_fit = (size_t)d->H * d->W * 4 <= kRowMapMaxBytes;
     return S.bytes + align256(sizeof(float) * 3 * (size_t)d->L) +
-           (logits_dtype == 1 ? align256(sizeof(float) * LBQ * d->H * d->W) : 0) + 256;
+           (logits_dtype == 1 && !rows_fit ? align256(sizeof(float) * LBQ * d->H * d->W) : 0) + 256;
 }
 
 }  // extern "C"

@@ -136,15 +136,18 @@ __global__ void label_cost_kernel(const float* z_all, const int64_t* y_all, floa
 }  // namespace mlb
 
 namespace mlb {
-__global__ void point_sort_kernel(const int64_t* targets, const float* coords, int Ht, int Wt, int P,
-                                  int gt_total, int bg, int gout, int32_t* perm, int32_t* scodes,
-                                  int32_t* ptotals);
-__global__ void f32_to_bf16_kernel(const float* src, __nv_bfloat16* dst, int64_t n);
-cudaError_t launch_point_sample(int dtype, const void* logits, const float* coords,
-                                const int32_t* perm, int B, int L, int Q, int H, int W, int P,
-                                int align, float* zs, cudaStream_t st);
-cudaError_t launch_point_grad(bool foc, const LossArgs& la, const float* zs, const float* coords,
-                              const int32_t* perm, const int32_t* scodes, int P, int align,
-                              float* gacc, int64_t rows, cudaStream_t st);
+constexpr int kSortWarps = 8;
+constexpr size_t kRowMapMaxBytes = 96 * 1024;  // per-row maps staged in shared memory up to this
+constexpr int kMaxSortPoints = 40960;          // points per image (sort keys live in shared memory)
+size_t point_sort_smem(int P, int gout);
+cudaError_t launch_point_sort(const int64_t* targets, const float* coords, int B, int Ht, int Wt,
+                              int P, int gt_total, int bg, int gout, int32_t* perm, int32_t* scodes,
+                              float* scoords, int32_t* ptotals, cudaStream_t st);
+cudaError_t launch_point_sample(int dtype, const void* logits, const float* scoords, int B, int L,
+                                int Q, int H, int W, int P, int align, float* zs, cudaStream_t st);
+cudaError_t launch_point_grad(bool foc, int dtype, const LossArgs& la, const float* zs,
+                              const float* scoords, const int32_t* scodes, int P, int align,
+                              void* grad_out, float* gacc, int64_t rows, bool* used_rows,
+                              cudaStream_t st);
 cudaError_t launch_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t st);
 }  // namespace mlb

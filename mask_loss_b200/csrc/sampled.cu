@@ -30,53 +30,82 @@ ML_INLINE int64_t point_label(const int64_t* tb, int Ht, int Wt, float x, float 
 
 // ---------------------------------------------------------------------------
 // One block per image: stable counting sort of the points by output column
-// (bucket 0 = no column).  Writes perm[b][pos] = point, scodes[b][pos] =
-// column (or kNone), and ptotals[b][label] = points per label id.
-// Dynamic shared memory: (gout + 2) ints.
+// (bucket 0 = no column).  Keys are computed in parallel into shared memory;
+// each warp histograms its contiguous segment, the segment offsets come from
+// a fixed-order prefix, and each warp scatters its segment in order, so the
+// result is deterministic.  Writes perm[b][pos] = point, scodes[b][pos] =
+// column (or kNone), scoords[b][pos] = the point's (x, y), and
+// ptotals[b][label] = points per label id.
+// Dynamic shared memory: P + (kSortWarps + 1) * (gout + 1) ints.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kSortWarps * 32)
 point_sort_kernel(const int64_t* __restrict__ targets, const float* __restrict__ coords, int Ht,
                   int Wt, int P, int gt_total, int bg, int gout, int32_t* __restrict__ perm,
-                  int32_t* __restrict__ scodes, int32_t* __restrict__ ptotals) {
-    extern __shared__ int32_t bucket[];  // [gout + 1] counts, then running offsets
+                  int32_t* __restrict__ scodes, float* __restrict__ scoords,
+                  int32_t* __restrict__ ptotals) {
+    extern __shared__ int32_t sm[];
+    const int NB = gout + 1;
+    int32_t* keys = sm;                    // [P]
+    int32_t* wcnt = keys + P;              // [kSortWarps][NB] counts, then offsets
+    int32_t* total = wcnt + kSortWarps * NB;  // [NB]
     const int b = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t* tb = targets + (int64_t)b * Ht * Wt;
     const float* cb = coords + (int64_t)b * P * 2;
     int32_t* pt = ptotals + (int64_t)b * gt_total;
-    for (int i = threadIdx.x; i <= gout; i += blockDim.x) bucket[i] = 0;
+    for (int i = tid; i < kSortWarps * NB; i += blockDim.x) wcnt[i] = 0;
     __syncthreads();
-    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    const int seg = (P + kSortWarps - 1) / kSortWarps;
+    const int s0 = min(P, warp * seg), s1 = min(P, s0 + seg);
+    for (int p = s0 + lane; p < s1; p += 32) {
         const int64_t lab = point_label(tb, Ht, Wt, cb[2 * p], cb[2 * p + 1]);
         if (lab >= 0 && lab < gt_total) atomicAdd(&pt[lab], 1);
-        atomicAdd(&bucket[label_to_col(lab, gt_total, bg) + 1], 1);
+        const int key = label_to_col(lab, gt_total, bg) + 1;
+        keys[p] = key;
+        atomicAdd(&wcnt[warp * NB + key], 1);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {  // exclusive prefix (gout is small)
+    // offsets: bucket-major, then warp order (fixed order -> stable, deterministic)
+    for (int k = tid; k < NB; k += blockDim.x) {
         int run = 0;
-        for (int i = 0; i <= gout; ++i) {
-            const int c = bucket[i];
-            bucket[i] = run;
+        for (int w = 0; w < kSortWarps; ++w) run += wcnt[w * NB + k];
+        total[k] = run;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int k = 0; k < NB; ++k) {
+            const int c = total[k];
+            total[k] = run;
             run += c;
         }
     }
     __syncthreads();
-    if (threadIdx.x >= 32) return;
-    // stable scatter: warp 0 walks the points in order, 32 at a time
-    const int lane = threadIdx.x;
-    for (int base = 0; base < P; base += 32) {
+    for (int k = tid; k < NB; k += blockDim.x) {
+        int run = total[k];
+        for (int w = 0; w < kSortWarps; ++w) {
+            const int c = wcnt[w * NB + k];
+            wcnt[w * NB + k] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    int32_t* off = wcnt + warp * NB;
+    for (int base = s0; base < s1; base += 32) {
         const int p = base + lane;
-        int key = -1;
-        if (p < P) key = label_to_col(point_label(tb, Ht, Wt, cb[2 * p], cb[2 * p + 1]), gt_total, bg) + 1;
+        const int key = p < s1 ? keys[p] : -1;
         const unsigned peers = __match_any_sync(0xffffffffu, key);
         const int rank = __popc(peers & ((1u << lane) - 1u));
-        int pos = 0;
-        if (p < P) pos = bucket[key] + rank;
+        const int pos = p < s1 ? off[key] + rank : 0;
         __syncwarp();
-        if (p < P && rank == 0) bucket[key] += __popc(peers);
+        if (p < s1 && rank == 0) off[key] += __popc(peers);
         __syncwarp();
-        if (p < P) {
-            perm[(int64_t)b * P + pos] = p;
-            scodes[(int64_t)b * P + pos] = key - 1;
+        if (p < s1) {
+            const int64_t o = (int64_t)b * P + pos;
+            perm[o] = p;
+            scodes[o] = key - 1;
+            scoords[2 * o] = cb[2 * p];
+            scoords[2 * o + 1] = cb[2 * p + 1];
         }
     }
 }
@@ -106,6 +135,12 @@ ML_INLINE Taps bilinear_taps(float x, float y, int H, int W, bool align) {
     return t;
 }
 
+ML_INLINE float to_f32(float v) { return v; }
+template <typename T> ML_INLINE T from_f32(float v);
+template <> ML_INLINE float from_f32<float>(float v) { return v; }
+template <> ML_INLINE __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+ML_INLINE float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
 template <typename T>
 ML_INLINE float ld_logit(const T* p);
 template <>
@@ -120,15 +155,13 @@ ML_INLINE float ld_logit<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloa
 // ---------------------------------------------------------------------------
 template <typename T>
 __device__ __forceinline__ void point_sample_body(const T* __restrict__ logits,
-                                                  const float* __restrict__ coords,
-                                                  const int32_t* __restrict__ perm, int B, int Q,
+                                                  const float* __restrict__ scoords, int B, int Q,
                                                   int H, int W, int P, int align,
                                                   float* __restrict__ zs) {
     const int pos = blockIdx.x * blockDim.x + threadIdx.x;
     const int lb = blockIdx.y, b = lb % B;
     if (pos >= P) return;
-    const int p = perm[(int64_t)b * P + pos];
-    const float* cb = coords + ((int64_t)b * P + p) * 2;
+    const float* cb = scoords + ((int64_t)b * P + pos) * 2;
     const Taps tp = bilinear_taps(cb[0], cb[1], H, W, align != 0);
     const int q0 = blockIdx.z * kSampleQ;
     const int q1 = min(Q, q0 + kSampleQ);
@@ -144,48 +177,99 @@ __device__ __forceinline__ void point_sample_body(const T* __restrict__ logits,
 }
 
 __global__ void __launch_bounds__(256)
-point_sample_f32_kernel(const float* logits, const float* coords, const int32_t* perm, int B, int Q,
-                        int H, int W, int P, int align, float* zs) {
-    point_sample_body<float>(logits, coords, perm, B, Q, H, W, P, align, zs);
+point_sample_f32_kernel(const float* logits, const float* scoords, int B, int Q, int H, int W, int P,
+                        int align, float* zs) {
+    point_sample_body<float>(logits, scoords, B, Q, H, W, P, align, zs);
 }
 
 __global__ void __launch_bounds__(256)
-point_sample_bf16_kernel(const __nv_bfloat16* logits, const float* coords, const int32_t* perm,
-                         int B, int Q, int H, int W, int P, int align, float* zs) {
-    point_sample_body<__nv_bfloat16>(logits, coords, perm, B, Q, H, W, P, align, zs);
+point_sample_bf16_kernel(const __nv_bfloat16* logits, const float* scoords, int B, int Q, int H,
+                         int W, int P, int align, float* zs) {
+    point_sample_body<__nv_bfloat16>(logits, scoords, B, Q, H, W, P, align, zs);
+}
+
+// Block per (l,b,q) row: the row's logit map is staged in shared memory, so
+// the 4 taps of every point are shared-memory reads and the sampled row is
+// written contiguously.
+template <typename T>
+__device__ __forceinline__ void point_sample_row_body(const T* __restrict__ logits,
+                                                      const float* __restrict__ scoords, int B,
+                                                      int Q, int H, int W, int P, int align,
+                                                      float* __restrict__ zs) {
+    extern __shared__ __align__(16) unsigned char smap_raw[];
+    T* map = reinterpret_cast<T*>(smap_raw);
+    const int64_t row = blockIdx.x;
+    const int b = (int)((row / Q) % B);
+    const int HW = H * W;
+    const T* src = logits + row * (int64_t)HW;
+    const int nvec = (HW * (int)sizeof(T)) / 16;  // 16-byte chunks
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        for (int i = threadIdx.x; i < nvec; i += blockDim.x)
+            reinterpret_cast<uint4*>(map)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+        for (int i = nvec * 16 / (int)sizeof(T) + threadIdx.x; i < HW; i += blockDim.x) map[i] = src[i];
+    } else {
+        for (int i = threadIdx.x; i < HW; i += blockDim.x) map[i] = src[i];
+    }
+    __syncthreads();
+    const float* cb = scoords + (int64_t)b * P * 2;
+    float* out = zs + row * P;
+    for (int pos = threadIdx.x; pos < P; pos += blockDim.x) {
+        const float2 c = reinterpret_cast<const float2*>(cb)[pos];
+        const Taps tp = bilinear_taps(c.x, c.y, H, W, align != 0);
+        float z = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) z += tp.w[k] * to_f32(map[tp.idx[k]]);
+        out[pos] = z;
+    }
+}
+
+__global__ void __launch_bounds__(256)
+point_sample_row_f32_kernel(const float* logits, const float* scoords, int B, int Q, int H, int W,
+                            int P, int align, float* zs) {
+    point_sample_row_body<float>(logits, scoords, B, Q, H, W, P, align, zs);
+}
+
+__global__ void __launch_bounds__(256)
+point_sample_row_bf16_kernel(const __nv_bfloat16* logits, const float* scoords, int B, int Q, int H,
+                             int W, int P, int align, float* zs) {
+    point_sample_row_body<__nv_bfloat16>(logits, scoords, B, Q, H, W, P, align, zs);
 }
 
 // ---------------------------------------------------------------------------
 // Backward of the sampled mask costs: per (query, sorted point) the point
-// gradient of the matched (or forced-empty) sigmoid-CE + dice terms, scattered
-// to the 4 bilinear taps with atomicAdd into the fp32 gradient map.
-// grid = (ceil(P/256), L*B*Q).  zs holds the forward's sampled values.
+// gradient of the matched (or forced-empty) sigmoid-CE + dice terms, spread
+// to the 4 bilinear taps.
 // ---------------------------------------------------------------------------
-template <bool FOC>
-__device__ __forceinline__ void point_grad_body(const LossArgs& a, const float* __restrict__ zs,
-                                                const float* __restrict__ coords,
-                                                const int32_t* __restrict__ perm,
-                                                const int32_t* __restrict__ scodes, int P,
-                                                int align, float* __restrict__ gacc) {
-    const int pos = blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t qi = blockIdx.y;
-    if (pos >= P) return;
-    const int lb = (int)(qi / a.Q), l = lb / a.B, b = lb % a.B;
+struct RowGrad {
+    bool active, matched;
+    int gcol;
+    float mcoef, dcoef, sf, den, num, inv_d2;
+};
+
+ML_INLINE RowGrad row_grad_setup(const LossArgs& a, int64_t qi) {
+    RowGrad r;
+    const int lb = (int)(qi / a.Q), l = lb / a.B;
     const int64_t og = a.pred_to_gt[qi];
     const int64_t ga = og + (og >= a.bg ? 1 : 0);
-    const bool matched = og >= 0 && ga < a.gt_total;
-    const float mcoef = a.coef[l * 3 + 0], dcoef = a.coef[l * 3 + 1];
-    if (!(matched || a.force_masks) || (mcoef == 0.0f && dcoef == 0.0f)) return;
+    r.matched = og >= 0 && ga < a.gt_total;
+    r.gcol = r.matched ? (int)og : -100;
+    r.mcoef = a.coef[l * 3 + 0];
+    r.dcoef = a.coef[l * 3 + 1];
+    r.active = (r.matched || a.force_masks) && !(r.mcoef == 0.0f && r.dcoef == 0.0f);
     const float* sv = a.stats_in + qi * kSaved;
-    const float Ps = sv[0], T = matched ? sv[1] : 0.0f, I = matched ? sv[2] : 0.0f, Wt = sv[3];
-    const float sf = a.sigmoid_scale / Wt;
-    const float den = Ps + T + a.smooth;
-    const float num = 2.0f * I + a.smooth;
-    const float inv_d2 = 1.0f / fmaxf(den * den, 1e-20f);
-    const float x = zs[qi * P + pos];
+    const float Ps = sv[0], T = r.matched ? sv[1] : 0.0f, I = r.matched ? sv[2] : 0.0f;
+    r.sf = a.sigmoid_scale / sv[3];
+    r.den = Ps + T + a.smooth;
+    r.num = 2.0f * I + a.smooth;
+    r.inv_d2 = 1.0f / fmaxf(r.den * r.den, 1e-20f);
+    return r;
+}
+
+template <bool FOC>
+ML_INLINE float point_grad_value(const LossArgs& a, const RowGrad& r, float x, int code) {
     const Elem e = elem(x);
     const float om = 1.0f - e.p, pp = e.p * om;
-    const float t = (matched && scodes[(int64_t)b * P + pos] == (int)og) ? 1.0f : 0.0f;
+    const float t = (code == r.gcol) ? 1.0f : 0.0f;
     const float ncnt = 1.0f - t;
     float gs;
     if (FOC) {
@@ -193,14 +277,28 @@ __device__ __forceinline__ void point_grad_body(const LossArgs& a, const float* 
         const float mp = f.use_gamma ? __powf(om, f.gamma) : 1.0f;
         const float mn = f.use_gamma ? __powf(e.p, f.gamma) : 1.0f;
         gs = (-f.alpha_pos * t * mp * (f.gamma * e.p * e.pos + om) +
-              f.alpha_neg * ncnt * mn * (f.gamma * om * e.neg + e.p)) * sf;
+              f.alpha_neg * ncnt * mn * (f.gamma * om * e.neg + e.p)) * r.sf;
     } else {
-        gs = (ncnt * e.p - t * om) * sf;
+        gs = (ncnt * e.p - t * om) * r.sf;
     }
-    const float gd = (num * pp - 2.0f * den * pp * t) * inv_d2 * a.dice_scale;
-    const float g = mcoef * gs + dcoef * gd;
-    const int p = perm[(int64_t)b * P + pos];
-    const float* cb = coords + ((int64_t)b * P + p) * 2;
+    const float gd = (r.num * pp - 2.0f * r.den * pp * t) * r.inv_d2 * a.dice_scale;
+    return r.mcoef * gs + r.dcoef * gd;
+}
+
+// Large maps: global fp32 accumulation (caller zeroes gacc).
+// grid = (ceil(P/256), L*B*Q).
+template <bool FOC>
+__device__ __forceinline__ void point_grad_global_body(const LossArgs& a, const float* zs,
+                                                       const float* scoords, const int32_t* scodes,
+                                                       int P, int align, float* gacc) {
+    const int pos = blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t qi = blockIdx.y;
+    if (pos >= P) return;
+    const RowGrad r = row_grad_setup(a, qi);
+    if (!r.active) return;
+    const int b = (int)((qi / a.Q) % a.B);
+    const float g = point_grad_value<FOC>(a, r, zs[qi * P + pos], scodes[(int64_t)b * P + pos]);
+    const float* cb = scoords + ((int64_t)b * P + pos) * 2;
     const Taps tp = bilinear_taps(cb[0], cb[1], a.H, a.W, align != 0);
     float* gm = gacc + qi * (int64_t)a.H * a.W;
 #pragma unroll
@@ -209,15 +307,70 @@ __device__ __forceinline__ void point_grad_body(const LossArgs& a, const float* 
 }
 
 __global__ void __launch_bounds__(256)
-point_grad_kernel(LossArgs a, const float* zs, const float* coords, const int32_t* perm,
-                  const int32_t* scodes, int P, int align, float* gacc) {
-    point_grad_body<false>(a, zs, coords, perm, scodes, P, align, gacc);
+point_grad_global_kernel(LossArgs a, const float* zs, const float* scoords, const int32_t* scodes,
+                         int P, int align, float* gacc) {
+    point_grad_global_body<false>(a, zs, scoords, scodes, P, align, gacc);
 }
 
 __global__ void __launch_bounds__(256)
-point_grad_focal_kernel(LossArgs a, const float* zs, const float* coords, const int32_t* perm,
-                        const int32_t* scodes, int P, int align, float* gacc) {
-    point_grad_body<true>(a, zs, coords, perm, scodes, P, align, gacc);
+point_grad_global_focal_kernel(LossArgs a, const float* zs, const float* scoords,
+                               const int32_t* scodes, int P, int align, float* gacc) {
+    point_grad_global_body<true>(a, zs, scoords, scodes, P, align, gacc);
+}
+
+// Block per (l,b,q) row: the gradient map is accumulated in shared memory
+// and written once in the logits' dtype (zeros for rows the loss does not
+// reach), so no memset, no global atomics and no conversion pass.
+template <bool FOC, typename TO>
+__device__ __forceinline__ void point_grad_row_body(const LossArgs& a, const float* zs,
+                                                    const float* scoords, const int32_t* scodes,
+                                                    int P, int align, TO* grad) {
+    extern __shared__ __align__(16) float gmap[];
+    const int64_t qi = blockIdx.x;
+    const int HW = a.H * a.W;
+    TO* out = grad + qi * (int64_t)HW;
+    const RowGrad r = row_grad_setup(a, qi);
+    if (!r.active) {
+        for (int i = threadIdx.x; i < HW; i += blockDim.x) out[i] = from_f32<TO>(0.0f);
+        return;
+    }
+    for (int i = threadIdx.x; i < HW; i += blockDim.x) gmap[i] = 0.0f;
+    __syncthreads();
+    const int b = (int)((qi / a.Q) % a.B);
+    const float* cb = scoords + (int64_t)b * P * 2;
+    const int32_t* cd = scodes + (int64_t)b * P;
+    const float* z = zs + qi * P;
+    for (int pos = threadIdx.x; pos < P; pos += blockDim.x) {
+        const float g = point_grad_value<FOC>(a, r, z[pos], cd[pos]);
+        const float2 c = reinterpret_cast<const float2*>(cb)[pos];
+        const Taps tp = bilinear_taps(c.x, c.y, a.H, a.W, align != 0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (tp.w[k] != 0.0f) atomicAdd(&gmap[tp.idx[k]], g * tp.w[k]);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < HW; i += blockDim.x) out[i] = from_f32<TO>(gmap[i]);
+}
+
+__global__ void __launch_bounds__(256)
+point_grad_row_f32_kernel(LossArgs a, const float* zs, const float* scoords, const int32_t* scodes,
+                          int P, int align, float* grad) {
+    point_grad_row_body<false, float>(a, zs, scoords, scodes, P, align, grad);
+}
+__global__ void __launch_bounds__(256)
+point_grad_row_focal_f32_kernel(LossArgs a, const float* zs, const float* scoords,
+                                const int32_t* scodes, int P, int align, float* grad) {
+    point_grad_row_body<true, float>(a, zs, scoords, scodes, P, align, grad);
+}
+__global__ void __launch_bounds__(256)
+point_grad_row_bf16_kernel(LossArgs a, const float* zs, const float* scoords, const int32_t* scodes,
+                           int P, int align, __nv_bfloat16* grad) {
+    point_grad_row_body<false, __nv_bfloat16>(a, zs, scoords, scodes, P, align, grad);
+}
+__global__ void __launch_bounds__(256)
+point_grad_row_focal_bf16_kernel(LossArgs a, const float* zs, const float* scoords,
+                                 const int32_t* scodes, int P, int align, __nv_bfloat16* grad) {
+    point_grad_row_body<true, __nv_bfloat16>(a, zs, scoords, scodes, P, align, grad);
 }
 
 __global__ void f32_to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
@@ -227,26 +380,86 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16*
         dst[i] = __float2bfloat16_rn(src[i]);
 }
 
-// Host-side launchers (kernels and launches live in this file).
-cudaError_t launch_point_sample(int dtype, const void* logits, const float* coords,
-                                const int32_t* perm, int B, int L, int Q, int H, int W, int P,
-                                int align, float* zs, cudaStream_t st) {
-    dim3 g((P + 255) / 256, (unsigned)(L * B), (Q + kSampleQ - 1) / kSampleQ);
-    if (dtype == 1)
-        point_sample_bf16_kernel<<<g, 256, 0, st>>>(
-            static_cast<const __nv_bfloat16*>(logits), coords, perm, B, Q, H, W, P, align, zs);
-    else
-        point_sample_f32_kernel<<<g, 256, 0, st>>>(static_cast<const float*>(logits), coords,
-                                                      perm, B, Q, H, W, P, align, zs);
+// ---------------------------------------------------------------------------
+// Host-side launchers (kernels and their launches live in this file).
+// ---------------------------------------------------------------------------
+size_t point_sort_smem(int P, int gout) {
+    return sizeof(int32_t) * ((size_t)P + (size_t)(kSortWarps + 1) * (gout + 1));
+}
+
+cudaError_t launch_point_sort(const int64_t* targets, const float* coords, int B, int Ht, int Wt,
+                              int P, int gt_total, int bg, int gout, int32_t* perm, int32_t* scodes,
+                              float* scoords, int32_t* ptotals, cudaStream_t st) {
+    const size_t smem = point_sort_smem(P, gout);
+    cudaError_t e = cudaFuncSetAttribute(point_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    point_sort_kernel<<<B, kSortWarps * 32, smem, st>>>(targets, coords, Ht, Wt, P, gt_total, bg, gout,
+                                                         perm, scodes, scoords, ptotals);
     return cudaGetLastError();
 }
 
-cudaError_t launch_point_grad(bool foc, const LossArgs& la, const float* zs, const float* coords,
-                              const int32_t* perm, const int32_t* scodes, int P, int align,
-                              float* gacc, int64_t rows, cudaStream_t st) {
+cudaError_t launch_point_sample(int dtype, const void* logits, const float* scoords, int B, int L,
+                                int Q, int H, int W, int P, int align, float* zs, cudaStream_t st) {
+    const size_t map = (size_t)H * W * (dtype == 1 ? 2 : 4);
+    const int64_t rows = (int64_t)L * B * Q;
+    if (map <= kRowMapMaxBytes) {
+        const int smem = (int)((map + 15) & ~size_t(15));
+        if (dtype == 1) {
+            cudaError_t e = cudaFuncSetAttribute(point_sample_row_bf16_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return e;
+            point_sample_row_bf16_kernel<<<(unsigned)rows, 256, smem, st>>>(
+                static_cast<const __nv_bfloat16*>(logits), scoords, B, Q, H, W, P, align, zs);
+        } else {
+            cudaError_t e = cudaFuncSetAttribute(point_sample_row_f32_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return e;
+            point_sample_row_f32_kernel<<<(unsigned)rows, 256, smem, st>>>(
+                static_cast<const float*>(logits), scoords, B, Q, H, W, P, align, zs);
+        }
+        return cudaGetLastError();
+    }
+    dim3 g((P + 255) / 256, (unsigned)(L * B), (Q + kSampleQ - 1) / kSampleQ);
+    if (dtype == 1)
+        point_sample_bf16_kernel<<<g, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), scoords,
+                                                    B, Q, H, W, P, align, zs);
+    else
+        point_sample_f32_kernel<<<g, 256, 0, st>>>(static_cast<const float*>(logits), scoords, B, Q, H,
+                                                   W, P, align, zs);
+    return cudaGetLastError();
+}
+
+// Returns true in *used_rows when the row kernel wrote grad_out directly;
+// otherwise the caller zeroed `gacc` (fp32) and must convert when needed.
+cudaError_t launch_point_grad(bool foc, int dtype, const LossArgs& la, const float* zs,
+                              const float* scoords, const int32_t* scodes, int P, int align,
+                              void* grad_out, float* gacc, int64_t rows, bool* used_rows,
+                              cudaStream_t st) {
+    const size_t map = (size_t)la.H * la.W * 4;
+    if (map <= kRowMapMaxBytes) {
+        *used_rows = true;
+        const int smem = (int)map;
+#define ML_PG(K, T)                                                                             \
+    do {                                                                                         \
+        cudaError_t e = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+        if (e != cudaSuccess) return e;                                                          \
+        K<<<(unsigned)rows, 256, smem, st>>>(la, zs, scoords, scodes, P, align, static_cast<T*>(grad_out)); \
+    } while (0)
+        if (dtype == 1) {
+            if (foc) ML_PG(point_grad_row_focal_bf16_kernel, __nv_bfloat16);
+            else ML_PG(point_grad_row_bf16_kernel, __nv_bfloat16);
+        } else {
+            if (foc) ML_PG(point_grad_row_focal_f32_kernel, float);
+            else ML_PG(point_grad_row_f32_kernel, float);
+        }
+#undef ML_PG
+        return cudaGetLastError();
+    }
+    *used_rows = false;
     dim3 g((P + 255) / 256, (unsigned)rows);
-    if (foc) point_grad_focal_kernel<<<g, 256, 0, st>>>(la, zs, coords, perm, scodes, P, align, gacc);
-    else point_grad_kernel<<<g, 256, 0, st>>>(la, zs, coords, perm, scodes, P, align, gacc);
+    if (foc) point_grad_global_focal_kernel<<<g, 256, 0, st>>>(la, zs, scoords, scodes, P, align, gacc);
+    else point_grad_global_kernel<<<g, 256, 0, st>>>(la, zs, scoords, scodes, P, align, gacc);
     return cudaGetLastError();
 }
 
@@ -255,6 +468,5 @@ cudaError_t launch_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t 
     f32_to_bf16_kernel<<<(unsigned)blocks, 256, 0, st>>>(src, static_cast<__nv_bfloat16*>(dst), n);
     return cudaGetLastError();
 }
-
 
 }  // namespace mlb

@@ -96,11 +96,11 @@ class MaskMatchingSampledFunction(Function):
         ml = mask_logits.contiguous()
         cl = cls_logits.contiguous().float()
         pc = point_coords.contiguous().float()
-        p2g, prd, means, saved, _ = ops.mask_matching_sampled_ex(
+        p2g, prd, means, saved, _, fws = ops.mask_matching_sampled_ex(
             ml, mask_targets.contiguous(), cl, cls_targets.contiguous(), pc, *args,
-            num_masks_dev=nm_dev, want_saved=True)
+            num_masks_dev=nm_dev, want_saved=True, want_workspace=True)
         ctx.save_for_backward(ml, mask_targets, cl, cls_targets, pc, p2g, saved,
-                              nm_dev if nm_dev is not None else torch.empty(0))
+                              nm_dev if nm_dev is not None else torch.empty(0), fws)
         ctx.args = args
         ctx.has_nm = nm_dev is not None
         ctx.mark_non_differentiable(p2g, prd)
@@ -108,7 +108,7 @@ class MaskMatchingSampledFunction(Function):
 
     @staticmethod
     def backward(ctx, _a, _b, gm_mean, gd_mean, gc_mean):
-        ml, mt, cl, ct, pc, p2g, saved, nm_dev = ctx.saved_tensors
+        ml, mt, cl, ct, pc, p2g, saved, nm_dev, fws = ctx.saved_tensors
         a = ctx.args
         L = ml.shape[0]
 
@@ -119,5 +119,5 @@ class MaskMatchingSampledFunction(Function):
         gm, gc = ops.mask_matching_sampled_backward(
             g(gm_mean), g(gd_mean), g(gc_mean), ml, mt, cl, ct, pc, p2g, saved, a[0], a[1], a[2],
             a[3], a[4], a[6], a[7], a[10], a[11], a[12], a[13], a[14], a[15], a[16],
-            num_masks_dev=nm_dev if ctx.has_nm else None)
+            num_masks_dev=nm_dev if ctx.has_nm else None, forward_workspace=fws)
         return (gm, None, gc) + (None,) * 19

@@ -519,9 +519,11 @@ def mask_matching_sampled_ex(mask_logits, mask_targets, cls_logits, cls_targets,
                              strategy_id=0, mask_gamma=0.0, mask_alpha=-1.0, cls_gamma=0.0,
                              cls_alpha=-1.0, void_class_index=-1, use_softmax_label_loss=False,
                              align_corners=False, *, num_masks_dev=None, want_saved=False,
-                             want_costs=False):
+                             want_costs=False, want_workspace=False):
     """Point-sampled counterpart of mask_matching_ex: returns (pred_to_gt,
-    pred_round, layer_means(3,L), saved or None, costs or None)."""
+    pred_round, layer_means(3,L), saved or None, costs or None) and, with
+    want_workspace, the forward workspace (whose sorted points and samples the
+    backward can reuse)."""
     check_status()
     _check_sampled(mask_logits, mask_targets, cls_logits, cls_targets, point_coords)
     lib = _lib_handle()
@@ -551,6 +553,8 @@ def mask_matching_sampled_ex(mask_logits, mask_targets, cls_logits, cls_targets,
         _ptr(point_coords), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd), _ptr(means), _ptr(costs),
         _ptr(saved), _ptr(status), _ptr(ws), ws.numel(), _stream(dev)))
     _track_status(status)
+    if want_workspace:
+        return p2g, prd, means, saved, costs, ws
     return p2g, prd, means, saved, costs
 
 
@@ -562,8 +566,11 @@ def mask_matching_sampled_backward(grad_layer_mask_mean, grad_layer_dice_mean,
                                    force_unmatched_class_to_background=False, mask_gamma=0.0,
                                    mask_alpha=-1.0, cls_gamma=0.0, cls_alpha=-1.0,
                                    void_class_index=-1, use_softmax_label_loss=False,
-                                   align_corners=False, *, num_masks_dev=None):
-    """[grad_mask_logits (logits dtype), grad_cls_logits] of the sampled op."""
+                                   align_corners=False, *, num_masks_dev=None,
+                                   forward_workspace=None):
+    """[grad_mask_logits (logits dtype), grad_cls_logits] of the sampled op.
+    ``forward_workspace``: the workspace returned by mask_matching_sampled_ex
+    for the same inputs (reuses its sorted points and samples)."""
     check_status()
     _check_sampled(mask_logits, mask_targets, cls_logits, cls_targets, point_coords)
     _check_input(saved, "saved")
@@ -585,6 +592,6 @@ def mask_matching_sampled_backward(grad_layer_mask_mean, grad_layer_dice_mean,
         ctypes.byref(d), ctypes.byref(p), P, int(bool(align_corners)), dt,
         _ptr(grad_layer_mask_mean), _ptr(grad_layer_dice_mean), _ptr(grad_layer_cls_mean),
         _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits), _ptr(cls_targets),
-        _ptr(point_coords), _ptr(pred_to_gt), _ptr(saved), _ptr(num_masks_dev), _ptr(gm), _ptr(gc),
-        _ptr(ws), ws.numel(), _stream(dev)))
+        _ptr(point_coords), _ptr(pred_to_gt), _ptr(saved), _ptr(num_masks_dev),
+        _ptr(forward_workspace), _ptr(gm), _ptr(gc), _ptr(ws), ws.numel(), _stream(dev)))
     return [gm, gc]

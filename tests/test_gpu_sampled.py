@@ -40,9 +40,11 @@ def test_sampled_costs_golden(name):
     close(out[1].cpu().numpy(), d["dice"])
 
 
-def _case(seed, dtype):
+def _case(seed, dtype, big=False):
     torch.manual_seed(seed)
     L, B, Q, H, W, s, C, Pn = 1, 3, 20, 16, 16, 4, 9, 777
+    if big:  # 160x160 fp32 gradient map exceeds the shared-memory row path
+        L, B, Q, H, W, s, C, Pn = 1, 2, 6, 160, 160, 1, 9, 1500
     cfg = synthetic.Config("pt", 12, L, B, Q, H, W, s, C, 3.0, "ellipse", ("fixed", 5), (0.02, 0.2))
     b = synthetic.make_batch(cfg)
     coords = torch.rand(B, Pn, 2)
@@ -53,14 +55,14 @@ def _case(seed, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("variant", ["softmax", "sigmoid_focal_k2"])
+@pytest.mark.parametrize("variant", ["softmax", "sigmoid_focal_k2", "big_map"])
 def test_sampled_matching_forward_backward(dtype, variant):
-    ml, mt, cl, ct, pc, C = _case(7, dtype)
+    ml, mt, cl, ct, pc, C = _case(7, dtype, big=variant == "big_map")
     kw = dict(smooth=1.0, sigmoid_scale=5.0, dice_scale=5.0, cls_scale=2.0, background_index=0,
               uncertainty_gamma=0.0, inf_thresh=1e30, num_masks=-1.0,
               force_unmatched_class_to_background=True, topk_matches=1, strategy_id=0,
               void_class_index=C - 1, use_softmax_label_loss=True)
-    if variant != "softmax":
+    if variant == "sigmoid_focal_k2":
         kw.update(use_softmax_label_loss=False, mask_gamma=2.0, mask_alpha=0.25, cls_gamma=1.0,
                   cls_alpha=0.3, topk_matches=2, num_masks=4.0)
     P = O.Params(**kw)
@@ -84,3 +86,19 @@ def test_sampled_matching_forward_backward(dtype, variant):
     tol = 1e-5 if dtype == torch.float32 else 1e-2  # bf16 gradient storage
     np.testing.assert_allclose(gm, egm, rtol=max(1e-4, tol), atol=tol * np.abs(egm).max())
     np.testing.assert_allclose(z.grad.cpu().numpy(), egc, rtol=1e-4, atol=1e-5 * np.abs(egc).max())
+
+
+def test_sampled_backward_without_forward_workspace():
+    """The op-level backward rebuilds the sorted points itself when it is not
+    handed the forward's workspace; both give the same gradients."""
+    ml, mt, cl, ct, pc, C = _case(9, torch.float32)
+    d = [t.to(DEV) for t in (ml, mt, cl, ct, pc)]
+    args = (1.0, 5.0, 5.0, 2.0, 0, 1e30, -1.0, True, 1, 0, 0.0, -1.0, 0.0, -1.0, C - 1, True, False)
+    p2g, prd, means, saved, _, fws = ops.mask_matching_sampled_ex(*d, *args, want_saved=True,
+                                                                  want_workspace=True)
+    g = torch.ones(1, device=DEV)
+    bargs = (1.0, 5.0, 5.0, 2.0, 0, -1.0, True, 0.0, -1.0, 0.0, -1.0, C - 1, True, False)
+    a = ops.mask_matching_sampled_backward(g, g, g, *d, p2g, saved, *bargs, forward_workspace=fws)
+    b = ops.mask_matching_sampled_backward(g, g, g, *d, p2g, saved, *bargs)
+    torch.testing.assert_close(a[0], b[0], rtol=1e-5, atol=1e-8)
+    torch.testing.assert_close(a[1], b[1], rtol=0, atol=0)
