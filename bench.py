@@ -342,8 +342,23 @@ def run_ours(args, cfg):
     gstep.check()
     ops.check_status(block=True)
 
+    def teardown():
+        """All ranks: free the captured graph (it holds NCCL work), barrier,
+        destroy the group.  A watchdog force-exits if teardown stalls, so a
+        finished benchmark never holds its GPUs."""
+        nonlocal gstep
+        gstep = None
+        torch.cuda.synchronize()
+        if ws > 1:
+            import threading
+            threading.Timer(60.0, lambda: os._exit(0)).start()
+            dist.barrier()
+            dist.destroy_process_group()
+            sys.stdout.flush()
+            os._exit(0)
+
     if rank != 0:
-        dist.destroy_process_group() if ws > 1 else None
+        teardown()
         return
     peaks = {}
     try:
@@ -399,8 +414,7 @@ def run_ours(args, cfg):
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
-    if ws > 1:
-        dist.destroy_process_group()
+    teardown()
 
 
 def main():
