@@ -48,7 +48,11 @@ typedef struct ml_params {
     int64_t background_index;          /* GT column dropped from the costs, or -1 */
     float uncertainty_gamma, uncertainty_gamma_min;
     double inf_thresh;                 /* costs >= this are treated as +inf */
-    double num_masks;                  /* <= 0: use the matched count */
+    double num_masks;                  /* > 0: the normaliser; -2: count the present
+                                          GT ids of this call on the device (the
+                                          forward then writes the count to
+                                          num_masks_dev when given); else <= 0:
+                                          use the matched count */
     int32_t force_unmatched_class_to_background;
     int32_t force_unmatched_masks_to_empty;
     int64_t topk_matches;              /* K >= 0 */

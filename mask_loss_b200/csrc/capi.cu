@@ -707,6 +707,11 @@ int ml_mask_matching(const ml_dims* d, const ml_params* p, const float* mask_log
     LossArgs la = loss_args(P, p);
     la.pred_to_gt = pred_to_gt; la.sep = a.sep; la.qstat = a.qstat; la.rawI = a.rawI; la.rawT = a.rawT;
     la.num_masks_dev = num_masks_dev; la.saved = saved; la.layer_means = layer_means;
+    if (p->num_masks == -2.0) {  // auto: counted on the device, written to num_masks_dev
+        la.auto_num_masks = 1;
+        la.totals = a.totals;
+        la.num_masks_out = const_cast<float*>(num_masks_dev);
+    }
     loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
     ML_CHECK_LAUNCH("loss_fwd_kernel");
     return ML_OK;
@@ -779,15 +784,12 @@ int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float*
     const int HW = P.H * P.W;
     const bool vec = (HW % 4 == 0) && (reinterpret_cast<uintptr_t>(mask_logits) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(grad_mask_logits) % 16 == 0);
-    const int64_t target = (int64_t)sm_count() * 8;
-    int64_t nch = (target + P.L * P.B - 1) / std::max<int64_t>(1, P.L * P.B);
-    int64_t ck = (HW + nch - 1) / nch;
-    ck = (ck + 127) / 128 * 128;
-    ck = std::max<int64_t>(256, std::min<int64_t>(ck, 8192));
+    // one block per (query row, contiguous range of cells)
+    const int64_t ck = std::min<int64_t>(((HW + 3) / 4) * 4, 4096);
     la.chunk_cells = (int)ck;
     const int nchunk = (int)((HW + ck - 1) / ck);
-    dim3 gg(nchunk, P.L * P.B);
-    const size_t gs = sizeof(int) * ck;
+    dim3 gg((unsigned)LBQ, nchunk);
+    const size_t gs = 0;
 #define ML_MG(U, F, V) mask_grad_kernel<U, F, V><<<gg, 256, gs, st>>>(la)
     {
     ProfScope prof(1, st);
@@ -870,6 +872,11 @@ int ml_mask_matching_sampled(const ml_dims* d, const ml_params* p, int64_t num_p
     LossArgs la = loss_args(P, p);
     la.pred_to_gt = pred_to_gt; la.sep = a.sep; la.qstat = a.qstat; la.rawI = a.rawI; la.rawT = a.rawT;
     la.num_masks_dev = num_masks_dev; la.saved = saved; la.layer_means = layer_means;
+    if (p->num_masks == -2.0) {  // auto: counted on the device, written to num_masks_dev
+        la.auto_num_masks = 1;
+        la.totals = a.totals;
+        la.num_masks_out = const_cast<float*>(num_masks_dev);
+    }
     loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
     ML_CHECK_LAUNCH("loss_fwd_kernel");
     return ML_OK;

@@ -115,6 +115,9 @@ struct LossArgs {
     float* grad_cls_logits;
     // scalars
     float num_masks;
+    int auto_num_masks;      // count present GT ids from `totals` (num_masks == -2)
+    const int32_t* totals;   // (B, GT_total) label histogram (auto mode)
+    float* num_masks_out;    // where the auto count is published, or null
     float smooth, sigmoid_scale, dice_scale, cls_scale;
     float ug, ugmin, mask_gamma, mask_alpha, cls_gamma, cls_alpha;
     int force_masks, force_cls, has_void, void_index, use_softmax, normalize_uncertainty;

@@ -66,6 +66,17 @@ ML_INLINE void denominators(const LossArgs& a, float matched, float* md, float* 
 __global__ void __launch_bounds__(512) loss_fwd_kernel(LossArgs a) {
     __shared__ float sh[32 * 4];
     const int l = blockIdx.x;
+    if (a.auto_num_masks) {
+        // num_masks = present non-background GT ids of this batch, clamped >= 1;
+        // block 0 publishes it for the backward
+        float c[1] = {0.0f};
+        for (int i = threadIdx.x; i < a.B * a.gt_total; i += blockDim.x)
+            if (i % a.gt_total != a.bg && a.totals[i] > 0) c[0] += 1.0f;
+        block_sum<1>(c, sh);
+        a.num_masks = fmaxf(c[0], 1.0f);
+        if (l == 0 && threadIdx.x == 0 && a.num_masks_out) *a.num_masks_out = a.num_masks;
+        a.num_masks_dev = nullptr;
+    }
     const int n = a.B * a.Q;
     const int64_t G = a.G;
     const int64_t slice = (int64_t)a.L * a.B * a.Q * G;
@@ -180,101 +191,82 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(LossArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Mask-logit gradient: grid = (nchunk, L*B), block = 256.  One pass over the
-// logits of every query of image b in the block's cell chunk.  Formula of
+// Mask-logit gradient: grid = (L*B*Q, nchunk), block = 256; a block owns one
+// query row and a contiguous range of chunk_cells cells.  Rows the loss does
+// not reach are pure 128-bit streaming stores of zeros (memset speed); the
+// matched (or forced) rows read logits and labels and write the gradient of
 // src/cuda/mask_matching_backward.cu:169-215.
 // ---------------------------------------------------------------------------
 template <bool UNC, bool FOC, bool VEC>
 __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
-    extern __shared__ int gcode[];  // [chunk] pure column / kNone / kMixed
-    const int lb = blockIdx.y, l = lb / a.B, b = lb % a.B;
+    const int64_t qi = blockIdx.x;
+    const int lb = (int)(qi / a.Q), l = lb / a.B, b = lb % a.B;
     const int HW = a.H * a.W;
-    const int c0 = blockIdx.x * a.chunk_cells;
+    const int c0 = blockIdx.y * a.chunk_cells;
     const int nc = min(a.chunk_cells, HW - c0);
-    const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
-    const int s = a.s, s2 = s * s;
-    for (int k = threadIdx.x; k < nc; k += blockDim.x) {
-        const int cell = c0 + k;
-        int c;
-        if (s == 1) {
-            c = label_to_col(tb[cell], a.gt_total, a.bg);
-        } else {
-            const int ci = cell / a.W, cj = cell - ci * a.W;
-            const int64_t* r0 = tb + (int64_t)(ci * s) * a.Wt + (int64_t)cj * s;
-            c = label_to_col(r0[0], a.gt_total, a.bg);
-            for (int pp = 1; pp < s2 && c != kMixed; ++pp) {
-                const int cc = label_to_col(r0[(int64_t)(pp / s) * a.Wt + (pp % s)], a.gt_total, a.bg);
-                if (cc != c) c = kMixed;
-            }
-        }
-        gcode[k] = c;
-    }
-    __syncthreads();
-    const float N2 = (float)s2;
-    const Focal f = make_focal(a.mask_gamma, a.mask_alpha);
+    float* gout = a.grad_mask_logits + qi * HW + c0;
     const float mcoef = a.coef[l * 3 + 0], dcoef = a.coef[l * 3 + 1];
-    // one warp per query: the per-query set-up is amortised over the whole
-    // cell chunk (128-bit accesses, 512 bytes per warp instruction)
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int q = warp; q < a.Q; q += nw) {
-        const int64_t qi = (int64_t)lb * a.Q + q;
-        const int64_t og = a.pred_to_gt[qi];
-        const int64_t ga = og + (og >= a.bg ? 1 : 0);
-        const bool matched = og >= 0 && ga < a.gt_total;
-        const int gcol = matched ? (int)og : -100;
-        float* gout = a.grad_mask_logits + qi * HW + c0;
-        const float* xin = a.mask_logits + qi * HW + c0;
-        const bool active = (matched || a.force_masks) && !(mcoef == 0.0f && dcoef == 0.0f);
-        if (!active) {
-            if (VEC) {
-#pragma unroll 4
-                for (int k = lane * 4; k < nc; k += 128)
-                    __stcs(reinterpret_cast<float4*>(gout + k), make_float4(0.f, 0.f, 0.f, 0.f));
-            } else {
-                for (int k = lane; k < nc; k += 32) gout[k] = 0.0f;
-            }
-            continue;
-        }
-        const float* sv = a.stats_in + qi * kSaved;
-        const float P = sv[0], T = matched ? sv[1] : 0.0f, I = matched ? sv[2] : 0.0f, Wt = sv[3];
-        const float sf = a.sigmoid_scale / Wt;
-        const float den = P + T + a.smooth;
-        const float num = 2.0f * I + a.smooth;
-        const float inv_d2 = 1.0f / fmaxf(den * den, 1e-20f);
-        const float two_den = 2.0f * den;
-        auto g1 = [&](float x, int k) -> float {
-            const Elem e = elem(x);
-            const float om = 1.0f - e.p, pp = e.p * om;
-            const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
-            const int cc = gcode[k];
-            float t = 0.0f;
-            if (cc == gcol) t = N2;
-            else if (cc == kMixed && matched) t = cell_count(tb, c0 + k, a.W, a.Wt, s, ga);
-            const float ncnt = fmaxf(N2 - t, 0.0f);
-            float gs;
-            if (FOC) {
-                const float mp = f.use_gamma ? __powf(om, f.gamma) : 1.0f;
-                const float mn = f.use_gamma ? __powf(e.p, f.gamma) : 1.0f;
-                const float gpos = -w * f.alpha_pos * t * mp * (f.gamma * e.p * e.pos + om);
-                const float gneg = w * f.alpha_neg * ncnt * mn * (f.gamma * om * e.neg + e.p);
-                gs = (gpos + gneg) * sf;
-            } else {
-                gs = (w * (ncnt * e.p - t * om)) * sf;
-            }
-            const float gd = (num * (w * pp * N2) - two_den * (w * pp * t)) * inv_d2 * a.dice_scale;
-            return mcoef * gs + dcoef * gd;
-        };
+    const int64_t og = a.pred_to_gt[qi];
+    const int64_t ga = og + (og >= a.bg ? 1 : 0);
+    const bool matched = og >= 0 && ga < a.gt_total;
+    const bool active = (matched || a.force_masks) && !(mcoef == 0.0f && dcoef == 0.0f);
+    if (!active) {
         if (VEC) {
-#pragma unroll 4
-            for (int k = lane * 4; k < nc; k += 128) {
-                const float4 xv = __ldcs(reinterpret_cast<const float4*>(xin + k));
-                float4 r;
-                r.x = g1(xv.x, k); r.y = g1(xv.y, k + 1); r.z = g1(xv.z, k + 2); r.w = g1(xv.w, k + 3);
-                __stcs(reinterpret_cast<float4*>(gout + k), r);
-            }
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4)
+                __stcs(reinterpret_cast<float4*>(gout + k), z);
         } else {
-            for (int k = lane; k < nc; k += 32) gout[k] = g1(xin[k], k);
+            for (int k = threadIdx.x; k < nc; k += blockDim.x) gout[k] = 0.0f;
         }
+        return;
+    }
+    const float* xin = a.mask_logits + qi * HW + c0;
+    const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
+    const int s = a.s;
+    const float N2 = (float)(s * s);
+    const Focal f = make_focal(a.mask_gamma, a.mask_alpha);
+    const float* sv = a.stats_in + qi * kSaved;
+    const float P = sv[0], T = matched ? sv[1] : 0.0f, I = matched ? sv[2] : 0.0f, Wt = sv[3];
+    const float sf = a.sigmoid_scale / Wt;
+    const float den = P + T + a.smooth;
+    const float num = 2.0f * I + a.smooth;
+    const float inv_d2 = 1.0f / fmaxf(den * den, 1e-20f);
+    const float two_den = 2.0f * den;
+    auto count = [&](int k) -> float {  // pixels of the matched label in cell c0 + k
+        if (!matched) return 0.0f;
+        if (s == 1) return tb[c0 + k] == ga ? 1.0f : 0.0f;
+        return cell_count(tb, c0 + k, a.W, a.Wt, s, ga);
+    };
+    auto g1 = [&](float x, float t) -> float {
+        const Elem e = elem(x);
+        const float om = 1.0f - e.p, pp = e.p * om;
+        const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
+        const float ncnt = fmaxf(N2 - t, 0.0f);
+        float gs;
+        if (FOC) {
+            const float mp = f.use_gamma ? __powf(om, f.gamma) : 1.0f;
+            const float mn = f.use_gamma ? __powf(e.p, f.gamma) : 1.0f;
+            const float gpos = -w * f.alpha_pos * t * mp * (f.gamma * e.p * e.pos + om);
+            const float gneg = w * f.alpha_neg * ncnt * mn * (f.gamma * om * e.neg + e.p);
+            gs = (gpos + gneg) * sf;
+        } else {
+            gs = (w * (ncnt * e.p - t * om)) * sf;
+        }
+        const float gd = (num * (w * pp * N2) - two_den * (w * pp * t)) * inv_d2 * a.dice_scale;
+        return mcoef * gs + dcoef * gd;
+    };
+    if (VEC) {
+        for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4) {
+            const float4 xv = __ldcs(reinterpret_cast<const float4*>(xin + k));
+            float4 r;
+            r.x = g1(xv.x, count(k));
+            r.y = g1(xv.y, count(k + 1));
+            r.z = g1(xv.z, count(k + 2));
+            r.w = g1(xv.w, count(k + 3));
+            __stcs(reinterpret_cast<float4*>(gout + k), r);
+        }
+    } else {
+        for (int k = threadIdx.x; k < nc; k += blockDim.x) gout[k] = g1(xin[k], count(k));
     }
 }
 

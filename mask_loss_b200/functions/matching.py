@@ -7,7 +7,9 @@ with the binding's own argument order.  The forward keeps the per-query
 statistics of the matched pairs, so the backward streams the logits once.
 
 ``num_masks`` may also be a CUDA fp32 scalar tensor (for instance the result
-of an all-reduce): it is then read on the device and never synchronised.
+of an all-reduce): it is then read on the device and never synchronised; or
+the string ``"auto"``: the number of present non-background GT ids of the
+batch, counted on the device from the forward's own label histogram.
 """
 from __future__ import annotations
 
@@ -42,7 +44,12 @@ def resolve_args(mask_logits, mask_targets, cls_logits, cls_targets, smooth, sig
         raise ValueError("uncertainty_gamma_min must be in [0, 1]")
     norm = bool(normalize_uncertainty if normalize_uncertainty is not None else True)
     nm_dev = None
-    if isinstance(num_masks, torch.Tensor):
+    if isinstance(num_masks, str) and num_masks == "auto":
+        # count the present GT ids on the device during the forward; the count
+        # lands in nm_dev and the backward reads it from there
+        nm_dev = torch.empty((), dtype=torch.float32, device=mask_logits.device)
+        nm = -2.0
+    elif isinstance(num_masks, torch.Tensor):
         nm_dev = num_masks.detach().reshape(()).to(torch.float32).contiguous()
         nm = -1.0
     else:

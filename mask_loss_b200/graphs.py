@@ -29,6 +29,11 @@ from . import ops, parallel
 from .functions import MaskMatchingFunction, MaskMatchingSampledFunction
 
 
+def _multi_rank() -> bool:
+    import torch.distributed as dist
+    return dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
+
+
 class MatchingLossStep:
     """With ``point_coords`` (B,P,2) the step runs the point-sampled op
     (MaskMatchingSampledFunction) and ``args`` are its 17 scalar arguments;
@@ -48,6 +53,10 @@ class MatchingLossStep:
         self.nm_slot = 6 if self.sampled else 9
         self.allreduce_num_masks = (isinstance(args[self.nm_slot], str) and
                                     args[self.nm_slot] == "allreduce")
+        if self.allreduce_num_masks and not self.sampled and not _multi_rank():
+            # one rank: the count needs no collective, take it from the forward
+            self.args[self.nm_slot] = "auto"
+            self.allreduce_num_masks = False
         self.w = loss_weights
         self.graph = None
         side = torch.cuda.Stream()

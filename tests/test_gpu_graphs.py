@@ -44,3 +44,19 @@ def test_graph_replay_matches_eager_and_tracks_inputs():
         torch.testing.assert_close(step.losses, losses, rtol=1e-5, atol=1e-6)
         torch.testing.assert_close(step.grad_mask_logits, gm, rtol=1e-5, atol=1e-9)
         torch.testing.assert_close(step.grad_cls_logits, gc, rtol=1e-5, atol=1e-9)
+
+
+def test_auto_num_masks_counts_present_gts():
+    cfg = synthetic.CONFIGS["cfg1"]
+    b = synthetic.make_batch(cfg, device=DEV)
+    ml, mt, cl, ct = (b[k].contiguous() for k in ("mask_logits", "mask_targets", "cls_logits",
+                                                  "cls_targets"))
+    args = _args(cfg)
+    present = sum(int((torch.unique(mt[i]) > 0).sum()) for i in range(cfg.B))
+    a_auto = list(args); a_auto[9] = "auto"
+    a_num = list(args); a_num[9] = float(present)
+    r1 = _eager(ml, mt, cl, ct, a_auto)
+    r2 = _eager(ml, mt, cl, ct, a_num)
+    # force_unmatched_class=True makes the class term use B*Q; mask/dice use num_masks
+    for x, y in zip(r1[1:], r2[1:]):
+        torch.testing.assert_close(x, y, rtol=1e-6, atol=1e-9)
