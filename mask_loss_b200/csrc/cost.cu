@@ -258,18 +258,28 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
         run_tiles = 0;
     };
 
-    // per-element update of the row sums and the run accumulators
+    // per-element update of the row sums and the run accumulators.  FAST keeps
+    // only tile sums (x, |x|, p); a run's sums of x and p are differences of
+    // the tile sums at its ends (close_run), which saves two FMAs per element.
     float trow[NROW] = {};
     float prod = 1.0f;
+    float tabs = 0.0f, sx0 = 0.0f, sp0 = 0.0f;
+    auto close_run = [&]() {
+        if (FAST) {
+            racc[0] = fmaf(m, trow[0] - sx0, racc[0]);
+            racc[1] = fmaf(m, trow[1] - sp0, racc[1]);
+            sx0 = trow[0];
+            sp0 = trow[1];
+        }
+    };
     auto element = [&](float x, int cell, auto mix_tag) {
         constexpr bool MIX = decltype(mix_tag)::value;
         if (FAST) {
             const Fast f = fast_elem(x);
             prod *= f.d;
-            trow[0] += fmaxf(x, 0.0f);
+            trow[0] += x;
+            tabs += fabsf(x);
             trow[1] += f.p;
-            racc[0] = fmaf(m, x, racc[0]);
-            racc[1] = fmaf(m, f.p, racc[1]);
             if (MIX && qvalid)
                 mixed_cell<UNC>(a.targets, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, -x, f.p, 1.0f);
         } else {
@@ -307,6 +317,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
 #pragma unroll
         for (int i = 0; i < NROW; ++i) trow[i] = 0.0f;
         prod = 1.0f;
+        tabs = sx0 = sp0 = 0.0f;
         if (nv == KBOX) {
 #pragma unroll 2
             for (int c = 0; c < KBOX / 4; ++c) {
@@ -320,6 +331,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         if ((b4 >> u) & 1u) {
+                            close_run();
                             flush();
                             cur = __shfl_sync(0xffffffffu, my_code, 4 * c + u);
                             m = cur >= 0 ? 1.0f : 0.0f;
@@ -335,6 +347,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
             for (int k = 0; k < nv; ++k) {
                 const float x = rowp[((((k >> 2) ^ (t & 7)) << 2)) + (k & 3)];
                 if ((bnd >> k) & 1u) {
+                    close_run();
                     flush();
                     cur = __shfl_sync(0xffffffffu, my_code, k);
                     m = cur >= 0 ? 1.0f : 0.0f;
@@ -346,6 +359,8 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
+        close_run();
+        if (FAST) trow[0] = 0.5f * (trow[0] + tabs);  // sum of max(x, 0)
 #pragma unroll
         for (int i = 0; i < NROW; ++i) rows[i] += trow[i];
         if (bnd != 0u) run_tiles = 0;
