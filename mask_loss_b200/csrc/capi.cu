@@ -188,6 +188,35 @@ int validate_params(const ml_params* p, int64_t C) {
     return ML_OK;
 }
 
+template <bool UNC, bool FOC, bool TMA, bool MIX>
+int cost_blocks_per_sm_t(size_t smem, int threads) {
+    auto k = cost_partial_kernel<UNC, FOC, TMA, MIX>;
+    int n = 0;
+    if (ensure_smem(k, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, threads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+// Resident cost CTAs per SM for the kernel instance the plan launches (its
+// registers and shared memory); without a device, the shared-memory bound.
+int cost_blocks_per_sm(const FwdPlan& P, int threads) {
+    const bool mix = P.s > 1;
+    int n = 0;
+#define ML_OCC(U, F) \
+    n = P.tma_ok ? (mix ? cost_blocks_per_sm_t<U, F, true, true>(P.cost_smem, threads)      \
+                        : cost_blocks_per_sm_t<U, F, true, false>(P.cost_smem, threads))    \
+                 : (mix ? cost_blocks_per_sm_t<U, F, false, true>(P.cost_smem, threads)     \
+                        : cost_blocks_per_sm_t<U, F, false, false>(P.cost_smem, threads))
+    if (P.unc) { if (P.foc) ML_OCC(true, true); else ML_OCC(true, false); }
+    else { if (P.foc) ML_OCC(false, true); else ML_OCC(false, false); }
+#undef ML_OCC
+    if (n < 1) n = (int)std::min<size_t>(228 * 1024 / (P.cost_smem + 1024), 2048 / threads);
+    return n < 1 ? 1 : n;
+}
+
 int make_plan(const ml_dims* d, const ml_params* p, FwdPlan* P) {
     int rc = validate_dims(d);
     if (rc) return rc;
@@ -209,8 +238,7 @@ int make_plan(const ml_dims* d, const ml_params* p, FwdPlan* P) {
     P->qrows_pad = (P->qrows + 31) / 32 * 32;
     P->cost_smem = cost_smem_bytes(P->qrows_pad);
     const int threads = 2 * P->qrows_pad + 32;
-    int per_sm = (int)std::min<size_t>(228 * 1024 / (P->cost_smem + 1024), 2048 / threads);
-    if (per_sm < 1) per_sm = 1;
+    int per_sm = cost_blocks_per_sm(*P, threads);
     // chunks per (image, query tile): the smallest count whose CTAs fill the
     // SMs in whole waves to >= 95 % (else the best found up to 4 waves)
     const int64_t base = (int64_t)P->L * P->B * P->nqt;
@@ -283,7 +311,7 @@ CostArgs cost_args(const FwdPlan& P, const ml_params* p, const float* ml, const 
 
 template <bool UNC, bool FOC, bool TMA>
 int launch_cost_t(const FwdPlan& P, const CUtensorMap& tm, const CostArgs& a, cudaStream_t st) {
-    auto k = cost_partial_kernel<UNC, FOC, TMA>;
+    auto k = P.s > 1 ? cost_partial_kernel<UNC, FOC, TMA, true> : cost_partial_kernel<UNC, FOC, TMA, false>;
     cudaError_t e = ensure_smem(k, P.cost_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cost_partial_kernel attributes");
     dim3 grid(P.nchunk, P.nqt, P.L * P.B);

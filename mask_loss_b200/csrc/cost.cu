@@ -134,8 +134,9 @@ __device__ __noinline__ void mixed_cell(const int64_t* targets, int W, int Ht, i
 //   UNC   entropy weights on (uncertainty_gamma != 0)
 //   FOC   focal gamma/alpha on the mask BCE
 //   TMA   logits rows are 16-byte strided so the bulk-tensor path is legal
+//   MIX   cells cover several target pixels (s > 1), so mixed cells occur
 // ---------------------------------------------------------------------------
-template <bool UNC, bool FOC, bool TMA>
+template <bool UNC, bool FOC, bool TMA, bool MIX>
 __global__ void __launch_bounds__(kCostThreads, 2)
 cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     constexpr int NACC = UNC ? 3 : 2;
@@ -273,14 +274,14 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
         }
     };
     auto element = [&](float x, int cell, auto mix_tag) {
-        constexpr bool MIX = decltype(mix_tag)::value;
+        constexpr bool MIXED_CELL = decltype(mix_tag)::value;
         if (FAST) {
             const Fast f = fast_elem(x);
             prod *= f.d;
             trow[0] += x;
             tabs += fabsf(x);
             trow[1] += f.p;
-            if (MIX && qvalid)
+            if (MIXED_CELL && qvalid)
                 mixed_cell<UNC>(a.targets, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, -x, f.p, 1.0f);
         } else {
             const Elem e = elem(x);
@@ -296,7 +297,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
             racc[0] = fmaf(m, dl, racc[0]);
             racc[1] = fmaf(m, w * e.p, racc[1]);
             if (UNC) racc[2] = fmaf(m, w, racc[2]);
-            if (MIX && qvalid)
+            if (MIXED_CELL && qvalid)
                 mixed_cell<UNC>(a.targets, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, dl, w * e.p, w);
         }
     };
@@ -313,6 +314,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
         const int prev = __shfl_up_sync(0xffffffffu, my_code, 1);
         const bool starts = lane < nv && (my_code == kMixed || my_code != (lane == 0 ? cur : prev));
         const uint32_t bnd = __ballot_sync(0xffffffffu, starts);
+        const uint32_t mixb = (FAST && MIX) ? __ballot_sync(0xffffffffu, my_code == kMixed) : 0u;
         const float* rowp = xs + (st * 2 + h) * box_floats + t * KBOX;
 #pragma unroll
         for (int i = 0; i < NROW; ++i) trow[i] = 0.0f;
@@ -327,6 +329,27 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                 if (b4 == 0u) {
 #pragma unroll
                     for (int u = 0; u < 4; ++u) element(xv[u], cell0 + h * KBOX + 4 * c + u, kNo);
+                } else if (FAST && (!MIX || ((mixb >> (4 * c)) & 0xFu) == 0u)) {
+                    // run starts but no mixed cell: the four elements first,
+                    // then the run switches between the sums
+                    Fast f[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        f[u] = fast_elem(xv[u]);
+                        prod *= f[u].d;
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        if ((b4 >> u) & 1u) {
+                            close_run();
+                            flush();
+                            cur = __shfl_sync(0xffffffffu, my_code, 4 * c + u);
+                            m = cur >= 0 ? 1.0f : 0.0f;
+                        }
+                        trow[0] += xv[u];
+                        tabs += fabsf(xv[u]);
+                        trow[1] += f[u].p;
+                    }
                 } else {
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
@@ -337,7 +360,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                             m = cur >= 0 ? 1.0f : 0.0f;
                         }
                         // a mixed cell is always a one-cell run
-                        if (cur == kMixed) element(xv[u], cell0 + h * KBOX + 4 * c + u, kYes);
+                        if (MIX && cur == kMixed) element(xv[u], cell0 + h * KBOX + 4 * c + u, kYes);
                         else element(xv[u], cell0 + h * KBOX + 4 * c + u, kNo);
                     }
                 }
@@ -352,7 +375,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                     cur = __shfl_sync(0xffffffffu, my_code, k);
                     m = cur >= 0 ? 1.0f : 0.0f;
                 }
-                if (cur == kMixed) element(x, cell0 + h * KBOX + k, kYes);
+                if (MIX && cur == kMixed) element(x, cell0 + h * KBOX + k, kYes);
                 else element(x, cell0 + h * KBOX + k, kNo);
                 if (FAST) { trow[2] += lg2_approx(prod); prod = 1.0f; }
             }
@@ -543,14 +566,22 @@ __global__ void __launch_bounds__(256) cost_pairs_kernel(CostArgs a) {
     if (a.rawI) { a.rawI[o] = acc[1]; a.rawT[o] = T; }
 }
 
-template __global__ void cost_partial_kernel<false, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<false, false, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, false, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<false, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<false, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, false, false>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, false, false>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, false, false>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, false, false>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
 template __global__ void cost_rows_kernel<false, false>(CostArgs);
 template __global__ void cost_rows_kernel<false, true>(CostArgs);
 template __global__ void cost_rows_kernel<true, false>(CostArgs);

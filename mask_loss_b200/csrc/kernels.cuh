@@ -11,7 +11,7 @@ namespace mlb {
 
 constexpr int KBOX = 32;          // cells per TMA box row (128 bytes, one swizzle span)
 constexpr int KC = 2 * KBOX;      // cells per pipeline tile (two boxes)
-constexpr int kStages = 3;        // TMA pipeline depth
+constexpr int kStages = 2;        // TMA pipeline depth (2 stages: 3 CTAs per SM)
 constexpr int kFlushTiles = 8;    // longest register run (tiles) before a flush
 constexpr int kCostThreads = 288; // 256 consumers + 1 producer warp (upper bound)
 constexpr int kHistSmemMax = 8192;
@@ -52,7 +52,7 @@ __global__ void label_code_kernel(const int64_t* __restrict__ targets, int B, in
                                   int s, int gt_total, int bg, int32_t* __restrict__ codes,
                                   int32_t* __restrict__ totals);
 
-template <bool UNC, bool FOC, bool TMA>
+template <bool UNC, bool FOC, bool TMA, bool MIX>
 __global__ void cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a);
 
 template <bool UNC, bool FAST>
