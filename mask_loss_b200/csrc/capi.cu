@@ -412,16 +412,19 @@ int launch_match(const CT* costs, int64_t N, int64_t Q, int64_t G, double thr, i
     a.costs = costs; a.pred_to_gt = p2g; a.pred_round = prnd; a.status = status;
     a.Q = (int)Q; a.G = (int)G; a.inf_thresh = thr; a.topk = K; a.strategy = (int)strat;
     const size_t limit = 200 * 1024;
-    size_t smem = match_smem_bytes((int)Q, (int)G, sizeof(CT), true);
-    a.stage_cost = smem <= limit;
-    if (!a.stage_cost) smem = match_smem_bytes((int)Q, (int)G, sizeof(CT), false);
+    a.stage_cost = 2;
+    size_t smem = match_smem_bytes((int)Q, (int)G, sizeof(CT), a.stage_cost);
+    while (a.stage_cost > 0 && smem > limit)
+        smem = match_smem_bytes((int)Q, (int)G, sizeof(CT), --a.stage_cost);
     if (smem > 227 * 1024) return fail(ML_EUNSUPPORTED, "solver state does not fit shared memory");
+    // one thread per solver column (Q + 1 of them) up to 256, whole warps
+    const int threads = (int)std::min<int64_t>(kMatchMaxThreads, std::max<int64_t>(64, (Q + 1 + 31) / 32 * 32));
     auto k = match_kernel<CT>;
     cudaError_t e = ensure_smem(k, smem);
     if (e != cudaSuccess) return cuda_fail(e, "match_kernel attributes");
     {
         ProfScope prof(2, st);
-        k<<<(unsigned)N, kMatchThreads, smem, st>>>(a);
+        k<<<(unsigned)N, threads, smem, st>>>(a);
     }
     ML_CHECK_LAUNCH("match_kernel");
     return ML_OK;

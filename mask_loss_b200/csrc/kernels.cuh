@@ -15,7 +15,7 @@ constexpr int kStages = 2;        // TMA pipeline depth (2 stages: 3 CTAs per SM
 constexpr int kFlushTiles = 8;    // longest register run (tiles) before a flush
 constexpr int kCostThreads = 288; // 256 consumers + 1 producer warp (upper bound)
 constexpr int kHistSmemMax = 8192;
-constexpr int kMatchThreads = 128; // warp 0 solves; all warps stage and rank
+constexpr int kMatchMaxThreads = 256;  // match block: one thread per solver column up to 255
 constexpr int kQStat = 8;         // per-query: P, Wtot, um_mask, um_dice, um_cls, base, cls_row, -
 constexpr int kSaved = 4;
 constexpr int kSampleQ = 8;        // queries per thread in point_sample_kernel         // saved for backward: P, T, I, Wtot
@@ -75,13 +75,13 @@ struct MatchArgs {
     double inf_thresh;
     int64_t topk;
     int strategy;
-    int stage_cost;
+    int stage_cost;        // 0 none, 1 transposed slice, 2 also the solver's double copy
 };
 
 template <typename CT>
 __global__ void match_kernel(MatchArgs<CT> a);
 
-size_t match_smem_bytes(int Q, int G, size_t cost_elem, bool stage);
+size_t match_smem_bytes(int Q, int G, size_t cost_elem, int stage);
 
 }  // namespace mlb
 

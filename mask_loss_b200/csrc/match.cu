@@ -1,4 +1,4 @@
-// match.cu -- on-device assignment solver, one warp per (l,b) slice.
+// match.cu -- on-device assignment solver, one thread block per (l,b) slice.
 //
 // Replaces the host loop of src/cpu/matching.cpp:690-722 (D2H copy of each
 // cost slice, C++ solve on a host thread, H2D of the results).  Restates
@@ -8,12 +8,16 @@
 //   * the shortest-augmenting-path Hungarian keeps the reference's operation
 //     order in double precision (cur = (c - u[i0]) - v[j]; u += delta;
 //     v -= delta; minv -= delta) with explicit _rn intrinsics, no FMA;
-//   * the per-step argmin over columns is a warp-shuffle reduction on
-//     (value, index) with ties to the lower index, which equals the
-//     reference's sequential strict-< scan in increasing j;
+//   * the per-step argmin over columns takes the smallest value with ties to
+//     the lower index, which equals the reference's sequential strict-< scan
+//     in increasing j;
 //   * greedy scans keep the reference's first-minimum-in-valid-column-order.
-// The cost slice is staged transposed ([col][query], fp32 or fp64) in shared
-// memory when it fits, so the inner scan reads are conflict-free.
+// Up to 4 * blockDim.x - 1 prediction columns the Hungarian runs on the whole
+// block with its per-column state in registers (hungarian_blk): fp64 issue is
+// the limit of a Dijkstra step on this part, so the columns are spread over
+// every SM sub-partition.  Larger slices use warp 0 and shared memory.
+// The cost slice is staged transposed ([col][query]) in shared memory when it
+// fits, with a double copy already mapped through ok_cost/BIG for the solver.
 // Every loop is bounded by construction (at most n+1 Dijkstra steps per row);
 // a step that finds no finite delta sets *status and abandons the slice.
 #include "common.cuh"
@@ -133,93 +137,200 @@ __device__ bool hungarian(const CostView<CT>& C, const int* preds, int n, const 
 }
 
 
-// Register-resident variant of `hungarian` for n <= 32*NJ - 1 columns: lane
-// `lane` owns columns j = lane + 32k (k < NJ) and keeps v, minv and the used
-// flags in registers; u, p and way stay in shared memory (random access).
-// Same operation order and tie rule as `hungarian`, so results are identical.
-template <int NJ, typename CT>
-__device__ bool hungarian_reg(const CostView<CT>& C, const int* preds, int n, const int* cols, int M,
-                              double thr, double BIG, int* asg, SolverMem& m) {
-    const int lane = threadIdx.x & 31;
-    for (int k = lane; k < n; k += 32) asg[k] = -1;
-    __syncwarp();
-    if (M == 0 || n == 0 || n < M) return true;
-    for (int i = lane; i <= M; i += 32) m.u[i] = 0.0;
-    for (int j = lane; j <= n; j += 32) { m.p[j] = 0; m.way[j] = 0; }
-    double v[NJ];
+// Order-preserving 64-bit key of a double (never NaN here: ok_cost maps NaN
+// to BIG); -0 and +0 get the same key, as they compare equal.
+ML_INLINE uint64_t order_key(double v) {
+    const uint64_t b = (uint64_t)__double_as_longlong(v + 0.0);  // -0 -> +0
+    return (b >> 63) ? ~b : (b | 0x8000000000000000ull);
+}
+
+ML_INLINE double from_key(uint64_t k) {
+    return __longlong_as_double((long long)((k >> 63) ? (k & 0x7fffffffffffffffull) : ~k));
+}
+
+template <int NJ, typename T>
+ML_INLINE T pick(const T (&a)[NJ], int k) {
+    T r = a[0];
 #pragma unroll
-    for (int k = 0; k < NJ; ++k) v[k] = 0.0;
-    __syncwarp();
+    for (int kk = 1; kk < NJ; ++kk)
+        if (k == kk) r = a[kk];
+    return r;
+}
+
+// Cross-warp state of the block solver.
+struct BlkShared {
+    uint32_t khi[kMatchMaxThreads / 32], klo[kMatchMaxThreads / 32];
+    int kj[kMatchMaxThreads / 32];
+    int i0;      // p[j0] of the column chosen last
+    double u0;   // u[p[j0]]
+    int flag;
+};
+
+// Block-wide variant of `hungarian` for n + 1 <= NJ * blockDim.x columns:
+// thread t owns columns j = t + blockDim.x * k and keeps, per column, its
+// prediction row, v, minv, way, p (row matched to the column) and the
+// potential u of that row in registers.  Every warp of the block scans its
+// columns in parallel (one fp64 pipe per SM sub-partition); the argmin is a
+// warp redux.sync on an order-preserving key followed by a fixed-order pick
+// over the warps' winners, so the result is the smallest value with ties to
+// the lower column index -- the reference's sequential strict-< scan.  u[p[j]]
+// of the reference is uc[j] here: the same operations in the same order,
+// moved along the augmenting path together with p.  `cd`, when set, is the
+// transposed slice already mapped through ok_cost/BIG in double.
+template <int NJ, typename CT>
+__device__ bool hungarian_blk(const CostView<CT>& C, const double* cd, const int* preds, int n,
+                              const int* cols, int M, double thr, double BIG, int* asg,
+                              SolverMem& m, BlkShared& sh) {
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
+    for (int k = tid; k < n; k += nthr) asg[k] = -1;
+    __syncthreads();
+    if (M == 0 || n == 0 || n < M) return true;
+    int pq[NJ], pc[NJ], wy[NJ];
+    double v[NJ], uc[NJ];
+#pragma unroll
+    for (int k = 0; k < NJ; ++k) {
+        const int j = tid + nthr * k;
+        pq[k] = (j >= 1 && j <= n) ? preds[j - 1] : 0;
+        pc[k] = 0;
+        wy[k] = 0;
+        v[k] = 0.0;
+        uc[k] = 0.0;
+    }
+    const int Qs = C.Q;
     for (int i = 1; i <= M; ++i) {
-        if (lane == 0) m.p[0] = i;
+        if (tid == 0) {  // column 0 holds the entering row; u[i] is still 0
+            pc[0] = i;
+            uc[0] = 0.0;
+            sh.i0 = i;
+            sh.u0 = 0.0;
+        }
         double minv[NJ];
 #pragma unroll
         for (int k = 0; k < NJ; ++k) minv[k] = kInf;
         uint32_t used = 0;
-        __syncwarp();
         int j0 = 0;
         int steps = 0;
-        do {
-            if ((j0 & 31) == lane) used |= 1u << (j0 >> 5);
-            const int i0 = m.p[j0];
+        __syncthreads();
+        while (true) {
+            if (j0 % nthr == tid) used |= 1u << (j0 / nthr);
+            const int i0 = sh.i0;
+            const double ui0 = sh.u0;
             const int col = cols[i0 - 1];
-            const double ui0 = m.u[i0];
+            double cij[NJ];
+#pragma unroll
+            for (int k = 0; k < NJ; ++k) {
+                const int j = tid + nthr * k;
+                if (j >= 1 && j <= n) {
+                    if (cd) {
+                        cij[k] = cd[col * Qs + pq[k]];
+                    } else {
+                        const double raw = C.at(pq[k], col);
+                        cij[k] = ok_cost(raw, thr) ? raw : BIG;
+                    }
+                } else {
+                    cij[k] = 0.0;
+                }
+            }
             double best = kInf;
             int bj = 0x7fffffff;
 #pragma unroll
             for (int k = 0; k < NJ; ++k) {
-                const int j = lane + 32 * k;
+                const int j = tid + nthr * k;
                 if (j < 1 || j > n || ((used >> k) & 1u)) continue;
-                const double raw = C.at(preds[j - 1], col);
-                const double cij = ok_cost(raw, thr) ? raw : BIG;
-                const double cur = __dsub_rn(__dsub_rn(cij, ui0), v[k]);
-                if (cur < minv[k]) { minv[k] = cur; m.way[j] = j0; }
+                const double cur = __dsub_rn(__dsub_rn(cij[k], ui0), v[k]);
+                if (cur < minv[k]) { minv[k] = cur; wy[k] = j0; }
                 if (minv[k] < best) { best = minv[k]; bj = j; }
             }
-            warp_argmin(best, bj);
-            if (!isfinite(best) || bj > n) return false;
+            {
+                const uint64_t key = order_key(best);
+                const uint32_t hi = (uint32_t)(key >> 32), lo = (uint32_t)key;
+                const uint32_t mh = __reduce_min_sync(0xffffffffu, hi);
+                const uint32_t ml = __reduce_min_sync(0xffffffffu, hi == mh ? lo : 0xffffffffu);
+                const uint32_t mj = __reduce_min_sync(0xffffffffu,
+                                                      (hi == mh && lo == ml) ? (uint32_t)bj : 0x7fffffffu);
+                if (lane == 0) { sh.khi[warp] = mh; sh.klo[warp] = ml; sh.kj[warp] = (int)mj; }
+            }
+            __syncthreads();
+            uint32_t bh = sh.khi[0], bl = sh.klo[0];
+            bj = sh.kj[0];
+            for (int w = 1; w < nw; ++w) {
+                const uint32_t h = sh.khi[w], l = sh.klo[w];
+                const int jj = sh.kj[w];
+                if (h < bh || (h == bh && (l < bl || (l == bl && jj < bj)))) { bh = h; bl = l; bj = jj; }
+            }
+            best = from_key(((uint64_t)bh << 32) | bl);
+            if (!isfinite(best) || bj > n) return false;  // uniform across the block
             const double delta = best;
 #pragma unroll
             for (int k = 0; k < NJ; ++k) {
-                const int j = lane + 32 * k;
+                const int j = tid + nthr * k;
                 if (j > n) continue;
                 if ((used >> k) & 1u) {
-                    const int r = m.p[j];
-                    m.u[r] = __dadd_rn(m.u[r], delta);
+                    uc[k] = __dadd_rn(uc[k], delta);
                     v[k] = __dsub_rn(v[k], delta);
                 } else {
                     minv[k] = __dsub_rn(minv[k], delta);
                 }
             }
-            __syncwarp();
             j0 = bj;
+            if (j0 % nthr == tid) {
+                const int k = j0 / nthr;
+                sh.i0 = pick(pc, k);
+                sh.u0 = pick(uc, k);
+            }
+            __syncthreads();
             if (++steps > n + 1) return false;
-        } while (m.p[j0] != 0);
-        if (lane == 0) {
+            if (sh.i0 == 0) break;  // free column reached
+        }
+        // augment along way[] (thread 0 walks the path in shared memory)
+#pragma unroll
+        for (int k = 0; k < NJ; ++k) {
+            const int j = tid + nthr * k;
+            if (j <= n) { m.way[j] = wy[k]; m.p[j] = pc[k]; m.minv[j] = uc[k]; }
+        }
+        __syncthreads();
+        if (tid == 0) {
             int jj = j0;
             int guard = 0;
             do {
                 const int j1 = m.way[jj];
                 m.p[jj] = m.p[j1];
+                m.minv[jj] = m.minv[j1];
                 jj = j1;
             } while (jj != 0 && ++guard <= n + 1);
         }
-        __syncwarp();
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < NJ; ++k) {
+            const int j = tid + nthr * k;
+            if (j <= n) { pc[k] = m.p[j]; uc[k] = m.minv[j]; }
+        }
     }
-    for (int j = 1 + lane; j <= n; j += 32)
-        if (m.p[j] > 0) asg[j - 1] = m.p[j] - 1;
-    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < NJ; ++k) {
+        const int j = tid + nthr * k;
+        if (j >= 1 && j <= n && pc[k] > 0) asg[j - 1] = pc[k] - 1;
+    }
+    __syncthreads();
     return true;
 }
 
+// Called by every thread of the block; returns the same value everywhere.
 template <typename CT>
-__device__ bool solve(const CostView<CT>& C, const int* preds, int n, const int* cols, int M,
-                      double thr, double BIG, int* asg, SolverMem& m) {
-    if (n < 32) return hungarian_reg<1>(C, preds, n, cols, M, thr, BIG, asg, m);
-    if (n < 64) return hungarian_reg<2>(C, preds, n, cols, M, thr, BIG, asg, m);
-    if (n < 128) return hungarian_reg<4>(C, preds, n, cols, M, thr, BIG, asg, m);
-    if (n < 256) return hungarian_reg<8>(C, preds, n, cols, M, thr, BIG, asg, m);
-    return hungarian(C, preds, n, cols, M, thr, BIG, asg, m);
+__device__ bool solve(const CostView<CT>& C, const double* cd, const int* preds, int n, const int* cols,
+                      int M, double thr, double BIG, int* asg, SolverMem& m, BlkShared& sh) {
+    const int nthr = blockDim.x;
+    if (n + 1 <= nthr) return hungarian_blk<1>(C, cd, preds, n, cols, M, thr, BIG, asg, m, sh);
+    if (n + 1 <= 2 * nthr) return hungarian_blk<2>(C, cd, preds, n, cols, M, thr, BIG, asg, m, sh);
+    if (n + 1 <= 4 * nthr) return hungarian_blk<4>(C, cd, preds, n, cols, M, thr, BIG, asg, m, sh);
+    bool r = true;
+    if (threadIdx.x < 32) r = hungarian(C, preds, n, cols, M, thr, BIG, asg, m);
+    if (threadIdx.x == 0) sh.flag = r ? 1 : 0;
+    __syncthreads();
+    r = sh.flag != 0;
+    __syncthreads();
+    return r;
 }
 
 // Greedy fill with capacities, src/cpu/matching.cpp:193-229.
@@ -269,18 +380,25 @@ ML_INLINE int warp_compact(int n, F flag, int* out, const int* in) {
 
 }  // namespace
 
-// One warp per slice.  Dynamic shared memory holds the solver state and,
-// when `stage_cost`, the transposed cost slice.
+// One block per slice; every strategy's control flow is block-uniform, the
+// Hungarian runs on all threads (hungarian_blk) and the compactions and the
+// greedy passes on warp 0.  Dynamic shared memory holds the solver state and,
+// by `stage_cost`: 1 the transposed cost slice, 2 also its ok_cost/BIG-mapped
+// copy in double for the solver.
 template <typename CT>
-__global__ void __launch_bounds__(kMatchThreads) match_kernel(MatchArgs<CT> a) {
+__global__ void __launch_bounds__(kMatchMaxThreads) match_kernel(MatchArgs<CT> a) {
     extern __shared__ __align__(16) unsigned char msh[];
+    __shared__ BlkShared sh;
+    __shared__ int sh_n, failed;
     const int slice = blockIdx.x;
     const int Q = a.Q, G = a.G;
-    const int lane = threadIdx.x & 31;
     const int tid = threadIdx.x, nthr = blockDim.x;
+    const int lane = tid & 31;
     const CT* cg = a.costs + (int64_t)slice * Q * G;
     int64_t* out_p = a.pred_to_gt + (int64_t)slice * Q;
     int64_t* out_r = a.pred_round + (int64_t)slice * Q;
+    const double thr = a.inf_thresh;
+    const double BIG = big_from(thr);
 
     unsigned char* cur = msh;
     auto take = [&](size_t bytes) {
@@ -303,65 +421,69 @@ __global__ void __launch_bounds__(kMatchThreads) match_kernel(MatchArgs<CT> a) {
     int* asg = reinterpret_cast<int*>(take(sizeof(int) * (Q + 1)));
     int* p2g = reinterpret_cast<int*>(take(sizeof(int) * (Q + 1)));
     CT* cs = nullptr;
-    if (a.stage_cost) {
-        cs = reinterpret_cast<CT*>(take(sizeof(CT) * (size_t)Q * G));
-#pragma unroll 4
-        for (int i = tid; i < Q * G; i += nthr) {
-            const int q = i / G, g = i - q * G;
-            cs[g * Q + q] = cg[i];
-        }
-    }
-    CostView<CT> C{cg, cs, Q, G};
-    const double thr = a.inf_thresh;
-    const int64_t K = a.topk;
-    __shared__ int failed;
+    double* cd = nullptr;
+    if (a.stage_cost >= 1) cs = reinterpret_cast<CT*>(take(sizeof(CT) * (size_t)Q * G));
+    if (a.stage_cost >= 2) cd = reinterpret_cast<double*>(take(sizeof(double) * (size_t)Q * G));
+    for (int g = tid; g < G; g += nthr) cap[g] = 0;  // valid-column flags first
     if (tid == 0) failed = 0;
     for (int q = tid; q < Q; q += nthr) p2g[q] = -1;
     __syncthreads();
-    if (threadIdx.x >= 32) goto rank;  // warp 0 runs the strategies
-    {
-
+    for (int i = tid; i < Q * G; i += nthr) {
+        const int q = i / G, g = i - q * G;
+        const CT c = cg[i];
+        const bool ok = ok_cost((double)c, thr);
+        if (cs) cs[g * Q + q] = c;
+        if (cd) cd[g * Q + q] = ok ? (double)c : BIG;
+        if (ok) cap[g] = 1;
+    }
+    __syncthreads();
+    CostView<CT> C{cg, cs, Q, G};
+    const int64_t K = a.topk;
     bool good = true;
     if (Q > 0 && G > 0 && K > 0) {
         // valid columns: any finite cost below the threshold
-        const int nv = warp_compact(G, [&](int g) {
-            for (int q = 0; q < Q; ++q)
-                if (ok_cost(C.at(q, g), thr)) return true;
-            return false;
-        }, valid, nullptr);
+        if (tid < 32) {
+            const int nv = warp_compact(G, [&](int g) { return cap[g] != 0; }, valid, nullptr);
+            if (lane == 0) sh_n = nv;
+        }
+        __syncthreads();
+        const int nv = sh_n;
         if (nv > 0) {
-            const double BIG = big_from(thr);
-            for (int t = lane; t < nv; t += 32) cap[valid[t]] = (int)(K < (int64_t)(1 << 30) ? K : (int64_t)(1 << 30));
-            for (int q = lane; q < Q; q += 32) preds[q] = q;
-            __syncwarp();
+            const int kc = (int)(K < (int64_t)(1 << 30) ? K : (int64_t)(1 << 30));
+            for (int t = tid; t < nv; t += nthr) cap[valid[t]] = kc;
+            for (int q = tid; q < Q; q += nthr) preds[q] = q;
+            __syncthreads();
             if (a.strategy == 0) {  // global, :239-286
-                int M = 0;
-                for (int64_t rep = 0; rep < K && M < Q; ++rep)
-                    for (int t = 0; t < nv && M < Q; ++t) {
-                        if (lane == 0) cols[M] = valid[t];
-                        ++M;
-                    }
-                __syncwarp();
-                good = solve(C, preds, Q, cols, M, thr, BIG, asg, m);
+                const int64_t kn = K * (int64_t)nv;
+                const int M = (int)(kn < (int64_t)Q ? kn : (int64_t)Q);
+                for (int t = tid; t < M; t += nthr) cols[t] = valid[t % nv];
+                __syncthreads();
+                good = solve(C, cd, preds, Q, cols, M, thr, BIG, asg, m, sh);
                 if (good)
-                    for (int q = lane; q < Q; q += 32)
+                    for (int q = tid; q < Q; q += nthr)
                         if (asg[q] >= 0) {
                             const int c = cols[asg[q]];
                             if (ok_cost(C.at(q, c), thr)) p2g[q] = c;
                         }
-                __syncwarp();
+                __syncthreads();
             } else if (a.strategy == 1) {  // round, :294-366
                 int nrem = Q;
                 int* pa = preds;
                 int* pb = preds2;
                 for (int64_t r = 0; r < K && good; ++r) {
-                    int M = warp_compact(nv, [&](int t) { return cap[valid[t]] > 0; }, cols, valid);
+                    if (tid < 32) {
+                        const int M = warp_compact(nv, [&](int t) { return cap[valid[t]] > 0; }, cols, valid);
+                        if (lane == 0) sh_n = M;
+                    }
+                    __syncthreads();
+                    int M = sh_n;
+                    __syncthreads();
                     if (M == 0 || nrem == 0) break;
                     if (M > nrem) M = nrem;
-                    good = solve(C, pa, nrem, cols, M, thr, BIG, asg, m);
+                    good = solve(C, cd, pa, nrem, cols, M, thr, BIG, asg, m, sh);
                     if (!good) break;
                     // assignments (distinct columns within a round)
-                    for (int k = lane; k < nrem; k += 32) {
+                    for (int k = tid; k < nrem; k += nthr) {
                         if (asg[k] >= 0) {
                             const int q = pa[k], c = cols[asg[k]];
                             if (ok_cost(C.at(q, c), thr)) {
@@ -370,21 +492,27 @@ __global__ void __launch_bounds__(kMatchThreads) match_kernel(MatchArgs<CT> a) {
                             }
                         }
                     }
-                    __syncwarp();
-                    const int nn = warp_compact(nrem, [&](int k) { return p2g[pa[k]] < 0; }, pb, pa);
+                    __syncthreads();
+                    if (tid < 32) {
+                        const int nn = warp_compact(nrem, [&](int k) { return p2g[pa[k]] < 0; }, pb, pa);
+                        if (lane == 0) sh_n = nn;
+                    }
+                    __syncthreads();
+                    nrem = sh_n;
+                    __syncthreads();
                     int* tmp = pa; pa = pb; pb = tmp;
-                    nrem = nn;
                     if (nrem == 0) break;
                 }
             } else if (a.strategy == 2) {  // greedy, :372-393
-                greedy(C, preds, Q, valid, nv, thr, cap, p2g);
+                if (tid < 32) greedy(C, preds, Q, valid, nv, thr, cap, p2g);
+                __syncthreads();
             } else {  // pseudo-greedy, :400-463
                 const int M = nv < Q ? nv : Q;
-                for (int t = lane; t < M; t += 32) cols[t] = valid[t];
-                __syncwarp();
-                good = solve(C, preds, Q, cols, M, thr, BIG, asg, m);
+                for (int t = tid; t < M; t += nthr) cols[t] = valid[t];
+                __syncthreads();
+                good = solve(C, cd, preds, Q, cols, M, thr, BIG, asg, m, sh);
                 if (good) {
-                    for (int q = lane; q < Q; q += 32)
+                    for (int q = tid; q < Q; q += nthr)
                         if (asg[q] >= 0) {
                             const int c = cols[asg[q]];
                             if (ok_cost(C.at(q, c), thr)) {
@@ -392,39 +520,42 @@ __global__ void __launch_bounds__(kMatchThreads) match_kernel(MatchArgs<CT> a) {
                                 if (cap[c] > 0) cap[c] -= 1;
                             }
                         }
-                    __syncwarp();
-                    const int nr = warp_compact(Q, [&](int q) { return p2g[q] < 0; }, preds2, nullptr);
-                    if (nr > 0) greedy(C, preds2, nr, valid, nv, thr, cap, p2g);
+                    __syncthreads();
+                    if (tid < 32) {
+                        const int nr = warp_compact(Q, [&](int q) { return p2g[q] < 0; }, preds2, nullptr);
+                        if (nr > 0) greedy(C, preds2, nr, valid, nv, thr, cap, p2g);
+                    }
+                    __syncthreads();
                 }
             }
         }
     }
-    __syncwarp();
-    if (!good && lane == 0) {
+    if (!good && tid == 0) {
         atomicOr(a.status, 1);
         failed = 1;
     }
-    }
-rank:
     __syncthreads();
     if (failed) {
         for (int q = tid; q < Q; q += nthr) { out_p[q] = -1; out_r[q] = -1; }
         return;
     }
-    // rank per GT by (cost, q), src/cpu/matching.cpp:538-565
+    // rank per GT by (cost, q), src/cpu/matching.cpp:538-565.  With K = 1
+    // every strategy gives a GT at most one prediction, so each rank is 0.
     for (int q = tid; q < Q; q += nthr) {
         const int g = p2g[q];
         int64_t pr = -1;
         int64_t pg = -1;
         if (g >= 0 && ok_cost(C.at(q, g), thr)) {
             pg = g;
-            const double c = C.at(q, g);
             int64_t rank = 0;
-            for (int q2 = 0; q2 < Q; ++q2) {
-                if (q2 == q || p2g[q2] != g) continue;
-                const double c2 = C.at(q2, g);
-                if (!ok_cost(c2, thr)) continue;
-                if (c2 < c || (c2 == c && q2 < q)) ++rank;
+            if (K > 1) {
+                const double c = C.at(q, g);
+                for (int q2 = 0; q2 < Q; ++q2) {
+                    if (q2 == q || p2g[q2] != g) continue;
+                    const double c2 = C.at(q2, g);
+                    if (!ok_cost(c2, thr)) continue;
+                    if (c2 < c || (c2 == c && q2 < q)) ++rank;
+                }
             }
             if (rank < K) pr = rank;
         }
@@ -436,12 +567,13 @@ rank:
 template __global__ void match_kernel<float>(MatchArgs<float>);
 template __global__ void match_kernel<double>(MatchArgs<double>);
 
-size_t match_smem_bytes(int Q, int G, size_t cost_elem, bool stage) {
+size_t match_smem_bytes(int Q, int G, size_t cost_elem, int stage) {
     auto r = [](size_t b) { return (b + 15) & ~size_t(15); };
     size_t s = 3 * r(sizeof(double) * (Q + 1)) + 3 * r(sizeof(int) * (Q + 1)) +
                2 * r(sizeof(int) * (G + 1)) + 4 * r(sizeof(int) * (Q + 1)) +
                r(sizeof(int) * ((Q > G ? Q : G) + 1));
-    if (stage) s += r(cost_elem * (size_t)Q * G);
+    if (stage >= 1) s += r(cost_elem * (size_t)Q * G);
+    if (stage >= 2) s += r(sizeof(double) * (size_t)Q * G);
     return s;
 }
 

@@ -125,7 +125,7 @@ def test_solver_reference_fixtures_bit_exact():
 @pytest.mark.parametrize("strategy", [0, 1, 2, 3])
 def test_solver_random_bit_exact(strategy):
     rng = np.random.default_rng(11 + strategy)
-    for Q, G in [(100, 15), (200, 200), (64, 100), (37, 5), (300, 120)]:
+    for Q, G in [(100, 15), (200, 200), (64, 100), (37, 5), (300, 120), (1100, 12)]:
         for K in (1, 2, 3):
             c = rng.random((3, Q, G))
             c[rng.random(c.shape) < 0.05] = np.inf
@@ -137,6 +137,24 @@ def test_solver_random_bit_exact(strategy):
                 ea, er = O.assign_slice(c[i], 1e30, K, strategy)
                 np.testing.assert_array_equal(a[i].cpu().numpy(), ea, err_msg=f"{Q}x{G} K={K}")
                 np.testing.assert_array_equal(r[i].cpu().numpy(), er, err_msg=f"{Q}x{G} K={K}")
+    ops.check_status(block=True)
+
+
+def test_solver_heavy_ties_signed_zero_bit_exact():
+    # costs from a 4-value set (most Dijkstra steps meet equal minima), some
+    # of them -0.0 and negative, every strategy, register and shared paths
+    rng = np.random.default_rng(23)
+    for Q, G in [(20, 7), (50, 30), (100, 21), (127, 60), (260, 40)]:
+        c = rng.integers(-1, 3, (2, Q, G)).astype(np.float64) * 0.25
+        c[c == 0.0] = np.where(rng.random(int((c == 0.0).sum())) < 0.5, -0.0, 0.0)
+        cd = torch.from_numpy(c).to(DEV)
+        for strategy in range(4):
+            for K in (1, 2):
+                a, r = ops.match_costs(cd, 1e30, K, strategy)
+                for i in range(2):
+                    ea, er = O.assign_slice(c[i], 1e30, K, strategy)
+                    np.testing.assert_array_equal(a[i].cpu().numpy(), ea, err_msg=f"{Q}x{G} s={strategy} K={K}")
+                    np.testing.assert_array_equal(r[i].cpu().numpy(), er, err_msg=f"{Q}x{G} s={strategy} K={K}")
     ops.check_status(block=True)
 
 
