@@ -157,26 +157,33 @@ ML_INLINE T pick(const T (&a)[NJ], int k) {
     return r;
 }
 
-// Cross-warp state of the block solver.
+// One warp's best column of a Dijkstra step, with what the next step needs
+// if it wins: p[j], u[p[j]] and cols[p[j] - 1].  Double-buffered by step
+// parity, so a step needs one block barrier.
+struct alignas(16) BlkCand {
+    uint32_t hi, lo;  // order_key of the value
+    int j;            // column (0x7fffffff: none)
+    int i0;           // p[j]
+    double u0;        // u[p[j]]
+    int col;          // cols[p[j] - 1] (p[j] > 0)
+    int pad;
+};
+
 struct BlkShared {
-    uint32_t khi[kMatchMaxThreads / 32], klo[kMatchMaxThreads / 32];
-    int kj[kMatchMaxThreads / 32];
-    int i0;      // p[j0] of the column chosen last
-    double u0;   // u[p[j0]]
+    BlkCand cand[2][kMatchMaxThreads / 32];
     int flag;
 };
 
 // Block-wide variant of `hungarian` for n + 1 <= NJ * blockDim.x columns:
 // thread t owns columns j = t + blockDim.x * k and keeps, per column, its
-// prediction row, v, minv, way, p (row matched to the column) and the
-// potential u of that row in registers.  Every warp of the block scans its
-// columns in parallel (one fp64 pipe per SM sub-partition); the argmin is a
-// warp redux.sync on an order-preserving key followed by a fixed-order pick
-// over the warps' winners, so the result is the smallest value with ties to
-// the lower column index -- the reference's sequential strict-< scan.  u[p[j]]
-// of the reference is uc[j] here: the same operations in the same order,
-// moved along the augmenting path together with p.  `cd`, when set, is the
-// transposed slice already mapped through ok_cost/BIG in double.
+// prediction row, v, minv, way, p (row matched to the column), the cost
+// column of that row and its potential u in registers.  Every warp scans its
+// columns in parallel; the argmin is a warp redux.sync on an order-preserving
+// key, then a fixed-order pick over the warps' candidates, so the result is
+// the smallest value with ties to the lower column index -- the reference's
+// sequential strict-< scan.  u[p[j]] of the reference is uc[j] here: the same
+// operations in the same order, moved along the augmenting path with p.
+// `cd`, when set, is the transposed slice already mapped through ok_cost/BIG.
 template <int NJ, typename CT>
 __device__ bool hungarian_blk(const CostView<CT>& C, const double* cd, const int* preds, int n,
                               const int* cols, int M, double thr, double BIG, int* asg,
@@ -186,7 +193,7 @@ __device__ bool hungarian_blk(const CostView<CT>& C, const double* cd, const int
     for (int k = tid; k < n; k += nthr) asg[k] = -1;
     __syncthreads();
     if (M == 0 || n == 0 || n < M) return true;
-    int pq[NJ], pc[NJ], wy[NJ];
+    int pq[NJ], pc[NJ], wy[NJ], cc[NJ];
     double v[NJ], uc[NJ];
 #pragma unroll
     for (int k = 0; k < NJ; ++k) {
@@ -194,29 +201,25 @@ __device__ bool hungarian_blk(const CostView<CT>& C, const double* cd, const int
         pq[k] = (j >= 1 && j <= n) ? preds[j - 1] : 0;
         pc[k] = 0;
         wy[k] = 0;
+        cc[k] = 0;
         v[k] = 0.0;
         uc[k] = 0.0;
     }
     const int Qs = C.Q;
+    int par = 0;
     for (int i = 1; i <= M; ++i) {
-        if (tid == 0) {  // column 0 holds the entering row; u[i] is still 0
-            pc[0] = i;
-            uc[0] = 0.0;
-            sh.i0 = i;
-            sh.u0 = 0.0;
-        }
+        // column 0 holds the entering row i; u[i] is still 0
+        int col = cols[i - 1];
+        double ui0 = 0.0;
+        if (tid == 0) { pc[0] = i; uc[0] = 0.0; cc[0] = col; }
         double minv[NJ];
 #pragma unroll
         for (int k = 0; k < NJ; ++k) minv[k] = kInf;
         uint32_t used = 0;
         int j0 = 0;
         int steps = 0;
-        __syncthreads();
         while (true) {
             if (j0 % nthr == tid) used |= 1u << (j0 / nthr);
-            const int i0 = sh.i0;
-            const double ui0 = sh.u0;
-            const int col = cols[i0 - 1];
             double cij[NJ];
 #pragma unroll
             for (int k = 0; k < NJ; ++k) {
@@ -247,20 +250,26 @@ __device__ bool hungarian_blk(const CostView<CT>& C, const double* cd, const int
                 const uint32_t hi = (uint32_t)(key >> 32), lo = (uint32_t)key;
                 const uint32_t mh = __reduce_min_sync(0xffffffffu, hi);
                 const uint32_t ml = __reduce_min_sync(0xffffffffu, hi == mh ? lo : 0xffffffffu);
-                const uint32_t mj = __reduce_min_sync(0xffffffffu,
-                                                      (hi == mh && lo == ml) ? (uint32_t)bj : 0x7fffffffu);
-                if (lane == 0) { sh.khi[warp] = mh; sh.klo[warp] = ml; sh.kj[warp] = (int)mj; }
+                const bool tie = hi == mh && lo == ml;
+                const uint32_t mj = __reduce_min_sync(0xffffffffu, tie ? (uint32_t)bj : 0x7fffffffu);
+                const uint32_t wl = __ballot_sync(0xffffffffu, tie && (uint32_t)bj == mj);
+                if (lane == __ffs(wl) - 1) {
+                    BlkCand c;
+                    c.hi = mh; c.lo = ml; c.j = (int)mj;
+                    const int k = bj <= n ? bj / nthr : 0;
+                    c.i0 = pick(pc, k); c.u0 = pick(uc, k); c.col = pick(cc, k); c.pad = 0;
+                    sh.cand[par][warp] = c;
+                }
             }
             __syncthreads();
-            uint32_t bh = sh.khi[0], bl = sh.klo[0];
-            bj = sh.kj[0];
-            for (int w = 1; w < nw; ++w) {
-                const uint32_t h = sh.khi[w], l = sh.klo[w];
-                const int jj = sh.kj[w];
-                if (h < bh || (h == bh && (l < bl || (l == bl && jj < bj)))) { bh = h; bl = l; bj = jj; }
+            BlkCand w = sh.cand[par][0];
+            for (int x = 1; x < nw; ++x) {
+                const BlkCand c = sh.cand[par][x];
+                if (c.hi < w.hi || (c.hi == w.hi && (c.lo < w.lo || (c.lo == w.lo && c.j < w.j)))) w = c;
             }
-            best = from_key(((uint64_t)bh << 32) | bl);
-            if (!isfinite(best) || bj > n) return false;  // uniform across the block
+            par ^= 1;
+            best = from_key(((uint64_t)w.hi << 32) | w.lo);
+            if (!isfinite(best) || w.j > n) return false;  // uniform across the block
             const double delta = best;
 #pragma unroll
             for (int k = 0; k < NJ; ++k) {
@@ -273,21 +282,17 @@ __device__ bool hungarian_blk(const CostView<CT>& C, const double* cd, const int
                     minv[k] = __dsub_rn(minv[k], delta);
                 }
             }
-            j0 = bj;
-            if (j0 % nthr == tid) {
-                const int k = j0 / nthr;
-                sh.i0 = pick(pc, k);
-                sh.u0 = pick(uc, k);
-            }
-            __syncthreads();
+            j0 = w.j;
             if (++steps > n + 1) return false;
-            if (sh.i0 == 0) break;  // free column reached
+            if (w.i0 == 0) break;  // free column reached
+            col = w.col;           // the chosen column is unused: its u is unchanged
+            ui0 = w.u0;
         }
         // augment along way[] (thread 0 walks the path in shared memory)
 #pragma unroll
         for (int k = 0; k < NJ; ++k) {
             const int j = tid + nthr * k;
-            if (j <= n) { m.way[j] = wy[k]; m.p[j] = pc[k]; m.minv[j] = uc[k]; }
+            if (j <= n) { m.way[j] = wy[k]; m.p[j] = pc[k]; m.minv[j] = uc[k]; m.used[j] = cc[k]; }
         }
         __syncthreads();
         if (tid == 0) {
@@ -297,6 +302,7 @@ __device__ bool hungarian_blk(const CostView<CT>& C, const double* cd, const int
                 const int j1 = m.way[jj];
                 m.p[jj] = m.p[j1];
                 m.minv[jj] = m.minv[j1];
+                m.used[jj] = m.used[j1];
                 jj = j1;
             } while (jj != 0 && ++guard <= n + 1);
         }
@@ -304,8 +310,9 @@ __device__ bool hungarian_blk(const CostView<CT>& C, const double* cd, const int
 #pragma unroll
         for (int k = 0; k < NJ; ++k) {
             const int j = tid + nthr * k;
-            if (j <= n) { pc[k] = m.p[j]; uc[k] = m.minv[j]; }
+            if (j <= n) { pc[k] = m.p[j]; uc[k] = m.minv[j]; cc[k] = m.used[j]; }
         }
+        __syncthreads();
     }
 #pragma unroll
     for (int k = 0; k < NJ; ++k) {
