@@ -353,9 +353,7 @@ int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaS
     int rc = ML_OK;
     const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
     if (LBQ == 0 || P.gout == 0) return ML_OK;
-    const size_t part_bytes = sizeof(float) * (size_t)P.L * P.B * P.nqt * P.nchunk * 2 * P.part_stride;
-    cudaError_t e = cudaMemsetAsync(a.part, 0, part_bytes, st);
-    if (e != cudaSuccess) return cuda_fail(e, "memset partials");
+    // the cost kernel clears its own partial slots (no memset)
     CUtensorMap tm;
     memset(&tm, 0, sizeof(tm));
     bool tma = P.tma_ok && (reinterpret_cast<uintptr_t>(mask_logits) % 16 == 0);
@@ -388,7 +386,7 @@ int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaS
     else if (P.foc) cost_rows_kernel<false, false><<<rb, 256, 0, st>>>(a);
     else cost_rows_kernel<false, true><<<rb, 256, 0, st>>>(a);
     ML_CHECK_LAUNCH("cost_rows_kernel");
-    dim3 pg((unsigned)((P.qrows * P.gout + 255) / 256), P.nqt, P.L * P.B);
+    dim3 pg((unsigned)((P.qrows * P.gout + 31) / 32), P.nqt, P.L * P.B);
     if (P.unc) cost_pairs_kernel<true><<<pg, 256, 0, st>>>(a);
     else cost_pairs_kernel<false><<<pg, 256, 0, st>>>(a);
     ML_CHECK_LAUNCH("cost_pairs_kernel");

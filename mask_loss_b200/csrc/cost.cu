@@ -56,21 +56,40 @@ label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int 
     const int64_t* tb = targets + (int64_t)b * HW * s * s;
     int32_t* cb = codes ? codes + (int64_t)b * HW : nullptr;
     int32_t* tot = totals + (int64_t)b * gt_total;
-    for (int cell = blockIdx.x * blockDim.x + threadIdx.x; cell < HW; cell += gridDim.x * blockDim.x) {
-        int c = -3;
-        const int ci = cell / W, cj = cell - ci * W;
-        const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
-        for (int dy = 0; dy < s; ++dy)
-            for (int dx = 0; dx < s; ++dx) {
-                const int64_t lab = r0[(int64_t)dy * Wt + dx];
-                if (lab >= 0 && lab < gt_total) {
-                    if (use_sh) atomicAdd(&hist[lab], 1);
-                    else atomicAdd(&tot[lab], 1);
+    int32_t* hc = use_sh ? hist : tot;
+    // every thread of the block runs the same number of iterations, so the
+    // warp-aggregated count below sees the whole warp
+    for (int base = blockIdx.x * blockDim.x; base < HW; base += gridDim.x * blockDim.x) {
+        const int cell = base + threadIdx.x;
+        int run = -1, rc = 0;  // this cell's last run of one in-range label
+        if (cell < HW) {
+            int c = -3;
+            const int ci = cell / W, cj = cell - ci * W;
+            const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
+            for (int dy = 0; dy < s; ++dy)
+                for (int dx = 0; dx < s; ++dx) {
+                    const int64_t lab = r0[(int64_t)dy * Wt + dx];
+                    const int key = (lab >= 0 && lab < gt_total) ? (int)lab : -1;
+                    if (key != run) {
+                        if (run >= 0) atomicAdd(&hc[run], rc);
+                        run = key;
+                        rc = 0;
+                    }
+                    ++rc;
+                    const int col = label_to_col(lab, gt_total, bg);
+                    c = (c == -3 || c == col) ? col : kMixed;
                 }
-                const int col = label_to_col(lab, gt_total, bg);
-                c = (c == -3 || c == col) ? col : kMixed;
+            if (cb) cb[cell] = c;
+        }
+        // one pixel per cell: lanes on the same label add with one atomic
+        const unsigned peers = __match_any_sync(0xffffffffu, run);
+        if (run >= 0) {
+            if (s == 1) {
+                if ((int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hc[run], __popc(peers));
+            } else {
+                atomicAdd(&hc[run], rc);
             }
-        if (cb) cb[cell] = c;
+        }
     }
     __syncthreads();
     if (use_sh)
@@ -236,6 +255,9 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     const float N2 = (float)(a.s * a.s);
     const Focal foc = make_focal(a.mask_gamma, a.mask_alpha);
 
+    // this thread is the only writer of column t of its slot: clear it here
+    // (program order puts these stores before its red.adds)
+    for (int x = 0; x < NACC * G; ++x) part[(int64_t)x * QP + t] = 0.0f;
     float racc[NACC];
 #pragma unroll
     for (int i = 0; i < NACC; ++i) racc[i] = 0.0f;
@@ -493,39 +515,49 @@ __global__ void __launch_bounds__(256) cost_rows_kernel(CostArgs a) {
 template <bool UNC>
 __global__ void __launch_bounds__(256) cost_pairs_kernel(CostArgs a) {
     constexpr int NACC = UNC ? 3 : 2;
+    __shared__ float red[8][NACC][32];
     const int qt = blockIdx.y, lb = blockIdx.z, b = lb % a.B;
     const int nq = min(a.qrows, a.Q - qt * a.qrows);
     const int G = a.gout;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= nq * G) return;
-    const int g = i / nq, t = i - g * nq;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // 32 consecutive (g, t) pairs per block (lane), the 8 warps split the
+    // chunk slots; the fixed-order combine keeps the sums deterministic
+    const int i = blockIdx.x * 32 + lane;
+    const bool pv = i < nq * G;
+    const int g = pv ? i / nq : 0, t = pv ? i - g * nq : 0;
     const int nslot = 2 * a.nchunk;
     const float* p = a.part + (((int64_t)lb * a.nqt + qt) * nslot) * (int64_t)a.part_stride +
                      (int64_t)g * a.qrows_pad + t;
-    // four interleaved partial sums (fixed association -> deterministic),
-    // so the slot loads are independent and overlap
-    float acc4[4][NACC];
+    float acc2[2][NACC];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-        for (int k = 0; k < NACC; ++k) acc4[j][k] = 0.0f;
-    int sl = 0;
-    for (; sl + 4 <= nslot; sl += 4) {
+        for (int k = 0; k < NACC; ++k) acc2[j][k] = 0.0f;
+    if (pv) {
+        int sl = warp;
+        for (; sl + 8 < nslot; sl += 16) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float* ps = p + (int64_t)(sl + j) * a.part_stride;
+            for (int j = 0; j < 2; ++j) {
+                const float* ps = p + (int64_t)(sl + 8 * j) * a.part_stride;
 #pragma unroll
-            for (int k = 0; k < NACC; ++k) acc4[j][k] += ps[(int64_t)k * G * a.qrows_pad];
+                for (int k = 0; k < NACC; ++k) acc2[j][k] += ps[(int64_t)k * G * a.qrows_pad];
+            }
+        }
+        if (sl < nslot) {
+            const float* ps = p + (int64_t)sl * a.part_stride;
+#pragma unroll
+            for (int k = 0; k < NACC; ++k) acc2[0][k] += ps[(int64_t)k * G * a.qrows_pad];
         }
     }
-    for (; sl < nslot; ++sl) {
-        const float* ps = p + (int64_t)sl * a.part_stride;
 #pragma unroll
-        for (int k = 0; k < NACC; ++k) acc4[0][k] += ps[(int64_t)k * G * a.qrows_pad];
-    }
+    for (int k = 0; k < NACC; ++k) red[warp][k][lane] = acc2[0][k] + acc2[1][k];
+    __syncthreads();
+    if (warp != 0 || !pv) return;
     float acc[NACC];
 #pragma unroll
-    for (int k = 0; k < NACC; ++k) acc[k] = (acc4[0][k] + acc4[1][k]) + (acc4[2][k] + acc4[3][k]);
+    for (int k = 0; k < NACC; ++k)
+        acc[k] = ((red[0][k][lane] + red[1][k][lane]) + (red[2][k][lane] + red[3][k][lane])) +
+                 ((red[4][k][lane] + red[5][k][lane]) + (red[6][k][lane] + red[7][k][lane]));
     const int ga = g + (g >= a.bg ? 1 : 0);
     const int64_t qi = (int64_t)lb * a.Q + qt * a.qrows + t;
     const int64_t o = qi * G + g;
