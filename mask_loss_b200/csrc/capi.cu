@@ -329,7 +329,7 @@ int run_prep(const FwdPlan& P, const CostArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return cuda_fail(e, "memset totals");
     const int HW = P.H * P.W;
     if (P.B > 0 && HW > 0) {
-        const int bx = std::max(1, std::min((HW + 255) / 256, (4 * sm_count() + P.B - 1) / std::max(1, P.B)));
+        const int bx = std::max(1, std::min((HW + 255) / 256, 65535));  // one cell per thread
         const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
         label_code_kernel<<<dim3(bx, P.B), 256, hs, st>>>(a.targets, P.B, P.H, P.W, P.Wt, P.s,
                                                           P.gt_total, P.bg,
@@ -528,7 +528,7 @@ int run_sampled_prep(const SampledPlan& S, const ml_params* p, const void* mask_
     if (e != cudaSuccess) return cuda_fail(e, "memset histograms");
     const int HW = S.H * S.W;
     if (P.B > 0) {
-        const int bx = std::max(1, std::min((HW + 255) / 256, (4 * sm_count() + P.B - 1) / std::max(1, P.B)));
+        const int bx = std::max(1, std::min((HW + 255) / 256, 65535));  // one cell per thread
         const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
         label_code_kernel<<<dim3(bx, P.B), 256, hs, st>>>(mask_targets, P.B, S.H, S.W, S.Wt, S.Ht / S.H,
                                                           P.gt_total, P.bg, nullptr, present);
@@ -796,8 +796,9 @@ int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float*
     la.cls_targets = cls_targets; la.pred_to_gt = pred_to_gt; la.num_masks_dev = num_masks_dev;
     la.grad_mask = grad_mask_mean; la.grad_dice = grad_dice_mean; la.grad_cls = grad_cls_mean;
     la.coef = coef; la.grad_mask_logits = grad_mask_logits; la.grad_cls_logits = grad_cls_logits;
-    bwd_coef_kernel<<<P.L, 256, 0, st>>>(la);
-    ML_CHECK_LAUNCH("bwd_coef_kernel");
+    // coefficients + class-logit gradient first; the mask gradient reads coef
+    bwd_cls_kernel<<<(unsigned)((LBQ + 7) / 8), 256, 0, st>>>(la);
+    ML_CHECK_LAUNCH("bwd_cls_kernel");
     const bool unc = p->uncertainty_gamma != 0.0f;
     const bool foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
     if (saved) {
@@ -832,11 +833,6 @@ int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float*
     }
 #undef ML_MG
     ML_CHECK_LAUNCH("mask_grad_kernel");
-    if (P.C > 0) {
-        const int64_t blocks = (LBQ * 32 + 255) / 256;
-        cls_grad_kernel<<<(unsigned)blocks, 256, 0, st>>>(la);
-        ML_CHECK_LAUNCH("cls_grad_kernel");
-    }
     return ML_OK;
 }
 
@@ -954,8 +950,9 @@ int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int6
     la.grad_cls = grad_cls_mean; la.coef = reinterpret_cast<float*>(ws + off_coef);
     la.stats_in = saved; la.grad_cls_logits = grad_cls_logits;
     if (LBQ == 0) return ML_OK;
-    bwd_coef_kernel<<<P.L, 256, 0, st>>>(la);
-    ML_CHECK_LAUNCH("bwd_coef_kernel");
+    // coefficients + class-logit gradient first; the mask gradient reads coef
+    bwd_cls_kernel<<<(unsigned)((LBQ + 7) / 8), 256, 0, st>>>(la);
+    ML_CHECK_LAUNCH("bwd_cls_kernel");
     const bool foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
     float* gacc = logits_dtype == 1 ? reinterpret_cast<float*>(ws + off_gacc)
                                     : static_cast<float*>(grad_mask_logits);
@@ -974,11 +971,6 @@ int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int6
         e = launch_to_bf16(gacc, grad_mask_logits, (int64_t)(LBQ * HWl), st);
         g_launches.fetch_add(1);
         if (e != cudaSuccess) return cuda_fail(e, "f32_to_bf16_kernel");
-    }
-    if (P.C > 0) {
-        const int64_t blocks = ((int64_t)LBQ * 32 + 255) / 256;
-        cls_grad_kernel<<<(unsigned)blocks, 256, 0, st>>>(la);
-        ML_CHECK_LAUNCH("cls_grad_kernel");
     }
     return ML_OK;
 }

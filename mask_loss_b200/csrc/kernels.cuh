@@ -125,10 +125,9 @@ struct LossArgs {
 
 __global__ void loss_fwd_kernel(LossArgs a);
 __global__ void count_masks_kernel(const int32_t* totals, int B, int gt_total, int bg, float* out);
-__global__ void bwd_coef_kernel(LossArgs a);
 template <bool UNC> __global__ void bwd_stats_kernel(LossArgs a);
 template <bool UNC, bool FOC, bool VEC> __global__ void mask_grad_kernel(LossArgs a);
-__global__ void cls_grad_kernel(LossArgs a);
+__global__ void bwd_cls_kernel(LossArgs a);
 
 }  // namespace mlb
 

@@ -125,27 +125,6 @@ __global__ void count_masks_kernel(const int32_t* totals, int B, int gt_total, i
     if (threadIdx.x == 0) *out = v[0];
 }
 
-// ---------------------------------------------------------------------------
-// Backward coefficients per layer: grid = L, block = 256.
-// coef[l] = {g_mask/md, g_dice/md, g_cls*cls_scale/cd}
-// ---------------------------------------------------------------------------
-__global__ void bwd_coef_kernel(LossArgs a) {
-    __shared__ float sh[32];
-    const int l = blockIdx.x;
-    const int n = a.B * a.Q;
-    float v[1] = {0.0f};
-    for (int i = threadIdx.x; i < n; i += blockDim.x) v[0] += a.pred_to_gt[(int64_t)l * n + i] >= 0;
-    block_sum<1>(v, sh);
-    if (threadIdx.x == 0) {
-        float md, cd;
-        denominators(a, v[0], &md, &cd);
-        const float im = 1.0f / md, ic = 1.0f / cd;
-        a.coef[l * 3 + 0] = a.grad_mask[l] * im;
-        a.coef[l * 3 + 1] = a.grad_dice[l] * im;
-        a.coef[l * 3 + 2] = a.grad_cls[l] * (ic * a.cls_scale);
-    }
-}
-
 // Count of pixels labelled `ga` in low-res cell `cell` (s x s block).
 ML_INLINE float cell_count(const int64_t* tb, int cell, int W, int Wt, int s, int64_t ga) {
     const int ci = cell / W, cj = cell - ci * W;
@@ -271,16 +250,11 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Class-logit gradient: one warp per (l,b,q) row, block = 256.
-// src/cuda/mask_matching_backward.cu:218-376.  Every element is written.
+// Class-logit gradient of one (l,b,q) row by one warp; `base` = the layer's
+// class coefficient.  src/cuda/mask_matching_backward.cu:218-376.  Every
+// element is written.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) cls_grad_kernel(LossArgs a) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    const int64_t rows = (int64_t)a.L * a.B * a.Q;
-    if (warp >= rows) return;
-    const int64_t qi = warp;
-    const int l = (int)(qi / ((int64_t)a.B * a.Q));
+ML_INLINE void cls_grad_row(const LossArgs& a, int64_t qi, int lane, float base) {
     const int b = (int)((qi / a.Q) % a.B);
     const int C = a.C;
     const float* z = a.cls_logits + qi * C;
@@ -289,7 +263,6 @@ __global__ void __launch_bounds__(256) cls_grad_kernel(LossArgs a) {
     const int64_t ga = og + (og >= a.bg ? 1 : 0);
     const bool matched = og >= 0 && ga < a.gt_total;
     const bool need = a.force_cls || a.has_void;
-    const float base = a.coef[l * 3 + 2];
     int y = -1;
     bool zero = !(matched || need) || base == 0.0f;
     if (!zero && matched) {
@@ -342,6 +315,43 @@ __global__ void __launch_bounds__(256) cls_grad_kernel(LossArgs a) {
         else g = 0.0f;
         gz[c] = g;
     }
+}
+
+// ---------------------------------------------------------------------------
+// Backward coefficients + class-logit gradient: grid = ceil(L*B*Q / 8),
+// block = 256, one warp per (l,b,q) row.  Each block counts the matched rows
+// of its layer(s) with the same fixed-order reduction (so every block gets
+// the same coefficients), and the block holding a layer's first row publishes
+// coef[l] for mask_grad_kernel, which runs after it.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) bwd_cls_kernel(LossArgs a) {
+    __shared__ float sh[32];
+    __shared__ float scoef[8][3];
+    const int64_t rows = (int64_t)a.L * a.B * a.Q;
+    const int64_t n = (int64_t)a.B * a.Q;
+    const int64_t r0 = (int64_t)blockIdx.x * 8;
+    const int64_t r1 = min(rows, r0 + 8) - 1;
+    const int l0 = (int)(r0 / n), l1 = (int)(r1 / n);
+    for (int l = l0; l <= l1; ++l) {
+        float v[1] = {0.0f};
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) v[0] += a.pred_to_gt[(int64_t)l * n + i] >= 0;
+        block_sum<1>(v, sh);
+        if (threadIdx.x == 0) {
+            float md, cd;
+            denominators(a, v[0], &md, &cd);
+            const float im = 1.0f / md, ic = 1.0f / cd;
+            const float c[3] = {a.grad_mask[l] * im, a.grad_dice[l] * im, a.grad_cls[l] * (ic * a.cls_scale)};
+            const bool first = (int64_t)l * n >= r0 && (int64_t)l * n <= r1;
+            for (int k = 0; k < 3; ++k) {
+                scoef[l - l0][k] = c[k];
+                if (first) a.coef[l * 3 + k] = c[k];
+            }
+        }
+    }
+    __syncthreads();
+    const int64_t qi = r0 + (threadIdx.x >> 5);
+    if (qi > r1 || a.C <= 0) return;
+    cls_grad_row(a, qi, threadIdx.x & 31, scoef[(int)(qi / n) - l0][2]);
 }
 
 template __global__ void bwd_stats_kernel<false>(LossArgs);
