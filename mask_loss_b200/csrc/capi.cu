@@ -528,7 +528,9 @@ int run_sampled_prep(const SampledPlan& S, const ml_params* p, const void* mask_
     if (e != cudaSuccess) return cuda_fail(e, "memset histograms");
     const int HW = S.H * S.W;
     if (P.B > 0) {
-        const int bx = std::max(1, std::min((HW + 255) / 256, 65535));  // one cell per thread
+        // histogram only: one label pixel per thread
+        const int64_t npix = (int64_t)S.Ht * S.Wt;
+        const int bx = (int)std::max<int64_t>(1, std::min<int64_t>((npix + 255) / 256, 65535));
         const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
         label_code_kernel<<<dim3(bx, P.B), 256, hs, st>>>(mask_targets, P.B, S.H, S.W, S.Wt, S.Ht / S.H,
                                                           P.gt_total, P.bg, nullptr, present);

@@ -57,6 +57,21 @@ label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int 
     int32_t* cb = codes ? codes + (int64_t)b * HW : nullptr;
     int32_t* tot = totals + (int64_t)b * gt_total;
     int32_t* hc = use_sh ? hist : tot;
+    if (!cb && s > 1) {
+        // histogram only: one pixel per thread, coalesced, warp-aggregated
+        const int64_t npix = (int64_t)HW * s * s;
+        for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < npix;
+             base += (int64_t)gridDim.x * blockDim.x) {
+            const int64_t px = base + threadIdx.x;
+            int key = -1;
+            if (px < npix) {
+                const int64_t lab = tb[px];
+                key = (lab >= 0 && lab < gt_total) ? (int)lab : -1;
+            }
+            const unsigned peers = __match_any_sync(0xffffffffu, key);
+            if (key >= 0 && (int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hc[key], __popc(peers));
+        }
+    } else
     // every thread of the block runs the same number of iterations, so the
     // warp-aggregated count below sees the whole warp
     for (int base = blockIdx.x * blockDim.x; base < HW; base += gridDim.x * blockDim.x) {

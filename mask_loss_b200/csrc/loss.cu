@@ -235,6 +235,26 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
         return mcoef * gs + dcoef * gd;
     };
     if (VEC) {
+        // one pixel per cell and 16-byte aligned labels: the four labels of a
+        // float4 are two 16-byte loads, issued with the logits
+        const bool lab2 = s == 1 && matched && ((reinterpret_cast<uintptr_t>(tb + c0) & 15) == 0);
+        if (lab2) {
+            const float* __restrict__ xr = xin;
+            const longlong2* __restrict__ lr = reinterpret_cast<const longlong2*>(tb + c0);
+            float* __restrict__ gr = gout;
+#pragma unroll 4
+            for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4) {
+                const float4 xv = __ldcs(reinterpret_cast<const float4*>(xr + k));
+                const longlong2 l01 = lr[k >> 1], l23 = lr[(k >> 1) + 1];
+                float4 r;
+                r.x = g1(xv.x, l01.x == ga ? 1.0f : 0.0f);
+                r.y = g1(xv.y, l01.y == ga ? 1.0f : 0.0f);
+                r.z = g1(xv.z, l23.x == ga ? 1.0f : 0.0f);
+                r.w = g1(xv.w, l23.y == ga ? 1.0f : 0.0f);
+                __stcs(reinterpret_cast<float4*>(gr + k), r);
+            }
+            return;
+        }
         for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4) {
             const float4 xv = __ldcs(reinterpret_cast<const float4*>(xin + k));
             float4 r;
