@@ -57,6 +57,36 @@ def pairwise_dice_loss_sampling(logits, targets, smooth=1.0, background_index=No
                           point_coords, 1, smooth=smooth, scale=scale)
 
 
+def resolve_sampled_args(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, inf_thresh,
+                         num_masks, force_unmatched_class_to_background, K, assignment_strategy,
+                         mask_focal_gamma, mask_focal_alpha, cls_focal_gamma, cls_focal_alpha,
+                         void_class_index=None, label_loss="sigmoid", align_corners=False):
+    """Defaulting and validation of the sampled Function's scalar arguments.
+    Returns the op's positional arguments and the device num_masks (or None)."""
+    if assignment_strategy not in STRATEGIES:
+        raise ValueError(f"Unknown assignment_strategy '{assignment_strategy}'.")
+    softmax = (label_loss or "sigmoid").lower() == "softmax"
+    vi = -1 if void_class_index is None else int(void_class_index)
+    if softmax and force_unmatched_class_to_background and vi == -1:
+        raise ValueError("void_class_index must be provided when using softmax label loss "
+                         "and forcing unmatched predictions to background")
+    mg = float(mask_focal_gamma or 0.0)
+    ma = -1.0 if mask_focal_alpha is None else float(mask_focal_alpha)
+    cg = mg if cls_focal_gamma is None else float(cls_focal_gamma)
+    ca = ma if cls_focal_alpha is None else float(cls_focal_alpha)
+    nm_dev = None
+    nm = -1.0
+    if isinstance(num_masks, torch.Tensor):
+        nm_dev = num_masks.detach().reshape(()).to(torch.float32).contiguous()
+    elif num_masks is not None:
+        nm = float(num_masks)
+    args = (float(smooth), float(sigmoid_scale), float(dice_scale), float(cls_scale),
+            _bg(background_index), float(inf_thresh), nm,
+            bool(force_unmatched_class_to_background), int(K), STRATEGIES[assignment_strategy],
+            mg, ma, cg, ca, vi, softmax, bool(align_corners))
+    return args, nm_dev
+
+
 class MaskMatchingSampledFunction(Function):
     """Inputs: mask_logits (L,B,Q,H,W) fp32/bf16, mask_targets, cls_logits,
     cls_targets, point_coords (B,P,2) in [0,1], then smooth, sigmoid_scale,
@@ -72,27 +102,11 @@ class MaskMatchingSampledFunction(Function):
                 force_unmatched_class_to_background, K, assignment_strategy, mask_focal_gamma,
                 mask_focal_alpha, cls_focal_gamma, cls_focal_alpha, void_class_index=None,
                 label_loss="sigmoid", align_corners=False):
-        if assignment_strategy not in STRATEGIES:
-            raise ValueError(f"Unknown assignment_strategy '{assignment_strategy}'.")
-        softmax = (label_loss or "sigmoid").lower() == "softmax"
-        vi = -1 if void_class_index is None else int(void_class_index)
-        if softmax and force_unmatched_class_to_background and vi == -1:
-            raise ValueError("void_class_index must be provided when using softmax label loss "
-                             "and forcing unmatched predictions to background")
-        mg = float(mask_focal_gamma or 0.0)
-        ma = -1.0 if mask_focal_alpha is None else float(mask_focal_alpha)
-        cg = mg if cls_focal_gamma is None else float(cls_focal_gamma)
-        ca = ma if cls_focal_alpha is None else float(cls_focal_alpha)
-        nm_dev = None
-        nm = -1.0
-        if isinstance(num_masks, torch.Tensor):
-            nm_dev = num_masks.detach().reshape(()).to(torch.float32).contiguous()
-        elif num_masks is not None:
-            nm = float(num_masks)
-        args = (float(smooth), float(sigmoid_scale), float(dice_scale), float(cls_scale),
-                _bg(background_index), float(inf_thresh), nm,
-                bool(force_unmatched_class_to_background), int(K), STRATEGIES[assignment_strategy],
-                mg, ma, cg, ca, vi, softmax, bool(align_corners))
+        args, nm_dev = resolve_sampled_args(
+            smooth, sigmoid_scale, dice_scale, cls_scale, background_index, inf_thresh, num_masks,
+            force_unmatched_class_to_background, K, assignment_strategy, mask_focal_gamma,
+            mask_focal_alpha, cls_focal_gamma, cls_focal_alpha, void_class_index, label_loss,
+            align_corners)
         ml = mask_logits.contiguous()
         cl = cls_logits.contiguous().float()
         pc = point_coords.contiguous().float()

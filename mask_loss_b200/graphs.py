@@ -26,7 +26,8 @@ from __future__ import annotations
 import torch
 
 from . import ops, parallel
-from .functions import MaskMatchingFunction, MaskMatchingSampledFunction
+from .functions.matching import resolve_args
+from .functions.sampled import resolve_sampled_args
 
 
 def _multi_rank() -> bool:
@@ -58,6 +59,7 @@ class MatchingLossStep:
             self.args[self.nm_slot] = "auto"
             self.allreduce_num_masks = False
         self.w = loss_weights
+        self._wts = None
         self.graph = None
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -79,23 +81,51 @@ class MatchingLossStep:
          self.grad_cls_logits) = out
 
     def _run(self):
+        """One step through the ops directly (the forward op, then the backward
+        op with the loss weights as upstream gradients): the same kernels and
+        results as MaskMatchingFunction + autograd, without autograd's glue
+        kernels in the graph."""
         ml = self.inputs["mask_logits"]
         mt = self.inputs["mask_targets"]
         cl = self.inputs["cls_logits"]
         ct = self.inputs["cls_targets"]
+        for t, n in ((ml, "mask_logits"), (cl, "cls_logits")):
+            if not t.is_contiguous():
+                raise RuntimeError(f"{n} must be contiguous")
+        if cl.dtype != torch.float32:
+            raise RuntimeError("cls_logits must be float32")
         a = list(self.args)
         if self.allreduce_num_masks:
             a[self.nm_slot] = parallel.global_num_masks(ops.count_masks(mt, ct.shape[1], int(a[4])))
-        x = ml.detach().requires_grad_(True)
-        z = cl.detach().requires_grad_(True)
+        L = ml.shape[0]
+        if self._wts is None:
+            self._wts = [torch.full((L,), float(w), dtype=torch.float32, device=ml.device)
+                         for w in self.w]
+        wm, wd, wc = self._wts
         if self.sampled:
-            p2g, prd, m, d, c = MaskMatchingSampledFunction.apply(
-                x, mt, z, ct, self.inputs["point_coords"], *a)
+            pc = self.inputs["point_coords"]
+            args, nm_dev = resolve_sampled_args(*a)
+            p2g, prd, means, saved, _, fws = ops.mask_matching_sampled_ex(
+                ml, mt, cl, ct, pc, *args, num_masks_dev=nm_dev, want_saved=True,
+                want_workspace=True)
+            gm, gc = ops.mask_matching_sampled_backward(
+                wm, wd, wc, ml, mt, cl, ct, pc, p2g, saved, args[0], args[1], args[2], args[3],
+                args[4], args[6], args[7], args[10], args[11], args[12], args[13], args[14],
+                args[15], args[16], num_masks_dev=nm_dev, forward_workspace=fws)
         else:
-            p2g, prd, m, d, c = MaskMatchingFunction.apply(x, mt, z, ct, *a)
-        losses = torch.stack([m, d, c])
-        (self.w[0] * m + self.w[1] * d + self.w[2] * c).sum().backward()
-        return p2g, prd, losses.detach(), x.grad, z.grad
+            if ml.dtype != torch.float32:
+                raise RuntimeError("mask_logits must be float32")
+            args, nm_dev = resolve_args(ml, mt, cl, ct, *a)
+            vi = args[17]
+            if vi != -1:  # functions/mask/matching.py:180-181
+                ops.defer_check((ct == vi).any(), "cls_targets must not contain the void class index")
+            p2g, prd, means, saved, _ = ops.mask_matching_ex(
+                ml, mt, cl, ct, *args, num_masks_dev=nm_dev, want_saved=True)
+            gm, gc = ops.mask_matching_backward(
+                wm, wd, wc, ml, mt, cl, ct, p2g, args[0], args[1], args[2], args[3], args[4],
+                args[5], args[6], args[8], args[9], args[10], args[13], args[14], args[15],
+                args[16], args[17], args[18], args[19], saved=saved, num_masks_dev=nm_dev)
+        return p2g, prd, means, gm, gc
 
     def replay(self) -> None:
         self.graph.replay()
