@@ -61,6 +61,11 @@ typedef struct ml_params {
     int64_t void_class_index;          /* -1: none */
     int32_t use_softmax_label_loss;
     int32_t normalize_uncertainty;
+    int32_t check_void_targets;        /* 1: ml_mask_matching sets bit 4 of dev_status
+                                          when a cls_targets entry equals
+                                          void_class_index (the check of
+                                          functions/mask/matching.py:180-181, done on
+                                          the device); 0: no check (the binding) */
 } ml_params;
 
 /* Human-readable text of a status code (static storage). */
@@ -172,7 +177,10 @@ int ml_match_f64(const double* costs, int64_t N, int64_t Q, int64_t GT_out,
 /*   num_masks_dev (nullable): device fp32 scalar overriding p->num_masks    */
 /*                            (used by data-parallel callers after an        */
 /*                            all-reduce, so no host sync is needed)         */
-/*   dev_status             : one device int32, 0 on success                */
+/*   dev_status             : one device int32, 0 on success; bits: 1 the   */
+/*                            solver failed, 2 a device wait timed out, 4    */
+/*                            cls_targets holds the void class (when         */
+/*                            p->check_void_targets)                         */
 /* ---------------------------------------------------------------------- */
 int ml_mask_matching(const ml_dims* d, const ml_params* p,
                      const float* mask_logits, const int64_t* mask_targets,

@@ -743,6 +743,10 @@ int ml_mask_matching(const ml_dims* d, const ml_params* p, const float* mask_log
         la.totals = a.totals;
         la.num_masks_out = const_cast<float*>(num_masks_dev);
     }
+    if (p->check_void_targets && la.has_void) {
+        la.cls_targets = cls_targets;
+        la.void_status = dev_status;
+    }
     loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
     ML_CHECK_LAUNCH("loss_fwd_kernel");
     return ML_OK;
@@ -903,6 +907,10 @@ int ml_mask_matching_sampled(const ml_dims* d, const ml_params* p, int64_t num_p
         la.auto_num_masks = 1;
         la.totals = a.totals;
         la.num_masks_out = const_cast<float*>(num_masks_dev);
+    }
+    if (p->check_void_targets && la.has_void) {
+        la.cls_targets = cls_targets;
+        la.void_status = dev_status;
     }
     loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
     ML_CHECK_LAUNCH("loss_fwd_kernel");

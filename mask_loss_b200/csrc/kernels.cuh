@@ -121,6 +121,7 @@ struct LossArgs {
     float smooth, sigmoid_scale, dice_scale, cls_scale;
     float ug, ugmin, mask_gamma, mask_alpha, cls_gamma, cls_alpha;
     int force_masks, force_cls, has_void, void_index, use_softmax, normalize_uncertainty;
+    int32_t* void_status;    // forward: bit 4 set when cls_targets holds void_index, or null
 };
 
 __global__ void loss_fwd_kernel(LossArgs a);

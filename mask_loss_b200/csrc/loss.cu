@@ -66,6 +66,12 @@ ML_INLINE void denominators(const LossArgs& a, float matched, float* md, float* 
 __global__ void __launch_bounds__(512) loss_fwd_kernel(LossArgs a) {
     __shared__ float sh[32 * 4];
     const int l = blockIdx.x;
+    if (a.void_status && l == 0) {  // functions/mask/matching.py:180-181
+        bool hit = false;
+        for (int i = threadIdx.x; i < a.B * a.gt_total; i += blockDim.x)
+            hit |= a.cls_targets[i] == (int64_t)a.void_index;
+        if (__any_sync(0xffffffffu, hit) && (threadIdx.x & 31) == 0) atomicOr(a.void_status, 4);
+    }
     if (a.auto_num_masks) {
         // num_masks = present non-background GT ids of this batch, clamped >= 1;
         // block 0 publishes it for the backward

@@ -125,13 +125,11 @@ class MaskMatchingFunction(Function):
             normalize_uncertainty, inf_thresh, num_masks, force_unmatched_class_to_background,
             force_unmatched_masks_to_empty, K, assignment_strategy, mask_focal_gamma,
             mask_focal_alpha, cls_focal_gamma, cls_focal_alpha, void_class_index, label_loss)
-        vi = args[17]
-        if vi != -1:  # functions/mask/matching.py:180-181, checked without a host sync
-            ops.defer_check((cls_targets == vi).any(),
-                            "cls_targets must not contain the void class index")
+        # functions/mask/matching.py:180-181 (void id in cls_targets) is checked
+        # on the device by the forward and raised without a host sync
         p2g, prd, means, saved, _ = ops.mask_matching_ex(
             mask_logits, mask_targets, cls_logits, cls_targets, *args,
-            num_masks_dev=nm_dev, want_saved=True)
+            num_masks_dev=nm_dev, want_saved=True, check_void_targets=True)
         ctx.save_for_backward(mask_logits, mask_targets, cls_logits, cls_targets, p2g, saved,
                               nm_dev if nm_dev is not None else torch.empty(0))
         ctx.args = args

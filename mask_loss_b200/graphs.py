@@ -116,11 +116,9 @@ class MatchingLossStep:
             if ml.dtype != torch.float32:
                 raise RuntimeError("mask_logits must be float32")
             args, nm_dev = resolve_args(ml, mt, cl, ct, *a)
-            vi = args[17]
-            if vi != -1:  # functions/mask/matching.py:180-181
-                ops.defer_check((ct == vi).any(), "cls_targets must not contain the void class index")
             p2g, prd, means, saved, _ = ops.mask_matching_ex(
-                ml, mt, cl, ct, *args, num_masks_dev=nm_dev, want_saved=True)
+                ml, mt, cl, ct, *args, num_masks_dev=nm_dev, want_saved=True,
+                check_void_targets=True)
             gm, gc = ops.mask_matching_backward(
                 wm, wd, wc, ml, mt, cl, ct, p2g, args[0], args[1], args[2], args[3], args[4],
                 args[5], args[6], args[8], args[9], args[10], args[13], args[14], args[15],
@@ -134,5 +132,6 @@ class MatchingLossStep:
         """Raise if the last replay's solver (or argument check) reported
         failure.  Synchronises."""
         for flag, msg in self._flags:
-            if int(flag.reshape(-1)[0].item()) != 0:
-                raise RuntimeError(msg)
+            v = int(flag.reshape(-1)[0].item())
+            if v != 0:
+                raise RuntimeError(msg(v) if callable(msg) else msg)

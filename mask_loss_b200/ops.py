@@ -60,8 +60,9 @@ def check_status(block: bool = False) -> None:
         if block:
             ev.synchronize()
         if ev.query():
-            if int(host.item()) != 0 and err is None:
-                err = RuntimeError(msg)
+            v = int(host.item())
+            if v != 0 and err is None:
+                err = RuntimeError(msg(v) if callable(msg) else msg)
             _pinned.append(host)
         else:
             keep.append((ev, host, msg))
@@ -103,8 +104,16 @@ def defer_check(flag: torch.Tensor, message: str) -> None:
     _defer(flag.reshape(1).to(torch.int32), message)
 
 
+def _status_message(v: int) -> str:
+    if v & 4:
+        return "cls_targets must not contain the void class index"
+    if v & 2:
+        return "mask_loss_b200: a device wait timed out (cost kernel pipeline)"
+    return "Hungarian: no augmenting path found; check costs/inf_thresh."
+
+
 def _track_status(status: torch.Tensor) -> None:
-    _defer(status, "Hungarian: no augmenting path found; check costs/inf_thresh.")
+    _defer(status, _status_message)
 
 
 def _params(smooth=1.0, sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0, background_index=-1,
@@ -112,7 +121,7 @@ def _params(smooth=1.0, sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0, backgr
             force_unmatched_class_to_background=False, force_unmatched_masks_to_empty=False,
             topk_matches=1, strategy_id=0, mask_gamma=0.0, mask_alpha=-1.0, cls_gamma=0.0,
             cls_alpha=-1.0, void_class_index=-1, use_softmax_label_loss=False,
-            normalize_uncertainty=True) -> _lib.Params:
+            normalize_uncertainty=True, check_void_targets=False) -> _lib.Params:
     return _lib.Params(float(smooth), float(sigmoid_scale), float(dice_scale), float(cls_scale),
                        int(background_index), float(uncertainty_gamma),
                        float(uncertainty_gamma_min), float(inf_thresh), float(num_masks),
@@ -120,7 +129,7 @@ def _params(smooth=1.0, sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0, backgr
                        int(bool(force_unmatched_masks_to_empty)), int(topk_matches),
                        int(strategy_id), float(mask_gamma), float(mask_alpha), float(cls_gamma),
                        float(cls_alpha), int(void_class_index), int(bool(use_softmax_label_loss)),
-                       int(bool(normalize_uncertainty)))
+                       int(bool(normalize_uncertainty)), int(bool(check_void_targets)))
 
 
 def _dims(mask_logits, mask_targets, cls_logits, cls_targets) -> _lib.Dims:
@@ -201,10 +210,14 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
                      mask_gamma=0.0, mask_alpha=-1.0, cls_gamma=0.0, cls_alpha=-1.0,
                      void_class_index=-1, use_softmax_label_loss=False, normalize_uncertainty=True,
                      *, num_masks_dev: Optional[torch.Tensor] = None, want_saved: bool = False,
-                     want_costs: bool = False):
+                     want_costs: bool = False, check_void_targets: bool = False):
     """``mask_matching`` plus the extras this implementation offers: a device
     ``num_masks_dev`` (fp32 scalar, e.g. after an all-reduce), the per-query
     statistics the backward can reuse (``saved``) and the cost slices.
+
+    ``check_void_targets``: raise (deferred) if cls_targets holds
+    void_class_index -- functions/mask/matching.py:180-181, checked on the
+    device.
 
     Returns (pred_to_gt, pred_round, layer_means(3,L), saved or None, costs or None)."""
     check_status()
@@ -220,7 +233,7 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
                 uncertainty_gamma_min, inf_thresh, num_masks, force_unmatched_class_to_background,
                 force_unmatched_masks_to_empty, topk_matches, strategy_id, mask_gamma, mask_alpha,
                 cls_gamma, cls_alpha, void_class_index, use_softmax_label_loss,
-                normalize_uncertainty)
+                normalize_uncertainty, check_void_targets)
     L, B, Q = mask_logits.shape[:3]
     G = lib.ml_gt_out(d.GT_total, p.background_index)
     p2g = torch.empty((L, B, Q), dtype=torch.int64, device=dev)

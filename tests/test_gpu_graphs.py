@@ -60,3 +60,33 @@ def test_auto_num_masks_counts_present_gts():
     # force_unmatched_class=True makes the class term use B*Q; mask/dice use num_masks
     for x, y in zip(r1[1:], r2[1:]):
         torch.testing.assert_close(x, y, rtol=1e-6, atol=1e-9)
+
+
+def test_void_class_in_targets_raises_deferred():
+    """functions/mask/matching.py:180-181: a void id in cls_targets is an
+    error of the Function (checked on the device, raised without a host
+    sync) and of the graph step; the binding-level op does not check."""
+    from mask_loss_b200 import ops
+    cfg = synthetic.CONFIGS["cfg1"]
+    b = synthetic.make_batch(cfg, device=DEV)
+    ml, mt, cl, ct = (b[k].contiguous() for k in ("mask_logits", "mask_targets", "cls_logits",
+                                                  "cls_targets"))
+    args = _args(cfg)
+    bad = ct.clone()
+    bad[0, 1] = args[18]  # a GT column labelled with the void class
+    ops.check_status(block=True)
+    F.MaskMatchingFunction.apply(ml, mt, cl, bad, *args)
+    with pytest.raises(RuntimeError, match="void class index"):
+        ops.check_status(block=True)
+    F.MaskMatchingFunction.apply(ml, mt, cl, ct, *args)
+    ops.check_status(block=True)  # clean targets: nothing pending
+    kw = synthetic.parity_kwargs(cfg)
+    ops.mask_matching(ml, mt, cl, bad, *list(kw.values()))
+    ops.check_status(block=True)  # the binding op has no such check
+    step = MatchingLossStep(ml.clone(), mt.clone(), cl.clone(), ct.clone(), *args)
+    step.replay()
+    step.check()
+    step.inputs["cls_targets"].copy_(bad)
+    step.replay()
+    with pytest.raises(RuntimeError, match="void class index"):
+        step.check()
