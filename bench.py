@@ -42,6 +42,29 @@ METRIC = "images/sec matching+loss fwd+bwd (Mask2Former shape)"
 UNIT = "images/s"
 
 
+_JSON_FD = None  # the original stdout when library chatter is moved to stderr
+
+
+def emit(line: dict) -> None:
+    """Print the one JSON result line on the real stdout."""
+    text = json.dumps(line) + "\n"
+    if _JSON_FD is None:
+        sys.stdout.write(text)
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, text.encode())
+
+
+def quiet_stdout() -> None:
+    """Send everything else written to fd 1 (NCCL's version banner, library
+    logs) to stderr, so stdout carries only the JSON line."""
+    global _JSON_FD
+    if _JSON_FD is None:
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
 def dist_info():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -174,7 +197,7 @@ def run_reference(args, cfg):
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -413,7 +436,7 @@ def run_ours(args, cfg):
         "clocks": clk,
         "cpu_baseline": cpu,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     teardown()
 
 
@@ -425,6 +448,8 @@ def main():
     ap.add_argument("--config", default="cfg2")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     args = ap.parse_args()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        quiet_stdout()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     from mask_loss_b200 import synthetic

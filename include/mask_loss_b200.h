@@ -21,6 +21,7 @@ extern "C" {
 #endif
 
 typedef struct CUstream_st* ml_stream_t; /* == cudaStream_t */
+typedef struct CUevent_st* ml_event_t;   /* == cudaEvent_t */
 
 typedef enum ml_status {
     ML_OK = 0,
@@ -189,6 +190,20 @@ int ml_mask_matching(const ml_dims* d, const ml_params* p,
                      int64_t* pred_to_gt, int64_t* pred_round, float* layer_means,
                      float* sep_costs, float* saved, int32_t* dev_status,
                      void* workspace, size_t workspace_bytes, ml_stream_t stream);
+
+/* ml_mask_matching with one more argument, no reference counterpart:
+ * loss_wait_event (nullable) -- the stream waits on it after the assignment
+ * and before the matched-loss kernel, the only one that reads num_masks_dev.
+ * A data-parallel caller records it after the all-reduce of the GT count on
+ * another stream, so the collective overlaps the cost and solver kernels. */
+int ml_mask_matching_ex(const ml_dims* d, const ml_params* p,
+                        const float* mask_logits, const int64_t* mask_targets,
+                        const float* cls_logits, const int64_t* cls_targets,
+                        const float* num_masks_dev,
+                        int64_t* pred_to_gt, int64_t* pred_round, float* layer_means,
+                        float* sep_costs, float* saved, int32_t* dev_status,
+                        void* workspace, size_t workspace_bytes, ml_stream_t stream,
+                        ml_event_t loss_wait_event);
 
 /* Per-image GT count (present, non-background GT ids) summed over the batch,
  * written as one fp32 to num_masks_out (device).  This is the num_masks a

@@ -68,6 +68,9 @@ SIGNATURES = {
     "ml_mask_matching": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_vp, c_vp,
                                         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                         c_sz, c_vp]),
+    "ml_mask_matching_ex": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_vp, c_vp,
+                                           c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                           c_vp, c_sz, c_vp, c_vp]),
     "ml_count_masks": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_vp, c_vp,
                                       c_vp, c_sz, c_vp]),
     "ml_mask_matching_backward": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params),

@@ -712,11 +712,12 @@ int ml_match_f64(const double* costs, int64_t N, int64_t Q, int64_t GT_out, doub
                                 pred_round, dev_status, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int ml_mask_matching(const ml_dims* d, const ml_params* p, const float* mask_logits,
-                     const int64_t* mask_targets, const float* cls_logits, const int64_t* cls_targets,
-                     const float* num_masks_dev, int64_t* pred_to_gt, int64_t* pred_round,
-                     float* layer_means, float* sep_costs, float* saved, int32_t* dev_status,
-                     void* workspace, size_t workspace_bytes, ml_stream_t stream) {
+static int mask_matching_impl(const ml_dims* d, const ml_params* p, const float* mask_logits,
+                              const int64_t* mask_targets, const float* cls_logits,
+                              const int64_t* cls_targets, const float* num_masks_dev,
+                              int64_t* pred_to_gt, int64_t* pred_round, float* layer_means,
+                              float* sep_costs, float* saved, int32_t* dev_status, void* workspace,
+                              size_t workspace_bytes, ml_stream_t stream, cudaEvent_t loss_wait) {
     FwdPlan P;
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
@@ -747,9 +748,35 @@ int ml_mask_matching(const ml_dims* d, const ml_params* p, const float* mask_log
         la.cls_targets = cls_targets;
         la.void_status = dev_status;
     }
+    if (loss_wait) {  // e.g. the all-reduce that produces num_masks_dev
+        cudaError_t e = cudaStreamWaitEvent(st, loss_wait, 0);
+        if (e != cudaSuccess) return cuda_fail(e, "wait for loss_wait_event");
+    }
     loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
     ML_CHECK_LAUNCH("loss_fwd_kernel");
     return ML_OK;
+}
+
+int ml_mask_matching(const ml_dims* d, const ml_params* p, const float* mask_logits,
+                     const int64_t* mask_targets, const float* cls_logits, const int64_t* cls_targets,
+                     const float* num_masks_dev, int64_t* pred_to_gt, int64_t* pred_round,
+                     float* layer_means, float* sep_costs, float* saved, int32_t* dev_status,
+                     void* workspace, size_t workspace_bytes, ml_stream_t stream) {
+    return mask_matching_impl(d, p, mask_logits, mask_targets, cls_logits, cls_targets, num_masks_dev,
+                              pred_to_gt, pred_round, layer_means, sep_costs, saved, dev_status,
+                              workspace, workspace_bytes, stream, nullptr);
+}
+
+int ml_mask_matching_ex(const ml_dims* d, const ml_params* p, const float* mask_logits,
+                        const int64_t* mask_targets, const float* cls_logits,
+                        const int64_t* cls_targets, const float* num_masks_dev, int64_t* pred_to_gt,
+                        int64_t* pred_round, float* layer_means, float* sep_costs, float* saved,
+                        int32_t* dev_status, void* workspace, size_t workspace_bytes,
+                        ml_stream_t stream, ml_event_t loss_wait_event) {
+    return mask_matching_impl(d, p, mask_logits, mask_targets, cls_logits, cls_targets, num_masks_dev,
+                              pred_to_gt, pred_round, layer_means, sep_costs, saved, dev_status,
+                              workspace, workspace_bytes, stream,
+                              reinterpret_cast<cudaEvent_t>(loss_wait_event));
 }
 
 int ml_count_masks(const ml_dims* d, const ml_params* p, const int64_t* mask_targets,

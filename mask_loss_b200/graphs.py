@@ -60,6 +60,8 @@ class MatchingLossStep:
             self.allreduce_num_masks = False
         self.w = loss_weights
         self._wts = None
+        self._side = None
+        self._ev = None
         self.graph = None
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -95,7 +97,21 @@ class MatchingLossStep:
         if cl.dtype != torch.float32:
             raise RuntimeError("cls_logits must be float32")
         a = list(self.args)
-        if self.allreduce_num_masks:
+        ev = None
+        main = torch.cuda.current_stream()
+        if self.allreduce_num_masks and not self.sampled:
+            # GT count + all-reduce on a side stream: only the forward's matched-loss
+            # kernel waits for it, so the collective overlaps costs and solver
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=ml.device)
+                self._ev = torch.cuda.Event()
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                a[self.nm_slot] = parallel.global_num_masks(
+                    ops.count_masks(mt, ct.shape[1], int(a[4])))
+                self._ev.record(self._side)
+            ev = self._ev
+        elif self.allreduce_num_masks:
             a[self.nm_slot] = parallel.global_num_masks(ops.count_masks(mt, ct.shape[1], int(a[4])))
         L = ml.shape[0]
         if self._wts is None:
@@ -118,7 +134,9 @@ class MatchingLossStep:
             args, nm_dev = resolve_args(ml, mt, cl, ct, *a)
             p2g, prd, means, saved, _ = ops.mask_matching_ex(
                 ml, mt, cl, ct, *args, num_masks_dev=nm_dev, want_saved=True,
-                check_void_targets=True)
+                check_void_targets=True, loss_wait_event=ev)
+            if ev is not None:
+                main.wait_stream(self._side)  # join the side branch
             gm, gc = ops.mask_matching_backward(
                 wm, wd, wc, ml, mt, cl, ct, p2g, args[0], args[1], args[2], args[3], args[4],
                 args[5], args[6], args[8], args[9], args[10], args[13], args[14], args[15],

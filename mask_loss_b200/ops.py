@@ -210,14 +210,17 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
                      mask_gamma=0.0, mask_alpha=-1.0, cls_gamma=0.0, cls_alpha=-1.0,
                      void_class_index=-1, use_softmax_label_loss=False, normalize_uncertainty=True,
                      *, num_masks_dev: Optional[torch.Tensor] = None, want_saved: bool = False,
-                     want_costs: bool = False, check_void_targets: bool = False):
+                     want_costs: bool = False, check_void_targets: bool = False,
+                     loss_wait_event: Optional[torch.cuda.Event] = None):
     """``mask_matching`` plus the extras this implementation offers: a device
     ``num_masks_dev`` (fp32 scalar, e.g. after an all-reduce), the per-query
     statistics the backward can reuse (``saved``) and the cost slices.
 
     ``check_void_targets``: raise (deferred) if cls_targets holds
     void_class_index -- functions/mask/matching.py:180-181, checked on the
-    device.
+    device.  ``loss_wait_event``: the matched-loss kernel (the only reader
+    of ``num_masks_dev``) waits for it, so an all-reduce producing that count
+    on another stream overlaps the cost and solver kernels.
 
     Returns (pred_to_gt, pred_round, layer_means(3,L), saved or None, costs or None)."""
     check_status()
@@ -250,10 +253,18 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
     if num_masks_dev is not None:
         _check_input(num_masks_dev, "num_masks_dev")
         _check_dtype(num_masks_dev, torch.float32, "num_masks_dev")
-    _lib.check(lib.ml_mask_matching(
-        ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits),
-        _ptr(cls_targets), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd), _ptr(means), _ptr(costs),
-        _ptr(saved), _ptr(status), _ptr(ws), ws.numel(), _stream(dev)))
+    if loss_wait_event is not None:
+        _lib.check(lib.ml_mask_matching_ex(
+            ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets),
+            _ptr(cls_logits), _ptr(cls_targets), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd),
+            _ptr(means), _ptr(costs), _ptr(saved), _ptr(status), _ptr(ws), ws.numel(),
+            _stream(dev), ctypes.c_void_p(loss_wait_event.cuda_event)))
+    else:
+        _lib.check(lib.ml_mask_matching(
+            ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets),
+            _ptr(cls_logits), _ptr(cls_targets), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd),
+            _ptr(means), _ptr(costs), _ptr(saved), _ptr(status), _ptr(ws), ws.numel(),
+            _stream(dev)))
     _track_status(status)
     return p2g, prd, means, saved, costs
 
