@@ -930,9 +930,9 @@ int ml_mask_matching_sampled(const ml_dims* d, const ml_params* p, int64_t num_p
     LossArgs la = loss_args(P, p);
     la.pred_to_gt = pred_to_gt; la.sep = a.sep; la.qstat = a.qstat; la.rawI = a.rawI; la.rawT = a.rawT;
     la.num_masks_dev = num_masks_dev; la.saved = saved; la.layer_means = layer_means;
-    if (p->num_masks == -2.0) {  // auto: counted on the device, written to num_masks_dev
+    if (p->num_masks == -2.0) {  // auto: GT ids present in the full label maps
         la.auto_num_masks = 1;
-        la.totals = a.totals;
+        la.totals = a.present ? a.present : a.totals;
         la.num_masks_out = const_cast<float*>(num_masks_dev);
     }
     if (p->check_void_targets && la.has_void) {

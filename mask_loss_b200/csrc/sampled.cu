@@ -57,12 +57,29 @@ point_sort_kernel(const int64_t* __restrict__ targets, const float* __restrict__
     __syncthreads();
     const int seg = (P + kSortWarps - 1) / kSortWarps;
     const int s0 = min(P, warp * seg), s1 = min(P, s0 + seg);
-    for (int p = s0 + lane; p < s1; p += 32) {
-        const int64_t lab = point_label(tb, Ht, Wt, cb[2 * p], cb[2 * p + 1]);
-        if (lab >= 0 && lab < gt_total) atomicAdd(&pt[lab], 1);
-        const int key = label_to_col(lab, gt_total, bg) + 1;
-        keys[p] = key;
-        atomicAdd(&wcnt[warp * NB + key], 1);
+    // four points per lane in flight: coordinates, then the label gathers,
+    // then the counts (the atomics would otherwise serialise the loads)
+    for (int p0 = s0; p0 < s1; p0 += 4 * 32) {
+        float x[4], y[4];
+        int64_t lab[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int p = p0 + 32 * u + lane;
+            x[u] = p < s1 ? cb[2 * p] : 0.0f;
+            y[u] = p < s1 ? cb[2 * p + 1] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            lab[u] = p0 + 32 * u + lane < s1 ? point_label(tb, Ht, Wt, x[u], y[u]) : -1;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int p = p0 + 32 * u + lane;
+            if (p >= s1) continue;
+            if (lab[u] >= 0 && lab[u] < gt_total) atomicAdd(&pt[lab[u]], 1);
+            const int key = label_to_col(lab[u], gt_total, bg) + 1;
+            keys[p] = key;
+            atomicAdd(&wcnt[warp * NB + key], 1);
+        }
     }
     __syncthreads();
     // offsets: bucket-major, then warp order (fixed order -> stable, deterministic)

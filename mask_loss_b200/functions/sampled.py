@@ -60,9 +60,13 @@ def pairwise_dice_loss_sampling(logits, targets, smooth=1.0, background_index=No
 def resolve_sampled_args(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, inf_thresh,
                          num_masks, force_unmatched_class_to_background, K, assignment_strategy,
                          mask_focal_gamma, mask_focal_alpha, cls_focal_gamma, cls_focal_alpha,
-                         void_class_index=None, label_loss="sigmoid", align_corners=False):
+                         void_class_index=None, label_loss="sigmoid", align_corners=False,
+                         device=None):
     """Defaulting and validation of the sampled Function's scalar arguments.
-    Returns the op's positional arguments and the device num_masks (or None)."""
+    Returns the op's positional arguments and the device num_masks (or None).
+    ``num_masks="auto"``: the present non-background GT ids of the batch,
+    counted on ``device`` by the forward from its full-resolution label
+    histogram."""
     if assignment_strategy not in STRATEGIES:
         raise ValueError(f"Unknown assignment_strategy '{assignment_strategy}'.")
     softmax = (label_loss or "sigmoid").lower() == "softmax"
@@ -76,7 +80,10 @@ def resolve_sampled_args(smooth, sigmoid_scale, dice_scale, cls_scale, backgroun
     ca = ma if cls_focal_alpha is None else float(cls_focal_alpha)
     nm_dev = None
     nm = -1.0
-    if isinstance(num_masks, torch.Tensor):
+    if isinstance(num_masks, str) and num_masks == "auto":
+        nm_dev = torch.empty((), dtype=torch.float32, device=device)
+        nm = -2.0
+    elif isinstance(num_masks, torch.Tensor):
         nm_dev = num_masks.detach().reshape(()).to(torch.float32).contiguous()
     elif num_masks is not None:
         nm = float(num_masks)
@@ -106,7 +113,7 @@ class MaskMatchingSampledFunction(Function):
             smooth, sigmoid_scale, dice_scale, cls_scale, background_index, inf_thresh, num_masks,
             force_unmatched_class_to_background, K, assignment_strategy, mask_focal_gamma,
             mask_focal_alpha, cls_focal_gamma, cls_focal_alpha, void_class_index, label_loss,
-            align_corners)
+            align_corners, device=mask_logits.device)
         ml = mask_logits.contiguous()
         cl = cls_logits.contiguous().float()
         pc = point_coords.contiguous().float()

@@ -54,7 +54,7 @@ class MatchingLossStep:
         self.nm_slot = 6 if self.sampled else 9
         self.allreduce_num_masks = (isinstance(args[self.nm_slot], str) and
                                     args[self.nm_slot] == "allreduce")
-        if self.allreduce_num_masks and not self.sampled and not _multi_rank():
+        if self.allreduce_num_masks and not _multi_rank():
             # one rank: the count needs no collective, take it from the forward
             self.args[self.nm_slot] = "auto"
             self.allreduce_num_masks = False
@@ -120,7 +120,7 @@ class MatchingLossStep:
         wm, wd, wc = self._wts
         if self.sampled:
             pc = self.inputs["point_coords"]
-            args, nm_dev = resolve_sampled_args(*a)
+            args, nm_dev = resolve_sampled_args(*a, device=ml.device)
             p2g, prd, means, saved, _, fws = ops.mask_matching_sampled_ex(
                 ml, mt, cl, ct, pc, *args, num_masks_dev=nm_dev, want_saved=True,
                 want_workspace=True)

@@ -102,3 +102,23 @@ def test_sampled_backward_without_forward_workspace():
     b = ops.mask_matching_sampled_backward(g, g, g, *d, p2g, saved, *bargs)
     torch.testing.assert_close(a[0], b[0], rtol=1e-5, atol=1e-8)
     torch.testing.assert_close(a[1], b[1], rtol=0, atol=0)
+
+
+def test_sampled_auto_num_masks_counts_present_gts():
+    """num_masks="auto": the present non-background GT ids of the full label
+    maps (not of the points), the same as passing that count."""
+    ml, mt, cl, ct, pc, C = _case(11, torch.float32)
+    d = [t.to(DEV) for t in (ml, mt, cl, ct, pc)]
+    present = sum(int((torch.unique(mt[i]) > 0).sum()) for i in range(mt.shape[0]))
+
+    def run(nm):
+        x = d[0].clone().requires_grad_(True)
+        z = d[2].clone().requires_grad_(True)
+        p2g, prd, m, dd, c = F.MaskMatchingSampledFunction.apply(
+            x, d[1], z, d[3], d[4], 1.0, 5.0, 5.0, 2.0, 0, 1e30, nm, False, 1, "global", 0.0,
+            None, None, None, C - 1, "softmax")
+        (m + dd + c).sum().backward()
+        return torch.stack([m, dd, c]).detach(), x.grad, z.grad
+
+    for u, v in zip(run("auto"), run(float(present))):
+        torch.testing.assert_close(u, v, rtol=1e-6, atol=1e-9)
