@@ -140,6 +140,7 @@ __global__ void label_cost_kernel(const float* z_all, const int64_t* y_all, floa
 
 namespace mlb {
 constexpr int kSortWarps = 16;
+constexpr int kPointRowThreads = 512;  // block of the per-row point sample / gradient kernels
 constexpr size_t kRowMapMaxBytes = 96 * 1024;  // per-row maps staged in shared memory up to this
 constexpr int kMaxSortPoints = 40960;          // points per image (sort keys live in shared memory)
 size_t point_sort_smem(int P, int gout);

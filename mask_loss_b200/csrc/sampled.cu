@@ -230,6 +230,7 @@ __device__ __forceinline__ void point_sample_row_body(const T* __restrict__ logi
     __syncthreads();
     const float* cb = scoords + (int64_t)b * P * 2;
     float* out = zs + row * P;
+#pragma unroll 4
     for (int pos = threadIdx.x; pos < P; pos += blockDim.x) {
         const float2 c = reinterpret_cast<const float2*>(cb)[pos];
         const Taps tp = bilinear_taps(c.x, c.y, H, W, align != 0);
@@ -240,13 +241,13 @@ __device__ __forceinline__ void point_sample_row_body(const T* __restrict__ logi
     }
 }
 
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kPointRowThreads)
 point_sample_row_f32_kernel(const float* logits, const float* scoords, int B, int Q, int H, int W,
                             int P, int align, float* zs) {
     point_sample_row_body<float>(logits, scoords, B, Q, H, W, P, align, zs);
 }
 
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kPointRowThreads)
 point_sample_row_bf16_kernel(const __nv_bfloat16* logits, const float* scoords, int B, int Q, int H,
                              int W, int P, int align, float* zs) {
     point_sample_row_body<__nv_bfloat16>(logits, scoords, B, Q, H, W, P, align, zs);
@@ -357,6 +358,7 @@ __device__ __forceinline__ void point_grad_row_body(const LossArgs& a, const flo
     const float* cb = scoords + (int64_t)b * P * 2;
     const int32_t* cd = scodes + (int64_t)b * P;
     const float* z = zs + qi * P;
+#pragma unroll 4
     for (int pos = threadIdx.x; pos < P; pos += blockDim.x) {
         const float g = point_grad_value<FOC>(a, r, z[pos], cd[pos]);
         const float2 c = reinterpret_cast<const float2*>(cb)[pos];
@@ -369,22 +371,22 @@ __device__ __forceinline__ void point_grad_row_body(const LossArgs& a, const flo
     for (int i = threadIdx.x; i < HW; i += blockDim.x) out[i] = from_f32<TO>(gmap[i]);
 }
 
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kPointRowThreads)
 point_grad_row_f32_kernel(LossArgs a, const float* zs, const float* scoords, const int32_t* scodes,
                           int P, int align, float* grad) {
     point_grad_row_body<false, float>(a, zs, scoords, scodes, P, align, grad);
 }
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kPointRowThreads)
 point_grad_row_focal_f32_kernel(LossArgs a, const float* zs, const float* scoords,
                                 const int32_t* scodes, int P, int align, float* grad) {
     point_grad_row_body<true, float>(a, zs, scoords, scodes, P, align, grad);
 }
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kPointRowThreads)
 point_grad_row_bf16_kernel(LossArgs a, const float* zs, const float* scoords, const int32_t* scodes,
                            int P, int align, __nv_bfloat16* grad) {
     point_grad_row_body<false, __nv_bfloat16>(a, zs, scoords, scodes, P, align, grad);
 }
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kPointRowThreads)
 point_grad_row_focal_bf16_kernel(LossArgs a, const float* zs, const float* scoords,
                                  const int32_t* scodes, int P, int align, __nv_bfloat16* grad) {
     point_grad_row_body<true, __nv_bfloat16>(a, zs, scoords, scodes, P, align, grad);
@@ -426,13 +428,13 @@ cudaError_t launch_point_sample(int dtype, const void* logits, const float* scoo
             cudaError_t e = cudaFuncSetAttribute(point_sample_row_bf16_kernel,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) return e;
-            point_sample_row_bf16_kernel<<<(unsigned)rows, 256, smem, st>>>(
+            point_sample_row_bf16_kernel<<<(unsigned)rows, kPointRowThreads, smem, st>>>(
                 static_cast<const __nv_bfloat16*>(logits), scoords, B, Q, H, W, P, align, zs);
         } else {
             cudaError_t e = cudaFuncSetAttribute(point_sample_row_f32_kernel,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) return e;
-            point_sample_row_f32_kernel<<<(unsigned)rows, 256, smem, st>>>(
+            point_sample_row_f32_kernel<<<(unsigned)rows, kPointRowThreads, smem, st>>>(
                 static_cast<const float*>(logits), scoords, B, Q, H, W, P, align, zs);
         }
         return cudaGetLastError();
@@ -461,7 +463,7 @@ cudaError_t launch_point_grad(bool foc, int dtype, const LossArgs& la, const flo
     do {                                                                                         \
         cudaError_t e = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
         if (e != cudaSuccess) return e;                                                          \
-        K<<<(unsigned)rows, 256, smem, st>>>(la, zs, scoords, scodes, P, align, static_cast<T*>(grad_out)); \
+        K<<<(unsigned)rows, kPointRowThreads, smem, st>>>(la, zs, scoords, scodes, P, align, static_cast<T*>(grad_out)); \
     } while (0)
         if (dtype == 1) {
             if (foc) ML_PG(point_grad_row_focal_bf16_kernel, __nv_bfloat16);
