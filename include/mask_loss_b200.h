@@ -281,6 +281,45 @@ int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int6
                                       void* grad_mask_logits, float* grad_cls_logits,
                                       void* workspace, size_t workspace_bytes, ml_stream_t stream);
 
+/* ---------------------------------------------------------------------- */
+/* Standalone semantic losses of (L,B,C,H,W) fp32 logits against a         */
+/* (B,Ht,Wt) int64 label map with classes in [0,C) (Ht = s*H, Wt = s*W,     */
+/* s <= 16, C <= 2048; labels outside [0,C) count for no class).           */
+/* Replace forward/backward_sigmoid_ce_loss (src/cuda/sigmoid_ce.cu:207-332, */
+/* src/bindings.cpp:158-159) and forward/backward_dice_loss                 */
+/* (src/cuda/dice_loss.cu:159-288, src/bindings.cpp:161-162).  Sums are     */
+/* fixed-order (deterministic).                                              */
+/* ---------------------------------------------------------------------- */
+/* Workspace of the forwards (dice = 0: sigmoid CE, 1: dice). */
+size_t ml_semantic_workspace_size(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W,
+                                  int64_t Ht, int64_t Wt, int32_t dice);
+
+/* out (L,): scale * sum of (focal) BCE over b, c and target pixels /
+ * (num_masks * Ht * Wt).  alpha < 0 disables the alpha weights. */
+int ml_sigmoid_ce_forward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ht,
+                          int64_t Wt, const float* logits, const int64_t* targets,
+                          float num_masks, float scale, float gamma, float alpha, float* out,
+                          void* workspace, size_t workspace_bytes, ml_stream_t stream);
+
+/* grad_logits (L,B,C,H,W) from grad_out (L,). */
+int ml_sigmoid_ce_backward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ht,
+                           int64_t Wt, const float* grad_out, const float* logits,
+                           const int64_t* targets, float num_masks, float scale, float gamma,
+                           float alpha, float* grad_logits, ml_stream_t stream);
+
+/* out (L,): scale * sum over (b,c) of 1 - (2I+smooth)/(P+T+smooth) / num_masks;
+ * int_sum, p_sum, t_sum (L,B,C): I, P, T of every (l,b,c). */
+int ml_dice_forward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ht, int64_t Wt,
+                    const float* logits, const int64_t* targets, float smooth, float num_masks,
+                    float scale, float* out, float* int_sum, float* p_sum, float* t_sum,
+                    void* workspace, size_t workspace_bytes, ml_stream_t stream);
+
+/* grad_logits (L,B,C,H,W) from grad_out (L,) and the forward's I, P, T. */
+int ml_dice_backward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ht, int64_t Wt,
+                     const float* grad_out, const float* logits, const int64_t* targets,
+                     const float* int_sum, const float* p_sum, const float* t_sum, float smooth,
+                     float num_masks, float scale, float* grad_logits, ml_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1022,4 +1022,133 @@ size_t ml_sampled_backward_workspace_size(const ml_dims* d, const ml_params* p, 
            (logits_dtype == 1 && !rows_fit ? align256(sizeof(float) * LBQ * d->H * d->W) : 0) + 256;
 }
 
+
+// ---------------------------------------------------------------------------
+// Standalone semantic losses (src/cuda/sigmoid_ce.cu, src/cuda/dice_loss.cu).
+// ---------------------------------------------------------------------------
+static int sem_setup(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ht, int64_t Wt,
+                     SemArgs* a) {
+    if (L < 0 || B < 0 || C < 0) return fail(ML_ESHAPE, "negative dimension");
+    if (H <= 0 || W <= 0) return fail(ML_ESHAPE, "logits must have positive spatial size");
+    if (Ht % H != 0 || Wt % W != 0 || Ht / H != Wt / W)
+        return fail(ML_ESHAPE, "target size must be the same integer multiple of the logits size in both dimensions");
+    if (Ht / H > 16) return fail(ML_EUNSUPPORTED, "downsample factor above 16 is not supported");
+    if (C > 2048) return fail(ML_EUNSUPPORTED, "more than 2048 classes is not supported");
+    if (H * W >= (int64_t(1) << 31) || B > 65535 || L * B > (int64_t(1) << 30) ||
+        Ht * Wt >= (int64_t(1) << 31))
+        return fail(ML_EUNSUPPORTED, "dimension product exceeds the supported range");
+    *a = SemArgs{};
+    a->L = (int)L; a->B = (int)B; a->C = (int)C; a->H = (int)H; a->W = (int)W;
+    a->Ht = (int)Ht; a->Wt = (int)Wt; a->s = (int)(Ht / H);
+    return ML_OK;
+}
+
+static size_t sem_ws(const SemArgs& a, int dice) {
+    const size_t nblk = (size_t)sem_blocks(a);
+    size_t n = align256(sizeof(double) * ((size_t)a.L * a.B * nblk + (size_t)a.L * a.B + 1));
+    if (dice) {
+        n += align256(sizeof(float) * (size_t)a.L * a.B * nblk * 2 * a.C);
+        n += align256(sizeof(int32_t) * (size_t)a.B * nblk * a.C);
+    }
+    return n + 256;
+}
+
+static void sem_carve(SemArgs* a, void* ws, int dice) {
+    unsigned char* w = ws_base(ws);
+    const size_t nblk = (size_t)sem_blocks(*a);
+    a->part_d = reinterpret_cast<double*>(w);
+    w += align256(sizeof(double) * ((size_t)a->L * a->B * nblk + (size_t)a->L * a->B + 1));
+    if (dice) {
+        a->part_f = reinterpret_cast<float*>(w);
+        w += align256(sizeof(float) * (size_t)a->L * a->B * nblk * 2 * a->C);
+        a->part_t = reinterpret_cast<int32_t*>(w);
+    }
+}
+
+size_t ml_semantic_workspace_size(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ht,
+                                  int64_t Wt, int32_t dice) {
+    SemArgs a;
+    if (sem_setup(L, B, C, H, W, Ht, Wt, &a)) return 0;
+    return sem_ws(a, dice);
+}
+
+int ml_sigmoid_ce_forward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ht, int64_t Wt,
+                          const float* logits, const int64_t* targets, float num_masks, float scale,
+                          float gamma, float alpha, float* out, void* workspace,
+                          size_t workspace_bytes, ml_stream_t stream) {
+    SemArgs a;
+    int rc = sem_setup(L, B, C, H, W, Ht, Wt, &a);
+    if (rc) return rc;
+    if (gamma < 0.0f) return fail(ML_EINVAL, "focal_gamma must be non-negative");
+    if (alpha > 1.0f) return fail(ML_EINVAL, "alpha must be in [0, 1]");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (L == 0) return ML_OK;
+    if (B * C == 0) {  // the reference returns zeros for empty logits
+        cudaError_t e = cudaMemsetAsync(out, 0, sizeof(float) * (size_t)L, st);
+        return e == cudaSuccess ? ML_OK : cuda_fail(e, "memset out");
+    }
+    if ((rc = check_ws(workspace, workspace_bytes, sem_ws(a, 0)))) return rc;
+    a.logits = logits; a.targets = targets; a.num_masks = num_masks; a.scale = scale;
+    a.gamma = gamma; a.alpha = alpha; a.out = out;
+    sem_carve(&a, workspace, 0);
+    cudaError_t e = launch_sce_forward(a, st);
+    g_launches.fetch_add(2);
+    return e == cudaSuccess ? ML_OK : cuda_fail(e, "sigmoid_ce forward");
+}
+
+int ml_sigmoid_ce_backward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ht, int64_t Wt,
+                           const float* grad_out, const float* logits, const int64_t* targets,
+                           float num_masks, float scale, float gamma, float alpha, float* grad_logits,
+                           ml_stream_t stream) {
+    SemArgs a;
+    int rc = sem_setup(L, B, C, H, W, Ht, Wt, &a);
+    if (rc) return rc;
+    if (gamma < 0.0f) return fail(ML_EINVAL, "focal_gamma must be non-negative");
+    if (alpha > 1.0f) return fail(ML_EINVAL, "alpha must be in [0, 1]");
+    if (L * B * C == 0) return ML_OK;
+    a.logits = logits; a.targets = targets; a.num_masks = num_masks; a.scale = scale;
+    a.gamma = gamma; a.alpha = alpha; a.grad_out = grad_out; a.grad = grad_logits;
+    cudaError_t e = launch_sce_backward(a, reinterpret_cast<cudaStream_t>(stream));
+    g_launches.fetch_add(1);
+    return e == cudaSuccess ? ML_OK : cuda_fail(e, "sigmoid_ce backward");
+}
+
+int ml_dice_forward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ht, int64_t Wt,
+                    const float* logits, const int64_t* targets, float smooth, float num_masks,
+                    float scale, float* out, float* int_sum, float* p_sum, float* t_sum,
+                    void* workspace, size_t workspace_bytes, ml_stream_t stream) {
+    SemArgs a;
+    int rc = sem_setup(L, B, C, H, W, Ht, Wt, &a);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (L == 0) return ML_OK;
+    if (B * C == 0) {
+        cudaError_t e = cudaMemsetAsync(out, 0, sizeof(float) * (size_t)L, st);
+        return e == cudaSuccess ? ML_OK : cuda_fail(e, "memset out");
+    }
+    if ((rc = check_ws(workspace, workspace_bytes, sem_ws(a, 1)))) return rc;
+    a.logits = logits; a.targets = targets; a.smooth = smooth; a.num_masks = num_masks;
+    a.scale = scale; a.out = out; a.I = int_sum; a.P = p_sum; a.T = t_sum;
+    sem_carve(&a, workspace, 1);
+    cudaError_t e = launch_dice_forward(a, st);
+    g_launches.fetch_add(3);
+    return e == cudaSuccess ? ML_OK : cuda_fail(e, "dice forward");
+}
+
+int ml_dice_backward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64_t Ht, int64_t Wt,
+                     const float* grad_out, const float* logits, const int64_t* targets,
+                     const float* int_sum, const float* p_sum, const float* t_sum, float smooth,
+                     float num_masks, float scale, float* grad_logits, ml_stream_t stream) {
+    SemArgs a;
+    int rc = sem_setup(L, B, C, H, W, Ht, Wt, &a);
+    if (rc) return rc;
+    if (L * B * C == 0) return ML_OK;
+    a.logits = logits; a.targets = targets; a.smooth = smooth; a.num_masks = num_masks;
+    a.scale = scale; a.grad_out = grad_out; a.grad = grad_logits;
+    a.I = const_cast<float*>(int_sum); a.P = const_cast<float*>(p_sum); a.T = const_cast<float*>(t_sum);
+    cudaError_t e = launch_dice_backward(a, reinterpret_cast<cudaStream_t>(stream));
+    g_launches.fetch_add(1);
+    return e == cudaSuccess ? ML_OK : cuda_fail(e, "dice backward");
+}
+
 }  // extern "C"

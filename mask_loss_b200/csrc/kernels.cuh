@@ -155,3 +155,26 @@ cudaError_t launch_point_grad(bool foc, int dtype, const LossArgs& la, const flo
                               cudaStream_t st);
 cudaError_t launch_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t st);
 }  // namespace mlb
+
+namespace mlb {
+// Standalone semantic losses (semantic.cu).
+struct SemArgs {
+    int L, B, C, H, W, Ht, Wt, s;
+    const float* logits;     // (L,B,C,H,W)
+    const int64_t* targets;  // (B,Ht,Wt)
+    float num_masks, scale, gamma, alpha, smooth;
+    const float* grad_out;   // (L,) backward
+    float* out;              // (L,) forward
+    float* grad;             // (L,B,C,H,W) backward
+    float *I, *P, *T;        // (L,B,C) dice sums (forward out, backward in)
+    double* part_d;          // workspace: per-block / per-(l,b) double partials
+    float* part_f;           // workspace: dice per-block partials (L,B,nblk,2,C)
+    int32_t* part_t;         // workspace: dice per-block histograms (B,nblk,C)
+};
+int sem_blocks(const SemArgs& a);
+size_t dice_fwd_smem(int C);
+cudaError_t launch_sce_forward(SemArgs a, cudaStream_t st);
+cudaError_t launch_sce_backward(SemArgs a, cudaStream_t st);
+cudaError_t launch_dice_forward(SemArgs a, cudaStream_t st);
+cudaError_t launch_dice_backward(SemArgs a, cudaStream_t st);
+}  // namespace mlb

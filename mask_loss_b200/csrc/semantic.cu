@@ -1,0 +1,345 @@
+// semantic.cu -- standalone semantic losses over C class channels.
+//
+// Replaces forward/backward_sigmoid_ce_loss (src/cuda/sigmoid_ce.cu:13-332)
+// and forward/backward_dice_loss (src/cuda/dice_loss.cu:13-288): per-layer
+// BCE (optionally focal) and dice of (L,B,C,H,W) logits against a (B,H_t,W_t)
+// label map with classes in [0,C), every logit standing for an s x s block of
+// target pixels (nearest upsampling).
+//
+// Layout: one block per (image, 256 consecutive cells), one thread per cell.
+// A thread reads its cell's s*s labels once, keeps up to four (label, count)
+// pairs in registers (cells with more labels count on demand), then streams
+// the cell's L*C logits plane by plane -- coalesced across the block, each
+// logit read once.  All sums use fixed-order reductions (per-block partials,
+// then a finalize pass), so the results are deterministic; the reference
+// accumulates with atomics.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mlb {
+
+namespace {
+
+constexpr int kSemThreads = 256;
+
+struct CellLabels {
+    int lab[4];
+    int cnt[4];
+    int n;
+    bool over;  // more than four labels in the cell: count per class on demand
+};
+
+ML_INLINE CellLabels cell_labels(const int64_t* tb, int cell, int W, int Wt, int s, int C) {
+    CellLabels r;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { r.lab[k] = -1; r.cnt[k] = 0; }
+    r.n = 0;
+    r.over = false;
+    const int ci = cell / W, cj = cell - ci * W;
+    const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
+    for (int dy = 0; dy < s; ++dy)
+        for (int dx = 0; dx < s; ++dx) {
+            const int64_t v = r0[(int64_t)dy * Wt + dx];
+            if (v < 0 || v >= C) continue;  // out-of-range labels count for no class
+            const int lab = (int)v;
+            bool found = false;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (k < r.n && r.lab[k] == lab) { ++r.cnt[k]; found = true; }
+            if (found) continue;
+            if (r.n < 4) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (k == r.n) { r.lab[k] = lab; r.cnt[k] = 1; }
+                ++r.n;
+            } else {
+                r.over = true;
+            }
+        }
+    return r;
+}
+
+// Pixels of class c in the cell.
+ML_INLINE float class_count(const CellLabels& cl, int c, const int64_t* tb, int cell, int W, int Wt,
+                            int s) {
+    if (!cl.over) {
+        int n = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) n += cl.lab[k] == c ? cl.cnt[k] : 0;
+        return (float)n;
+    }
+    const int ci = cell / W, cj = cell - ci * W;
+    const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
+    int n = 0;
+    for (int dy = 0; dy < s; ++dy)
+        for (int dx = 0; dx < s; ++dx) n += r0[(int64_t)dy * Wt + dx] == c;
+    return (float)n;
+}
+
+ML_INLINE double block_sum_d(double v, double* sh /* [32] */) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    double t = 0.0;
+    if (threadIdx.x == 0)
+        for (int w = 0; w < nw; ++w) t += sh[w];
+    return t;  // valid in thread 0
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Sigmoid CE forward: per (l, b, block) the sum over the block's cells and all
+// classes of  alpha+ * m+ * softplus(-x) * n_c + alpha- * m- * softplus(x) * (s^2 - n_c)
+// (src/cuda/sigmoid_ce.cu:13-114).  part_d: (L, B, nblk) double.
+// ---------------------------------------------------------------------------
+template <bool FOC>
+__device__ __forceinline__ void sce_fwd_body(const SemArgs& a) {
+    __shared__ double sh[32];
+    const int b = blockIdx.y;
+    const int HW = a.H * a.W;
+    const int cell = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool valid = cell < HW;
+    const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
+    CellLabels cl;
+    if (valid) cl = cell_labels(tb, cell, a.W, a.Wt, a.s, a.C);
+    const Focal f = make_focal(a.gamma, a.alpha);
+    const float N2 = (float)(a.s * a.s);
+    for (int l = 0; l < a.L; ++l) {
+        float acc = 0.0f;
+        if (valid) {
+            const float* x = a.logits + ((int64_t)l * a.B + b) * a.C * HW + cell;
+#pragma unroll 4
+            for (int c = 0; c < a.C; ++c) {
+                const Elem e = elem(__ldcs(x + (int64_t)c * HW));
+                const float n = class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
+                const float lp = FOC ? focal_pos(f, e) : f.alpha_pos * e.pos;
+                const float ln = FOC ? focal_neg(f, e) : f.alpha_neg * e.neg;
+                acc += lp * n + ln * (N2 - n);
+            }
+        }
+        const double t = block_sum_d((double)acc, sh);
+        if (threadIdx.x == 0) a.part_d[((int64_t)l * a.B + b) * gridDim.x + blockIdx.x] = t;
+    }
+}
+
+__global__ void __launch_bounds__(kSemThreads) sce_fwd_kernel(SemArgs a) { sce_fwd_body<false>(a); }
+__global__ void __launch_bounds__(kSemThreads) sce_fwd_focal_kernel(SemArgs a) { sce_fwd_body<true>(a); }
+
+// out[l] = scale * sum_{b,blocks} part / (num_masks * H_t * W_t); grid = L.
+__global__ void __launch_bounds__(kSemThreads) sce_finalize_kernel(SemArgs a, int nblk) {
+    __shared__ double sh[32];
+    const int l = blockIdx.x;
+    double v = 0.0;
+    const int64_t n = (int64_t)a.B * nblk;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) v += a.part_d[(int64_t)l * n + i];
+    const double t = block_sum_d(v, sh);
+    if (threadIdx.x == 0)
+        a.out[l] = (float)(t * (double)a.scale) / (a.num_masks * (float)a.Ht * (float)a.Wt);
+}
+
+// ---------------------------------------------------------------------------
+// Sigmoid CE backward (src/cuda/sigmoid_ce.cu:116-205): elementwise
+// g = -a+ n m+ (gamma p ce+ + 1 - p) + a- (s^2 - n) m- (gamma (1-p) ce- + p),
+// times grad_out[l] * scale / (num_masks * H_t * W_t).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kSemThreads) sce_bwd_kernel(SemArgs a) {
+    const int b = blockIdx.y;
+    const int HW = a.H * a.W;
+    const int cell = blockIdx.x * blockDim.x + threadIdx.x;
+    if (cell >= HW) return;
+    const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
+    const CellLabels cl = cell_labels(tb, cell, a.W, a.Wt, a.s, a.C);
+    const Focal f = make_focal(a.gamma, a.alpha);
+    const float N2 = (float)(a.s * a.s);
+    const float norm = a.scale / (a.num_masks * (float)a.Ht * (float)a.Wt);
+    for (int l = 0; l < a.L; ++l) {
+        const float go = a.grad_out[l] * norm;
+        const int64_t base = ((int64_t)l * a.B + b) * a.C * HW + cell;
+#pragma unroll 4
+        for (int c = 0; c < a.C; ++c) {
+            const Elem e = elem(__ldcs(a.logits + base + (int64_t)c * HW));
+            const float n = class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
+            const float om = 1.0f - e.p;
+            const float mp = f.use_gamma ? __powf(om, f.gamma) : 1.0f;
+            const float mn = f.use_gamma ? __powf(e.p, f.gamma) : 1.0f;
+            const float gp = -f.alpha_pos * n * mp * (f.gamma * e.p * e.pos + om);
+            const float gn = f.alpha_neg * (N2 - n) * mn * (f.gamma * om * e.neg + e.p);
+            __stcs(a.grad + base + (int64_t)c * HW, (gp + gn) * go);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Dice forward (src/cuda/dice_loss.cu:13-82): per (l,b,c) the block's partial
+// I = sum p n_c and sum p (P = s^2 * sum p), and per (b,c) the block's label
+// histogram (T).  Dynamic shared memory: (nwarps * 2 + 1) * C words.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kSemThreads) dice_fwd_kernel(SemArgs a) {
+    extern __shared__ float dsm[];
+    const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int C = a.C;
+    float* ws = dsm;                                               // [nw][2][C]
+    int* hist = reinterpret_cast<int*>(dsm + (size_t)nw * 2 * C);  // [C]
+    const int b = blockIdx.y;
+    const int HW = a.H * a.W;
+    const int nblk = gridDim.x;
+    const int cell = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool valid = cell < HW;
+    const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) hist[c] = 0;
+    __syncthreads();
+    CellLabels cl;
+    if (valid) {
+        cl = cell_labels(tb, cell, a.W, a.Wt, a.s, C);
+        if (!cl.over) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (k < cl.n) atomicAdd(&hist[cl.lab[k]], cl.cnt[k]);
+        } else {
+            const int ci = cell / a.W, cj = cell - ci * a.W;
+            const int64_t* r0 = tb + (int64_t)(ci * a.s) * a.Wt + (int64_t)cj * a.s;
+            for (int dy = 0; dy < a.s; ++dy)
+                for (int dx = 0; dx < a.s; ++dx) {
+                    const int64_t v = r0[(int64_t)dy * a.Wt + dx];
+                    if (v >= 0 && v < C) atomicAdd(&hist[(int)v], 1);
+                }
+        }
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x)
+        a.part_t[((int64_t)b * nblk + blockIdx.x) * C + c] = hist[c];
+    for (int l = 0; l < a.L; ++l) {
+        const float* x = a.logits + ((int64_t)l * a.B + b) * C * HW + cell;
+        for (int c = 0; c < C; ++c) {
+            float pi = 0.0f, pp = 0.0f;
+            if (valid) {
+                const float p = elem(__ldcs(x + (int64_t)c * HW)).p;
+                pi = p * class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
+                pp = p;
+            }
+            pi = warp_sum(pi);
+            pp = warp_sum(pp);
+            if (lane == 0) { ws[(warp * 2) * C + c] = pi; ws[(warp * 2 + 1) * C + c] = pp; }
+        }
+        __syncthreads();
+        const int64_t o = (((int64_t)l * a.B + b) * nblk + blockIdx.x) * C;
+        for (int c = threadIdx.x; c < C; c += blockDim.x) {
+            float si = 0.0f, sp = 0.0f;
+            for (int w = 0; w < nw; ++w) { si += ws[(w * 2) * C + c]; sp += ws[(w * 2 + 1) * C + c]; }
+            a.part_f[2 * o + c] = si;
+            a.part_f[2 * o + C + c] = sp;
+        }
+        __syncthreads();
+    }
+}
+
+// I, P, T per (l,b,c) and the per-(l,b) sum of 1 - dice; grid = L*B.
+__global__ void __launch_bounds__(kSemThreads) dice_reduce_kernel(SemArgs a, int nblk) {
+    __shared__ double sh[32];
+    const int lb = blockIdx.x, b = lb % a.B;
+    const int C = a.C;
+    const float N2 = (float)(a.s * a.s);
+    double loss = 0.0;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float I = 0.0f, P = 0.0f;
+        int T = 0;
+        for (int k = 0; k < nblk; ++k) {
+            const int64_t o = ((int64_t)lb * nblk + k) * C;
+            I += a.part_f[2 * o + c];
+            P += a.part_f[2 * o + C + c];
+            T += a.part_t[((int64_t)b * nblk + k) * C + c];
+        }
+        P *= N2;
+        const float Tf = (float)T;
+        a.I[(int64_t)lb * C + c] = I;
+        a.P[(int64_t)lb * C + c] = P;
+        a.T[(int64_t)lb * C + c] = Tf;
+        const float dice = (2.0f * I + a.smooth) / (P + Tf + a.smooth);
+        loss += (double)(1.0f - dice);
+    }
+    const double t = block_sum_d(loss, sh);
+    if (threadIdx.x == 0) a.part_d[lb] = t;
+}
+
+// out[l] = scale * sum_b part[l,b] / num_masks; one block.
+__global__ void dice_finalize_kernel(SemArgs a) {
+    for (int l = threadIdx.x; l < a.L; l += blockDim.x) {
+        double t = 0.0;
+        for (int b = 0; b < a.B; ++b) t += a.part_d[(int64_t)l * a.B + b];
+        a.out[l] = (float)t / a.num_masks * a.scale;
+    }
+}
+
+// Dice backward (src/cuda/dice_loss.cu:84-157): elementwise
+// -grad_out[l] * scale / num_masks * (2 n (P+T+smooth) - s^2 (2I+smooth)) / den^2 * p(1-p).
+__global__ void __launch_bounds__(kSemThreads) dice_bwd_kernel(SemArgs a) {
+    const int b = blockIdx.y;
+    const int HW = a.H * a.W;
+    const int cell = blockIdx.x * blockDim.x + threadIdx.x;
+    if (cell >= HW) return;
+    const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
+    const CellLabels cl = cell_labels(tb, cell, a.W, a.Wt, a.s, a.C);
+    const float N2 = (float)(a.s * a.s);
+    for (int l = 0; l < a.L; ++l) {
+        const float go = -a.grad_out[l] / a.num_masks * a.scale;
+        const int64_t lb = (int64_t)l * a.B + b;
+        const int64_t base = lb * a.C * HW + cell;
+#pragma unroll 4
+        for (int c = 0; c < a.C; ++c) {
+            const float p = elem(__ldcs(a.logits + base + (int64_t)c * HW)).p;
+            const float n = class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
+            const float I = a.I[lb * a.C + c], P = a.P[lb * a.C + c], T = a.T[lb * a.C + c];
+            const float den = P + T + a.smooth;
+            const float d = (2.0f * n * den - N2 * (2.0f * I + a.smooth)) / (den * den);
+            __stcs(a.grad + base + (int64_t)c * HW, go * d * (p * (1.0f - p)));
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers (non-template entry points called from capi.cu).
+// ---------------------------------------------------------------------------
+int sem_blocks(const SemArgs& a) { return (a.H * a.W + kSemThreads - 1) / kSemThreads; }
+
+cudaError_t launch_sce_forward(SemArgs a, cudaStream_t st) {
+    const int nblk = sem_blocks(a);
+    dim3 g(nblk, a.B);
+    if (a.gamma > 0.0f) sce_fwd_focal_kernel<<<g, kSemThreads, 0, st>>>(a);
+    else sce_fwd_kernel<<<g, kSemThreads, 0, st>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    sce_finalize_kernel<<<a.L, kSemThreads, 0, st>>>(a, nblk);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_sce_backward(SemArgs a, cudaStream_t st) {
+    sce_bwd_kernel<<<dim3(sem_blocks(a), a.B), kSemThreads, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+size_t dice_fwd_smem(int C) { return sizeof(float) * ((size_t)(kSemThreads / 32) * 2 + 1) * C; }
+
+cudaError_t launch_dice_forward(SemArgs a, cudaStream_t st) {
+    const int nblk = sem_blocks(a);
+    const size_t smem = dice_fwd_smem(a.C);
+    cudaError_t e = cudaFuncSetAttribute(dice_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    dice_fwd_kernel<<<dim3(nblk, a.B), kSemThreads, smem, st>>>(a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    dice_reduce_kernel<<<a.L * a.B, kSemThreads, 0, st>>>(a, nblk);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    dice_finalize_kernel<<<1, 128, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dice_backward(SemArgs a, cudaStream_t st) {
+    dice_bwd_kernel<<<dim3(sem_blocks(a), a.B), kSemThreads, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace mlb

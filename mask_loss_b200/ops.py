@@ -405,19 +405,82 @@ def forward_pw_softmax_label_loss(logits, targets, background_index=-1, scale=1.
                        "pairwise_softmax_label_loss_forward")
 
 
-def _not_built(name):
-    def fn(*args, **kwargs):
-        raise NotImplementedError(
-            f"mask_loss_b200: {name} (standalone semantic loss, not on the matching path) "
-            "is not implemented in this build")
-    fn.__name__ = name
-    return fn
+def _sem_shape(logits, targets):
+    _check_input(logits, "logits")
+    _check_input(targets, "targets")
+    _check_dtype(logits, torch.float32, "logits")
+    _check_dtype(targets, torch.int64, "targets")
+    if logits.dim() != 5 or targets.dim() != 3:
+        raise RuntimeError("logits must be (L,B,C,H,W) and targets (B,H_t,W_t)")
+    if logits.device != targets.device:
+        raise RuntimeError("logits and targets must be on the same device")
+    L, B, C, H, W = logits.shape
+    if targets.shape[0] != B:
+        raise RuntimeError("Batch size mismatch between logits and targets")
+    return (L, B, C, H, W, targets.shape[1], targets.shape[2])
 
 
-forward_sigmoid_ce_loss = _not_built("forward_sigmoid_ce_loss")
-backward_sigmoid_ce_loss = _not_built("backward_sigmoid_ce_loss")
-forward_dice_loss = _not_built("forward_dice_loss")
-backward_dice_loss = _not_built("backward_dice_loss")
+def forward_sigmoid_ce_loss(logits, targets, num_masks, scale=1.0, gamma=0.0, alpha=-1.0):
+    """(L,) per-layer (focal) sigmoid BCE, src/cuda/sigmoid_ce.cu:207-267."""
+    shp = _sem_shape(logits, targets)
+    lib = _lib_handle()
+    out = torch.zeros(shp[0], dtype=torch.float32, device=logits.device)
+    nbytes = lib.ml_semantic_workspace_size(*shp, 0)
+    if nbytes == 0:
+        raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
+    ws = _workspace(nbytes, logits.device)
+    _lib.check(lib.ml_sigmoid_ce_forward(*shp, _ptr(logits), _ptr(targets), float(num_masks),
+                                         float(scale), float(gamma), float(alpha), _ptr(out),
+                                         _ptr(ws), ws.numel(), _stream(logits.device)))
+    return out
+
+
+def backward_sigmoid_ce_loss(grad_out, logits, targets, num_masks, scale=1.0, gamma=0.0,
+                             alpha=-1.0):
+    """dL/dlogits of forward_sigmoid_ce_loss, src/cuda/sigmoid_ce.cu:269-332."""
+    shp = _sem_shape(logits, targets)
+    go = grad_out.contiguous().float()
+    _check_input(go, "grad_out")
+    grad = torch.empty_like(logits)
+    _lib.check(_lib_handle().ml_sigmoid_ce_backward(
+        *shp, _ptr(go), _ptr(logits), _ptr(targets), float(num_masks), float(scale), float(gamma),
+        float(alpha), _ptr(grad), _stream(logits.device)))
+    return grad
+
+
+def forward_dice_loss(logits, targets, smooth, num_masks, scale=1.0):
+    """[loss (L,), int_sum, p_sum, t_sum (L,B,C)], src/cuda/dice_loss.cu:159-223."""
+    shp = _sem_shape(logits, targets)
+    L, B, C = shp[:3]
+    lib = _lib_handle()
+    dev = logits.device
+    out = torch.zeros(L, dtype=torch.float32, device=dev)
+    I = torch.zeros((L, B, C), dtype=torch.float32, device=dev)
+    P = torch.zeros((L, B, C), dtype=torch.float32, device=dev)
+    T = torch.zeros((L, B, C), dtype=torch.float32, device=dev)
+    nbytes = lib.ml_semantic_workspace_size(*shp, 1)
+    if nbytes == 0:
+        raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
+    ws = _workspace(nbytes, dev)
+    _lib.check(lib.ml_dice_forward(*shp, _ptr(logits), _ptr(targets), float(smooth),
+                                   float(num_masks), float(scale), _ptr(out), _ptr(I), _ptr(P),
+                                   _ptr(T), _ptr(ws), ws.numel(), _stream(dev)))
+    return [out, I, P, T]
+
+
+def backward_dice_loss(grad_out, logits, targets, int_sum, p_sum, t_sum, smooth, num_masks,
+                       scale=1.0):
+    """dL/dlogits of forward_dice_loss, src/cuda/dice_loss.cu:225-288."""
+    shp = _sem_shape(logits, targets)
+    go = grad_out.contiguous().float()
+    sums = [t.contiguous().float() for t in (int_sum, p_sum, t_sum)]
+    for t, n in zip([go] + sums, ("grad_out", "int_sum", "p_sum", "t_sum")):
+        _check_input(t, n)
+    grad = torch.empty_like(logits)
+    _lib.check(_lib_handle().ml_dice_backward(
+        *shp, _ptr(go), _ptr(logits), _ptr(targets), _ptr(sums[0]), _ptr(sums[1]), _ptr(sums[2]),
+        float(smooth), float(num_masks), float(scale), _ptr(grad), _stream(logits.device)))
+    return grad
 
 
 # ---------------------------------------------------------------------------

@@ -101,8 +101,10 @@ def test_function_argument_validation():
         F.MaskMatchingFunction.apply(*base, None, "hinge")
 
 
-def test_not_built_semantic_losses_raise():
-    with pytest.raises(NotImplementedError):
-        ops.forward_sigmoid_ce_loss(None, None, 1.0)
-    with pytest.raises(NotImplementedError):
-        ops.backward_dice_loss()
+def test_semantic_losses_reject_cpu_tensors():
+    """The semantic ops run on the GPU only (no CPU fallback)."""
+    import torch
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.forward_sigmoid_ce_loss(torch.zeros(1, 1, 2, 4, 4), torch.zeros(1, 4, 4, dtype=torch.long), 1.0)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.forward_dice_loss(torch.zeros(1, 1, 2, 4, 4), torch.zeros(1, 4, 4, dtype=torch.long), 1.0, 1.0)
