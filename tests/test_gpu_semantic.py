@@ -91,4 +91,4 @@ def test_semantic_deterministic_and_edges():
     assert torch.equal(ops.forward_sigmoid_ce_loss(e, td_, 1.0), torch.zeros(2, device=DEV))
     assert torch.equal(ops.forward_dice_loss(e, td_, 1.0, 1.0)[0], torch.zeros(2, device=DEV))
     with pytest.raises(RuntimeError, match="integer multiple"):
-        ops.forward_sigmoid_ce_loss(xd_, td_[:, :23], 1.0)
+        ops.forward_sigmoid_ce_loss(xd_, td_[:, :23].contiguous(), 1.0)
