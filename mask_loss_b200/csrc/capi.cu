@@ -1040,27 +1040,28 @@ static int sem_setup(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int6
     *a = SemArgs{};
     a->L = (int)L; a->B = (int)B; a->C = (int)C; a->H = (int)H; a->W = (int)W;
     a->Ht = (int)Ht; a->Wt = (int)Wt; a->s = (int)(Ht / H);
+    a->cps = a->C; a->ncs = 1;
     return ML_OK;
 }
 
 static size_t sem_ws(const SemArgs& a, int dice) {
-    const size_t nblk = (size_t)sem_blocks(a);
-    size_t n = align256(sizeof(double) * ((size_t)a.L * a.B * nblk + (size_t)a.L * a.B + 1));
+    const size_t nblk = (size_t)sem_blocks(a), dblk = (size_t)dice_blocks(a);
+    size_t n = align256(sizeof(double) * ((size_t)a.L * a.B * a.ncs * nblk + (size_t)a.L * a.B + 1));
     if (dice) {
-        n += align256(sizeof(float) * (size_t)a.L * a.B * nblk * 2 * a.C);
-        n += align256(sizeof(int32_t) * (size_t)a.B * nblk * a.C);
+        n += align256(sizeof(float) * (size_t)a.L * a.B * dblk * 2 * a.C);
+        n += align256(sizeof(int32_t) * (size_t)a.B * dblk * a.C);
     }
     return n + 256;
 }
 
 static void sem_carve(SemArgs* a, void* ws, int dice) {
     unsigned char* w = ws_base(ws);
-    const size_t nblk = (size_t)sem_blocks(*a);
+    const size_t nblk = (size_t)sem_blocks(*a), dblk = (size_t)dice_blocks(*a);
     a->part_d = reinterpret_cast<double*>(w);
-    w += align256(sizeof(double) * ((size_t)a->L * a->B * nblk + (size_t)a->L * a->B + 1));
+    w += align256(sizeof(double) * ((size_t)a->L * a->B * a->ncs * nblk + (size_t)a->L * a->B + 1));
     if (dice) {
         a->part_f = reinterpret_cast<float*>(w);
-        w += align256(sizeof(float) * (size_t)a->L * a->B * nblk * 2 * a->C);
+        w += align256(sizeof(float) * (size_t)a->L * a->B * dblk * 2 * a->C);
         a->part_t = reinterpret_cast<int32_t*>(w);
     }
 }
@@ -1069,6 +1070,7 @@ size_t ml_semantic_workspace_size(int64_t L, int64_t B, int64_t C, int64_t H, in
                                   int64_t Wt, int32_t dice) {
     SemArgs a;
     if (sem_setup(L, B, C, H, W, Ht, Wt, &a)) return 0;
+    sem_slices(&a, dice ? dice_blocks(a) : sem_blocks(a));
     return sem_ws(a, dice);
 }
 
@@ -1079,6 +1081,7 @@ int ml_sigmoid_ce_forward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W,
     SemArgs a;
     int rc = sem_setup(L, B, C, H, W, Ht, Wt, &a);
     if (rc) return rc;
+    sem_slices(&a, sem_blocks(a));
     if (gamma < 0.0f) return fail(ML_EINVAL, "focal_gamma must be non-negative");
     if (alpha > 1.0f) return fail(ML_EINVAL, "alpha must be in [0, 1]");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -1103,6 +1106,7 @@ int ml_sigmoid_ce_backward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W
     SemArgs a;
     int rc = sem_setup(L, B, C, H, W, Ht, Wt, &a);
     if (rc) return rc;
+    sem_slices(&a, sem_blocks(a));
     if (gamma < 0.0f) return fail(ML_EINVAL, "focal_gamma must be non-negative");
     if (alpha > 1.0f) return fail(ML_EINVAL, "alpha must be in [0, 1]");
     if (L * B * C == 0) return ML_OK;
@@ -1120,6 +1124,7 @@ int ml_dice_forward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int64
     SemArgs a;
     int rc = sem_setup(L, B, C, H, W, Ht, Wt, &a);
     if (rc) return rc;
+    sem_slices(&a, dice_blocks(a));
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (L == 0) return ML_OK;
     if (B * C == 0) {
@@ -1142,6 +1147,7 @@ int ml_dice_backward(int64_t L, int64_t B, int64_t C, int64_t H, int64_t W, int6
     SemArgs a;
     int rc = sem_setup(L, B, C, H, W, Ht, Wt, &a);
     if (rc) return rc;
+    sem_slices(&a, sem_blocks(a));
     if (L * B * C == 0) return ML_OK;
     a.logits = logits; a.targets = targets; a.smooth = smooth; a.num_masks = num_masks;
     a.scale = scale; a.grad_out = grad_out; a.grad = grad_logits;

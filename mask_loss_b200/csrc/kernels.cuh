@@ -160,6 +160,7 @@ namespace mlb {
 // Standalone semantic losses (semantic.cu).
 struct SemArgs {
     int L, B, C, H, W, Ht, Wt, s;
+    int cps, ncs;            // classes per slice, class slices (grid.z)
     const float* logits;     // (L,B,C,H,W)
     const int64_t* targets;  // (B,Ht,Wt)
     float num_masks, scale, gamma, alpha, smooth;
@@ -172,7 +173,9 @@ struct SemArgs {
     int32_t* part_t;         // workspace: dice per-block histograms (B,nblk,C)
 };
 int sem_blocks(const SemArgs& a);
-size_t dice_fwd_smem(int C);
+int dice_blocks(const SemArgs& a);
+void sem_slices(SemArgs* a, int blocks_per_slice);
+size_t dice_fwd_smem(int C, int cps);
 cudaError_t launch_sce_forward(SemArgs a, cudaStream_t st);
 cudaError_t launch_sce_backward(SemArgs a, cudaStream_t st);
 cudaError_t launch_dice_forward(SemArgs a, cudaStream_t st);

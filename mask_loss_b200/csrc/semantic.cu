@@ -6,13 +6,17 @@
 // label map with classes in [0,C), every logit standing for an s x s block of
 // target pixels (nearest upsampling).
 //
-// Layout: one block per (image, 256 consecutive cells), one thread per cell.
-// A thread reads its cell's s*s labels once, keeps up to four (label, count)
-// pairs in registers (cells with more labels count on demand), then streams
-// the cell's L*C logits plane by plane -- coalesced across the block, each
-// logit read once.  All sums use fixed-order reductions (per-block partials,
-// then a finalize pass), so the results are deterministic; the reference
-// accumulates with atomics.
+// Layout: one block per (image, run of consecutive cells, slice of classes),
+// one thread per cell (four for the dice forward, which amortises its warp
+// sums over them).  A thread reads its cell's s*s labels once, keeps up to
+// four (label, count) pairs in registers (cells with more labels count on
+// demand), then streams the cell's logits of its class slice plane by plane
+// -- coalesced across the block, each logit read once.  The class slices give
+// the grid enough blocks to keep HBM busy at a few images.  All sums use
+// fixed-order reductions (per-block partials, then a finalize pass), so the
+// results are deterministic; the reference accumulates with atomics.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -29,33 +33,60 @@ struct CellLabels {
     bool over;  // more than four labels in the cell: count per class on demand
 };
 
-ML_INLINE CellLabels cell_labels(const int64_t* tb, int cell, int W, int Wt, int s, int C) {
+ML_INLINE void add_label(CellLabels& r, int64_t v, int C) {
+    if (v < 0 || v >= C) return;  // out-of-range labels count for no class
+    const int lab = (int)v;
+    bool found = false;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        if (k < r.n && r.lab[k] == lab) { ++r.cnt[k]; found = true; }
+    if (found) return;
+    if (r.n < 4) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if (k == r.n) { r.lab[k] = lab; r.cnt[k] = 1; }
+        ++r.n;
+    } else {
+        r.over = true;
+    }
+}
+
+ML_INLINE CellLabels empty_labels() {
     CellLabels r;
 #pragma unroll
     for (int k = 0; k < 4; ++k) { r.lab[k] = -1; r.cnt[k] = 0; }
     r.n = 0;
     r.over = false;
+    return r;
+}
+
+// Small fixed factors: all S*S label loads are issued before any is used.
+template <int S>
+ML_INLINE CellLabels cell_labels_t(const int64_t* r0, int Wt, int C) {
+    int64_t v[S * S];
+#pragma unroll
+    for (int dy = 0; dy < S; ++dy)
+#pragma unroll
+        for (int dx = 0; dx < S; ++dx) v[dy * S + dx] = r0[(int64_t)dy * Wt + dx];
+    CellLabels r = empty_labels();
+#pragma unroll
+    for (int k = 0; k < S * S; ++k) add_label(r, v[k], C);
+    return r;
+}
+
+ML_INLINE CellLabels cell_labels(const int64_t* tb, int cell, int W, int Wt, int s, int C) {
     const int ci = cell / W, cj = cell - ci * W;
     const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
+    switch (s) {
+        case 1: return cell_labels_t<1>(r0, Wt, C);
+        case 2: return cell_labels_t<2>(r0, Wt, C);
+        case 3: return cell_labels_t<3>(r0, Wt, C);
+        case 4: return cell_labels_t<4>(r0, Wt, C);
+        default: break;
+    }
+    CellLabels r = empty_labels();
     for (int dy = 0; dy < s; ++dy)
-        for (int dx = 0; dx < s; ++dx) {
-            const int64_t v = r0[(int64_t)dy * Wt + dx];
-            if (v < 0 || v >= C) continue;  // out-of-range labels count for no class
-            const int lab = (int)v;
-            bool found = false;
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                if (k < r.n && r.lab[k] == lab) { ++r.cnt[k]; found = true; }
-            if (found) continue;
-            if (r.n < 4) {
-#pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (k == r.n) { r.lab[k] = lab; r.cnt[k] = 1; }
-                ++r.n;
-            } else {
-                r.over = true;
-            }
-        }
+        for (int dx = 0; dx < s; ++dx) add_label(r, r0[(int64_t)dy * Wt + dx], C);
     return r;
 }
 
@@ -94,7 +125,7 @@ ML_INLINE double block_sum_d(double v, double* sh /* [32] */) {
 // ---------------------------------------------------------------------------
 // Sigmoid CE forward: per (l, b, block) the sum over the block's cells and all
 // classes of  alpha+ * m+ * softplus(-x) * n_c + alpha- * m- * softplus(x) * (s^2 - n_c)
-// (src/cuda/sigmoid_ce.cu:13-114).  part_d: (L, B, nblk) double.
+// (src/cuda/sigmoid_ce.cu:13-114).  part_d: (L, B, ncs, nblk) double.
 // ---------------------------------------------------------------------------
 template <bool FOC>
 __device__ __forceinline__ void sce_fwd_body(const SemArgs& a) {
@@ -108,12 +139,13 @@ __device__ __forceinline__ void sce_fwd_body(const SemArgs& a) {
     if (valid) cl = cell_labels(tb, cell, a.W, a.Wt, a.s, a.C);
     const Focal f = make_focal(a.gamma, a.alpha);
     const float N2 = (float)(a.s * a.s);
+    const int c0 = blockIdx.z * a.cps, c1 = min(a.C, c0 + a.cps);
     for (int l = 0; l < a.L; ++l) {
         float acc = 0.0f;
         if (valid) {
             const float* x = a.logits + ((int64_t)l * a.B + b) * a.C * HW + cell;
-#pragma unroll 4
-            for (int c = 0; c < a.C; ++c) {
+#pragma unroll 8
+            for (int c = c0; c < c1; ++c) {
                 const Elem e = elem(__ldcs(x + (int64_t)c * HW));
                 const float n = class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
                 const float lp = FOC ? focal_pos(f, e) : f.alpha_pos * e.pos;
@@ -122,7 +154,8 @@ __device__ __forceinline__ void sce_fwd_body(const SemArgs& a) {
             }
         }
         const double t = block_sum_d((double)acc, sh);
-        if (threadIdx.x == 0) a.part_d[((int64_t)l * a.B + b) * gridDim.x + blockIdx.x] = t;
+        if (threadIdx.x == 0)
+            a.part_d[(((int64_t)l * a.B + b) * a.ncs + blockIdx.z) * gridDim.x + blockIdx.x] = t;
     }
 }
 
@@ -134,7 +167,7 @@ __global__ void __launch_bounds__(kSemThreads) sce_finalize_kernel(SemArgs a, in
     __shared__ double sh[32];
     const int l = blockIdx.x;
     double v = 0.0;
-    const int64_t n = (int64_t)a.B * nblk;
+    const int64_t n = (int64_t)a.B * a.ncs * nblk;
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) v += a.part_d[(int64_t)l * n + i];
     const double t = block_sum_d(v, sh);
     if (threadIdx.x == 0)
@@ -159,8 +192,9 @@ __global__ void __launch_bounds__(kSemThreads) sce_bwd_kernel(SemArgs a) {
     for (int l = 0; l < a.L; ++l) {
         const float go = a.grad_out[l] * norm;
         const int64_t base = ((int64_t)l * a.B + b) * a.C * HW + cell;
-#pragma unroll 4
-        for (int c = 0; c < a.C; ++c) {
+        const int c0 = blockIdx.z * a.cps, c1 = min(a.C, c0 + a.cps);
+#pragma unroll 8
+        for (int c = c0; c < c1; ++c) {
             const Elem e = elem(__ldcs(a.logits + base + (int64_t)c * HW));
             const float n = class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
             const float om = 1.0f - e.p;
@@ -175,61 +209,83 @@ __global__ void __launch_bounds__(kSemThreads) sce_bwd_kernel(SemArgs a) {
 
 // ---------------------------------------------------------------------------
 // Dice forward (src/cuda/dice_loss.cu:13-82): per (l,b,c) the block's partial
-// I = sum p n_c and sum p (P = s^2 * sum p), and per (b,c) the block's label
-// histogram (T).  Dynamic shared memory: (nwarps * 2 + 1) * C words.
+// I = sum p n_c and sum p (P = s^2 * sum p), and (class slice 0) per (b,c) the
+// block's label histogram (T).  A thread covers kDiceCells cells spaced one
+// block apart, so each warp sum covers 32 * kDiceCells logits.
+// Dynamic shared memory: (nwarps * 2 * cps + C) words.
 // ---------------------------------------------------------------------------
+constexpr int kDiceCells = 4;
+
 __global__ void __launch_bounds__(kSemThreads) dice_fwd_kernel(SemArgs a) {
     extern __shared__ float dsm[];
     const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int C = a.C;
-    float* ws = dsm;                                               // [nw][2][C]
-    int* hist = reinterpret_cast<int*>(dsm + (size_t)nw * 2 * C);  // [C]
+    const int C = a.C, cps = a.cps;
+    float* ws = dsm;                                                 // [nw][2][cps]
+    int* hist = reinterpret_cast<int*>(dsm + (size_t)nw * 2 * cps);  // [C]
     const int b = blockIdx.y;
     const int HW = a.H * a.W;
     const int nblk = gridDim.x;
-    const int cell = blockIdx.x * blockDim.x + threadIdx.x;
-    const bool valid = cell < HW;
+    const int c0 = blockIdx.z * cps, c1 = min(C, c0 + cps);
     const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
-    for (int c = threadIdx.x; c < C; c += blockDim.x) hist[c] = 0;
-    __syncthreads();
-    CellLabels cl;
-    if (valid) {
-        cl = cell_labels(tb, cell, a.W, a.Wt, a.s, C);
-        if (!cl.over) {
+    const int cell0 = blockIdx.x * blockDim.x * kDiceCells + threadIdx.x;
+    CellLabels cl[kDiceCells];
+    bool valid[kDiceCells];
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-                if (k < cl.n) atomicAdd(&hist[cl.lab[k]], cl.cnt[k]);
-        } else {
-            const int ci = cell / a.W, cj = cell - ci * a.W;
-            const int64_t* r0 = tb + (int64_t)(ci * a.s) * a.Wt + (int64_t)cj * a.s;
-            for (int dy = 0; dy < a.s; ++dy)
-                for (int dx = 0; dx < a.s; ++dx) {
-                    const int64_t v = r0[(int64_t)dy * a.Wt + dx];
-                    if (v >= 0 && v < C) atomicAdd(&hist[(int)v], 1);
-                }
-        }
+    for (int k = 0; k < kDiceCells; ++k) {
+        const int cell = cell0 + k * blockDim.x;
+        valid[k] = cell < HW;
+        if (valid[k]) cl[k] = cell_labels(tb, cell, a.W, a.Wt, a.s, C);
     }
-    __syncthreads();
-    for (int c = threadIdx.x; c < C; c += blockDim.x)
-        a.part_t[((int64_t)b * nblk + blockIdx.x) * C + c] = hist[c];
+    if (blockIdx.z == 0) {
+        for (int c = threadIdx.x; c < C; c += blockDim.x) hist[c] = 0;
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kDiceCells; ++k) {
+            if (!valid[k]) continue;
+            if (!cl[k].over) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < cl[k].n) atomicAdd(&hist[cl[k].lab[j]], cl[k].cnt[j]);
+            } else {
+                const int cell = cell0 + k * blockDim.x;
+                const int ci = cell / a.W, cj = cell - ci * a.W;
+                const int64_t* r0 = tb + (int64_t)(ci * a.s) * a.Wt + (int64_t)cj * a.s;
+                for (int dy = 0; dy < a.s; ++dy)
+                    for (int dx = 0; dx < a.s; ++dx) {
+                        const int64_t v = r0[(int64_t)dy * a.Wt + dx];
+                        if (v >= 0 && v < C) atomicAdd(&hist[(int)v], 1);
+                    }
+            }
+        }
+        __syncthreads();
+        for (int c = threadIdx.x; c < C; c += blockDim.x)
+            a.part_t[((int64_t)b * nblk + blockIdx.x) * C + c] = hist[c];
+    }
     for (int l = 0; l < a.L; ++l) {
-        const float* x = a.logits + ((int64_t)l * a.B + b) * C * HW + cell;
-        for (int c = 0; c < C; ++c) {
+        const float* x = a.logits + ((int64_t)l * a.B + b) * C * HW;
+        for (int c = c0; c < c1; ++c) {
             float pi = 0.0f, pp = 0.0f;
-            if (valid) {
-                const float p = elem(__ldcs(x + (int64_t)c * HW)).p;
-                pi = p * class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
-                pp = p;
+#pragma unroll
+            for (int k = 0; k < kDiceCells; ++k) {
+                const int cell = cell0 + k * blockDim.x;
+                if (valid[k]) {
+                    const float p = elem(__ldcs(x + (int64_t)c * HW + cell)).p;
+                    pi += p * class_count(cl[k], c, tb, cell, a.W, a.Wt, a.s);
+                    pp += p;
+                }
             }
             pi = warp_sum(pi);
             pp = warp_sum(pp);
-            if (lane == 0) { ws[(warp * 2) * C + c] = pi; ws[(warp * 2 + 1) * C + c] = pp; }
+            if (lane == 0) { ws[(warp * 2) * cps + (c - c0)] = pi; ws[(warp * 2 + 1) * cps + (c - c0)] = pp; }
         }
         __syncthreads();
         const int64_t o = (((int64_t)l * a.B + b) * nblk + blockIdx.x) * C;
-        for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        for (int c = c0 + threadIdx.x; c < c1; c += blockDim.x) {
             float si = 0.0f, sp = 0.0f;
-            for (int w = 0; w < nw; ++w) { si += ws[(w * 2) * C + c]; sp += ws[(w * 2 + 1) * C + c]; }
+            for (int w = 0; w < nw; ++w) {
+                si += ws[(w * 2) * cps + (c - c0)];
+                sp += ws[(w * 2 + 1) * cps + (c - c0)];
+            }
             a.part_f[2 * o + c] = si;
             a.part_f[2 * o + C + c] = sp;
         }
@@ -288,8 +344,9 @@ __global__ void __launch_bounds__(kSemThreads) dice_bwd_kernel(SemArgs a) {
         const float go = -a.grad_out[l] / a.num_masks * a.scale;
         const int64_t lb = (int64_t)l * a.B + b;
         const int64_t base = lb * a.C * HW + cell;
-#pragma unroll 4
-        for (int c = 0; c < a.C; ++c) {
+        const int c0 = blockIdx.z * a.cps, c1 = min(a.C, c0 + a.cps);
+#pragma unroll 8
+        for (int c = c0; c < c1; ++c) {
             const float p = elem(__ldcs(a.logits + base + (int64_t)c * HW)).p;
             const float n = class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
             const float I = a.I[lb * a.C + c], P = a.P[lb * a.C + c], T = a.T[lb * a.C + c];
@@ -304,10 +361,23 @@ __global__ void __launch_bounds__(kSemThreads) dice_bwd_kernel(SemArgs a) {
 // Launchers (non-template entry points called from capi.cu).
 // ---------------------------------------------------------------------------
 int sem_blocks(const SemArgs& a) { return (a.H * a.W + kSemThreads - 1) / kSemThreads; }
+int dice_blocks(const SemArgs& a) {
+    return (a.H * a.W + kSemThreads * kDiceCells - 1) / (kSemThreads * kDiceCells);
+}
+
+// Class slices: enough blocks for about 16 per SM of a 148-SM part.
+void sem_slices(SemArgs* a, int blocks_per_slice) {
+    const int64_t want = 148 * 16;
+    const int64_t per = (int64_t)blocks_per_slice * a->B;
+    int ncs = (int)std::max<int64_t>(1, std::min<int64_t>(a->C, (want + per - 1) / std::max<int64_t>(per, 1)));
+    if (ncs > 65535) ncs = 65535;
+    a->cps = std::max(1, (a->C + ncs - 1) / ncs);
+    a->ncs = std::max(1, (a->C + a->cps - 1) / a->cps);
+}
 
 cudaError_t launch_sce_forward(SemArgs a, cudaStream_t st) {
     const int nblk = sem_blocks(a);
-    dim3 g(nblk, a.B);
+    dim3 g(nblk, a.B, a.ncs);
     if (a.gamma > 0.0f) sce_fwd_focal_kernel<<<g, kSemThreads, 0, st>>>(a);
     else sce_fwd_kernel<<<g, kSemThreads, 0, st>>>(a);
     cudaError_t e = cudaGetLastError();
@@ -317,19 +387,21 @@ cudaError_t launch_sce_forward(SemArgs a, cudaStream_t st) {
 }
 
 cudaError_t launch_sce_backward(SemArgs a, cudaStream_t st) {
-    sce_bwd_kernel<<<dim3(sem_blocks(a), a.B), kSemThreads, 0, st>>>(a);
+    sce_bwd_kernel<<<dim3(sem_blocks(a), a.B, a.ncs), kSemThreads, 0, st>>>(a);
     return cudaGetLastError();
 }
 
-size_t dice_fwd_smem(int C) { return sizeof(float) * ((size_t)(kSemThreads / 32) * 2 + 1) * C; }
+size_t dice_fwd_smem(int C, int cps) {
+    return sizeof(float) * ((size_t)(kSemThreads / 32) * 2 * cps + C);
+}
 
 cudaError_t launch_dice_forward(SemArgs a, cudaStream_t st) {
-    const int nblk = sem_blocks(a);
-    const size_t smem = dice_fwd_smem(a.C);
+    const int nblk = dice_blocks(a);
+    const size_t smem = dice_fwd_smem(a.C, a.cps);
     cudaError_t e = cudaFuncSetAttribute(dice_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
-    dice_fwd_kernel<<<dim3(nblk, a.B), kSemThreads, smem, st>>>(a);
+    dice_fwd_kernel<<<dim3(nblk, a.B, a.ncs), kSemThreads, smem, st>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     dice_reduce_kernel<<<a.L * a.B, kSemThreads, 0, st>>>(a, nblk);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -338,7 +410,7 @@ cudaError_t launch_dice_forward(SemArgs a, cudaStream_t st) {
 }
 
 cudaError_t launch_dice_backward(SemArgs a, cudaStream_t st) {
-    dice_bwd_kernel<<<dim3(sem_blocks(a), a.B), kSemThreads, 0, st>>>(a);
+    dice_bwd_kernel<<<dim3(sem_blocks(a), a.B, a.ncs), kSemThreads, 0, st>>>(a);
     return cudaGetLastError();
 }
 
