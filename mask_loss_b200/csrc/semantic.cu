@@ -25,6 +25,8 @@ namespace mlb {
 namespace {
 
 constexpr int kSemThreads = 256;
+constexpr int kClassBatch = 8;       // class planes loaded together per thread
+constexpr int kDiceClassBatch = 4;   // dice forward: x kDiceCells cells
 
 struct CellLabels {
     int lab[4];
@@ -144,13 +146,20 @@ __device__ __forceinline__ void sce_fwd_body(const SemArgs& a) {
         float acc = 0.0f;
         if (valid) {
             const float* x = a.logits + ((int64_t)l * a.B + b) * a.C * HW + cell;
-#pragma unroll 8
-            for (int c = c0; c < c1; ++c) {
-                const Elem e = elem(__ldcs(x + (int64_t)c * HW));
-                const float n = class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
-                const float lp = FOC ? focal_pos(f, e) : f.alpha_pos * e.pos;
-                const float ln = FOC ? focal_neg(f, e) : f.alpha_neg * e.neg;
-                acc += lp * n + ln * (N2 - n);
+            for (int cb = c0; cb < c1; cb += kClassBatch) {
+                float xv[kClassBatch];  // all loads of the batch in flight first
+#pragma unroll
+                for (int k = 0; k < kClassBatch; ++k)
+                    xv[k] = cb + k < c1 ? __ldcs(x + (int64_t)(cb + k) * HW) : 0.0f;
+#pragma unroll
+                for (int k = 0; k < kClassBatch; ++k) {
+                    if (cb + k >= c1) break;
+                    const Elem e = elem(xv[k]);
+                    const float n = class_count(cl, cb + k, tb, cell, a.W, a.Wt, a.s);
+                    const float lp = FOC ? focal_pos(f, e) : f.alpha_pos * e.pos;
+                    const float ln = FOC ? focal_neg(f, e) : f.alpha_neg * e.neg;
+                    acc += lp * n + ln * (N2 - n);
+                }
             }
         }
         const double t = block_sum_d((double)acc, sh);
@@ -193,16 +202,23 @@ __global__ void __launch_bounds__(kSemThreads) sce_bwd_kernel(SemArgs a) {
         const float go = a.grad_out[l] * norm;
         const int64_t base = ((int64_t)l * a.B + b) * a.C * HW + cell;
         const int c0 = blockIdx.z * a.cps, c1 = min(a.C, c0 + a.cps);
-#pragma unroll 8
-        for (int c = c0; c < c1; ++c) {
-            const Elem e = elem(__ldcs(a.logits + base + (int64_t)c * HW));
-            const float n = class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
-            const float om = 1.0f - e.p;
-            const float mp = f.use_gamma ? __powf(om, f.gamma) : 1.0f;
-            const float mn = f.use_gamma ? __powf(e.p, f.gamma) : 1.0f;
-            const float gp = -f.alpha_pos * n * mp * (f.gamma * e.p * e.pos + om);
-            const float gn = f.alpha_neg * (N2 - n) * mn * (f.gamma * om * e.neg + e.p);
-            __stcs(a.grad + base + (int64_t)c * HW, (gp + gn) * go);
+        for (int cb = c0; cb < c1; cb += kClassBatch) {
+            float xv[kClassBatch];
+#pragma unroll
+            for (int k = 0; k < kClassBatch; ++k)
+                xv[k] = cb + k < c1 ? __ldcs(a.logits + base + (int64_t)(cb + k) * HW) : 0.0f;
+#pragma unroll
+            for (int k = 0; k < kClassBatch; ++k) {
+                if (cb + k >= c1) break;
+                const Elem e = elem(xv[k]);
+                const float n = class_count(cl, cb + k, tb, cell, a.W, a.Wt, a.s);
+                const float om = 1.0f - e.p;
+                const float mp = f.use_gamma ? __powf(om, f.gamma) : 1.0f;
+                const float mn = f.use_gamma ? __powf(e.p, f.gamma) : 1.0f;
+                const float gp = -f.alpha_pos * n * mp * (f.gamma * e.p * e.pos + om);
+                const float gn = f.alpha_neg * (N2 - n) * mn * (f.gamma * om * e.neg + e.p);
+                __stcs(a.grad + base + (int64_t)(cb + k) * HW, (gp + gn) * go);
+            }
         }
     }
 }
@@ -263,20 +279,31 @@ __global__ void __launch_bounds__(kSemThreads) dice_fwd_kernel(SemArgs a) {
     }
     for (int l = 0; l < a.L; ++l) {
         const float* x = a.logits + ((int64_t)l * a.B + b) * C * HW;
-        for (int c = c0; c < c1; ++c) {
-            float pi = 0.0f, pp = 0.0f;
+        for (int cb = c0; cb < c1; cb += kDiceClassBatch) {
+            float xv[kDiceClassBatch][kDiceCells];  // all loads of the batch in flight first
 #pragma unroll
-            for (int k = 0; k < kDiceCells; ++k) {
-                const int cell = cell0 + k * blockDim.x;
-                if (valid[k]) {
-                    const float p = elem(__ldcs(x + (int64_t)c * HW + cell)).p;
-                    pi += p * class_count(cl[k], c, tb, cell, a.W, a.Wt, a.s);
+            for (int j = 0; j < kDiceClassBatch; ++j)
+#pragma unroll
+                for (int k = 0; k < kDiceCells; ++k)
+                    xv[j][k] = (cb + j < c1 && valid[k])
+                                   ? __ldcs(x + (int64_t)(cb + j) * HW + cell0 + k * blockDim.x)
+                                   : 0.0f;
+#pragma unroll
+            for (int j = 0; j < kDiceClassBatch; ++j) {
+                const int c = cb + j;
+                if (c >= c1) break;
+                float pi = 0.0f, pp = 0.0f;
+#pragma unroll
+                for (int k = 0; k < kDiceCells; ++k) {
+                    if (!valid[k]) continue;
+                    const float p = elem(xv[j][k]).p;
+                    pi += p * class_count(cl[k], c, tb, cell0 + k * blockDim.x, a.W, a.Wt, a.s);
                     pp += p;
                 }
+                pi = warp_sum(pi);
+                pp = warp_sum(pp);
+                if (lane == 0) { ws[(warp * 2) * cps + (c - c0)] = pi; ws[(warp * 2 + 1) * cps + (c - c0)] = pp; }
             }
-            pi = warp_sum(pi);
-            pp = warp_sum(pp);
-            if (lane == 0) { ws[(warp * 2) * cps + (c - c0)] = pi; ws[(warp * 2 + 1) * cps + (c - c0)] = pp; }
         }
         __syncthreads();
         const int64_t o = (((int64_t)l * a.B + b) * nblk + blockIdx.x) * C;
@@ -345,14 +372,22 @@ __global__ void __launch_bounds__(kSemThreads) dice_bwd_kernel(SemArgs a) {
         const int64_t lb = (int64_t)l * a.B + b;
         const int64_t base = lb * a.C * HW + cell;
         const int c0 = blockIdx.z * a.cps, c1 = min(a.C, c0 + a.cps);
-#pragma unroll 8
-        for (int c = c0; c < c1; ++c) {
-            const float p = elem(__ldcs(a.logits + base + (int64_t)c * HW)).p;
-            const float n = class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
-            const float I = a.I[lb * a.C + c], P = a.P[lb * a.C + c], T = a.T[lb * a.C + c];
-            const float den = P + T + a.smooth;
-            const float d = (2.0f * n * den - N2 * (2.0f * I + a.smooth)) / (den * den);
-            __stcs(a.grad + base + (int64_t)c * HW, go * d * (p * (1.0f - p)));
+        for (int cb = c0; cb < c1; cb += kClassBatch) {
+            float xv[kClassBatch];
+#pragma unroll
+            for (int k = 0; k < kClassBatch; ++k)
+                xv[k] = cb + k < c1 ? __ldcs(a.logits + base + (int64_t)(cb + k) * HW) : 0.0f;
+#pragma unroll
+            for (int k = 0; k < kClassBatch; ++k) {
+                const int c = cb + k;
+                if (c >= c1) break;
+                const float p = elem(xv[k]).p;
+                const float n = class_count(cl, c, tb, cell, a.W, a.Wt, a.s);
+                const float I = a.I[lb * a.C + c], P = a.P[lb * a.C + c], T = a.T[lb * a.C + c];
+                const float den = P + T + a.smooth;
+                const float d = (2.0f * n * den - N2 * (2.0f * I + a.smooth)) / (den * den);
+                __stcs(a.grad + base + (int64_t)c * HW, go * d * (p * (1.0f - p)));
+            }
         }
     }
 }
