@@ -400,9 +400,10 @@ int dice_blocks(const SemArgs& a) {
     return (a.H * a.W + kSemThreads * kDiceCells - 1) / (kSemThreads * kDiceCells);
 }
 
-// Class slices: enough blocks for about 16 per SM of a 148-SM part.
+// Class slices: about 4 blocks per SM of a 148-SM part (more slices re-read
+// the labels more often than they add parallelism).
 void sem_slices(SemArgs* a, int blocks_per_slice) {
-    const int64_t want = 148 * 16;
+    const int64_t want = 148 * 4;
     const int64_t per = (int64_t)blocks_per_slice * a->B;
     int ncs = (int)std::max<int64_t>(1, std::min<int64_t>(a->C, (want + per - 1) / std::max<int64_t>(per, 1)));
     if (ncs > 65535) ncs = 65535;
