@@ -282,6 +282,42 @@ int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int6
                                       void* workspace, size_t workspace_bytes, ml_stream_t stream);
 
 /* ---------------------------------------------------------------------- */
+/* Dense per-GT mask targets -- no counterpart in the reference, whose API  */
+/* takes a label map only (src/bindings.cpp:66).  mask_masks: (B, GT_total,  */
+/* Ht, Wt) uint8, nonzero = inside, aligned with cls_targets' columns; masks */
+/* may overlap.  Costs, matching and losses follow the label-map entries     */
+/* with each GT's pixel count per cell in place of the one-hot count; on     */
+/* non-overlapping masks the results equal the label-map path.  d->GT_total  */
+/* is the mask count.  Workspace: ml_dense_workspace_size (forwards); the    */
+/* backward uses ml_mask_matching_backward_workspace_size and needs the     */
+/* forward's saved statistics.                                               */
+/* ---------------------------------------------------------------------- */
+size_t ml_dense_workspace_size(const ml_dims* d, const ml_params* p);
+
+int ml_pairwise_mask_loss_dense_forward(const ml_dims* d, const ml_params* p,
+                                        const float* mask_logits, const uint8_t* mask_masks,
+                                        const float* cls_logits, const int64_t* cls_targets,
+                                        float* out, void* workspace, size_t workspace_bytes,
+                                        ml_stream_t stream);
+
+int ml_mask_matching_dense(const ml_dims* d, const ml_params* p,
+                           const float* mask_logits, const uint8_t* mask_masks,
+                           const float* cls_logits, const int64_t* cls_targets,
+                           const float* num_masks_dev,
+                           int64_t* pred_to_gt, int64_t* pred_round, float* layer_means,
+                           float* sep_costs, float* saved, int32_t* dev_status,
+                           void* workspace, size_t workspace_bytes, ml_stream_t stream);
+
+int ml_mask_matching_dense_backward(const ml_dims* d, const ml_params* p,
+                                    const float* grad_mask_mean, const float* grad_dice_mean,
+                                    const float* grad_cls_mean, const float* mask_logits,
+                                    const uint8_t* mask_masks, const float* cls_logits,
+                                    const int64_t* cls_targets, const int64_t* pred_to_gt,
+                                    const float* saved, const float* num_masks_dev,
+                                    float* grad_mask_logits, float* grad_cls_logits,
+                                    void* workspace, size_t workspace_bytes, ml_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
 /* Standalone semantic losses of (L,B,C,H,W) fp32 logits against a         */
 /* (B,Ht,Wt) int64 label map with classes in [0,C) (Ht = s*H, Wt = s*W,     */
 /* s <= 16, C <= 2048; labels outside [0,C) count for no class).           */

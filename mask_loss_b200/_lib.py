@@ -73,6 +73,14 @@ SIGNATURES = {
                                            c_vp, c_sz, c_vp, c_vp]),
     "ml_count_masks": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_vp, c_vp,
                                       c_vp, c_sz, c_vp]),
+    "ml_dense_workspace_size": (c_sz, [ctypes.POINTER(Dims), ctypes.POINTER(Params)]),
+    "ml_pairwise_mask_loss_dense_forward": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                           c_vp, c_sz, c_vp]),
+    "ml_mask_matching_dense": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                              c_vp, c_vp, c_vp, c_vp, c_vp, c_sz, c_vp]),
+    "ml_mask_matching_dense_backward": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                       c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                       c_sz, c_vp]),
     "ml_semantic_workspace_size": (c_sz, [c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, ctypes.c_int32]),
     "ml_sigmoid_ce_forward": (ctypes.c_int, [c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, c_f32, c_f32, c_f32,
                                              c_f32, c_vp, c_vp, c_sz, c_vp]),

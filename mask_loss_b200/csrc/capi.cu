@@ -342,6 +342,8 @@ int run_prep(const FwdPlan& P, const CostArgs& a, cudaStream_t st) {
 
 int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStream_t st);
 
+int run_finalize(const FwdPlan& P, CostArgs& a, cudaStream_t st);
+
 int run_costs(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStream_t st) {
     int rc = run_prep(P, a, st);
     if (rc) return rc;
@@ -381,6 +383,12 @@ int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaS
         else rc = tma ? launch_cost_t<false, false, true>(P, tm, a, st) : launch_cost_t<false, false, false>(P, tm, a, st);
     }
     if (rc) return rc;
+    return run_finalize(P, a, st);
+}
+
+// Row statistics and pair costs from the chunk partials (both target modes).
+int run_finalize(const FwdPlan& P, CostArgs& a, cudaStream_t st) {
+    const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
     const unsigned rb = (unsigned)((LBQ * 32 + 255) / 256);
     if (P.unc) cost_rows_kernel<true, false><<<rb, 256, 0, st>>>(a);
     else if (P.foc) cost_rows_kernel<false, false><<<rb, 256, 0, st>>>(a);
@@ -391,6 +399,32 @@ int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaS
     else cost_pairs_kernel<false><<<pg, 256, 0, st>>>(a);
     ML_CHECK_LAUNCH("cost_pairs_kernel");
     return ML_OK;
+}
+
+// Dense per-GT masks: counts + areas, then the dense cost kernel, then the
+// same finalize.  The counts live after the plan's workspace.
+size_t dense_count_bytes(const FwdPlan& P) {
+    return align256(sizeof(uint16_t) * (size_t)P.B * P.H * P.W * std::max(P.gt_total, 1));
+}
+
+int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigned char* ws,
+                    cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(const_cast<int32_t*>(a.totals), 0,
+                                    sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
+    if (e != cudaSuccess) return cuda_fail(e, "memset mask areas");
+    uint16_t* cnt = reinterpret_cast<uint16_t*>(ws + (P.bytes - 256));
+    if (P.B > 0 && P.gt_total > 0) {
+        e = launch_dense_count(masks, P.B, P.H, P.W, P.Ht, P.Wt, P.s, P.gt_total, cnt,
+                               const_cast<int32_t*>(a.totals), st);
+        g_launches.fetch_add(1);
+        if (e != cudaSuccess) return cuda_fail(e, "dense_count_kernel");
+    }
+    const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
+    if (LBQ == 0 || P.gout == 0) return ML_OK;
+    e = launch_dense_cost(a, P.unc, P.foc, cnt, st);
+    g_launches.fetch_add(1);
+    if (e != cudaSuccess) return cuda_fail(e, "dense_cost_kernel");
+    return run_finalize(P, a, st);
 }
 
 int check_ws(void* ws, size_t have, size_t need) {
@@ -717,20 +751,24 @@ static int mask_matching_impl(const ml_dims* d, const ml_params* p, const float*
                               const int64_t* cls_targets, const float* num_masks_dev,
                               int64_t* pred_to_gt, int64_t* pred_round, float* layer_means,
                               float* sep_costs, float* saved, int32_t* dev_status, void* workspace,
-                              size_t workspace_bytes, ml_stream_t stream, cudaEvent_t loss_wait) {
+                              size_t workspace_bytes, ml_stream_t stream, cudaEvent_t loss_wait,
+                              const uint8_t* dense_masks = nullptr) {
     FwdPlan P;
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
     if ((rc = make_plan(d, p, &P))) return rc;
     if (P.gout == 0)
         return fail(ML_ESHAPE, "pairwise_sigmoid_dice_loss_forward must return {3,L,B,Q,GT_out}");
-    if ((rc = check_ws(workspace, workspace_bytes, P.bytes))) return rc;
+    const size_t need = P.bytes + (dense_masks ? dense_count_bytes(P) : 0);
+    if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
     if (!dev_status) return fail(ML_EINVAL, "dev_status is null");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char* ws = ws_base(workspace);
     CostArgs a = cost_args(P, p, mask_logits, mask_targets, cls_logits, cls_targets, ws, dev_status);
     if (sep_costs) a.sep = sep_costs;
-    if ((rc = run_costs(P, a, mask_logits, st))) return rc;
+    if (dense_masks) rc = run_dense_costs(P, a, dense_masks, ws, st);
+    else rc = run_costs(P, a, mask_logits, st);
+    if (rc) return rc;
     if ((rc = launch_match<float>(a.total, (int64_t)P.L * P.B, P.Q, P.gout, p->inf_thresh,
                                   p->topk_matches, p->strategy_id, pred_to_gt, pred_round,
                                   dev_status, st)))
@@ -797,14 +835,16 @@ int ml_count_masks(const ml_dims* d, const ml_params* p, const int64_t* mask_tar
     return ML_OK;
 }
 
-int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float* grad_mask_mean,
-                              const float* grad_dice_mean, const float* grad_cls_mean,
-                              const float* mask_logits, const int64_t* mask_targets,
-                              const float* cls_logits, const int64_t* cls_targets,
-                              const int64_t* pred_to_gt, const float* saved,
-                              const float* num_masks_dev, float* grad_mask_logits,
-                              float* grad_cls_logits, void* workspace, size_t workspace_bytes,
-                              ml_stream_t stream) {
+static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad_mask_mean,
+                         const float* grad_dice_mean, const float* grad_cls_mean,
+                         const float* mask_logits, const int64_t* mask_targets,
+                         const float* cls_logits, const int64_t* cls_targets,
+                         const int64_t* pred_to_gt, const float* saved,
+                         const float* num_masks_dev, float* grad_mask_logits,
+                         float* grad_cls_logits, void* workspace, size_t workspace_bytes,
+                         ml_stream_t stream, const uint8_t* dense_masks) {
+    if (dense_masks && !saved)
+        return fail(ML_EINVAL, "dense mask targets need the forward's saved statistics");
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
     if ((rc = validate_dims(d))) return rc;
@@ -829,6 +869,7 @@ int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float*
     la.cls_targets = cls_targets; la.pred_to_gt = pred_to_gt; la.num_masks_dev = num_masks_dev;
     la.grad_mask = grad_mask_mean; la.grad_dice = grad_dice_mean; la.grad_cls = grad_cls_mean;
     la.coef = coef; la.grad_mask_logits = grad_mask_logits; la.grad_cls_logits = grad_cls_logits;
+    la.masks = dense_masks;
     // coefficients + class-logit gradient first; the mask gradient reads coef
     bwd_cls_kernel<<<(unsigned)((LBQ + 7) / 8), 256, 0, st>>>(la);
     ML_CHECK_LAUNCH("bwd_cls_kernel");
@@ -867,6 +908,72 @@ int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float*
 #undef ML_MG
     ML_CHECK_LAUNCH("mask_grad_kernel");
     return ML_OK;
+}
+
+int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float* grad_mask_mean,
+                              const float* grad_dice_mean, const float* grad_cls_mean,
+                              const float* mask_logits, const int64_t* mask_targets,
+                              const float* cls_logits, const int64_t* cls_targets,
+                              const int64_t* pred_to_gt, const float* saved,
+                              const float* num_masks_dev, float* grad_mask_logits,
+                              float* grad_cls_logits, void* workspace, size_t workspace_bytes,
+                              ml_stream_t stream) {
+    return backward_impl(d, p, grad_mask_mean, grad_dice_mean, grad_cls_mean, mask_logits,
+                         mask_targets, cls_logits, cls_targets, pred_to_gt, saved, num_masks_dev,
+                         grad_mask_logits, grad_cls_logits, workspace, workspace_bytes, stream,
+                         nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// Dense per-GT mask targets (no reference counterpart; dense.cu).
+// ---------------------------------------------------------------------------
+size_t ml_dense_workspace_size(const ml_dims* d, const ml_params* p) {
+    FwdPlan P;
+    if (!p || make_plan(d, p, &P)) return 0;
+    return P.bytes + dense_count_bytes(P);
+}
+
+int ml_pairwise_mask_loss_dense_forward(const ml_dims* d, const ml_params* p, const float* mask_logits,
+                                        const uint8_t* mask_masks, const float* cls_logits,
+                                        const int64_t* cls_targets, float* out, void* workspace,
+                                        size_t workspace_bytes, ml_stream_t stream) {
+    FwdPlan P;
+    int rc = validate_params(p, d ? d->C : 0);
+    if (rc) return rc;
+    if ((rc = make_plan(d, p, &P))) return rc;
+    if ((rc = check_ws(workspace, workspace_bytes, P.bytes + dense_count_bytes(P)))) return rc;
+    if (P.gout == 0) return ML_OK;
+    unsigned char* ws = ws_base(workspace);
+    CostArgs a = cost_args(P, p, mask_logits, nullptr, cls_logits, cls_targets, ws, nullptr);
+    a.sep = out; a.total = nullptr; a.rawI = nullptr; a.rawT = nullptr;
+    return run_dense_costs(P, a, mask_masks, ws, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ml_mask_matching_dense(const ml_dims* d, const ml_params* p, const float* mask_logits,
+                           const uint8_t* mask_masks, const float* cls_logits,
+                           const int64_t* cls_targets, const float* num_masks_dev,
+                           int64_t* pred_to_gt, int64_t* pred_round, float* layer_means,
+                           float* sep_costs, float* saved, int32_t* dev_status, void* workspace,
+                           size_t workspace_bytes, ml_stream_t stream) {
+    if (!mask_masks) return fail(ML_EINVAL, "mask_masks is null");
+    return mask_matching_impl(d, p, mask_logits, nullptr, cls_logits, cls_targets, num_masks_dev,
+                              pred_to_gt, pred_round, layer_means, sep_costs, saved, dev_status,
+                              workspace, workspace_bytes, stream, nullptr, mask_masks);
+}
+
+int ml_mask_matching_dense_backward(const ml_dims* d, const ml_params* p, const float* grad_mask_mean,
+                                    const float* grad_dice_mean, const float* grad_cls_mean,
+                                    const float* mask_logits, const uint8_t* mask_masks,
+                                    const float* cls_logits, const int64_t* cls_targets,
+                                    const int64_t* pred_to_gt, const float* saved,
+                                    const float* num_masks_dev, float* grad_mask_logits,
+                                    float* grad_cls_logits, void* workspace,
+                                    size_t workspace_bytes, ml_stream_t stream) {
+    if (!mask_masks) return fail(ML_EINVAL, "mask_masks is null");
+    return backward_impl(d, p, grad_mask_mean, grad_dice_mean, grad_cls_mean, mask_logits, nullptr,
+                         cls_logits, cls_targets, pred_to_gt, saved, num_masks_dev,
+                         grad_mask_logits, grad_cls_logits, workspace, workspace_bytes, stream,
+                         mask_masks);
 }
 
 

@@ -122,6 +122,7 @@ struct LossArgs {
     float ug, ugmin, mask_gamma, mask_alpha, cls_gamma, cls_alpha;
     int force_masks, force_cls, has_void, void_index, use_softmax, normalize_uncertainty;
     int32_t* void_status;    // forward: bit 4 set when cls_targets holds void_index, or null
+    const uint8_t* masks;    // dense (B,GT_total,Ht,Wt) targets instead of the label map, or null
 };
 
 __global__ void loss_fwd_kernel(LossArgs a);
@@ -180,4 +181,13 @@ cudaError_t launch_sce_forward(SemArgs a, cudaStream_t st);
 cudaError_t launch_sce_backward(SemArgs a, cudaStream_t st);
 cudaError_t launch_dice_forward(SemArgs a, cudaStream_t st);
 cudaError_t launch_dice_backward(SemArgs a, cudaStream_t st);
+}  // namespace mlb
+
+namespace mlb {
+// Dense per-GT mask targets (dense.cu).
+size_t dense_cost_smem(int qrows_pad, bool unc);
+cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht, int Wt, int s,
+                               int gt_total, uint16_t* cnt, int32_t* totals, cudaStream_t st);
+cudaError_t launch_dense_cost(const CostArgs& a, bool unc, bool foc, const uint16_t* cnt,
+                              cudaStream_t st);
 }  // namespace mlb

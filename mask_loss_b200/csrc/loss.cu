@@ -217,8 +217,20 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
     const float num = 2.0f * I + a.smooth;
     const float inv_d2 = 1.0f / fmaxf(den * den, 1e-20f);
     const float two_den = 2.0f * den;
+    // dense targets: the matched GT's own mask
+    const uint8_t* mb = (a.masks && matched) ? a.masks + ((int64_t)b * a.gt_total + ga) * a.Ht * a.Wt
+                                             : nullptr;
     auto count = [&](int k) -> float {  // pixels of the matched label in cell c0 + k
         if (!matched) return 0.0f;
+        if (mb) {
+            if (s == 1) return mb[c0 + k] != 0 ? 1.0f : 0.0f;
+            const int cell = c0 + k, ci = cell / a.W, cj = cell - ci * a.W;
+            const uint8_t* r0 = mb + (int64_t)(ci * s) * a.Wt + (int64_t)cj * s;
+            int n = 0;
+            for (int dy = 0; dy < s; ++dy)
+                for (int dx = 0; dx < s; ++dx) n += r0[(int64_t)dy * a.Wt + dx] != 0;
+            return (float)n;
+        }
         if (s == 1) return tb[c0 + k] == ga ? 1.0f : 0.0f;
         return cell_count(tb, c0 + k, a.W, a.Wt, s, ga);
     };
@@ -243,7 +255,7 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
     if (VEC) {
         // one pixel per cell and 16-byte aligned labels: the four labels of a
         // float4 are two 16-byte loads, issued with the logits
-        const bool lab2 = s == 1 && matched && ((reinterpret_cast<uintptr_t>(tb + c0) & 15) == 0);
+        const bool lab2 = s == 1 && matched && !a.masks && ((reinterpret_cast<uintptr_t>(tb + c0) & 15) == 0);
         if (lab2) {
             const float* __restrict__ xr = xin;
             const longlong2* __restrict__ lr = reinterpret_cast<const longlong2*>(tb + c0);
