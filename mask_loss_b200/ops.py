@@ -132,9 +132,15 @@ def _params(smooth=1.0, sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0, backgr
                        int(bool(normalize_uncertainty)), int(bool(check_void_targets)))
 
 
+def is_dense(mask_targets) -> bool:
+    """Dense per-GT masks (B, GT_total, H_t, W_t) uint8/bool instead of a
+    (B, H_t, W_t) label map (no reference counterpart; overlap allowed)."""
+    return mask_targets.dim() == 4
+
+
 def _dims(mask_logits, mask_targets, cls_logits, cls_targets) -> _lib.Dims:
     L, B, Q, H, W = mask_logits.shape
-    _, Ht, Wt = mask_targets.shape
+    Ht, Wt = mask_targets.shape[-2:]
     return _lib.Dims(L, B, Q, H, W, Ht, Wt, cls_logits.shape[3], cls_targets.shape[1])
 
 
@@ -144,15 +150,21 @@ def _check_quad(mask_logits, mask_targets, cls_logits, cls_targets):
         _check_input(t, n)
     if mask_logits.dim() != 5:
         raise RuntimeError("mask_logits must be (L,B,Q,H,W)")
-    if mask_targets.dim() != 3:
-        raise RuntimeError("mask_targets must be (B,H_t,W_t)")
+    if mask_targets.dim() not in (3, 4):
+        raise RuntimeError("mask_targets must be (B,H_t,W_t) labels or (B,GT,H_t,W_t) masks")
     if cls_logits.dim() != 4:
         raise RuntimeError("cls_logits must be (L,B,Q,C)")
     if cls_targets.dim() != 2:
         raise RuntimeError("cls_targets must be (B,GT)")
     _check_dtype(mask_logits, torch.float32, "mask_logits")
     _check_dtype(cls_logits, torch.float32, "cls_logits")
-    _check_dtype(mask_targets, torch.int64, "mask_targets")
+    if is_dense(mask_targets):
+        if mask_targets.dtype not in (torch.uint8, torch.bool):
+            raise RuntimeError("dense mask_targets must be uint8 or bool")
+        if mask_targets.shape[1] != cls_targets.shape[1]:
+            raise RuntimeError("dense mask_targets must have one mask per cls_targets column")
+    else:
+        _check_dtype(mask_targets, torch.int64, "mask_targets")
     _check_dtype(cls_targets, torch.int64, "cls_targets")
     L, B, Q = mask_logits.shape[:3]
     if mask_targets.shape[0] != B or cls_targets.shape[0] != B:
@@ -189,13 +201,16 @@ def pairwise_mask_loss_forward(mask_logits, mask_targets, cls_logits, cls_target
     if G == 0:
         return torch.zeros((L, B, Q, 0), dtype=torch.float32, device=mask_logits.device)
     out = torch.empty((3, L, B, Q, G), dtype=torch.float32, device=mask_logits.device)
-    nbytes = lib.ml_mask_matching_workspace_size(ctypes.byref(d), ctypes.byref(p))
+    dense = is_dense(mask_targets)
+    size_fn = lib.ml_dense_workspace_size if dense else lib.ml_mask_matching_workspace_size
+    nbytes = size_fn(ctypes.byref(d), ctypes.byref(p))
     if nbytes == 0:
         raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
     ws = _workspace(nbytes, mask_logits.device)
-    _lib.check(lib.ml_pairwise_mask_loss_forward(
-        ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits),
-        _ptr(cls_targets), _ptr(out), _ptr(ws), ws.numel(), _stream(mask_logits.device)))
+    fn = lib.ml_pairwise_mask_loss_dense_forward if dense else lib.ml_pairwise_mask_loss_forward
+    _lib.check(fn(ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets),
+                  _ptr(cls_logits), _ptr(cls_targets), _ptr(out), _ptr(ws), ws.numel(),
+                  _stream(mask_logits.device)))
     return out
 
 
@@ -246,14 +261,24 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
     costs = (torch.empty((3, L, B, Q, G), dtype=torch.float32, device=dev)
              if want_costs and G > 0 else None)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    nbytes = lib.ml_mask_matching_workspace_size(ctypes.byref(d), ctypes.byref(p))
+    dense = is_dense(mask_targets)
+    size_fn = lib.ml_dense_workspace_size if dense else lib.ml_mask_matching_workspace_size
+    nbytes = size_fn(ctypes.byref(d), ctypes.byref(p))
     if nbytes == 0:
         raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
     ws = _workspace(nbytes, dev)
     if num_masks_dev is not None:
         _check_input(num_masks_dev, "num_masks_dev")
         _check_dtype(num_masks_dev, torch.float32, "num_masks_dev")
-    if loss_wait_event is not None:
+    if dense:
+        if loss_wait_event is not None:
+            raise RuntimeError("loss_wait_event is not supported with dense mask targets")
+        _lib.check(lib.ml_mask_matching_dense(
+            ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets),
+            _ptr(cls_logits), _ptr(cls_targets), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd),
+            _ptr(means), _ptr(costs), _ptr(saved), _ptr(status), _ptr(ws), ws.numel(),
+            _stream(dev)))
+    elif loss_wait_event is not None:
         _lib.check(lib.ml_mask_matching_ex(
             ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets),
             _ptr(cls_logits), _ptr(cls_targets), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd),
@@ -323,7 +348,10 @@ def mask_matching_backward(grad_layer_mask_mean, grad_layer_dice_mean, grad_laye
     ws = _workspace(nbytes, dev)
     if saved is not None:
         _check_input(saved, "saved")
-    _lib.check(lib.ml_mask_matching_backward(
+    if is_dense(mask_targets) and saved is None:
+        raise RuntimeError("dense mask targets need the forward's saved statistics (saved=)")
+    fn = lib.ml_mask_matching_dense_backward if is_dense(mask_targets) else lib.ml_mask_matching_backward
+    _lib.check(fn(
         ctypes.byref(d), ctypes.byref(p), _ptr(grad_layer_mask_mean), _ptr(grad_layer_dice_mean),
         _ptr(grad_layer_cls_mean), _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits),
         _ptr(cls_targets), _ptr(pred_to_gt), _ptr(saved), _ptr(num_masks_dev), _ptr(gm), _ptr(gc),
@@ -542,7 +570,13 @@ def _check_sampled(mask_logits, mask_targets, cls_logits, cls_targets, point_coo
         _check_input(t, n)
     _dtype_code(mask_logits)
     _check_dtype(cls_logits, torch.float32, "cls_logits")
-    _check_dtype(mask_targets, torch.int64, "mask_targets")
+    if is_dense(mask_targets):
+        if mask_targets.dtype not in (torch.uint8, torch.bool):
+            raise RuntimeError("dense mask_targets must be uint8 or bool")
+        if mask_targets.shape[1] != cls_targets.shape[1]:
+            raise RuntimeError("dense mask_targets must have one mask per cls_targets column")
+    else:
+        _check_dtype(mask_targets, torch.int64, "mask_targets")
     _check_dtype(cls_targets, torch.int64, "cls_targets")
     _check_dtype(point_coords, torch.float32, "point_coords")
     B = mask_logits.shape[1]
