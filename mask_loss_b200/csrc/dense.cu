@@ -10,9 +10,9 @@
 // Two kernels feed the label path's finalize (cost_rows / cost_pairs), the
 // solver and the matched loss unchanged:
 //   dense_count_kernel  per (image, cell) the pixel count of every GT
-//                       (uint16, [b][cell][GT_total]) and per (image, GT) the
+//                       (uint16, [b][GT_total][cell]) and per (image, GT) the
 //                       mask area (the histogram the label path builds);
-//   dense_cost_kernel   per (layer*image, query tile, cell chunk, GT chunk)
+//   dense_cost_kernel   per (layer*image, query tile, cell chunk, GT chunk of up to 64)
 //                       the chunk partials in the label path's layout: row
 //                       sums, and per GT sum(val * count) accumulated in shared
 //                       memory from a per-tile list of the non-zero
@@ -42,14 +42,13 @@ dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int 
     const int cell = blockIdx.x * blockDim.x + threadIdx.x;
     if (cell < HW) {
         const int ci = cell / W, cj = cell - ci * W;
-        uint16_t* out = cnt + ((int64_t)b * HW + cell) * gt_total;
         for (int g = 0; g < gt_total; ++g) {
             const uint8_t* mg = masks + ((int64_t)b * gt_total + g) * Ht * Wt +
                                 (int64_t)(ci * s) * Wt + (int64_t)cj * s;
             int n = 0;
             for (int dy = 0; dy < s; ++dy)
                 for (int dx = 0; dx < s; ++dx) n += mg[(int64_t)dy * Wt + dx] != 0;
-            out[g] = (uint16_t)n;
+            cnt[((int64_t)b * gt_total + g) * HW + cell] = (uint16_t)n;
             if (n) atomicAdd(&area[g], n);
         }
     }
@@ -61,15 +60,15 @@ dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int 
 // grid = (nchunk * ngc, nqt, L*B), block = QP threads (query row t of the tile).
 // Dynamic shared memory: see dense_cost_smem.
 template <bool UNC, bool FOC>
-__device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_t* cnt) {
+__device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_t* cnt, int GC) {
     constexpr int NACC = UNC ? 3 : 2;
     constexpr int NROW = UNC ? 5 : 3;
     constexpr bool FAST = !UNC && !FOC;
     extern __shared__ __align__(16) float dsh[];
     const int QP = a.qrows_pad, G = a.gout;
-    const int ngc = (G + kDenseGC - 1) / kDenseGC;
+    const int ngc = (G + GC - 1) / GC;
     const int chunk = blockIdx.x / ngc, gc = blockIdx.x - chunk * ngc;
-    const int g0 = gc * kDenseGC, g1 = min(G, g0 + kDenseGC), gn = g1 - g0;
+    const int g0 = gc * GC, g1 = min(G, g0 + GC), gn = g1 - g0;
     const int qt = blockIdx.y, lb = blockIdx.z, b = lb % a.B;
     const int t = threadIdx.x;
     const int q = qt * a.qrows + t;
@@ -78,49 +77,77 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
     const int cell_begin = chunk * a.chunk_cells;
     const int cell_end = min(HW, cell_begin + a.chunk_cells);
     float* xs = dsh;                                         // [QP][kDenseTile + 1]
-    float* acc = xs + QP * (kDenseTile + 1);                 // [NACC][kDenseGC][QP]
-    int* lcnt = reinterpret_cast<int*>(acc + NACC * kDenseGC * QP);  // [kDenseTile]
-    int* lg = lcnt + kDenseTile;                             // [kDenseTile][kDenseGC]
-    float* ln = reinterpret_cast<float*>(lg + kDenseTile * kDenseGC);  // [kDenseTile][kDenseGC]
-    for (int i = t; i < NACC * kDenseGC * QP; i += blockDim.x) acc[i] = 0.0f;
+    float* acc = xs + QP * (kDenseTile + 1);                 // [NACC][GC][QP]
+    int* lcnt = reinterpret_cast<int*>(acc + NACC * GC * QP);  // [kDenseTile]
+    int* lg = lcnt + kDenseTile;                             // [kDenseTile][GC]
+    float* ln = reinterpret_cast<float*>(lg + kDenseTile * GC);  // [kDenseTile][GC]
+    float* ct = ln + kDenseTile * GC;                        // [GC][kDenseTile]
+    for (int i = t; i < NACC * GC * QP; i += blockDim.x) acc[i] = 0.0f;
     const int row0 = lb * a.Q + qt * a.qrows;
     const Focal foc = make_focal(a.mask_gamma, a.mask_alpha);
     float rows[NROW];
 #pragma unroll
     for (int i = 0; i < NROW; ++i) rows[i] = 0.0f;
-    const int nwarps = blockDim.x >> 5, warp = t >> 5, lane = t & 31;
+    const int warp = t >> 5, lane = t & 31;
+    // logits tile in registers: thread t holds float4 (t + m*QP), m < 8 --
+    // row i >> 3, cells 4*(i & 7) .. +3 -- so the next tile's loads are in
+    // flight while the current one is computed.  Rows and cells are
+    // 16-byte aligned when vec (H*W % 4 == 0, aligned logits).
+    const bool vec = (HW % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
+    float4 pre[8];
+    auto load_tile = [&](int c0n) {
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int i = t + m * QP, r = i >> 3, c = (i & 7) * 4;
+            const int qq = qt * a.qrows + r;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r < a.qrows && qq < a.Q) {
+                const float* src = a.logits + (int64_t)(row0 + r) * HW + c0n + c;
+                if (vec) {
+                    if (c0n + c < cell_end) v = __ldcs(reinterpret_cast<const float4*>(src));
+                } else {
+                    v.x = c0n + c < cell_end ? src[0] : 0.0f;
+                    v.y = c0n + c + 1 < cell_end ? src[1] : 0.0f;
+                    v.z = c0n + c + 2 < cell_end ? src[2] : 0.0f;
+                    v.w = c0n + c + 3 < cell_end ? src[3] : 0.0f;
+                }
+            }
+            pre[m] = v;
+        }
+    };
+    if (cell_begin < cell_end) load_tile(cell_begin);
     for (int c0 = cell_begin; c0 < cell_end; c0 += kDenseTile) {
         const int nv = min(kDenseTile, cell_end - c0);
         __syncthreads();  // previous tile consumed
-        // logits tile: warp w loads rows w, w+nwarps, ... (coalesced per row)
-        for (int r = warp; r < a.qrows; r += nwarps) {
-            const int qq = qt * a.qrows + r;
-            float v = 0.0f;
-            if (lane < nv && qq < a.Q) v = a.logits[(int64_t)(row0 + r) * HW + c0 + lane];
-            xs[r * (kDenseTile + 1) + lane] = v;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int i = t + m * QP, r = i >> 3, c = (i & 7) * 4;
+            float* d = xs + r * (kDenseTile + 1) + c;
+            d[0] = pre[m].x; d[1] = pre[m].y; d[2] = pre[m].z; d[3] = pre[m].w;
         }
-        // non-zero (GT, count) list of every cell of the tile
-        for (int k = warp; k < nv; k += nwarps) {
-            const uint16_t* cc = cnt + ((int64_t)b * HW + c0 + k) * a.gt_total;
-            int base = 0;
-            for (int j0 = 0; j0 < gn; j0 += 32) {
-                const int j = j0 + lane;
-                int n = 0;
-                if (j < gn) {
-                    const int g = g0 + j;
-                    n = cc[g + (g >= a.bg ? 1 : 0)];
-                }
-                const unsigned bal = __ballot_sync(0xffffffffu, n != 0);
-                if (n) {
-                    const int pos = base + __popc(bal & ((1u << lane) - 1u));
-                    lg[k * kDenseGC + pos] = j;
-                    ln[k * kDenseGC + pos] = (float)n;
-                }
-                base += __popc(bal);
-            }
-            if (lane == 0) lcnt[k] = base;
+        // the tile's counts, coalesced per GT plane
+        for (int i = t; i < gn * kDenseTile; i += blockDim.x) {
+            const int j = i / kDenseTile, k = i - j * kDenseTile;
+            const int g = g0 + j;
+            ct[i] = k < nv ? (float)cnt[((int64_t)b * a.gt_total + g + (g >= a.bg ? 1 : 0)) * HW + c0 + k]
+                           : 0.0f;
         }
         __syncthreads();
+        // non-zero (GT, count) list of every cell: warp 0, lane = cell
+        if (warp == 0) {
+            int m = 0;
+            for (int j = 0; j < gn; ++j) {
+                const float n = ct[j * kDenseTile + lane];
+                if (n != 0.0f) {
+                    lg[lane * GC + m] = j;
+                    ln[lane * GC + m] = n;
+                    ++m;
+                }
+            }
+            lcnt[lane] = m;
+        }
+        __syncthreads();
+        if (c0 + kDenseTile < cell_end) load_tile(c0 + kDenseTile);
         if (t < a.qrows) {
             for (int k = 0; k < nv; ++k) {
                 const float x = xs[t * (kDenseTile + 1) + k];
@@ -152,10 +179,10 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
                 }
                 const int m = lcnt[k];
                 for (int i = 0; i < m; ++i) {
-                    const int j = lg[k * kDenseGC + i];
-                    const float n = ln[k * kDenseGC + i];
+                    const int j = lg[k * GC + i];
+                    const float n = ln[k * GC + i];
 #pragma unroll
-                    for (int z = 0; z < NACC; ++z) acc[(z * kDenseGC + j) * QP + t] += v[z] * n;
+                    for (int z = 0; z < NACC; ++z) acc[(z * GC + j) * QP + t] += v[z] * n;
                 }
             }
         }
@@ -168,7 +195,7 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
     for (int z = 0; z < NACC; ++z)
         for (int j = 0; j < gn; ++j) {
             const int64_t o = ((int64_t)z * G + g0 + j) * QP + t;
-            part0[o] = acc[(z * kDenseGC + j) * QP + t];
+            part0[o] = acc[(z * GC + j) * QP + t];
             part1[o] = 0.0f;
         }
     if (gc == 0) {
@@ -181,24 +208,26 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
     }
 }
 
-__global__ void __launch_bounds__(128) dense_cost_kernel(CostArgs a, const uint16_t* cnt) {
-    dense_cost_body<false, false>(a, cnt);
+__global__ void __launch_bounds__(128) dense_cost_kernel(CostArgs a, const uint16_t* cnt, int GC) {
+    dense_cost_body<false, false>(a, cnt, GC);
 }
-__global__ void __launch_bounds__(128) dense_cost_unc_kernel(CostArgs a, const uint16_t* cnt) {
-    dense_cost_body<true, false>(a, cnt);
+__global__ void __launch_bounds__(128) dense_cost_unc_kernel(CostArgs a, const uint16_t* cnt, int GC) {
+    dense_cost_body<true, false>(a, cnt, GC);
 }
-__global__ void __launch_bounds__(128) dense_cost_foc_kernel(CostArgs a, const uint16_t* cnt) {
-    dense_cost_body<false, true>(a, cnt);
+__global__ void __launch_bounds__(128) dense_cost_foc_kernel(CostArgs a, const uint16_t* cnt, int GC) {
+    dense_cost_body<false, true>(a, cnt, GC);
 }
-__global__ void __launch_bounds__(128) dense_cost_unc_foc_kernel(CostArgs a, const uint16_t* cnt) {
-    dense_cost_body<true, true>(a, cnt);
+__global__ void __launch_bounds__(128) dense_cost_unc_foc_kernel(CostArgs a, const uint16_t* cnt, int GC) {
+    dense_cost_body<true, true>(a, cnt, GC);
 }
 
-size_t dense_cost_smem(int qrows_pad, bool unc) {
+// GT columns per block: all of them up to kDenseGC (shared memory scales with it).
+int dense_gc(int gout) { return std::max(1, std::min(gout, kDenseGC)); }
+
+size_t dense_cost_smem(int qrows_pad, bool unc, int gc) {
     const int nacc = unc ? 3 : 2;
-    return sizeof(float) * ((size_t)qrows_pad * (kDenseTile + 1) + (size_t)nacc * kDenseGC * qrows_pad) +
-           sizeof(int) * (kDenseTile + (size_t)kDenseTile * kDenseGC) +
-           sizeof(float) * (size_t)kDenseTile * kDenseGC;
+    return sizeof(float) * ((size_t)qrows_pad * (kDenseTile + 1) + (size_t)nacc * gc * qrows_pad) +
+           sizeof(int) * (kDenseTile + (size_t)kDenseTile * gc) + 2 * sizeof(float) * (size_t)kDenseTile * gc;
 }
 
 cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht, int Wt, int s,
@@ -212,14 +241,15 @@ cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht
 
 cudaError_t launch_dense_cost(const CostArgs& a, bool unc, bool foc, const uint16_t* cnt,
                               cudaStream_t st) {
-    const size_t smem = dense_cost_smem(a.qrows_pad, unc);
-    const int ngc = (a.gout + kDenseGC - 1) / kDenseGC;
+    const int gc = dense_gc(a.gout);
+    const size_t smem = dense_cost_smem(a.qrows_pad, unc, gc);
+    const int ngc = (a.gout + gc - 1) / gc;
     dim3 g(a.nchunk * ngc, a.nqt, a.L * a.B);
     auto k = unc ? (foc ? dense_cost_unc_foc_kernel : dense_cost_unc_kernel)
                  : (foc ? dense_cost_foc_kernel : dense_cost_kernel);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    k<<<g, a.qrows_pad, smem, st>>>(a, cnt);
+    k<<<g, a.qrows_pad, smem, st>>>(a, cnt, gc);
     return cudaGetLastError();
 }
 

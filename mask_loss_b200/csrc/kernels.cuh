@@ -185,7 +185,8 @@ cudaError_t launch_dice_backward(SemArgs a, cudaStream_t st);
 
 namespace mlb {
 // Dense per-GT mask targets (dense.cu).
-size_t dense_cost_smem(int qrows_pad, bool unc);
+size_t dense_cost_smem(int qrows_pad, bool unc, int gc);
+int dense_gc(int gout);
 cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht, int Wt, int s,
                                int gt_total, uint16_t* cnt, int32_t* totals, cudaStream_t st);
 cudaError_t launch_dense_cost(const CostArgs& a, bool unc, bool foc, const uint16_t* cnt,
