@@ -30,7 +30,8 @@ constexpr int kDenseTile = 32;   // cells per staged tile
 constexpr int kDenseGC = 64;     // GT columns per block (grid chunk)
 }  // namespace
 
-// grid = (ceil(HW / 256), B), block 256: thread per cell.
+// grid = (ceil(HW / 256), B), block 256: thread per cell; eight GT planes'
+// loads in flight per thread, areas summed per warp.
 __global__ void __launch_bounds__(256)
 dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int Wt, int s,
                    int gt_total, uint16_t* __restrict__ cnt, int32_t* __restrict__ totals) {
@@ -40,16 +41,32 @@ dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int 
     for (int g = threadIdx.x; g < gt_total; g += blockDim.x) area[g] = 0;
     __syncthreads();
     const int cell = blockIdx.x * blockDim.x + threadIdx.x;
-    if (cell < HW) {
-        const int ci = cell / W, cj = cell - ci * W;
-        for (int g = 0; g < gt_total; ++g) {
-            const uint8_t* mg = masks + ((int64_t)b * gt_total + g) * Ht * Wt +
-                                (int64_t)(ci * s) * Wt + (int64_t)cj * s;
-            int n = 0;
-            for (int dy = 0; dy < s; ++dy)
-                for (int dx = 0; dx < s; ++dx) n += mg[(int64_t)dy * Wt + dx] != 0;
-            cnt[((int64_t)b * gt_total + g) * HW + cell] = (uint16_t)n;
-            if (n) atomicAdd(&area[g], n);
+    const bool valid = cell < HW;
+    const int ci = valid ? cell / W : 0, cj = valid ? cell - ci * W : 0;
+    const int64_t off = (int64_t)(ci * s) * Wt + (int64_t)cj * s;
+    for (int g0 = 0; g0 < gt_total; g0 += 8) {
+        int n[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            n[u] = 0;
+            const int g = g0 + u;
+            if (valid && g < gt_total) {
+                const uint8_t* mg = masks + ((int64_t)b * gt_total + g) * Ht * Wt + off;
+                if (s == 1) {
+                    n[u] = mg[0] != 0;
+                } else {
+                    for (int dy = 0; dy < s; ++dy)
+                        for (int dx = 0; dx < s; ++dx) n[u] += mg[(int64_t)dy * Wt + dx] != 0;
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int g = g0 + u;
+            if (g >= gt_total) break;
+            if (valid) cnt[((int64_t)b * gt_total + g) * HW + cell] = (uint16_t)n[u];
+            const int sum = (int)__reduce_add_sync(0xffffffffu, (unsigned)n[u]);
+            if ((threadIdx.x & 31) == 0 && sum) atomicAdd(&area[g], sum);
         }
     }
     __syncthreads();
@@ -57,7 +74,7 @@ dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int 
         if (area[g]) atomicAdd(&totals[(int64_t)b * gt_total + g], area[g]);
 }
 
-// grid = (nchunk * ngc, nqt, L*B), block = QP threads (query row t of the tile).
+// grid = (nchunk * 2 halves * ngc, nqt, L*B), block = QP threads (query row t of the tile).
 // Dynamic shared memory: see dense_cost_smem.
 template <bool UNC, bool FOC>
 __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_t* cnt, int GC) {
@@ -67,15 +84,18 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
     extern __shared__ __align__(16) float dsh[];
     const int QP = a.qrows_pad, G = a.gout;
     const int ngc = (G + GC - 1) / GC;
-    const int chunk = blockIdx.x / ngc, gc = blockIdx.x - chunk * ngc;
+    const int slot = blockIdx.x / ngc, gc = blockIdx.x - slot * ngc;  // slot = 2 * chunk + half
+    const int chunk = slot >> 1, half = slot & 1;
     const int g0 = gc * GC, g1 = min(G, g0 + GC), gn = g1 - g0;
     const int qt = blockIdx.y, lb = blockIdx.z, b = lb % a.B;
     const int t = threadIdx.x;
     const int q = qt * a.qrows + t;
     const bool qvalid = t < a.qrows && q < a.Q;
     const int HW = a.H * a.W;
-    const int cell_begin = chunk * a.chunk_cells;
-    const int cell_end = min(HW, cell_begin + a.chunk_cells);
+    // each half of a chunk (a multiple of 64 cells) fills its own partial slot
+    const int half_cells = a.chunk_cells / 2;
+    const int cell_begin = min(HW, chunk * a.chunk_cells + half * half_cells);
+    const int cell_end = min(HW, cell_begin + half_cells);
     float* xs = dsh;                                         // [QP][kDenseTile + 1]
     float* acc = xs + QP * (kDenseTile + 1);                 // [NACC][GC][QP]
     int* lcnt = reinterpret_cast<int*>(acc + NACC * GC * QP);  // [kDenseTile]
@@ -89,6 +109,17 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
 #pragma unroll
     for (int i = 0; i < NROW; ++i) rows[i] = 0.0f;
     const int warp = t >> 5, lane = t & 31;
+    // two register slots cache the running sums of the last two GTs seen (runs
+    // of cells of one GT are the common case); others go to shared memory
+    int cj0 = -1, cj1 = -1;
+    float s0[NACC], s1[NACC];
+#pragma unroll
+    for (int z = 0; z < NACC; ++z) { s0[z] = 0.0f; s1[z] = 0.0f; }
+    auto flush = [&](int j, const float* c) {
+        if (j < 0) return;
+#pragma unroll
+        for (int z = 0; z < NACC; ++z) acc[(z * GC + j) * QP + t] += c[z];
+    };
     // logits tile in registers: thread t holds float4 (t + m*QP), m < 8 --
     // row i >> 3, cells 4*(i & 7) .. +3 -- so the next tile's loads are in
     // flight while the current one is computed.  Rows and cells are
@@ -177,34 +208,38 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
                     v[1] = w * e.p;
                     if (UNC) v[NACC - 1] = w;
                 }
-                const int m = lcnt[k];
+                const int m = lcnt[k];  // same list for every thread: uniform branches
                 for (int i = 0; i < m; ++i) {
                     const int j = lg[k * GC + i];
                     const float n = ln[k * GC + i];
+                    if (j == cj0) {
 #pragma unroll
-                    for (int z = 0; z < NACC; ++z) acc[(z * GC + j) * QP + t] += v[z] * n;
+                        for (int z = 0; z < NACC; ++z) s0[z] = fmaf(v[z], n, s0[z]);
+                    } else if (j == cj1) {
+#pragma unroll
+                        for (int z = 0; z < NACC; ++z) s1[z] = fmaf(v[z], n, s1[z]);
+                    } else {
+                        flush(cj1, s1);
+                        cj1 = cj0;
+#pragma unroll
+                        for (int z = 0; z < NACC; ++z) { s1[z] = s0[z]; s0[z] = v[z] * n; }
+                        cj0 = j;
+                    }
                 }
             }
         }
     }
+    flush(cj1, s1);
+    flush(cj0, s0);
     __syncthreads();
     if (!qvalid) return;
-    // slot h = 0 carries the chunk, slot h = 1 is cleared (the finalize sums both)
-    float* part0 = a.part + (((int64_t)lb * a.nqt + qt) * a.nchunk + chunk) * 2 * (int64_t)a.part_stride;
-    float* part1 = part0 + a.part_stride;
+    float* part = a.part + ((((int64_t)lb * a.nqt + qt) * a.nchunk + chunk) * 2 + half) * (int64_t)a.part_stride;
     for (int z = 0; z < NACC; ++z)
-        for (int j = 0; j < gn; ++j) {
-            const int64_t o = ((int64_t)z * G + g0 + j) * QP + t;
-            part0[o] = acc[(z * GC + j) * QP + t];
-            part1[o] = 0.0f;
-        }
+        for (int j = 0; j < gn; ++j)
+            part[((int64_t)z * G + g0 + j) * QP + t] = acc[(z * GC + j) * QP + t];
     if (gc == 0) {
 #pragma unroll
-        for (int i = 0; i < NROW; ++i) {
-            const int64_t o = (int64_t)NACC * G * QP + (int64_t)i * QP + t;
-            part0[o] = (FAST && i == 2) ? rows[2] : rows[i];
-            part1[o] = 0.0f;
-        }
+        for (int i = 0; i < NROW; ++i) part[(int64_t)NACC * G * QP + (int64_t)i * QP + t] = rows[i];
     }
 }
 
@@ -244,7 +279,7 @@ cudaError_t launch_dense_cost(const CostArgs& a, bool unc, bool foc, const uint1
     const int gc = dense_gc(a.gout);
     const size_t smem = dense_cost_smem(a.qrows_pad, unc, gc);
     const int ngc = (a.gout + gc - 1) / gc;
-    dim3 g(a.nchunk * ngc, a.nqt, a.L * a.B);
+    dim3 g(a.nchunk * 2 * ngc, a.nqt, a.L * a.B);
     auto k = unc ? (foc ? dense_cost_unc_foc_kernel : dense_cost_unc_kernel)
                  : (foc ? dense_cost_foc_kernel : dense_cost_kernel);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
