@@ -203,9 +203,9 @@ def run_reference(args, cfg):
 # ---------------------------------------------------------------------------
 # GPU implementation
 # ---------------------------------------------------------------------------
-def read_traffic(cfg_name: str):
+def read_traffic(cfg_name: str, kernel: str = "cost_partial_kernel"):
     """DRAM bytes per launch of the cost kernel from the committed ncu summary."""
-    p = os.path.join(REPO, "profiles", f"cost_partial_kernel_{cfg_name}.md")
+    p = os.path.join(REPO, "profiles", f"{kernel}_{cfg_name}.md")
     try:
         for line in open(p):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -239,6 +239,12 @@ def run_ours(args, cfg):
     kw = synthetic.parity_kwargs(cfg)
     GT_total = ct.shape[1]
     sampled = cfg.name == "cfg3"
+    dense = args.targets == "dense"
+    if dense:
+        # per-GT masks (B, GT_total, Ht, Wt) uint8 cut from the label maps
+        if ws > 1 or sampled:
+            raise SystemExit("--targets dense runs on one GPU with a label-map config")
+        mt = torch.stack([mt == g for g in range(GT_total)], 1).to(torch.uint8).contiguous()
     pc = None
     if sampled:  # point-sampled configuration: bf16 logits, P points per image
         ml = ml.to(torch.bfloat16)
@@ -251,8 +257,11 @@ def run_ours(args, cfg):
                 None, kw["void_class_index"], "softmax", False)
 
     def step(ml_in, mt_in, cl_in, ct_in):
-        nm = parallel.global_num_masks(ops.count_masks(mt_in, ct_in.shape[1],
-                                                       kw["background_index"]))
+        if dense:
+            nm = "auto"  # the forward counts the non-empty masks itself
+        else:
+            nm = parallel.global_num_masks(ops.count_masks(mt_in, ct_in.shape[1],
+                                                           kw["background_index"]))
         x = ml_in.detach().requires_grad_(True)
         z = cl_in.detach().requires_grad_(True)
         if sampled:
@@ -394,14 +403,17 @@ def run_ours(args, cfg):
     # roofline of the dominant kernel: the streaming cost kernel reads every
     # logit once plus one int32 code per cell and image
     cells = synthetic.CFG3_POINTS if sampled else cfg.H * cfg.W  # sampled values are fp32
-    cost_bytes = cfg.L * cfg.B * cfg.Q * cells * 4 + cfg.B * cells * 4
+    cost_kernel = "dense_cost_kernel" if dense else "cost_partial_kernel"
+    # dense: every logit plus each GT's uint16 count per cell
+    cost_bytes = (cfg.L * cfg.B * cfg.Q * cells * 4 +
+                  (cfg.B * cells * (GT_total - 1) * 2 if dense else cfg.B * cells * 4))
     cost_ms = float(kms[0] / max(kn[0], 1))
     achieved = cost_bytes / (cost_ms / 1e3) / 1e9
-    traffic = read_traffic(cfg.name)
+    traffic = read_traffic(cfg.name, cost_kernel)
     grad_ms = float(kms[1] / max(kn[1], 1))
     match_ms = float(kms[2] / max(kn[2], 1))
     cpu = None
-    if ws == 1 and not sampled:
+    if ws == 1 and not sampled and not dense:
         threads = max(1, os.cpu_count() or 1)
         n_img = min(threads, 2 * cfg.B)
         v, dt, solver = cpu_images_per_sec(cfg, n_img, threads)
@@ -417,18 +429,20 @@ def run_ours(args, cfg):
         "data": (f"synthetic (seeded, {cfg.name} shapes)" +
                  (f"; {synthetic.CFG3_POINTS} uniform points per image" if sampled else
                   "; inputs > L2, no flush needed")),
-        "config": {"workload": cfg.name, "images_per_gpu": cfg.B, "global_batch": ws * cfg.B,
+        "config": {"workload": cfg.name + ("-dense" if dense else ""),
+                   "targets": ("per-GT uint8 masks (B,GT,Ht,Wt)" if dense else "label map (B,Ht,Wt)"),
+                   "images_per_gpu": cfg.B, "global_batch": ws * cfg.B,
                    "Q": cfg.Q, "HW": f"{cfg.H}x{cfg.W}", "classes": cfg.C, "K": 1,
                    "strategy": "global", "label_loss": "softmax", "parallelism": f"dp{ws}",
                    "l2": ("inputs larger than L2" if not flush_ms else
                           f"L2 flushed before every step (256 MB write, {flush_ms:.3f} ms, subtracted)")},
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": ms_e2e},
-        "roofline": {"bound": "hbm", "kernel": "cost_partial_kernel", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": cost_kernel, "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "algorithmic_bytes_per_launch": cost_bytes, "avg_launch_ms": cost_ms,
                      "peak_source": peak_src},
-        "stages_ms": {"cost_partial_kernel": cost_ms, "mask_grad_kernel": grad_ms,
+        "stages_ms": {cost_kernel: cost_ms, "mask_grad_kernel": grad_ms,
                       "match_kernel": match_ms, "eager_step": ms_eager},
         "execution": "value and e2e replay the step as one CUDA graph "
                      "(mask_loss_b200.graphs.MatchingLossStep); stage times from eager steps",
@@ -447,6 +461,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--targets", default="labels", choices=["labels", "dense"],
+                    help="dense: per-GT uint8 masks instead of the label map (one GPU)")
     args = ap.parse_args()
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         quiet_stdout()

@@ -421,7 +421,10 @@ int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigne
     }
     const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
     if (LBQ == 0 || P.gout == 0) return ML_OK;
-    e = launch_dense_cost(a, P.unc, P.foc, cnt, st);
+    {
+        ProfScope prof(0, st);  // profiled as the cost stage
+        e = launch_dense_cost(a, P.unc, P.foc, cnt, st);
+    }
     g_launches.fetch_add(1);
     if (e != cudaSuccess) return cuda_fail(e, "dense_cost_kernel");
     return run_finalize(P, a, st);
