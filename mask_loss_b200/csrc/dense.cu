@@ -180,6 +180,7 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
         __syncthreads();
         if (c0 + kDenseTile < cell_end) load_tile(c0 + kDenseTile);
         if (t < a.qrows) {
+#pragma unroll 4
             for (int k = 0; k < nv; ++k) {
                 const float x = xs[t * (kDenseTile + 1) + k];
                 float v[NACC];
