@@ -89,7 +89,7 @@ def _overlap_case(seed, L, B, Q, H, W, s, C, GT):
     return ml, masks, cl, ct
 
 
-@pytest.mark.parametrize("variant", ["softmax", "unc_sigmoid_focal", "s2_forced_k2"])
+@pytest.mark.parametrize("variant", ["softmax", "unc_sigmoid_focal", "s2_forced_k2", "s3_unc_nobg"])
 def test_dense_overlapping_against_oracle(variant):
     if variant == "softmax":
         shp = (2, 2, 12, 8, 9, 1, 7, 6)
@@ -101,6 +101,11 @@ def test_dense_overlapping_against_oracle(variant):
         P = O.Params(smooth=1.0, sigmoid_scale=2.0, dice_scale=3.0, cls_scale=1.5,
                      background_index=0, uncertainty_gamma=1.0, num_masks=4.0, mask_gamma=2.0,
                      mask_alpha=0.25, cls_gamma=1.5, cls_alpha=0.3)
+    elif variant == "s3_unc_nobg":
+        shp = (2, 2, 9, 5, 7, 3, 4, 6)
+        P = O.Params(smooth=0.5, sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0,
+                     background_index=-1, uncertainty_gamma=1.0, uncertainty_gamma_min=0.1,
+                     strategy_id=1, topk_matches=2)
     else:
         shp = (1, 2, 14, 6, 6, 2, 6, 5)
         P = O.Params(smooth=1.0, sigmoid_scale=5.0, dice_scale=5.0, cls_scale=2.0,

@@ -57,7 +57,8 @@ def _random_case(seed, L, B, C, H, W, s, noisy):
 
 @pytest.mark.parametrize("case", [
     (1, 2, 3, 9, 13, 1, False), (2, 1, 7, 16, 16, 4, True), (1, 3, 20, 8, 8, 2, True),
-    (3, 2, 133, 16, 16, 1, False), (1, 1, 5, 17, 19, 3, True)])
+    (3, 2, 133, 16, 16, 1, False), (1, 1, 5, 17, 19, 3, True),
+    (1, 2, 300, 9, 7, 5, True), (2, 1, 11, 6, 5, 6, False)])
 def test_semantic_random_against_oracle(case):
     x, t, go = _random_case(sum(case[:6]), *case)
     xd_, td_, god = x.to(DEV), t.to(DEV), go.to(DEV)
