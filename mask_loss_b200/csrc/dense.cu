@@ -14,9 +14,11 @@
 //                       mask area (the histogram the label path builds);
 //   dense_cost_kernel   per (layer*image, query tile, cell chunk, GT chunk of up to 64)
 //                       the chunk partials in the label path's layout: row
-//                       sums, and per GT sum(val * count) accumulated in shared
-//                       memory from a per-tile list of the non-zero
-//                       (GT, count) pairs of each cell.  Deterministic: every
+//                       sums, and per GT sum(val * count) from a per-tile list
+//                       of the non-zero (GT, count) pairs of each cell; cells
+//                       with equal lists form runs whose value sums are applied
+//                       once per run (registers for the last two GTs, shared
+//                       memory for the rest).  Deterministic: every
 //                       accumulator has one owner thread.
 #include <algorithm>
 
@@ -102,6 +104,7 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
     int* lg = lcnt + kDenseTile;                             // [kDenseTile][GC]
     float* ln = reinterpret_cast<float*>(lg + kDenseTile * GC);  // [kDenseTile][GC]
     float* ct = ln + kDenseTile * GC;                        // [GC][kDenseTile]
+    unsigned* rmask = reinterpret_cast<unsigned*>(ct + kDenseTile * GC);  // run starts of the tile
     for (int i = t; i < NACC * GC * QP; i += blockDim.x) acc[i] = 0.0f;
     const int row0 = lb * a.Q + qt * a.qrows;
     const Focal foc = make_focal(a.mask_gamma, a.mask_alpha);
@@ -115,10 +118,31 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
     float s0[NACC], s1[NACC];
 #pragma unroll
     for (int z = 0; z < NACC; ++z) { s0[z] = 0.0f; s1[z] = 0.0f; }
-    auto flush = [&](int j, const float* c) {
+    auto flush = [&](int j, const float (&c)[NACC]) {
         if (j < 0) return;
 #pragma unroll
         for (int z = 0; z < NACC; ++z) acc[(z * GC + j) * QP + t] += c[z];
+    };
+    // a run's sums times each (GT, count) of its list, through the cache
+    auto apply_run = [&](int kr, const float (&rsum)[NACC]) {
+        const int m = lcnt[kr];
+        for (int i = 0; i < m; ++i) {
+            const int j = lg[kr * GC + i];
+            const float n = ln[kr * GC + i];
+            if (j == cj0) {
+#pragma unroll
+                for (int z = 0; z < NACC; ++z) s0[z] = fmaf(rsum[z], n, s0[z]);
+            } else if (j == cj1) {
+#pragma unroll
+                for (int z = 0; z < NACC; ++z) s1[z] = fmaf(rsum[z], n, s1[z]);
+            } else {
+                flush(cj1, s1);
+                cj1 = cj0;
+#pragma unroll
+                for (int z = 0; z < NACC; ++z) { s1[z] = s0[z]; s0[z] = rsum[z] * n; }
+                cj0 = j;
+            }
+        }
     };
     // logits tile in registers: thread t holds float4 (t + m*QP), m < 8 --
     // row i >> 3, cells 4*(i & 7) .. +3 -- so the next tile's loads are in
@@ -176,10 +200,27 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
                 }
             }
             lcnt[lane] = m;
+            __syncwarp();
+            // run starts: a cell whose list differs from the previous cell's
+            bool start = lane == 0;
+            if (lane > 0 && lane < nv) {
+                const int mp = lcnt[lane - 1];
+                start = mp != m;
+                for (int i = 0; i < m && !start; ++i)
+                    start = lg[lane * GC + i] != lg[(lane - 1) * GC + i] ||
+                            ln[lane * GC + i] != ln[(lane - 1) * GC + i];
+            }
+            const unsigned rm = __ballot_sync(0xffffffffu, start && lane < nv);
+            if (lane == 0) *rmask = rm;
         }
         __syncthreads();
         if (c0 + kDenseTile < cell_end) load_tile(c0 + kDenseTile);
         if (t < a.qrows) {
+            const unsigned rm = *rmask;  // same for every thread: uniform branches
+            float rs[NACC];               // this thread's sums over the current run
+#pragma unroll
+            for (int z = 0; z < NACC; ++z) rs[z] = 0.0f;
+            int kr = 0;
 #pragma unroll 4
             for (int k = 0; k < nv; ++k) {
                 const float x = xs[t * (kDenseTile + 1) + k];
@@ -209,25 +250,16 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
                     v[1] = w * e.p;
                     if (UNC) v[NACC - 1] = w;
                 }
-                const int m = lcnt[k];  // same list for every thread: uniform branches
-                for (int i = 0; i < m; ++i) {
-                    const int j = lg[k * GC + i];
-                    const float n = ln[k * GC + i];
-                    if (j == cj0) {
+                if (k > 0 && ((rm >> k) & 1u)) {
+                    apply_run(kr, rs);
 #pragma unroll
-                        for (int z = 0; z < NACC; ++z) s0[z] = fmaf(v[z], n, s0[z]);
-                    } else if (j == cj1) {
-#pragma unroll
-                        for (int z = 0; z < NACC; ++z) s1[z] = fmaf(v[z], n, s1[z]);
-                    } else {
-                        flush(cj1, s1);
-                        cj1 = cj0;
-#pragma unroll
-                        for (int z = 0; z < NACC; ++z) { s1[z] = s0[z]; s0[z] = v[z] * n; }
-                        cj0 = j;
-                    }
+                    for (int z = 0; z < NACC; ++z) rs[z] = 0.0f;
+                    kr = k;
                 }
+#pragma unroll
+                for (int z = 0; z < NACC; ++z) rs[z] += v[z];
             }
+            if (nv > 0) apply_run(kr, rs);
         }
     }
     flush(cj1, s1);
@@ -263,7 +295,8 @@ int dense_gc(int gout) { return std::max(1, std::min(gout, kDenseGC)); }
 size_t dense_cost_smem(int qrows_pad, bool unc, int gc) {
     const int nacc = unc ? 3 : 2;
     return sizeof(float) * ((size_t)qrows_pad * (kDenseTile + 1) + (size_t)nacc * gc * qrows_pad) +
-           sizeof(int) * (kDenseTile + (size_t)kDenseTile * gc) + 2 * sizeof(float) * (size_t)kDenseTile * gc;
+           sizeof(int) * (kDenseTile + (size_t)kDenseTile * gc) + 2 * sizeof(float) * (size_t)kDenseTile * gc +
+           16;
 }
 
 cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht, int Wt, int s,
