@@ -135,6 +135,14 @@ EncodeTiledFn encode_fn() {
 // ---------------------------------------------------------------------------
 // Forward plan: tiling, workspace layout.
 // ---------------------------------------------------------------------------
+// The mixed-cell table replaces per-pixel label reads for s > 1 (see
+// common.cuh for its layout and limits).
+bool mixtab_usable(int s, int gout) {
+    return s > 1 && s <= 255 && gout <= kMixMaxCols;
+}
+
+size_t mixtab_bytes(int B, int HW) { return align256(sizeof(uint4) * (size_t)B * HW); }
+
 struct FwdPlan {
     int L, B, Q, H, W, Ht, Wt, s, C, gt_total, gout, bg;
     bool unc, foc, tma_ok;
@@ -143,6 +151,7 @@ struct FwdPlan {
     size_t cost_smem;
     // workspace offsets
     size_t off_totals, off_codes, off_part, off_sep, off_total, off_rawI, off_rawT, off_qstat, bytes;
+    size_t off_mixtab;  // mixed-cell table (s > 1), or SIZE_MAX when not used
 };
 
 size_t cost_smem_bytes(int qrows_pad) {
@@ -264,6 +273,11 @@ int make_plan(const ml_dims* d, const ml_params* p, FwdPlan* P) {
     size_t off = 0;
     P->off_totals = off; off += align256(sizeof(int32_t) * (size_t)P->B * P->gt_total);
     P->off_codes = off; off += align256(sizeof(int32_t) * (size_t)P->B * HW);
+    P->off_mixtab = SIZE_MAX;
+    if (mixtab_usable(P->s, P->gout)) {
+        P->off_mixtab = off;
+        off += mixtab_bytes(P->B, HW);
+    }
     P->off_part = off;
     off += align256(sizeof(float) * (size_t)base * P->nchunk * 2 * P->part_stride);
     P->off_sep = off; off += align256(sizeof(float) * 3 * LBQG);
@@ -285,6 +299,7 @@ CostArgs cost_args(const FwdPlan& P, const ml_params* p, const float* ml, const 
     a.logits = ml; a.targets = mt; a.cls_logits = cl; a.cls_targets = ct;
     a.totals = reinterpret_cast<int32_t*>(ws + P.off_totals);
     a.codes = reinterpret_cast<int32_t*>(ws + P.off_codes);
+    a.mixtab = P.off_mixtab != SIZE_MAX ? reinterpret_cast<const uint4*>(ws + P.off_mixtab) : nullptr;
     a.part = reinterpret_cast<float*>(ws + P.off_part);
     a.sep = reinterpret_cast<float*>(ws + P.off_sep);
     a.total = reinterpret_cast<float*>(ws + P.off_total);
@@ -334,7 +349,8 @@ int run_prep(const FwdPlan& P, const CostArgs& a, cudaStream_t st) {
         label_code_kernel<<<dim3(bx, P.B), 256, hs, st>>>(a.targets, P.B, P.H, P.W, P.Wt, P.s,
                                                           P.gt_total, P.bg,
                                                           const_cast<int32_t*>(a.codes),
-                                                          const_cast<int32_t*>(a.totals));
+                                                          const_cast<int32_t*>(a.totals),
+                                                          const_cast<uint4*>(a.mixtab));
         ML_CHECK_LAUNCH("label_code_kernel");
     }
     return ML_OK;
@@ -570,7 +586,7 @@ int run_sampled_prep(const SampledPlan& S, const ml_params* p, const void* mask_
         const int bx = (int)std::max<int64_t>(1, std::min<int64_t>((npix + 255) / 256, 65535));
         const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
         label_code_kernel<<<dim3(bx, P.B), 256, hs, st>>>(mask_targets, P.B, S.H, S.W, S.Wt, S.Ht / S.H,
-                                                          P.gt_total, P.bg, nullptr, present);
+                                                          P.gt_total, P.bg, nullptr, present, nullptr);
         ML_CHECK_LAUNCH("label_code_kernel");
         cudaError_t le = launch_point_sort(mask_targets, coords, P.B, S.Ht, S.Wt, S.P, P.gt_total, P.bg,
                                            P.gout, perm, const_cast<int32_t*>(a.codes), scoords,
@@ -650,10 +666,36 @@ size_t ml_mask_matching_workspace_size(const ml_dims* d, const ml_params* p) {
 
 size_t ml_match_workspace_size(int64_t, int64_t, int64_t, int64_t) { return 0; }
 
-size_t ml_mask_matching_backward_workspace_size(const ml_dims* d, const ml_params*) {
-    if (!d) return 0;
+// Backward scratch: coef | statistics | (s > 1 label map) codes | mixed-cell table.
+struct BwdLayout {
+    size_t off_stats, off_codes, off_mixtab, bytes;
+    bool cells;  // codes + table present
+};
+
+static BwdLayout bwd_layout(const ml_dims* d, const ml_params* p) {
+    BwdLayout o{};
     const size_t LBQ = (size_t)d->L * d->B * d->Q;
-    return align256(sizeof(float) * 3 * (size_t)d->L) + align256(sizeof(float) * kSaved * LBQ) + 256;
+    size_t off = align256(sizeof(float) * 3 * (size_t)d->L);
+    o.off_stats = off;
+    off += align256(sizeof(float) * kSaved * LBQ);
+    const int s = d->H > 0 ? (int)(d->Ht / d->H) : 1;
+    const bool skip = p && p->background_index >= 0 && p->background_index < d->GT_total;
+    const int gout = (int)(d->GT_total - (skip ? 1 : 0));
+    const int HW = (int)(d->H * d->W);
+    o.cells = mixtab_usable(s, gout);
+    if (o.cells) {
+        o.off_codes = off;
+        off += align256(sizeof(int32_t) * (size_t)d->B * HW);
+        o.off_mixtab = off;
+        off += mixtab_bytes((int)d->B, HW);
+    }
+    o.bytes = off + 256;
+    return o;
+}
+
+size_t ml_mask_matching_backward_workspace_size(const ml_dims* d, const ml_params* p) {
+    if (!d) return 0;
+    return bwd_layout(d, p).bytes;
 }
 
 int ml_pairwise_mask_loss_forward(const ml_dims* d, const ml_params* p, const float* mask_logits,
@@ -680,14 +722,15 @@ int ml_pairwise_mask_loss_forward_noalloc(const ml_dims* d, const ml_params* p,
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
     if ((rc = make_plan(d, p, &P))) return rc;
-    // scratch layout: totals | codes | chunk partials | per-query statistics
+    // scratch layout: totals | codes | chunk partials | per-query statistics | mixed-cell table
     const size_t LBQ = (size_t)P.L * P.B * P.Q;
     const size_t n_tot = align256(sizeof(int32_t) * (size_t)P.B * P.gt_total);
     const size_t n_codes = align256(sizeof(int32_t) * (size_t)P.B * P.H * P.W);
     const size_t n_part =
         align256(sizeof(float) * (size_t)P.L * P.B * P.nqt * P.nchunk * 2 * P.part_stride);
     const size_t n_qstat = align256(sizeof(float) * kQStat * LBQ);
-    const size_t need = n_tot + n_codes + n_part + n_qstat;
+    const size_t n_mix = P.off_mixtab != SIZE_MAX ? mixtab_bytes(P.B, P.H * P.W) : 0;
+    const size_t need = n_tot + n_codes + n_part + n_qstat + n_mix;
     if (need > kNoAllocScratchBytes)
         return fail(ML_EUNSUPPORTED,
                     "ml_pairwise_mask_loss_forward_noalloc: this call needs %zu bytes of scratch, "
@@ -701,6 +744,8 @@ int ml_pairwise_mask_loss_forward_noalloc(const ml_dims* d, const ml_params* p,
     a.codes = reinterpret_cast<int32_t*>(scratch + n_tot);
     a.part = reinterpret_cast<float*>(scratch + n_tot + n_codes);
     a.qstat = reinterpret_cast<float*>(scratch + n_tot + n_codes + n_part);
+    a.mixtab = n_mix ? reinterpret_cast<const uint4*>(scratch + n_tot + n_codes + n_part + n_qstat)
+                     : nullptr;
     a.sep = out; a.total = nullptr; a.rawI = nullptr; a.rawT = nullptr;
     // run_costs clears the histogram and the partials before use (the array
     // keeps the previous call's contents); codes and statistics are fully
@@ -863,8 +908,9 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
     P.gout = P.gt_total - (skip ? 1 : 0);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char* ws = ws_base(workspace);
+    const BwdLayout lay = bwd_layout(d, p);
     float* coef = reinterpret_cast<float*>(ws);
-    float* stats = reinterpret_cast<float*>(ws + align256(sizeof(float) * 3 * (size_t)P.L));
+    float* stats = reinterpret_cast<float*>(ws + lay.off_stats);
     const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
     if (LBQ == 0) return ML_OK;
     LossArgs la = loss_args(P, p);
@@ -873,6 +919,19 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
     la.grad_mask = grad_mask_mean; la.grad_dice = grad_dice_mean; la.grad_cls = grad_cls_mean;
     la.coef = coef; la.grad_mask_logits = grad_mask_logits; la.grad_cls_logits = grad_cls_logits;
     la.masks = dense_masks;
+    const int HW = P.H * P.W;
+    if (lay.cells && !dense_masks && HW > 0) {
+        // per-cell column codes + mixed-cell table: the gradient kernels read
+        // 4 bytes per cell (16 more on a label boundary) instead of s*s labels
+        int32_t* codes = reinterpret_cast<int32_t*>(ws + lay.off_codes);
+        uint4* mixtab = reinterpret_cast<uint4*>(ws + lay.off_mixtab);
+        const int bx = std::max(1, std::min((HW + 255) / 256, 65535));
+        label_code_kernel<<<dim3(bx, P.B), 256, 0, st>>>(mask_targets, P.B, P.H, P.W, P.Wt, P.s,
+                                                         P.gt_total, P.bg, codes, nullptr, mixtab);
+        ML_CHECK_LAUNCH("label_code_kernel");
+        la.codes = codes;
+        la.mixtab = mixtab;
+    }
     // coefficients + class-logit gradient first; the mask gradient reads coef
     bwd_cls_kernel<<<(unsigned)((LBQ + 7) / 8), 256, 0, st>>>(la);
     ML_CHECK_LAUNCH("bwd_cls_kernel");
@@ -888,7 +947,6 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
         else bwd_stats_kernel<false><<<g, 256, 0, st>>>(la);
         ML_CHECK_LAUNCH("bwd_stats_kernel");
     }
-    const int HW = P.H * P.W;
     const bool vec = (HW % 4 == 0) && (reinterpret_cast<uintptr_t>(mask_logits) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(grad_mask_logits) % 16 == 0);
     // one block per (query row, contiguous range of cells)

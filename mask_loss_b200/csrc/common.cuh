@@ -14,6 +14,31 @@ constexpr int kNone = -1;   // cell/pixel carries no output column
 constexpr int kMixed = -2;  // cell holds more than one label (s > 1 only)
 
 // ----------------------------------------------------------------------------
+// Mixed-cell table (s > 1): one uint4 per low-res cell, written only for cells
+// whose code is kMixed.  Each word packs one output column of the cell and its
+// pixel count as ((col + 1) << 16) | count; 0 = empty slot.  A cell with more
+// than four distinct columns is marked wide (x == kMixWide) and its readers
+// count its pixels from the label map instead.  Needs gout < 65535 and
+// s * s < 65536.
+// ----------------------------------------------------------------------------
+constexpr uint32_t kMixWide = 0xFFFFFFFFu;
+constexpr int kMixMaxCols = 65534;
+
+ML_INLINE int mix_col(uint32_t v) { return (int)(v >> 16) - 1; }
+ML_INLINE float mix_cnt(uint32_t v) { return (float)(v & 0xFFFFu); }
+
+// Pixels of column `col` in a table entry (the entry must not be wide).
+ML_INLINE float mix_count(const uint4& e, int col) {
+    const uint32_t key = (uint32_t)(col + 1) << 16;
+    float n = 0.0f;
+    n = ((e.x & 0xFFFF0000u) == key) ? mix_cnt(e.x) : n;
+    n = ((e.y & 0xFFFF0000u) == key) ? mix_cnt(e.y) : n;
+    n = ((e.z & 0xFFFF0000u) == key) ? mix_cnt(e.z) : n;
+    n = ((e.w & 0xFFFF0000u) == key) ? mix_cnt(e.w) : n;
+    return n;
+}
+
+// ----------------------------------------------------------------------------
 // Label -> output column (GT_out index).  The background column is dropped
 // and later columns shift down by one (src/cuda/utils.cuh:38-40 inverted);
 // labels outside [0, GT_total) belong to no column (src/cuda/utils.cuh:27).

@@ -45,18 +45,19 @@ namespace mlb {
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
 label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int Wt, int s,
-                  int gt_total, int bg, int32_t* __restrict__ codes, int32_t* __restrict__ totals) {
+                  int gt_total, int bg, int32_t* __restrict__ codes, int32_t* __restrict__ totals,
+                  uint4* __restrict__ mixtab) {
     extern __shared__ int32_t hist[];
     const int b = blockIdx.y;
-    const bool use_sh = gt_total <= kHistSmemMax;
+    const bool use_sh = totals && gt_total <= kHistSmemMax;
     if (use_sh)
         for (int i = threadIdx.x; i < gt_total; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const int HW = H * W;
     const int64_t* tb = targets + (int64_t)b * HW * s * s;
     int32_t* cb = codes ? codes + (int64_t)b * HW : nullptr;
-    int32_t* tot = totals + (int64_t)b * gt_total;
-    int32_t* hc = use_sh ? hist : tot;
+    int32_t* tot = totals ? totals + (int64_t)b * gt_total : nullptr;
+    int32_t* hc = use_sh ? hist : tot;  // null: codes only, no histogram
     if (!cb && s > 1) {
         // histogram only: one pixel per thread, coalesced, warp-aggregated
         const int64_t npix = (int64_t)HW * s * s;
@@ -81,24 +82,41 @@ label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int 
             int c = -3;
             const int ci = cell / W, cj = cell - ci * W;
             const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
+            uint32_t e[4] = {0u, 0u, 0u, 0u};  // (col + 1, count) of the cell's columns
+            bool wide = false;
             for (int dy = 0; dy < s; ++dy)
                 for (int dx = 0; dx < s; ++dx) {
                     const int64_t lab = r0[(int64_t)dy * Wt + dx];
                     const int key = (lab >= 0 && lab < gt_total) ? (int)lab : -1;
                     if (key != run) {
-                        if (run >= 0) atomicAdd(&hc[run], rc);
+                        if (run >= 0 && hc) atomicAdd(&hc[run], rc);
                         run = key;
                         rc = 0;
                     }
                     ++rc;
                     const int col = label_to_col(lab, gt_total, bg);
                     c = (c == -3 || c == col) ? col : kMixed;
+                    if (mixtab && col >= 0) {
+                        // slots fill in order, so a column already held sits
+                        // before the first empty slot
+                        const uint32_t kc = (uint32_t)(col + 1) << 16;
+                        bool done = false;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            if (!done && (e[i] & 0xFFFF0000u) == kc) { e[i] += 1u; done = true; }
+                            else if (!done && e[i] == 0u) { e[i] = kc | 1u; done = true; }
+                        }
+                        wide |= !done;
+                    }
                 }
             if (cb) cb[cell] = c;
+            if (mixtab && c == kMixed)
+                mixtab[(int64_t)b * HW + cell] =
+                    wide ? make_uint4(kMixWide, 0u, 0u, 0u) : make_uint4(e[0], e[1], e[2], e[3]);
         }
         // one pixel per cell: lanes on the same label add with one atomic
         const unsigned peers = __match_any_sync(0xffffffffu, run);
-        if (run >= 0) {
+        if (run >= 0 && hc) {
             if (s == 1) {
                 if ((int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hc[run], __popc(peers));
             } else {
@@ -142,9 +160,27 @@ ML_INLINE void red_add(float* p, float v) {
 // Mixed cell (s > 1 on a label boundary): add the cell's per-pixel counts to
 // the columns they belong to, one red.add per pixel and accumulator.
 template <bool UNC>
-__device__ __noinline__ void mixed_cell(const int64_t* targets, int W, int Ht, int Wt, int s,
-                                        int gt_total, int bg, float* part, int b, int cell, int t,
-                                        int QP, int G, float dl, float wp, float w) {
+__device__ __noinline__ void mixed_cell(const int64_t* targets, const uint4* mixtab, int W, int Ht,
+                                        int Wt, int s, int gt_total, int bg, float* part, int b,
+                                        int cell, int t, int QP, int G, float dl, float wp, float w) {
+    if (mixtab) {
+        // one red.add per column of the cell and accumulator, weighted by the
+        // column's pixel count
+        const uint4 e = mixtab[(int64_t)b * (Ht / s) * W + cell];
+        if (e.x != kMixWide) {
+            const uint32_t v[4] = {e.x, e.y, e.z, e.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (v[i] == 0u) break;
+                const float n = mix_cnt(v[i]);
+                float* pc = part + (int64_t)mix_col(v[i]) * QP + t;
+                red_add(pc, n * dl);
+                red_add(pc + (int64_t)G * QP, n * wp);
+                if (UNC) red_add(pc + 2 * (int64_t)G * QP, n * w);
+            }
+            return;
+        }
+    }
     const int ci = cell / W, cj = cell - ci * W;
     const int64_t* r0 = targets + ((int64_t)b * Ht + (int64_t)ci * s) * Wt + (int64_t)cj * s;
     for (int pp = 0; pp < s * s; ++pp) {
@@ -319,7 +355,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
             tabs += fabsf(x);
             trow[1] += f.p;
             if (MIXED_CELL && qvalid)
-                mixed_cell<UNC>(a.targets, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, -x, f.p, 1.0f);
+                mixed_cell<UNC>(a.targets, a.mixtab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, -x, f.p, 1.0f);
         } else {
             const Elem e = elem(x);
             const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
@@ -335,7 +371,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
             racc[1] = fmaf(m, w * e.p, racc[1]);
             if (UNC) racc[2] = fmaf(m, w, racc[2]);
             if (MIXED_CELL && qvalid)
-                mixed_cell<UNC>(a.targets, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, dl, w * e.p, w);
+                mixed_cell<UNC>(a.targets, a.mixtab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, dl, w * e.p, w);
         }
     };
 

@@ -27,6 +27,7 @@ struct CostArgs {
     const int64_t* cls_targets;
     const int32_t* totals;   // (B, GT_total)
     const int32_t* codes;    // (B, H*W) per-cell column code
+    const uint4* mixtab;     // (B, H*W) mixed-cell table (s > 1), or null
     const int32_t* present;  // (B, GT_total) full-image label counts for the +inf mask, or null
     float* part;             // chunk partials
     float* sep;              // (3,L,B,Q,G) or null
@@ -50,7 +51,7 @@ struct CostArgs {
 
 __global__ void label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int Wt,
                                   int s, int gt_total, int bg, int32_t* __restrict__ codes,
-                                  int32_t* __restrict__ totals);
+                                  int32_t* __restrict__ totals, uint4* __restrict__ mixtab);
 
 template <bool UNC, bool FOC, bool TMA, bool MIX>
 __global__ void cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a);
@@ -123,6 +124,8 @@ struct LossArgs {
     int force_masks, force_cls, has_void, void_index, use_softmax, normalize_uncertainty;
     int32_t* void_status;    // forward: bit 4 set when cls_targets holds void_index, or null
     const uint8_t* masks;    // dense (B,GT_total,Ht,Wt) targets instead of the label map, or null
+    const int32_t* codes;    // (B, H*W) per-cell column codes (s > 1 label map), or null
+    const uint4* mixtab;     // (B, H*W) mixed-cell table beside `codes`, or null
 };
 
 __global__ void loss_fwd_kernel(LossArgs a);

@@ -141,6 +141,19 @@ ML_INLINE float cell_count(const int64_t* tb, int cell, int W, int Wt, int s, in
     return (float)c;
 }
 
+// The same count from the per-cell codes of the image (codes_b) and its
+// mixed-cell table (mix_b): a pure cell is all or nothing, a mixed cell reads
+// its table entry, and a wide cell falls back to the label map.  `gcol` is the
+// output column of label `ga`.
+ML_INLINE float cell_count_coded(const int32_t* codes_b, const uint4* mix_b, const int64_t* tb,
+                                 int cell, int W, int Wt, int s, int64_t ga, int gcol, float N2) {
+    const int code = codes_b[cell];
+    if (code != kMixed) return code == gcol ? N2 : 0.0f;
+    const uint4 e = mix_b[cell];
+    if (e.x != kMixWide) return mix_count(e, gcol);
+    return cell_count(tb, cell, W, Wt, s, ga);
+}
+
 // ---------------------------------------------------------------------------
 // Statistics pass for the standalone backward (no saved statistics):
 // grid = (Q, L*B), block = 256.  Mirrors the first loop of
@@ -159,11 +172,16 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(LossArgs a) {
     const float N2 = (float)(a.s * a.s);
     const float* x = a.mask_logits + qi * HW;
     const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
+    const int32_t* codes_b = a.codes ? a.codes + (int64_t)b * HW : nullptr;
+    const uint4* mix_b = a.codes ? a.mixtab + (int64_t)b * HW : nullptr;
+    const int gcol = matched ? label_to_col(ga, a.gt_total, a.bg) : kNone;
     float v[4] = {0.f, 0.f, 0.f, 0.f};  // sum w p, sum w t, sum w p t, sum w
     for (int j = threadIdx.x; j < HW; j += blockDim.x) {
         const Elem e = elem(x[j]);
         const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
-        const float t = matched ? cell_count(tb, j, a.W, a.Wt, a.s, ga) : 0.0f;
+        const float t = !matched ? 0.0f
+                        : codes_b ? cell_count_coded(codes_b, mix_b, tb, j, a.W, a.Wt, a.s, ga, gcol, N2)
+                                  : cell_count(tb, j, a.W, a.Wt, a.s, ga);
         v[0] += w * e.p; v[1] += w * t; v[2] += w * e.p * t; v[3] += w;
     }
     block_sum<4>(v, sh);
@@ -220,6 +238,9 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
     // dense targets: the matched GT's own mask
     const uint8_t* mb = (a.masks && matched) ? a.masks + ((int64_t)b * a.gt_total + ga) * a.Ht * a.Wt
                                              : nullptr;
+    const int32_t* codes_b = a.codes ? a.codes + (int64_t)b * HW : nullptr;
+    const uint4* mix_b = a.codes ? a.mixtab + (int64_t)b * HW : nullptr;
+    const int gcol = matched ? label_to_col(ga, a.gt_total, a.bg) : kNone;
     auto count = [&](int k) -> float {  // pixels of the matched label in cell c0 + k
         if (!matched) return 0.0f;
         if (mb) {
@@ -232,6 +253,7 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
             return (float)n;
         }
         if (s == 1) return tb[c0 + k] == ga ? 1.0f : 0.0f;
+        if (codes_b) return cell_count_coded(codes_b, mix_b, tb, c0 + k, a.W, a.Wt, s, ga, gcol, N2);
         return cell_count(tb, c0 + k, a.W, a.Wt, s, ga);
     };
     auto g1 = [&](float x, float t) -> float {

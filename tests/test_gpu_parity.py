@@ -266,6 +266,40 @@ def test_strided_targets_against_oracle(variant):
         close_grad(gc.cpu().numpy(), egc, "grad cls")
 
 
+@pytest.mark.parametrize("ug", [0.0, 1.0])
+def test_wide_mixed_cells_against_oracle(ug):
+    # uniform random labels at s = 4: most cells hold more than four output
+    # columns, so the mixed-cell table marks them wide and the kernels count
+    # those cells from the label map; the rest go through the table
+    torch.manual_seed(11)
+    L, B, Q, H, W, s, C = 1, 2, 12, 8, 12, 4, 7
+    ml = torch.randn(L, B, Q, H, W) * 3
+    mt = torch.randint(-1, 11, (B, H * s, W * s))
+    mt[:, : 2 * s, : 2 * s] = 3            # a pure block
+    mt[:, 2 * s:3 * s, :] = mt[:, 2 * s:3 * s, :] % 3   # at most three labels per cell
+    G = 11
+    ct = torch.randint(0, C - 1, (B, G))
+    ct[:, 0] = -1
+    cl = torch.randn(L, B, Q, C)
+    P = O.Params(background_index=0, uncertainty_gamma=ug, num_masks=-1.0, void_class_index=C - 1,
+                 use_softmax_label_loss=True, force_unmatched_class_to_background=True)
+    d = [v.to(DEV).contiguous() for v in (ml, mt, cl, ct)]
+    p2g, prd, means, saved, costs = ops.mask_matching_ex(*d, *op_args(P), want_saved=True,
+                                                         want_costs=True)
+    ep2g, eprd, em, ed, ec, esep = O.mask_matching(ml.numpy(), mt.numpy(), cl.numpy(), ct.numpy(), P)
+    close(costs.cpu().numpy(), esep, what="costs")
+    np.testing.assert_array_equal(p2g.cpu().numpy(), ep2g)
+    close(means.cpu().numpy(), np.stack([em, ed, ec]), what="means")
+    g = torch.tensor([[1.2], [0.8], [1.0]], device=DEV)
+    for sv in (saved, None):
+        gm, gc = ops.mask_matching_backward(g[0].contiguous(), g[1].contiguous(), g[2].contiguous(),
+                                            *d[:4], p2g, *bwd_args(P), saved=sv)
+        egm, egc = O.mask_matching_backward([1.2], [0.8], [1.0], ml.numpy(), mt.numpy(),
+                                            cl.numpy(), ct.numpy(), ep2g, P)
+        close_grad(gm.cpu().numpy(), egm, "grad mask")
+        close_grad(gc.cpu().numpy(), egc, "grad cls")
+
+
 def test_label_ops_against_oracle():
     torch.manual_seed(0)
     L, B, Q, C, G = 2, 3, 17, 40, 9

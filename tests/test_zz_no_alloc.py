@@ -61,8 +61,9 @@ def _close(a, b):
 
 
 def test_noalloc_matches_workspace_entry_on_two_calls():
-    # call 1: the Mask2Former COCO shape; call 2: a different, smaller batch
-    for cfg_name, seed, ug in (("cfg2", 1, 0.0), ("cfg1", 2, 1.0)):
+    # call 1: the Mask2Former COCO shape; call 2: a different, smaller batch;
+    # call 3: a 4x label map (codes plus the mixed-cell table in the scratch)
+    for cfg_name, seed, ug in (("cfg2", 1, 0.0), ("cfg1", 2, 1.0), ("cfg3", 3, 0.0)):
         cfg, ml, mt, cl, ct = _inputs(cfg_name, seed)
         kw = synthetic.parity_kwargs(cfg, uncertainty_gamma=ug)
         kw.pop("inf_thresh"); kw.pop("num_masks"); kw.pop("force_unmatched_class_to_background")
