@@ -231,6 +231,22 @@ int ml_mask_matching_backward(const ml_dims* d, const ml_params* p,
                               float* grad_mask_logits, float* grad_cls_logits,
                               void* workspace, size_t workspace_bytes, ml_stream_t stream);
 
+/* As ml_mask_matching_backward, plus forward_workspace (nullable): the      */
+/* workspace of the ml_mask_matching / ml_mask_matching_ex call with the same */
+/* dims and params, left untouched since.  With an s > 1 label map its per-  */
+/* cell codes are reused instead of being rebuilt from the label map.  No    */
+/* reference counterpart (the reference's backward has no workspace).       */
+int ml_mask_matching_backward_ex(const ml_dims* d, const ml_params* p,
+                                 const float* grad_mask_mean, const float* grad_dice_mean,
+                                 const float* grad_cls_mean,
+                                 const float* mask_logits, const int64_t* mask_targets,
+                                 const float* cls_logits, const int64_t* cls_targets,
+                                 const int64_t* pred_to_gt, const float* saved,
+                                 const float* num_masks_dev,
+                                 float* grad_mask_logits, float* grad_cls_logits,
+                                 void* workspace, size_t workspace_bytes, ml_stream_t stream,
+                                 const void* forward_workspace);
+
 /* ---------------------------------------------------------------------- */
 /* Point-sampled costs and matching (config 3).  Replaces                    */
 /* pairwise_sigmoid_cross_entropy_loss_sampling_py                           */

@@ -93,6 +93,9 @@ SIGNATURES = {
     "ml_mask_matching_backward": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params),
                                                  c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                                  c_vp, c_vp, c_vp, c_vp, c_vp, c_sz, c_vp]),
+    "ml_mask_matching_backward_ex": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params),
+                                                    c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                    c_vp, c_vp, c_vp, c_vp, c_vp, c_sz, c_vp, c_vp]),
     "ml_sampled_workspace_size": (c_sz, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_i64]),
     "ml_sampled_backward_workspace_size": (c_sz, [ctypes.POINTER(Dims), ctypes.POINTER(Params),
                                                   c_i64, c_i32]),

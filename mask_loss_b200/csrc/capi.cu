@@ -342,17 +342,17 @@ int run_prep(const FwdPlan& P, const CostArgs& a, cudaStream_t st) {
     cudaError_t e = cudaMemsetAsync(const_cast<int32_t*>(a.totals), 0,
                                     sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
     if (e != cudaSuccess) return cuda_fail(e, "memset totals");
-    const int HW = P.H * P.W;
-    if (P.B > 0 && HW > 0) {
-        const int bx = std::max(1, std::min((HW + 255) / 256, 65535));  // one cell per thread
-        const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
-        label_code_kernel<<<dim3(bx, P.B), 256, hs, st>>>(a.targets, P.B, P.H, P.W, P.Wt, P.s,
-                                                          P.gt_total, P.bg,
-                                                          const_cast<int32_t*>(a.codes),
-                                                          const_cast<int32_t*>(a.totals),
-                                                          const_cast<uint4*>(a.mixtab));
-        ML_CHECK_LAUNCH("label_code_kernel");
+    cudaError_t le;
+    if (a.codes) {
+        le = launch_label_code(a.targets, P.B, P.H, P.W, P.Wt, P.s, P.gt_total, P.bg,
+                               const_cast<int32_t*>(a.codes), const_cast<int32_t*>(a.totals),
+                               const_cast<uint4*>(a.mixtab), st);
+    } else {  // histogram only
+        le = launch_label_hist(a.targets, P.B, (int64_t)P.Ht * P.Wt, P.gt_total,
+                               const_cast<int32_t*>(a.totals), st);
     }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (le != cudaSuccess) return cuda_fail(le, a.codes ? "label_code_kernel" : "label_hist_kernel");
     return ML_OK;
 }
 
@@ -581,13 +581,10 @@ int run_sampled_prep(const SampledPlan& S, const ml_params* p, const void* mask_
     if (e != cudaSuccess) return cuda_fail(e, "memset histograms");
     const int HW = S.H * S.W;
     if (P.B > 0) {
-        // histogram only: one label pixel per thread
-        const int64_t npix = (int64_t)S.Ht * S.Wt;
-        const int bx = (int)std::max<int64_t>(1, std::min<int64_t>((npix + 255) / 256, 65535));
-        const size_t hs = P.gt_total <= kHistSmemMax ? sizeof(int32_t) * P.gt_total : 0;
-        label_code_kernel<<<dim3(bx, P.B), 256, hs, st>>>(mask_targets, P.B, S.H, S.W, S.Wt, S.Ht / S.H,
-                                                          P.gt_total, P.bg, nullptr, present, nullptr);
-        ML_CHECK_LAUNCH("label_code_kernel");
+        cudaError_t he = launch_label_hist(mask_targets, P.B, (int64_t)S.Ht * S.Wt, P.gt_total,
+                                           present, st);
+        g_launches.fetch_add(1, std::memory_order_relaxed);
+        if (he != cudaSuccess) return cuda_fail(he, "label_hist_kernel");
         cudaError_t le = launch_point_sort(mask_targets, coords, P.B, S.Ht, S.Wt, S.P, P.gt_total, P.bg,
                                            P.gout, perm, const_cast<int32_t*>(a.codes), scoords,
                                            const_cast<int32_t*>(a.totals), st);
@@ -890,7 +887,8 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
                          const int64_t* pred_to_gt, const float* saved,
                          const float* num_masks_dev, float* grad_mask_logits,
                          float* grad_cls_logits, void* workspace, size_t workspace_bytes,
-                         ml_stream_t stream, const uint8_t* dense_masks) {
+                         ml_stream_t stream, const uint8_t* dense_masks,
+                         const void* forward_workspace = nullptr) {
     if (dense_masks && !saved)
         return fail(ML_EINVAL, "dense mask targets need the forward's saved statistics");
     int rc = validate_params(p, d ? d->C : 0);
@@ -923,12 +921,22 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
     if (lay.cells && !dense_masks && HW > 0) {
         // per-cell column codes + mixed-cell table: the gradient kernels read
         // 4 bytes per cell (16 more on a label boundary) instead of s*s labels
-        int32_t* codes = reinterpret_cast<int32_t*>(ws + lay.off_codes);
-        uint4* mixtab = reinterpret_cast<uint4*>(ws + lay.off_mixtab);
-        const int bx = std::max(1, std::min((HW + 255) / 256, 65535));
-        label_code_kernel<<<dim3(bx, P.B), 256, 0, st>>>(mask_targets, P.B, P.H, P.W, P.Wt, P.s,
-                                                         P.gt_total, P.bg, codes, nullptr, mixtab);
-        ML_CHECK_LAUNCH("label_code_kernel");
+        int32_t* codes = nullptr;
+        uint4* mixtab = nullptr;
+        FwdPlan FP;
+        if (forward_workspace && make_plan(d, p, &FP) == ML_OK && FP.off_mixtab != SIZE_MAX) {
+            // the forward of the same call built them already
+            unsigned char* fws = ws_base(const_cast<void*>(forward_workspace));
+            codes = reinterpret_cast<int32_t*>(fws + FP.off_codes);
+            mixtab = reinterpret_cast<uint4*>(fws + FP.off_mixtab);
+        } else {
+            codes = reinterpret_cast<int32_t*>(ws + lay.off_codes);
+            mixtab = reinterpret_cast<uint4*>(ws + lay.off_mixtab);
+            cudaError_t ce = launch_label_code(mask_targets, P.B, P.H, P.W, P.Wt, P.s, P.gt_total,
+                                               P.bg, codes, nullptr, mixtab, st);
+            g_launches.fetch_add(1, std::memory_order_relaxed);
+            if (ce != cudaSuccess) return cuda_fail(ce, "label_code_kernel");
+        }
         la.codes = codes;
         la.mixtab = mixtab;
     }
@@ -983,6 +991,20 @@ int ml_mask_matching_backward(const ml_dims* d, const ml_params* p, const float*
                          mask_targets, cls_logits, cls_targets, pred_to_gt, saved, num_masks_dev,
                          grad_mask_logits, grad_cls_logits, workspace, workspace_bytes, stream,
                          nullptr);
+}
+
+int ml_mask_matching_backward_ex(const ml_dims* d, const ml_params* p, const float* grad_mask_mean,
+                                 const float* grad_dice_mean, const float* grad_cls_mean,
+                                 const float* mask_logits, const int64_t* mask_targets,
+                                 const float* cls_logits, const int64_t* cls_targets,
+                                 const int64_t* pred_to_gt, const float* saved,
+                                 const float* num_masks_dev, float* grad_mask_logits,
+                                 float* grad_cls_logits, void* workspace, size_t workspace_bytes,
+                                 ml_stream_t stream, const void* forward_workspace) {
+    return backward_impl(d, p, grad_mask_mean, grad_dice_mean, grad_cls_mean, mask_logits,
+                         mask_targets, cls_logits, cls_targets, pred_to_gt, saved, num_masks_dev,
+                         grad_mask_logits, grad_cls_logits, workspace, workspace_bytes, stream,
+                         nullptr, forward_workspace);
 }
 
 // ---------------------------------------------------------------------------

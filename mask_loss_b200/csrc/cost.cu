@@ -31,7 +31,7 @@
 // order.
 #include <cuda.h>
 
-#include <type_traits>
+#include <algorithm>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -39,15 +39,20 @@
 namespace mlb {
 
 // ---------------------------------------------------------------------------
-// Prep: per-cell code (pure output column / kNone / kMixed) and the per-image
-// label histogram totals[b, lab], lab in [0, GT_total) (the counts.sum({2,3})
-// of src/cuda/pw_mask.cu:391).  grid = (cell blocks, B).
+// Prep: per-cell code (pure output column / kNone / kMixed), the mixed-cell
+// table (s > 1) and the per-image label histogram totals[b, lab], lab in
+// [0, GT_total) (the counts.sum({2,3}) of src/cuda/pw_mask.cu:391).  Each of
+// the three outputs may be null.  One low-res cell per thread; S is s at
+// compile time (0: read from `s_rt`), so a thread issues all s*s label loads
+// before it looks at any.  grid = (cell blocks, B).
 // ---------------------------------------------------------------------------
+template <int S>
 __global__ void __launch_bounds__(256)
-label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int Wt, int s,
+label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int Wt, int s_rt,
                   int gt_total, int bg, int32_t* __restrict__ codes, int32_t* __restrict__ totals,
                   uint4* __restrict__ mixtab) {
     extern __shared__ int32_t hist[];
+    const int s = S > 0 ? S : s_rt;
     const int b = blockIdx.y;
     const bool use_sh = totals && gt_total <= kHistSmemMax;
     if (use_sh)
@@ -57,22 +62,8 @@ label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int 
     const int64_t* tb = targets + (int64_t)b * HW * s * s;
     int32_t* cb = codes ? codes + (int64_t)b * HW : nullptr;
     int32_t* tot = totals ? totals + (int64_t)b * gt_total : nullptr;
-    int32_t* hc = use_sh ? hist : tot;  // null: codes only, no histogram
-    if (!cb && s > 1) {
-        // histogram only: one pixel per thread, coalesced, warp-aggregated
-        const int64_t npix = (int64_t)HW * s * s;
-        for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < npix;
-             base += (int64_t)gridDim.x * blockDim.x) {
-            const int64_t px = base + threadIdx.x;
-            int key = -1;
-            if (px < npix) {
-                const int64_t lab = tb[px];
-                key = (lab >= 0 && lab < gt_total) ? (int)lab : -1;
-            }
-            const unsigned peers = __match_any_sync(0xffffffffu, key);
-            if (key >= 0 && (int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hc[key], __popc(peers));
-        }
-    } else
+    int32_t* hc = use_sh ? hist : tot;  // null: no histogram
+    const bool tab = mixtab != nullptr && s > 1;
     // every thread of the block runs the same number of iterations, so the
     // warp-aggregated count below sees the whole warp
     for (int base = blockIdx.x * blockDim.x; base < HW; base += gridDim.x * blockDim.x) {
@@ -80,54 +71,142 @@ label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int 
         int run = -1, rc = 0;  // this cell's last run of one in-range label
         if (cell < HW) {
             int c = -3;
-            const int ci = cell / W, cj = cell - ci * W;
-            const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
             uint32_t e[4] = {0u, 0u, 0u, 0u};  // (col + 1, count) of the cell's columns
             bool wide = false;
-            for (int dy = 0; dy < s; ++dy)
-                for (int dx = 0; dx < s; ++dx) {
-                    const int64_t lab = r0[(int64_t)dy * Wt + dx];
-                    const int key = (lab >= 0 && lab < gt_total) ? (int)lab : -1;
-                    if (key != run) {
-                        if (run >= 0 && hc) atomicAdd(&hc[run], rc);
-                        run = key;
-                        rc = 0;
-                    }
-                    ++rc;
-                    const int col = label_to_col(lab, gt_total, bg);
-                    c = (c == -3 || c == col) ? col : kMixed;
-                    if (mixtab && col >= 0) {
-                        // slots fill in order, so a column already held sits
-                        // before the first empty slot
-                        const uint32_t kc = (uint32_t)(col + 1) << 16;
-                        bool done = false;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            if (!done && (e[i] & 0xFFFF0000u) == kc) { e[i] += 1u; done = true; }
-                            else if (!done && e[i] == 0u) { e[i] = kc | 1u; done = true; }
-                        }
-                        wide |= !done;
-                    }
+            const int ci = cell / W, cj = cell - ci * W;
+            const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
+            auto pixel = [&](int64_t lab) {
+                const int key = (lab >= 0 && lab < gt_total) ? (int)lab : -1;
+                if (key != run) {
+                    if (run >= 0 && hc) atomicAdd(&hc[run], rc);
+                    run = key;
+                    rc = 0;
                 }
+                ++rc;
+                const int col = label_to_col(lab, gt_total, bg);
+                c = (c == -3 || c == col) ? col : kMixed;
+                if (tab && col >= 0) {
+                    // slots fill in order, so a column already held sits
+                    // before the first empty slot
+                    const uint32_t kc = (uint32_t)(col + 1) << 16;
+                    bool done = false;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        if (!done && (e[i] & 0xFFFF0000u) == kc) { e[i] += 1u; done = true; }
+                        else if (!done && e[i] == 0u) { e[i] = kc | 1u; done = true; }
+                    }
+                    wide |= !done;
+                }
+            };
+            if (S > 0) {
+                int64_t v[S > 0 ? S * S : 1];
+#pragma unroll
+                for (int dy = 0; dy < S; ++dy)
+#pragma unroll
+                    for (int dx = 0; dx < S; ++dx) v[dy * S + dx] = r0[(int64_t)dy * Wt + dx];
+#pragma unroll
+                for (int i = 0; i < (S > 0 ? S * S : 1); ++i) pixel(v[i]);
+            } else {
+                for (int dy = 0; dy < s; ++dy)
+                    for (int dx = 0; dx < s; ++dx) pixel(r0[(int64_t)dy * Wt + dx]);
+            }
             if (cb) cb[cell] = c;
-            if (mixtab && c == kMixed)
+            if (tab && c == kMixed)
                 mixtab[(int64_t)b * HW + cell] =
                     wide ? make_uint4(kMixWide, 0u, 0u, 0u) : make_uint4(e[0], e[1], e[2], e[3]);
         }
-        // one pixel per cell: lanes on the same label add with one atomic
-        const unsigned peers = __match_any_sync(0xffffffffu, run);
-        if (run >= 0 && hc) {
-            if (s == 1) {
-                if ((int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hc[run], __popc(peers));
-            } else {
-                atomicAdd(&hc[run], rc);
-            }
+        // lanes whose last runs share a label add them with one atomic
+        if (hc) {
+            const unsigned peers = __match_any_sync(0xffffffffu, run);
+            const int n = (int)__reduce_add_sync(peers, (unsigned)rc);
+            if (run >= 0 && (int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hc[run], n);
         }
     }
     __syncthreads();
     if (use_sh)
         for (int i = threadIdx.x; i < gt_total; i += blockDim.x)
             if (hist[i]) atomicAdd(&tot[i], hist[i]);
+}
+
+// Histogram only, over the flat label map of each image (any shape): a thread
+// counts 8 consecutive pixels as runs in registers; runs that end inside its
+// pixels go straight to the shared histogram, and the warp adds the last runs
+// with one atomic per label.  grid = (pixel blocks, B).
+__global__ void __launch_bounds__(256)
+label_hist_kernel(const int64_t* __restrict__ targets, int64_t npix, int gt_total,
+                  int32_t* __restrict__ totals) {
+    extern __shared__ int32_t hist[];
+    const int b = blockIdx.y;
+    const bool use_sh = gt_total <= kHistSmemMax;
+    if (use_sh)
+        for (int i = threadIdx.x; i < gt_total; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const int64_t* tb = targets + (int64_t)b * npix;
+    int32_t* tot = totals + (int64_t)b * gt_total;
+    int32_t* hc = use_sh ? hist : tot;
+    const bool vec = (reinterpret_cast<uintptr_t>(tb) & 15) == 0;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x * 8;
+    for (int64_t base = ((int64_t)blockIdx.x * blockDim.x) * 8; base < npix; base += step) {
+        const int64_t p0 = base + (int64_t)threadIdx.x * 8;
+        int64_t v[8];
+        if (vec && p0 + 8 <= npix) {
+            const longlong2* q = reinterpret_cast<const longlong2*>(tb + p0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const longlong2 t2 = q[i];
+                v[2 * i] = t2.x;
+                v[2 * i + 1] = t2.y;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = p0 + i < npix ? tb[p0 + i] : -1;
+        }
+        int run = -1, rc = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int key = (v[i] >= 0 && v[i] < gt_total) ? (int)v[i] : -1;
+            if (key != run) {
+                if (run >= 0) atomicAdd(&hc[run], rc);
+                run = key;
+                rc = 0;
+            }
+            ++rc;
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, run);
+        const int n = (int)__reduce_add_sync(peers, (unsigned)rc);
+        if (run >= 0 && (int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hc[run], n);
+    }
+    __syncthreads();
+    if (use_sh)
+        for (int i = threadIdx.x; i < gt_total; i += blockDim.x)
+            if (hist[i]) atomicAdd(&tot[i], hist[i]);
+}
+
+cudaError_t launch_label_hist(const int64_t* targets, int B, int64_t npix, int gt_total,
+                              int32_t* totals, cudaStream_t st) {
+    if (B <= 0 || npix <= 0 || gt_total <= 0) return cudaSuccess;
+    const int64_t want = (npix + 8 * 256 - 1) / (8 * 256);
+    const int bx = (int)std::max<int64_t>(1, std::min<int64_t>(want, 65535));
+    const size_t hs = gt_total <= kHistSmemMax ? sizeof(int32_t) * gt_total : 0;
+    label_hist_kernel<<<dim3(bx, B), 256, hs, st>>>(targets, npix, gt_total, totals);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_label_code(const int64_t* targets, int B, int H, int W, int Wt, int s,
+                              int gt_total, int bg, int32_t* codes, int32_t* totals, uint4* mixtab,
+                              cudaStream_t st) {
+    const int HW = H * W;
+    if (B <= 0 || HW <= 0) return cudaSuccess;
+    const int bx = std::max(1, std::min((HW + 255) / 256, 65535));
+    const size_t hs = (totals && gt_total <= kHistSmemMax) ? sizeof(int32_t) * gt_total : 0;
+    const dim3 grid(bx, B);
+    switch (s) {
+        case 1: label_code_kernel<1><<<grid, 256, hs, st>>>(targets, B, H, W, Wt, s, gt_total, bg, codes, totals, mixtab); break;
+        case 2: label_code_kernel<2><<<grid, 256, hs, st>>>(targets, B, H, W, Wt, s, gt_total, bg, codes, totals, mixtab); break;
+        case 4: label_code_kernel<4><<<grid, 256, hs, st>>>(targets, B, H, W, Wt, s, gt_total, bg, codes, totals, mixtab); break;
+        default: label_code_kernel<0><<<grid, 256, hs, st>>>(targets, B, H, W, Wt, s, gt_total, bg, codes, totals, mixtab); break;
+    }
+    return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
@@ -139,8 +218,6 @@ struct Fast {
     float d, p;
 };
 
-constexpr std::integral_constant<bool, false> kNo{};
-constexpr std::integral_constant<bool, true> kYes{};
 
 ML_INLINE Fast fast_elem(float x) {
     const float e = ex2_approx(-fabsf(x) * 1.4426950408889634f);
@@ -160,7 +237,7 @@ ML_INLINE void red_add(float* p, float v) {
 // Mixed cell (s > 1 on a label boundary): add the cell's per-pixel counts to
 // the columns they belong to, one red.add per pixel and accumulator.
 template <bool UNC>
-__device__ __noinline__ void mixed_cell(const int64_t* targets, const uint4* mixtab, int W, int Ht,
+__device__ __forceinline__ void mixed_cell(const int64_t* targets, const uint4* mixtab, int W, int Ht,
                                         int Wt, int s, int gt_total, int bg, float* part, int b,
                                         int cell, int t, int QP, int G, float dl, float wp, float w) {
     if (mixtab) {
@@ -207,7 +284,7 @@ __device__ __noinline__ void mixed_cell(const int64_t* targets, const uint4* mix
 //   MIX   cells cover several target pixels (s > 1), so mixed cells occur
 // ---------------------------------------------------------------------------
 template <bool UNC, bool FOC, bool TMA, bool MIX>
-__global__ void __launch_bounds__(kCostThreads, 2)
+__global__ void __launch_bounds__(kCostThreads, (MIX && !UNC && !FOC) ? 3 : 2)
 cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     constexpr int NACC = UNC ? 3 : 2;
     constexpr int NROW = UNC ? 5 : 3;
@@ -346,16 +423,13 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
             sp0 = trow[1];
         }
     };
-    auto element = [&](float x, int cell, auto mix_tag) {
-        constexpr bool MIXED_CELL = decltype(mix_tag)::value;
+    auto element = [&](float x) {
         if (FAST) {
             const Fast f = fast_elem(x);
             prod *= f.d;
             trow[0] += x;
             tabs += fabsf(x);
             trow[1] += f.p;
-            if (MIXED_CELL && qvalid)
-                mixed_cell<UNC>(a.targets, a.mixtab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, -x, f.p, 1.0f);
         } else {
             const Elem e = elem(x);
             const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
@@ -370,8 +444,27 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
             racc[0] = fmaf(m, dl, racc[0]);
             racc[1] = fmaf(m, w * e.p, racc[1]);
             if (UNC) racc[2] = fmaf(m, w, racc[2]);
-            if (MIXED_CELL && qvalid)
-                mixed_cell<UNC>(a.targets, a.mixtab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b, cell, t, QP, G, dl, w * e.p, w);
+        }
+    };
+    // A mixed cell is a one-cell run with m = 0 in the element loop (its row
+    // sums count there); its contractions are added after the box from the
+    // same shared-memory tile, outside the hot loop.
+    auto mixed_cells = [&](uint32_t mb, const float* rowp, int cbase) {
+        while (mb) {
+            const int k = __ffs(mb) - 1;
+            mb &= mb - 1u;
+            const float x = rowp[((((k >> 2) ^ (t & 7)) << 2)) + (k & 3)];
+            if (FAST) {
+                const Fast f = fast_elem(x);
+                mixed_cell<UNC>(a.targets, a.mixtab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b,
+                                cbase + k, t, QP, G, -x, f.p, 1.0f);
+            } else {
+                const Elem e = elem(x);
+                const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
+                const float dl = FOC ? w * (focal_pos(foc, e) - focal_neg(foc, e)) : -w * x;
+                mixed_cell<UNC>(a.targets, a.mixtab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b,
+                                cbase + k, t, QP, G, dl, w * e.p, w);
+            }
         }
     };
 
@@ -387,7 +480,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
         const int prev = __shfl_up_sync(0xffffffffu, my_code, 1);
         const bool starts = lane < nv && (my_code == kMixed || my_code != (lane == 0 ? cur : prev));
         const uint32_t bnd = __ballot_sync(0xffffffffu, starts);
-        const uint32_t mixb = (FAST && MIX) ? __ballot_sync(0xffffffffu, my_code == kMixed) : 0u;
+        const uint32_t mixb = MIX ? __ballot_sync(0xffffffffu, my_code == kMixed) : 0u;
         const float* rowp = xs + (st * 2 + h) * box_floats + t * KBOX;
 #pragma unroll
         for (int i = 0; i < NROW; ++i) trow[i] = 0.0f;
@@ -401,8 +494,8 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                 const uint32_t b4 = (bnd >> (4 * c)) & 0xFu;
                 if (b4 == 0u) {
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) element(xv[u], cell0 + h * KBOX + 4 * c + u, kNo);
-                } else if (FAST && (!MIX || ((mixb >> (4 * c)) & 0xFu) == 0u)) {
+                    for (int u = 0; u < 4; ++u) element(xv[u]);
+                } else if (FAST) {
                     // run starts but no mixed cell: the four elements first,
                     // then the run switches between the sums
                     Fast f[4];
@@ -432,9 +525,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                             cur = __shfl_sync(0xffffffffu, my_code, 4 * c + u);
                             m = cur >= 0 ? 1.0f : 0.0f;
                         }
-                        // a mixed cell is always a one-cell run
-                        if (MIX && cur == kMixed) element(xv[u], cell0 + h * KBOX + 4 * c + u, kYes);
-                        else element(xv[u], cell0 + h * KBOX + 4 * c + u, kNo);
+                        element(xv[u]);
                     }
                 }
                 if (FAST && (c & 1)) { trow[2] += lg2_approx(prod); prod = 1.0f; }
@@ -448,11 +539,11 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                     cur = __shfl_sync(0xffffffffu, my_code, k);
                     m = cur >= 0 ? 1.0f : 0.0f;
                 }
-                if (MIX && cur == kMixed) element(x, cell0 + h * KBOX + k, kYes);
-                else element(x, cell0 + h * KBOX + k, kNo);
+                element(x);
                 if (FAST) { trow[2] += lg2_approx(prod); prod = 1.0f; }
             }
         }
+        if (MIX && mixb != 0u && qvalid) mixed_cells(mixb, rowp, cell0 + h * KBOX);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
         close_run();

@@ -49,9 +49,13 @@ struct CostArgs {
     int use_softmax, force_cls, has_void, void_index;
 };
 
-__global__ void label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int Wt,
-                                  int s, int gt_total, int bg, int32_t* __restrict__ codes,
-                                  int32_t* __restrict__ totals, uint4* __restrict__ mixtab);
+// Per-cell codes, mixed-cell table and label histogram (each output nullable).
+cudaError_t launch_label_code(const int64_t* targets, int B, int H, int W, int Wt, int s,
+                              int gt_total, int bg, int32_t* codes, int32_t* totals, uint4* mixtab,
+                              cudaStream_t st);
+// Label histogram only, over B flat label maps of npix pixels each.
+cudaError_t launch_label_hist(const int64_t* targets, int B, int64_t npix, int gt_total,
+                              int32_t* totals, cudaStream_t st);
 
 template <bool UNC, bool FOC, bool TMA, bool MIX>
 __global__ void cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a);

@@ -132,15 +132,19 @@ class MatchingLossStep:
             if ml.dtype != torch.float32:
                 raise RuntimeError("mask_logits must be float32")
             args, nm_dev = resolve_args(ml, mt, cl, ct, *a)
-            p2g, prd, means, saved, _ = ops.mask_matching_ex(
+            dense = ops.is_dense(mt)
+            out = ops.mask_matching_ex(
                 ml, mt, cl, ct, *args, num_masks_dev=nm_dev, want_saved=True,
-                check_void_targets=True, loss_wait_event=ev)
+                check_void_targets=True, loss_wait_event=ev, want_workspace=not dense)
+            p2g, prd, means, saved = out[:4]
+            fws = None if dense else out[5]
             if ev is not None:
                 main.wait_stream(self._side)  # join the side branch
             gm, gc = ops.mask_matching_backward(
                 wm, wd, wc, ml, mt, cl, ct, p2g, args[0], args[1], args[2], args[3], args[4],
                 args[5], args[6], args[8], args[9], args[10], args[13], args[14], args[15],
-                args[16], args[17], args[18], args[19], saved=saved, num_masks_dev=nm_dev)
+                args[16], args[17], args[18], args[19], saved=saved, num_masks_dev=nm_dev,
+                forward_workspace=fws)
         return p2g, prd, means, gm, gc
 
     def replay(self) -> None:

@@ -226,7 +226,8 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
                      void_class_index=-1, use_softmax_label_loss=False, normalize_uncertainty=True,
                      *, num_masks_dev: Optional[torch.Tensor] = None, want_saved: bool = False,
                      want_costs: bool = False, check_void_targets: bool = False,
-                     loss_wait_event: Optional[torch.cuda.Event] = None):
+                     loss_wait_event: Optional[torch.cuda.Event] = None,
+                     want_workspace: bool = False):
     """``mask_matching`` plus the extras this implementation offers: a device
     ``num_masks_dev`` (fp32 scalar, e.g. after an all-reduce), the per-query
     statistics the backward can reuse (``saved``) and the cost slices.
@@ -237,7 +238,11 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
     of ``num_masks_dev``) waits for it, so an all-reduce producing that count
     on another stream overlaps the cost and solver kernels.
 
-    Returns (pred_to_gt, pred_round, layer_means(3,L), saved or None, costs or None)."""
+    ``want_workspace``: also return the forward workspace, which
+    mask_matching_backward(forward_workspace=) reuses (label-map targets).
+
+    Returns (pred_to_gt, pred_round, layer_means(3,L), saved or None, costs or None)
+    [+ workspace]."""
     check_status()
     _check_quad(mask_logits, mask_targets, cls_logits, cls_targets)
     if topk_matches < 0:
@@ -291,6 +296,8 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
             _ptr(means), _ptr(costs), _ptr(saved), _ptr(status), _ptr(ws), ws.numel(),
             _stream(dev)))
     _track_status(status)
+    if want_workspace:
+        return p2g, prd, means, saved, costs, ws
     return p2g, prd, means, saved, costs
 
 
@@ -323,8 +330,12 @@ def mask_matching_backward(grad_layer_mask_mean, grad_layer_dice_mean, grad_laye
                            mask_gamma, mask_alpha, cls_gamma, cls_alpha, void_class_index,
                            use_softmax_label_loss=False, normalize_uncertainty=True, *,
                            saved: Optional[torch.Tensor] = None,
-                           num_masks_dev: Optional[torch.Tensor] = None) -> List[torch.Tensor]:
-    """[grad_mask_logits, grad_cls_logits] (src/cuda/mask_matching_backward.cu:378-621)."""
+                           num_masks_dev: Optional[torch.Tensor] = None,
+                           forward_workspace: Optional[torch.Tensor] = None) -> List[torch.Tensor]:
+    """[grad_mask_logits, grad_cls_logits] (src/cuda/mask_matching_backward.cu:378-621).
+
+    ``forward_workspace``: the workspace returned by mask_matching_ex(want_workspace=True)
+    for the same inputs and arguments; its per-cell label codes are reused."""
     check_status()
     for t, n in ((grad_layer_mask_mean, "grad_layer_mask_mean"),
                  (grad_layer_dice_mean, "grad_layer_dice_mean"),
@@ -350,12 +361,18 @@ def mask_matching_backward(grad_layer_mask_mean, grad_layer_dice_mean, grad_laye
         _check_input(saved, "saved")
     if is_dense(mask_targets) and saved is None:
         raise RuntimeError("dense mask targets need the forward's saved statistics (saved=)")
-    fn = lib.ml_mask_matching_dense_backward if is_dense(mask_targets) else lib.ml_mask_matching_backward
-    _lib.check(fn(
-        ctypes.byref(d), ctypes.byref(p), _ptr(grad_layer_mask_mean), _ptr(grad_layer_dice_mean),
-        _ptr(grad_layer_cls_mean), _ptr(mask_logits), _ptr(mask_targets), _ptr(cls_logits),
-        _ptr(cls_targets), _ptr(pred_to_gt), _ptr(saved), _ptr(num_masks_dev), _ptr(gm), _ptr(gc),
-        _ptr(ws), ws.numel(), _stream(dev)))
+    args = (ctypes.byref(d), ctypes.byref(p), _ptr(grad_layer_mask_mean),
+            _ptr(grad_layer_dice_mean), _ptr(grad_layer_cls_mean), _ptr(mask_logits),
+            _ptr(mask_targets), _ptr(cls_logits), _ptr(cls_targets), _ptr(pred_to_gt),
+            _ptr(saved), _ptr(num_masks_dev), _ptr(gm), _ptr(gc), _ptr(ws), ws.numel(),
+            _stream(dev))
+    if is_dense(mask_targets):
+        _lib.check(lib.ml_mask_matching_dense_backward(*args))
+    elif forward_workspace is not None:
+        _check_input(forward_workspace, "forward_workspace")
+        _lib.check(lib.ml_mask_matching_backward_ex(*args, _ptr(forward_workspace)))
+    else:
+        _lib.check(lib.ml_mask_matching_backward(*args))
     return [gm, gc]
 
 

@@ -284,20 +284,25 @@ def test_wide_mixed_cells_against_oracle(ug):
     P = O.Params(background_index=0, uncertainty_gamma=ug, num_masks=-1.0, void_class_index=C - 1,
                  use_softmax_label_loss=True, force_unmatched_class_to_background=True)
     d = [v.to(DEV).contiguous() for v in (ml, mt, cl, ct)]
-    p2g, prd, means, saved, costs = ops.mask_matching_ex(*d, *op_args(P), want_saved=True,
-                                                         want_costs=True)
+    p2g, prd, means, saved, costs, fws = ops.mask_matching_ex(
+        *d, *op_args(P), want_saved=True, want_costs=True, want_workspace=True)
     ep2g, eprd, em, ed, ec, esep = O.mask_matching(ml.numpy(), mt.numpy(), cl.numpy(), ct.numpy(), P)
     close(costs.cpu().numpy(), esep, what="costs")
     np.testing.assert_array_equal(p2g.cpu().numpy(), ep2g)
     close(means.cpu().numpy(), np.stack([em, ed, ec]), what="means")
     g = torch.tensor([[1.2], [0.8], [1.0]], device=DEV)
-    for sv in (saved, None):
+    egm, egc = O.mask_matching_backward([1.2], [0.8], [1.0], ml.numpy(), mt.numpy(),
+                                        cl.numpy(), ct.numpy(), ep2g, P)
+    got = []
+    for sv, fw in ((saved, None), (None, None), (saved, fws)):
         gm, gc = ops.mask_matching_backward(g[0].contiguous(), g[1].contiguous(), g[2].contiguous(),
-                                            *d[:4], p2g, *bwd_args(P), saved=sv)
-        egm, egc = O.mask_matching_backward([1.2], [0.8], [1.0], ml.numpy(), mt.numpy(),
-                                            cl.numpy(), ct.numpy(), ep2g, P)
+                                            *d[:4], p2g, *bwd_args(P), saved=sv,
+                                            forward_workspace=fw)
         close_grad(gm.cpu().numpy(), egm, "grad mask")
         close_grad(gc.cpu().numpy(), egc, "grad cls")
+        got.append(gm)
+    # the forward's codes give the same gradient, bit for bit
+    assert torch.equal(got[0], got[2])
 
 
 def test_label_ops_against_oracle():
