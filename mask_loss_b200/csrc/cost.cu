@@ -64,6 +64,9 @@ label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int 
     int32_t* tot = totals ? totals + (int64_t)b * gt_total : nullptr;
     int32_t* hc = use_sh ? hist : tot;  // null: no histogram
     const bool tab = mixtab != nullptr && s > 1;
+    // even S, even row pitch and a 16-byte aligned map: 16-byte label loads
+    const bool vec = (S % 2 == 0) && (Wt % 2 == 0) &&
+                     (reinterpret_cast<uintptr_t>(targets) & 15) == 0;
     // every thread of the block runs the same number of iterations, so the
     // warp-aggregated count below sees the whole warp
     for (int base = blockIdx.x * blockDim.x; base < HW; base += gridDim.x * blockDim.x) {
@@ -75,7 +78,7 @@ label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int 
             bool wide = false;
             const int ci = cell / W, cj = cell - ci * W;
             const int64_t* r0 = tb + (int64_t)(ci * s) * Wt + (int64_t)cj * s;
-            auto pixel = [&](int64_t lab) {
+            auto pixel = [&](int64_t lab) {  // histogram runs + cell code
                 const int key = (lab >= 0 && lab < gt_total) ? (int)lab : -1;
                 if (key != run) {
                     if (run >= 0 && hc) atomicAdd(&hc[run], rc);
@@ -85,30 +88,61 @@ label_code_kernel(const int64_t* __restrict__ targets, int B, int H, int W, int 
                 ++rc;
                 const int col = label_to_col(lab, gt_total, bg);
                 c = (c == -3 || c == col) ? col : kMixed;
-                if (tab && col >= 0) {
-                    // slots fill in order, so a column already held sits
-                    // before the first empty slot
-                    const uint32_t kc = (uint32_t)(col + 1) << 16;
-                    bool done = false;
+            };
+            auto table = [&](int64_t lab) {  // mixed cells only
+                const int col = label_to_col(lab, gt_total, bg);
+                if (col < 0) return;
+                // slots fill in order, so a column already held sits before
+                // the first empty slot
+                const uint32_t kc = (uint32_t)(col + 1) << 16;
+                bool done = false;
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        if (!done && (e[i] & 0xFFFF0000u) == kc) { e[i] += 1u; done = true; }
-                        else if (!done && e[i] == 0u) { e[i] = kc | 1u; done = true; }
-                    }
-                    wide |= !done;
+                for (int i = 0; i < 4; ++i) {
+                    if (!done && (e[i] & 0xFFFF0000u) == kc) { e[i] += 1u; done = true; }
+                    else if (!done && e[i] == 0u) { e[i] = kc | 1u; done = true; }
                 }
+                wide |= !done;
             };
             if (S > 0) {
-                int64_t v[S > 0 ? S * S : 1];
+                constexpr int N = S > 0 ? S * S : 1;
+                int64_t v[N];
+                if (vec) {  // rows of S labels as 16-byte pairs
 #pragma unroll
-                for (int dy = 0; dy < S; ++dy)
+                    for (int dy = 0; dy < S; ++dy)
 #pragma unroll
-                    for (int dx = 0; dx < S; ++dx) v[dy * S + dx] = r0[(int64_t)dy * Wt + dx];
+                        for (int dx = 0; dx < S; dx += 2) {
+                            const longlong2 t2 =
+                                *reinterpret_cast<const longlong2*>(r0 + (int64_t)dy * Wt + dx);
+                            v[dy * S + dx] = t2.x;
+                            v[dy * S + dx + 1] = t2.y;
+                        }
+                } else {
 #pragma unroll
-                for (int i = 0; i < (S > 0 ? S * S : 1); ++i) pixel(v[i]);
+                    for (int dy = 0; dy < S; ++dy)
+#pragma unroll
+                        for (int dx = 0; dx < S; ++dx) v[dy * S + dx] = r0[(int64_t)dy * Wt + dx];
+                }
+                bool same = true;
+#pragma unroll
+                for (int i = 1; i < N; ++i) same &= v[i] == v[0];
+                if (same) {  // most cells: one label
+                    run = (v[0] >= 0 && v[0] < gt_total) ? (int)v[0] : -1;
+                    rc = N;
+                    c = label_to_col(v[0], gt_total, bg);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < N; ++i) pixel(v[i]);
+                    if (tab && c == kMixed) {
+#pragma unroll
+                        for (int i = 0; i < N; ++i) table(v[i]);
+                    }
+                }
             } else {
                 for (int dy = 0; dy < s; ++dy)
                     for (int dx = 0; dx < s; ++dx) pixel(r0[(int64_t)dy * Wt + dx]);
+                if (tab && c == kMixed)
+                    for (int dy = 0; dy < s; ++dy)
+                        for (int dx = 0; dx < s; ++dx) table(r0[(int64_t)dy * Wt + dx]);
             }
             if (cb) cb[cell] = c;
             if (tab && c == kMixed)
@@ -234,29 +268,27 @@ ML_INLINE void red_add(float* p, float v) {
     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 
-// Mixed cell (s > 1 on a label boundary): add the cell's per-pixel counts to
-// the columns they belong to, one red.add per pixel and accumulator.
+// Mixed cell (s > 1 on a label boundary) with table entry `e`: one red.add
+// per column of the cell and accumulator, weighted by the column's pixel
+// count.  Without a table (tab false) or for a wide cell, one red.add per
+// pixel from the label map.
 template <bool UNC>
-__device__ __forceinline__ void mixed_cell(const int64_t* targets, const uint4* mixtab, int W, int Ht,
-                                        int Wt, int s, int gt_total, int bg, float* part, int b,
-                                        int cell, int t, int QP, int G, float dl, float wp, float w) {
-    if (mixtab) {
-        // one red.add per column of the cell and accumulator, weighted by the
-        // column's pixel count
-        const uint4 e = mixtab[(int64_t)b * (Ht / s) * W + cell];
-        if (e.x != kMixWide) {
-            const uint32_t v[4] = {e.x, e.y, e.z, e.w};
+__device__ __forceinline__ void mixed_cell(const int64_t* targets, const uint4& e, bool tab, int W,
+                                           int Ht, int Wt, int s, int gt_total, int bg, float* part,
+                                           int b, int cell, int t, int QP, int G, float dl, float wp,
+                                           float w) {
+    if (tab && e.x != kMixWide) {
+        const uint32_t v[4] = {e.x, e.y, e.z, e.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                if (v[i] == 0u) break;
-                const float n = mix_cnt(v[i]);
-                float* pc = part + (int64_t)mix_col(v[i]) * QP + t;
-                red_add(pc, n * dl);
-                red_add(pc + (int64_t)G * QP, n * wp);
-                if (UNC) red_add(pc + 2 * (int64_t)G * QP, n * w);
-            }
-            return;
+        for (int i = 0; i < 4; ++i) {
+            if (v[i] == 0u) break;
+            const float n = mix_cnt(v[i]);
+            float* pc = part + (int64_t)mix_col(v[i]) * QP + t;
+            red_add(pc, n * dl);
+            red_add(pc + (int64_t)G * QP, n * wp);
+            if (UNC) red_add(pc + 2 * (int64_t)G * QP, n * w);
         }
+        return;
     }
     const int ci = cell / W, cj = cell - ci * W;
     const int64_t* r0 = targets + ((int64_t)b * Ht + (int64_t)ci * s) * Wt + (int64_t)cj * s;
@@ -449,20 +481,29 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     // A mixed cell is a one-cell run with m = 0 in the element loop (its row
     // sums count there); its contractions are added after the box from the
     // same shared-memory tile, outside the hot loop.
-    auto mixed_cells = [&](uint32_t mb, const float* rowp, int cbase) {
+    // `mye` is lane k's table entry for cell k of the box (loaded before the
+    // element loop); the warp walks the mixed cells together.
+    const bool tab = MIX && a.mixtab != nullptr;
+    auto mixed_cells = [&](uint32_t mb, const float* rowp, int cbase, const uint4& mye) {
         while (mb) {
             const int k = __ffs(mb) - 1;
             mb &= mb - 1u;
+            uint4 ek;
+            ek.x = __shfl_sync(0xffffffffu, mye.x, k);
+            ek.y = __shfl_sync(0xffffffffu, mye.y, k);
+            ek.z = __shfl_sync(0xffffffffu, mye.z, k);
+            ek.w = __shfl_sync(0xffffffffu, mye.w, k);
+            if (!qvalid) continue;
             const float x = rowp[((((k >> 2) ^ (t & 7)) << 2)) + (k & 3)];
             if (FAST) {
                 const Fast f = fast_elem(x);
-                mixed_cell<UNC>(a.targets, a.mixtab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b,
+                mixed_cell<UNC>(a.targets, ek, tab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b,
                                 cbase + k, t, QP, G, -x, f.p, 1.0f);
             } else {
                 const Elem e = elem(x);
                 const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
                 const float dl = FOC ? w * (focal_pos(foc, e) - focal_neg(foc, e)) : -w * x;
-                mixed_cell<UNC>(a.targets, a.mixtab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b,
+                mixed_cell<UNC>(a.targets, ek, tab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b,
                                 cbase + k, t, QP, G, dl, w * e.p, w);
             }
         }
@@ -481,6 +522,8 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
         const bool starts = lane < nv && (my_code == kMixed || my_code != (lane == 0 ? cur : prev));
         const uint32_t bnd = __ballot_sync(0xffffffffu, starts);
         const uint32_t mixb = MIX ? __ballot_sync(0xffffffffu, my_code == kMixed) : 0u;
+        uint4 mye = make_uint4(0u, 0u, 0u, 0u);
+        if (tab && ((mixb >> lane) & 1u)) mye = a.mixtab[(int64_t)b * HW + cell0 + h * KBOX + lane];
         const float* rowp = xs + (st * 2 + h) * box_floats + t * KBOX;
 #pragma unroll
         for (int i = 0; i < NROW; ++i) trow[i] = 0.0f;
@@ -543,7 +586,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                 if (FAST) { trow[2] += lg2_approx(prod); prod = 1.0f; }
             }
         }
-        if (MIX && mixb != 0u && qvalid) mixed_cells(mixb, rowp, cell0 + h * KBOX);
+        if (MIX && mixb != 0u) mixed_cells(mixb, rowp, cell0 + h * KBOX, mye);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
         close_run();
