@@ -246,6 +246,13 @@ def run_ours(args, cfg):
             raise SystemExit("--targets dense runs on one GPU with a label-map config")
         mt = torch.stack([mt == g for g in range(GT_total)], 1).to(torch.uint8).contiguous()
     pc = None
+    half = {"bf16": torch.bfloat16, "fp16": torch.float16}.get(args.logits)
+    if half is not None and not sampled:
+        # 16-bit mask logits end to end (the kernels widen them; the gradient
+        # is written in the same type)
+        if dense:
+            raise SystemExit("--logits bf16/fp16 needs label-map targets")
+        ml = ml.to(half)
     if sampled:  # point-sampled configuration: bf16 logits, P points per image
         ml = ml.to(torch.bfloat16)
         gp = torch.Generator(device=dev).manual_seed(31 + rank)
@@ -405,7 +412,8 @@ def run_ours(args, cfg):
     cells = synthetic.CFG3_POINTS if sampled else cfg.H * cfg.W  # sampled values are fp32
     cost_kernel = "dense_cost_kernel" if dense else "cost_partial_kernel"
     # dense: every logit plus each GT's uint16 count per cell
-    cost_bytes = (cfg.L * cfg.B * cfg.Q * cells * 4 +
+    esize = 2 if (half is not None and not sampled) else 4
+    cost_bytes = (cfg.L * cfg.B * cfg.Q * cells * esize +
                   (cfg.B * cells * (GT_total - 1) * 2 if dense else cfg.B * cells * 4))
     cost_ms = float(kms[0] / max(kn[0], 1))
     achieved = cost_bytes / (cost_ms / 1e3) / 1e9
@@ -425,11 +433,13 @@ def run_ours(args, cfg):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16 logits, f32 math" if sampled else "f32",
+        "dtype": ("bf16 logits, f32 math" if sampled else
+                  f"{args.logits} logits, f32 math" if half is not None else "f32"),
         "data": (f"synthetic (seeded, {cfg.name} shapes)" +
                  (f"; {synthetic.CFG3_POINTS} uniform points per image" if sampled else
                   "; inputs > L2, no flush needed")),
-        "config": {"workload": cfg.name + ("-dense" if dense else ""),
+        "config": {"workload": cfg.name + ("-dense" if dense else "") +
+                               (f"-{args.logits}" if half is not None and not sampled else ""),
                    "targets": ("per-GT uint8 masks (B,GT,Ht,Wt)" if dense else "label map (B,Ht,Wt)"),
                    "images_per_gpu": cfg.B, "global_batch": ws * cfg.B,
                    "Q": cfg.Q, "HW": f"{cfg.H}x{cfg.W}", "classes": cfg.C, "K": 1,
@@ -461,6 +471,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--logits", default="fp32", choices=["fp32", "bf16", "fp16"],
+                    help="mask-logit type of the label-map configs (cfg3 is always bf16)")
     ap.add_argument("--targets", default="labels", choices=["labels", "dense"],
                     help="dense: per-GT uint8 masks instead of the label map (one GPU)")
     args = ap.parse_args()

@@ -36,7 +36,7 @@ class Params(ctypes.Structure):
         ("mask_gamma", c_f32), ("mask_alpha", c_f32), ("cls_gamma", c_f32), ("cls_alpha", c_f32),
         ("void_class_index", c_i64),
         ("use_softmax_label_loss", c_i32), ("normalize_uncertainty", c_i32),
-        ("check_void_targets", c_i32),
+        ("check_void_targets", c_i32), ("logits_dtype", c_i32),
     ]
 
 

@@ -146,6 +146,7 @@ size_t mixtab_bytes(int B, int HW) { return align256(sizeof(uint4) * (size_t)B *
 struct FwdPlan {
     int L, B, Q, H, W, Ht, Wt, s, C, gt_total, gout, bg;
     bool unc, foc, tma_ok;
+    int ldt, esize;  // mask-logit type (0 fp32, 1 bf16, 2 fp16) and its bytes
     int nacc, nrow;
     int qrows, qrows_pad, nqt, chunk_cells, nchunk, part_stride;
     size_t cost_smem;
@@ -154,8 +155,16 @@ struct FwdPlan {
     size_t off_mixtab;  // mixed-cell table (s > 1), or SIZE_MAX when not used
 };
 
-size_t cost_smem_bytes(int qrows_pad) {
-    return 1024 + (size_t)kStages * (2 * (size_t)qrows_pad * KBOX * 4 + KC * 4) + 16 * kStages;
+size_t cost_smem_bytes(int qrows_pad, int esize) {
+    return 1024 + (size_t)kStages * (2 * (size_t)qrows_pad * KBOX * esize + KC * 4) + 16 * kStages;
+}
+
+// Calls f(T{}) with T the plan's mask-logit element type.
+template <typename F>
+int with_logit_type(int ldt, F&& f) {
+    if (ldt == 1) return f(__nv_bfloat16{});
+    if (ldt == 2) return f(__half{});
+    return f(float{});
 }
 
 int validate_dims(const ml_dims* d) {
@@ -189,6 +198,8 @@ int validate_params(const ml_params* p, int64_t C) {
         return fail(ML_EINVAL, "uncertainty_gamma_min must be in [0,1]");
     if (p->topk_matches < 0) return fail(ML_EINVAL, "K must be non-negative");
     if (p->strategy_id < 0 || p->strategy_id > 3) return fail(ML_EINVAL, "Invalid matching strategy id");
+    if (p->logits_dtype < 0 || p->logits_dtype > 2)
+        return fail(ML_EINVAL, "logits_dtype must be 0 (fp32), 1 (bf16) or 2 (fp16)");
     const bool has_void = p->void_class_index >= 0 && p->void_class_index < C;
     if (p->use_softmax_label_loss && p->force_unmatched_class_to_background && !has_void)
         return fail(ML_EINVAL,
@@ -197,9 +208,9 @@ int validate_params(const ml_params* p, int64_t C) {
     return ML_OK;
 }
 
-template <bool UNC, bool FOC, bool TMA, bool MIX>
+template <bool UNC, bool FOC, bool TMA, bool MIX, typename T>
 int cost_blocks_per_sm_t(size_t smem, int threads) {
-    auto k = cost_partial_kernel<UNC, FOC, TMA, MIX>;
+    auto k = cost_partial_kernel<UNC, FOC, TMA, MIX, T>;
     int n = 0;
     if (ensure_smem(k, smem) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, threads, smem) != cudaSuccess) {
@@ -213,15 +224,19 @@ int cost_blocks_per_sm_t(size_t smem, int threads) {
 // registers and shared memory); without a device, the shared-memory bound.
 int cost_blocks_per_sm(const FwdPlan& P, int threads) {
     const bool mix = P.s > 1;
-    int n = 0;
+    int n = with_logit_type(P.ldt, [&](auto tag) -> int {
+        using T = decltype(tag);
+        int r = 0;
 #define ML_OCC(U, F) \
-    n = P.tma_ok ? (mix ? cost_blocks_per_sm_t<U, F, true, true>(P.cost_smem, threads)      \
-                        : cost_blocks_per_sm_t<U, F, true, false>(P.cost_smem, threads))    \
-                 : (mix ? cost_blocks_per_sm_t<U, F, false, true>(P.cost_smem, threads)     \
-                        : cost_blocks_per_sm_t<U, F, false, false>(P.cost_smem, threads))
-    if (P.unc) { if (P.foc) ML_OCC(true, true); else ML_OCC(true, false); }
-    else { if (P.foc) ML_OCC(false, true); else ML_OCC(false, false); }
+    r = P.tma_ok ? (mix ? cost_blocks_per_sm_t<U, F, true, true, T>(P.cost_smem, threads)      \
+                        : cost_blocks_per_sm_t<U, F, true, false, T>(P.cost_smem, threads))    \
+                 : (mix ? cost_blocks_per_sm_t<U, F, false, true, T>(P.cost_smem, threads)     \
+                        : cost_blocks_per_sm_t<U, F, false, false, T>(P.cost_smem, threads))
+        if (P.unc) { if (P.foc) ML_OCC(true, true); else ML_OCC(true, false); }
+        else { if (P.foc) ML_OCC(false, true); else ML_OCC(false, false); }
 #undef ML_OCC
+        return r;
+    });
     if (n < 1) n = (int)std::min<size_t>(228 * 1024 / (P.cost_smem + 1024), 2048 / threads);
     return n < 1 ? 1 : n;
 }
@@ -239,13 +254,15 @@ int make_plan(const ml_dims* d, const ml_params* p, FwdPlan* P) {
     P->foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
     P->nacc = P->unc ? 3 : 2;
     P->nrow = P->unc ? 5 : 3;
+    P->ldt = (int)p->logits_dtype;
+    P->esize = P->ldt ? 2 : 4;
     const int HW = P->H * P->W;
-    P->tma_ok = (HW % 4) == 0;
+    P->tma_ok = ((int64_t)HW * P->esize) % 16 == 0;  // TMA row pitch: a multiple of 16 bytes
     const int Q = P->Q > 0 ? P->Q : 1;
     P->nqt = (Q + 127) / 128;
     P->qrows = (Q + P->nqt - 1) / P->nqt;
     P->qrows_pad = (P->qrows + 31) / 32 * 32;
-    P->cost_smem = cost_smem_bytes(P->qrows_pad);
+    P->cost_smem = cost_smem_bytes(P->qrows_pad, P->esize);
     const int threads = 2 * P->qrows_pad + 32;
     int per_sm = cost_blocks_per_sm(*P, threads);
     // chunks per (image, query tile): the smallest count whose CTAs fill the
@@ -324,9 +341,10 @@ CostArgs cost_args(const FwdPlan& P, const ml_params* p, const float* ml, const 
     return a;
 }
 
-template <bool UNC, bool FOC, bool TMA>
+template <bool UNC, bool FOC, bool TMA, typename T>
 int launch_cost_t(const FwdPlan& P, const CUtensorMap& tm, const CostArgs& a, cudaStream_t st) {
-    auto k = P.s > 1 ? cost_partial_kernel<UNC, FOC, TMA, true> : cost_partial_kernel<UNC, FOC, TMA, false>;
+    auto k = P.s > 1 ? cost_partial_kernel<UNC, FOC, TMA, true, T>
+                     : cost_partial_kernel<UNC, FOC, TMA, false, T>;
     cudaError_t e = ensure_smem(k, P.cost_smem);
     if (e != cudaSuccess) return cuda_fail(e, "cost_partial_kernel attributes");
     dim3 grid(P.nchunk, P.nqt, P.L * P.B);
@@ -380,24 +398,31 @@ int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaS
         if (!enc) {
             tma = false;
         } else {
+            // rows of 32 cells: 128 bytes (fp32, 128-byte swizzle) or 64 bytes
+            // (16-bit, 64-byte swizzle); the kernel's Tile<T> reads either
+            const CUtensorMapDataType dt = P.ldt == 1   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                           : P.ldt == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
             const cuuint64_t dims[2] = {(cuuint64_t)P.H * P.W, (cuuint64_t)LBQ};
-            const cuuint64_t strides[1] = {(cuuint64_t)P.H * P.W * sizeof(float)};
+            const cuuint64_t strides[1] = {(cuuint64_t)P.H * P.W * P.esize};
             const cuuint32_t box[2] = {(cuuint32_t)KBOX, (cuuint32_t)P.qrows};
             const cuuint32_t es[2] = {1, 1};
-            CUresult r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(mask_logits),
-                             dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            CUresult r = enc(&tm, dt, 2, const_cast<float*>(mask_logits), dims, strides, box, es,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             P.esize == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             if (r != CUDA_SUCCESS) tma = false;
         }
     }
-    if (P.unc) {
-        if (P.foc) rc = tma ? launch_cost_t<true, true, true>(P, tm, a, st) : launch_cost_t<true, true, false>(P, tm, a, st);
-        else rc = tma ? launch_cost_t<true, false, true>(P, tm, a, st) : launch_cost_t<true, false, false>(P, tm, a, st);
-    } else {
-        if (P.foc) rc = tma ? launch_cost_t<false, true, true>(P, tm, a, st) : launch_cost_t<false, true, false>(P, tm, a, st);
-        else rc = tma ? launch_cost_t<false, false, true>(P, tm, a, st) : launch_cost_t<false, false, false>(P, tm, a, st);
-    }
+    rc = with_logit_type(P.ldt, [&](auto tag) -> int {
+        using T = decltype(tag);
+        if (P.unc) {
+            if (P.foc) return tma ? launch_cost_t<true, true, true, T>(P, tm, a, st) : launch_cost_t<true, true, false, T>(P, tm, a, st);
+            return tma ? launch_cost_t<true, false, true, T>(P, tm, a, st) : launch_cost_t<true, false, false, T>(P, tm, a, st);
+        }
+        if (P.foc) return tma ? launch_cost_t<false, true, true, T>(P, tm, a, st) : launch_cost_t<false, true, false, T>(P, tm, a, st);
+        return tma ? launch_cost_t<false, false, true, T>(P, tm, a, st) : launch_cost_t<false, false, false, T>(P, tm, a, st);
+    });
     if (rc) return rc;
     return run_finalize(P, a, st);
 }
@@ -552,7 +577,9 @@ int make_sampled_plan(const ml_dims* d, const ml_params* p, int64_t P, SampledPl
         return fail(ML_EUNSUPPORTED, "uncertainty weights are not used by point-sampled costs: pass uncertainty_gamma=0");
     ml_dims dv = *d;
     dv.H = 1; dv.W = P; dv.Ht = 1; dv.Wt = P;
-    if ((rc = make_plan(&dv, p, &S->cp))) return rc;
+    ml_params pf = *p;
+    pf.logits_dtype = 0;  // the cost kernel reads the fp32 samples
+    if ((rc = make_plan(&dv, &pf, &S->cp))) return rc;
     if (point_sort_smem((int)P, S->cp.gout) > 200 * 1024)
         return fail(ML_EUNSUPPORTED, "too many points x GT columns for the point sort");
     S->H = (int)d->H; S->W = (int)d->W; S->Ht = (int)d->Ht; S->Wt = (int)d->Wt; S->P = (int)P;
@@ -718,6 +745,8 @@ int ml_pairwise_mask_loss_forward_noalloc(const ml_dims* d, const ml_params* p,
     FwdPlan P;
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
+    if (p->logits_dtype != 0)
+        return fail(ML_EUNSUPPORTED, "ml_pairwise_mask_loss_forward_noalloc takes fp32 mask_logits");
     if ((rc = make_plan(d, p, &P))) return rc;
     // scratch layout: totals | codes | chunk partials | per-query statistics | mixed-cell table
     const size_t LBQ = (size_t)P.L * P.B * P.Q;
@@ -801,6 +830,8 @@ static int mask_matching_impl(const ml_dims* d, const ml_params* p, const float*
     FwdPlan P;
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
+    if (dense_masks && p->logits_dtype != 0)
+        return fail(ML_EUNSUPPORTED, "dense mask targets take fp32 mask_logits");
     if ((rc = make_plan(d, p, &P))) return rc;
     if (P.gout == 0)
         return fail(ML_ESHAPE, "pairwise_sigmoid_dice_loss_forward must return {3,L,B,Q,GT_out}");
@@ -893,6 +924,9 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
         return fail(ML_EINVAL, "dense mask targets need the forward's saved statistics");
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
+    const int ldt = (int)p->logits_dtype;
+    if (dense_masks && ldt != 0)
+        return fail(ML_EUNSUPPORTED, "dense mask targets take fp32 mask_logits");
     if ((rc = validate_dims(d))) return rc;
     const size_t need = ml_mask_matching_backward_workspace_size(d, p);
     if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
@@ -951,28 +985,38 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
         la.stats_out = stats;
         la.stats_in = stats;
         dim3 g(P.Q, P.L * P.B);
-        if (unc) bwd_stats_kernel<true><<<g, 256, 0, st>>>(la);
-        else bwd_stats_kernel<false><<<g, 256, 0, st>>>(la);
+        with_logit_type(ldt, [&](auto tag) -> int {
+            using T = decltype(tag);
+            if (unc) bwd_stats_kernel<true, T><<<g, 256, 0, st>>>(la);
+            else bwd_stats_kernel<false, T><<<g, 256, 0, st>>>(la);
+            return 0;
+        });
         ML_CHECK_LAUNCH("bwd_stats_kernel");
     }
-    const bool vec = (HW % 4 == 0) && (reinterpret_cast<uintptr_t>(mask_logits) % 16 == 0) &&
-                     (reinterpret_cast<uintptr_t>(grad_mask_logits) % 16 == 0);
+    // four elements per access: 16 bytes (fp32) or 8 bytes (16-bit)
+    const uintptr_t va = ldt ? 8 : 16;
+    const bool vec = (HW % 4 == 0) && (reinterpret_cast<uintptr_t>(mask_logits) % va == 0) &&
+                     (reinterpret_cast<uintptr_t>(grad_mask_logits) % va == 0);
     // one block per (query row, contiguous range of cells)
     const int64_t ck = std::min<int64_t>(((HW + 3) / 4) * 4, 4096);
     la.chunk_cells = (int)ck;
     const int nchunk = (int)((HW + ck - 1) / ck);
     dim3 gg((unsigned)LBQ, nchunk);
     const size_t gs = 0;
-#define ML_MG(U, F, V) mask_grad_kernel<U, F, V><<<gg, 256, gs, st>>>(la)
+#define ML_MG(U, F, V) mask_grad_kernel<U, F, V, T><<<gg, 256, gs, st>>>(la)
     {
     ProfScope prof(1, st);
-    if (unc) {
-        if (foc) { if (vec) ML_MG(true, true, true); else ML_MG(true, true, false); }
-        else { if (vec) ML_MG(true, false, true); else ML_MG(true, false, false); }
-    } else {
-        if (foc) { if (vec) ML_MG(false, true, true); else ML_MG(false, true, false); }
-        else { if (vec) ML_MG(false, false, true); else ML_MG(false, false, false); }
-    }
+    with_logit_type(ldt, [&](auto tag) -> int {
+        using T = decltype(tag);
+        if (unc) {
+            if (foc) { if (vec) ML_MG(true, true, true); else ML_MG(true, true, false); }
+            else { if (vec) ML_MG(true, false, true); else ML_MG(true, false, false); }
+        } else {
+            if (foc) { if (vec) ML_MG(false, true, true); else ML_MG(false, true, false); }
+            else { if (vec) ML_MG(false, false, true); else ML_MG(false, false, false); }
+        }
+        return 0;
+    });
     }
 #undef ML_MG
     ML_CHECK_LAUNCH("mask_grad_kernel");
@@ -1023,6 +1067,7 @@ int ml_pairwise_mask_loss_dense_forward(const ml_dims* d, const ml_params* p, co
     FwdPlan P;
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
+    if (p->logits_dtype != 0) return fail(ML_EUNSUPPORTED, "dense mask targets take fp32 mask_logits");
     if ((rc = make_plan(d, p, &P))) return rc;
     if ((rc = check_ws(workspace, workspace_bytes, P.bytes + dense_count_bytes(P)))) return rc;
     if (P.gout == 0) return ML_OK;

@@ -1,6 +1,8 @@
 // common.cuh -- shared device helpers for the mask_loss_b200 kernels.
 #pragma once
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -9,6 +11,58 @@
 #define ML_INLINE __device__ __forceinline__
 
 namespace mlb {
+
+// Mask-logit element types (ml_params.logits_dtype): fp32, bf16, fp16.  All
+// arithmetic is fp32; 16-bit values widen exactly and gradients round to
+// nearest-even on the way out.
+ML_INLINE float to_f(float x) { return x; }
+ML_INLINE float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+ML_INLINE float to_f(__half x) { return __half2float(x); }
+template <typename T> ML_INLINE T from_f(float x);
+template <> ML_INLINE float from_f<float>(float x) { return x; }
+template <> ML_INLINE __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> ML_INLINE __half from_f<__half>(float x) { return __float2half_rn(x); }
+
+// two packed 16-bit values -> two floats (exact), and back (round to nearest)
+ML_INLINE void widen2(uint32_t w, float& lo, float& hi, const __nv_bfloat16*) {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xFFFF0000u);
+}
+ML_INLINE void widen2(uint32_t w, float& lo, float& hi, const __half*) {
+    lo = __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu)));
+    hi = __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+ML_INLINE uint32_t narrow2(float lo, float hi, const __nv_bfloat16*) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+ML_INLINE uint32_t narrow2(float lo, float hi, const __half*) {
+    const __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Four consecutive elements with streaming (evict-first) accesses: one
+// 16-byte access for fp32, one 8-byte access for 16-bit types.
+template <typename T>
+ML_INLINE float4 ld4cs(const T* p) {
+    if constexpr (sizeof(T) == 4) {
+        return __ldcs(reinterpret_cast<const float4*>(p));
+    } else {
+        const uint2 v = __ldcs(reinterpret_cast<const uint2*>(p));
+        float4 r;
+        widen2(v.x, r.x, r.y, p);
+        widen2(v.y, r.z, r.w, p);
+        return r;
+    }
+}
+template <typename T>
+ML_INLINE void st4cs(T* p, const float4& v) {
+    if constexpr (sizeof(T) == 4) {
+        __stcs(reinterpret_cast<float4*>(p), v);
+    } else {
+        __stcs(reinterpret_cast<uint2*>(p), make_uint2(narrow2(v.x, v.y, p), narrow2(v.z, v.w, p)));
+    }
+}
 
 constexpr int kNone = -1;   // cell/pixel carries no output column
 constexpr int kMixed = -2;  // cell holds more than one label (s > 1 only)

@@ -304,6 +304,37 @@ __device__ __forceinline__ void mixed_cell(const int64_t* targets, const uint4& 
 }
 
 // ---------------------------------------------------------------------------
+// Shared-memory layout of one 32-cell box row, per logit type.  The TMA box
+// rows are 128 bytes (fp32, 128-byte swizzle: 16-byte granule g of row r at
+// g ^ (r & 7)) or 64 bytes (16-bit, 64-byte swizzle: g ^ ((r >> 1) & 3)); both
+// keep a warp's 128-bit row reads conflict-free.  GR = elements per granule.
+// ---------------------------------------------------------------------------
+template <typename T> struct Tile {
+    static constexpr int GR = 16 / (int)sizeof(T);
+    ML_INLINE static int gran(int r, int g) {
+        if constexpr (sizeof(T) == 4) return (g ^ (r & 7)) << 2;
+        else return (g ^ ((r >> 1) & 3)) << 3;
+    }
+    ML_INLINE static float at(const T* row, int r, int k) { return to_f(row[gran(r, k / GR) + k % GR]); }
+    // elements [8o, 8o + 8) of the row
+    ML_INLINE static void octet(const T* row, int r, int o, float (&x)[8]) {
+        if constexpr (sizeof(T) == 4) {
+            const float* fr = reinterpret_cast<const float*>(row);
+            const float4 v0 = *reinterpret_cast<const float4*>(fr + gran(r, 2 * o));
+            const float4 v1 = *reinterpret_cast<const float4*>(fr + gran(r, 2 * o + 1));
+            x[0] = v0.x; x[1] = v0.y; x[2] = v0.z; x[3] = v0.w;
+            x[4] = v1.x; x[5] = v1.y; x[6] = v1.z; x[7] = v1.w;
+        } else {
+            const uint4 v = *reinterpret_cast<const uint4*>(row + gran(r, o));
+            widen2(v.x, x[0], x[1], row);
+            widen2(v.y, x[2], x[3], row);
+            widen2(v.z, x[4], x[5], row);
+            widen2(v.w, x[6], x[7], row);
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------
 // The streaming cost kernel.  grid = (nchunk, nqt, L*B); block = 2*qrows_pad
 // consumer threads plus one producer warp.  The producer fills a 3-stage ring
 // (full/empty mbarriers, no block-wide barrier in the loop); consumer thread
@@ -315,7 +346,7 @@ __device__ __forceinline__ void mixed_cell(const int64_t* targets, const uint4& 
 //   TMA   logits rows are 16-byte strided so the bulk-tensor path is legal
 //   MIX   cells cover several target pixels (s > 1), so mixed cells occur
 // ---------------------------------------------------------------------------
-template <bool UNC, bool FOC, bool TMA, bool MIX>
+template <bool UNC, bool FOC, bool TMA, bool MIX, typename T>
 __global__ void __launch_bounds__(kCostThreads, (MIX && !UNC && !FOC) ? 3 : 2)
 cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     constexpr int NACC = UNC ? 3 : 2;
@@ -325,9 +356,9 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int QP = a.qrows_pad;
-    const int box_floats = QP * KBOX;                  // one 32-cell box
-    float* xs = reinterpret_cast<float*>(base);        // [stage][2][QP][32]
-    int32_t* cs = reinterpret_cast<int32_t*>(xs + kStages * 2 * box_floats);  // [stage][KC]
+    const int box_elems = QP * KBOX;                   // one 32-cell box
+    T* xs = reinterpret_cast<T*>(base);                // [stage][2][QP][32]
+    int32_t* cs = reinterpret_cast<int32_t*>(xs + kStages * 2 * box_elems);  // [stage][KC]
     uint64_t* full = reinterpret_cast<uint64_t*>(cs + kStages * KC);
     uint64_t* empty = full + kStages;
 
@@ -368,32 +399,33 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
             if (TMA) {
                 if (lane == 0) {
                     const uint32_t cbytes = (uint32_t)min(KC, HW - c0) * 4u;
-                    mbar_arrive_expect_tx(&full[st], 2u * a.qrows * KBOX * 4u + cbytes);
+                    mbar_arrive_expect_tx(&full[st], 2u * a.qrows * KBOX * (uint32_t)sizeof(T) + cbytes);
 #pragma unroll
                     for (int bx = 0; bx < 2; ++bx)
                         asm volatile(
                             "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
                             " [%0], [%1, {%2, %3}], [%4];"
-                            ::"r"(smem_u32(xs + (st * 2 + bx) * box_floats)), "l"(&tmap),
+                            ::"r"(smem_u32(xs + (st * 2 + bx) * box_elems)), "l"(&tmap),
                               "r"(c0 + bx * KBOX), "r"(row0), "r"(smem_u32(&full[st])) : "memory");
                     bulk_g2s(cs + st * KC, codes_b + c0, cbytes, &full[st]);
                 }
             } else {
                 // plain loads into the same swizzled layout, then one arrive
-                for (int i = lane; i < 2 * a.qrows * (KBOX / 4); i += 32) {
-                    const int bx = i / (a.qrows * (KBOX / 4));
-                    const int rem = i - bx * a.qrows * (KBOX / 4);
-                    const int r = rem / (KBOX / 4), c = rem - r * (KBOX / 4);
-                    const float* src = a.logits + (int64_t)(row0 + r) * HW + c0 + bx * KBOX + c * 4;
-                    float4 v;
-                    float* vv = reinterpret_cast<float*>(&v);
+                constexpr int GR = Tile<T>::GR;
+                const T* lg = reinterpret_cast<const T*>(a.logits);
+                for (int i = lane; i < 2 * a.qrows * (KBOX / GR); i += 32) {
+                    const int bx = i / (a.qrows * (KBOX / GR));
+                    const int rem = i - bx * a.qrows * (KBOX / GR);
+                    const int r = rem / (KBOX / GR), c = rem - r * (KBOX / GR);
+                    const T* src = lg + (int64_t)(row0 + r) * HW + c0 + bx * KBOX + c * GR;
+                    alignas(16) T vv[GR];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int k = bx * KBOX + c * 4 + u;
-                        vv[u] = (k < nvalid) ? src[u] : 0.0f;
+                    for (int u = 0; u < GR; ++u) {
+                        const int k = bx * KBOX + c * GR + u;
+                        vv[u] = (k < nvalid) ? src[u] : from_f<T>(0.0f);
                     }
-                    *reinterpret_cast<float4*>(xs + (st * 2 + bx) * box_floats + r * KBOX +
-                                               ((c ^ (r & 7)) << 2)) = v;
+                    *reinterpret_cast<uint4*>(xs + (st * 2 + bx) * box_elems + r * KBOX +
+                                              Tile<T>::gran(r, c)) = *reinterpret_cast<const uint4*>(vv);
                 }
                 for (int k = lane; k < KC; k += 32) cs[st * KC + k] = k < nvalid ? codes_b[c0 + k] : kNone;
                 __syncwarp();
@@ -484,7 +516,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
     // `mye` is lane k's table entry for cell k of the box (loaded before the
     // element loop); the warp walks the mixed cells together.
     const bool tab = MIX && a.mixtab != nullptr;
-    auto mixed_cells = [&](uint32_t mb, const float* rowp, int cbase, const uint4& mye) {
+    auto mixed_cells = [&](uint32_t mb, const T* rowp, int cbase, const uint4& mye) {
         while (mb) {
             const int k = __ffs(mb) - 1;
             mb &= mb - 1u;
@@ -494,7 +526,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
             ek.z = __shfl_sync(0xffffffffu, mye.z, k);
             ek.w = __shfl_sync(0xffffffffu, mye.w, k);
             if (!qvalid) continue;
-            const float x = rowp[((((k >> 2) ^ (t & 7)) << 2)) + (k & 3)];
+            const float x = Tile<T>::at(rowp, t, k);
             if (FAST) {
                 const Fast f = fast_elem(x);
                 mixed_cell<UNC>(a.targets, ek, tab, a.W, a.Ht, a.Wt, a.s, a.gt_total, a.bg, part, b,
@@ -524,16 +556,19 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
         const uint32_t mixb = MIX ? __ballot_sync(0xffffffffu, my_code == kMixed) : 0u;
         uint4 mye = make_uint4(0u, 0u, 0u, 0u);
         if (tab && ((mixb >> lane) & 1u)) mye = a.mixtab[(int64_t)b * HW + cell0 + h * KBOX + lane];
-        const float* rowp = xs + (st * 2 + h) * box_floats + t * KBOX;
+        const T* rowp = xs + (st * 2 + h) * box_elems + t * KBOX;
 #pragma unroll
         for (int i = 0; i < NROW; ++i) trow[i] = 0.0f;
         prod = 1.0f;
         tabs = sx0 = sp0 = 0.0f;
         if (nv == KBOX) {
-#pragma unroll 2
-            for (int c = 0; c < KBOX / 4; ++c) {
-                const float4 v = *reinterpret_cast<const float4*>(rowp + ((c ^ (t & 7)) << 2));
-                const float xv[4] = {v.x, v.y, v.z, v.w};
+            for (int o = 0; o < KBOX / 8; ++o) {
+              float xo[8];
+              Tile<T>::octet(rowp, t, o, xo);
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                const int c = 2 * o + j;
+                const float xv[4] = {xo[4 * j], xo[4 * j + 1], xo[4 * j + 2], xo[4 * j + 3]};
                 const uint32_t b4 = (bnd >> (4 * c)) & 0xFu;
                 if (b4 == 0u) {
 #pragma unroll
@@ -571,11 +606,12 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                         element(xv[u]);
                     }
                 }
-                if (FAST && (c & 1)) { trow[2] += lg2_approx(prod); prod = 1.0f; }
+              }
+              if (FAST) { trow[2] += lg2_approx(prod); prod = 1.0f; }
             }
         } else {  // last, partial tile of the image
             for (int k = 0; k < nv; ++k) {
-                const float x = rowp[((((k >> 2) ^ (t & 7)) << 2)) + (k & 3)];
+                const float x = Tile<T>::at(rowp, t, k);
                 if ((bnd >> k) & 1u) {
                     close_run();
                     flush();
@@ -783,22 +819,54 @@ __global__ void __launch_bounds__(256) cost_pairs_kernel(CostArgs a) {
     if (a.rawI) { a.rawI[o] = acc[1]; a.rawT[o] = T; }
 }
 
-template __global__ void cost_partial_kernel<false, false, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<false, false, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<false, false, false, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<false, false, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, false, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, false, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, false, false, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, false, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<false, true, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<false, true, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<false, true, false, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<false, true, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, true, true, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, true, true, true>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, true, false, false>(const __grid_constant__ CUtensorMap, CostArgs);
-template __global__ void cost_partial_kernel<true, true, false, true>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, false, false, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, false, true, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, true, false, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, true, true, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, false, false, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, false, true, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, true, false, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, true, true, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, false, false, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, false, true, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, true, false, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, true, true, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, false, false, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, false, true, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, true, false, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, true, true, float>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, false, false, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, false, true, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, true, false, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, true, true, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, false, false, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, false, true, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, true, false, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, true, true, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, false, false, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, false, true, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, true, false, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, true, true, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, false, false, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, false, true, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, true, false, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, true, true, __nv_bfloat16>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, false, false, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, false, true, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, true, false, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, false, true, true, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, false, false, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, false, true, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, true, false, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<false, true, true, true, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, false, false, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, false, true, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, true, false, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, false, true, true, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, false, false, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, false, true, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, true, false, __half>(const __grid_constant__ CUtensorMap, CostArgs);
+template __global__ void cost_partial_kernel<true, true, true, true, __half>(const __grid_constant__ CUtensorMap, CostArgs);
 template __global__ void cost_rows_kernel<false, false>(CostArgs);
 template __global__ void cost_rows_kernel<false, true>(CostArgs);
 template __global__ void cost_rows_kernel<true, false>(CostArgs);

@@ -57,7 +57,9 @@ cudaError_t launch_label_code(const int64_t* targets, int B, int H, int W, int W
 cudaError_t launch_label_hist(const int64_t* targets, int B, int64_t npix, int gt_total,
                               int32_t* totals, cudaStream_t st);
 
-template <bool UNC, bool FOC, bool TMA, bool MIX>
+// T: mask-logit element type (float, __nv_bfloat16, __half); a.logits points
+// at T values.
+template <bool UNC, bool FOC, bool TMA, bool MIX, typename T = float>
 __global__ void cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a);
 
 template <bool UNC, bool FAST>
@@ -134,8 +136,9 @@ struct LossArgs {
 
 __global__ void loss_fwd_kernel(LossArgs a);
 __global__ void count_masks_kernel(const int32_t* totals, int B, int gt_total, int bg, float* out);
-template <bool UNC> __global__ void bwd_stats_kernel(LossArgs a);
-template <bool UNC, bool FOC, bool VEC> __global__ void mask_grad_kernel(LossArgs a);
+// T: mask-logit element type; a.mask_logits / a.grad_mask_logits point at T.
+template <bool UNC, typename T = float> __global__ void bwd_stats_kernel(LossArgs a);
+template <bool UNC, bool FOC, bool VEC, typename T = float> __global__ void mask_grad_kernel(LossArgs a);
 __global__ void bwd_cls_kernel(LossArgs a);
 
 }  // namespace mlb

@@ -159,7 +159,7 @@ ML_INLINE float cell_count_coded(const int32_t* codes_b, const uint4* mix_b, con
 // grid = (Q, L*B), block = 256.  Mirrors the first loop of
 // src/cuda/mask_matching_backward.cu:110-138 with a fixed-order reduction.
 // ---------------------------------------------------------------------------
-template <bool UNC>
+template <bool UNC, typename T>
 __global__ void __launch_bounds__(256) bwd_stats_kernel(LossArgs a) {
     __shared__ float sh[32 * 4];
     const int q = blockIdx.x, lb = blockIdx.y, b = lb % a.B;
@@ -170,14 +170,14 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(LossArgs a) {
     if (!matched && !a.force_masks) return;
     const int HW = a.H * a.W;
     const float N2 = (float)(a.s * a.s);
-    const float* x = a.mask_logits + qi * HW;
+    const T* x = reinterpret_cast<const T*>(a.mask_logits) + qi * HW;
     const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
     const int32_t* codes_b = a.codes ? a.codes + (int64_t)b * HW : nullptr;
     const uint4* mix_b = a.codes ? a.mixtab + (int64_t)b * HW : nullptr;
     const int gcol = matched ? label_to_col(ga, a.gt_total, a.bg) : kNone;
     float v[4] = {0.f, 0.f, 0.f, 0.f};  // sum w p, sum w t, sum w p t, sum w
     for (int j = threadIdx.x; j < HW; j += blockDim.x) {
-        const Elem e = elem(x[j]);
+        const Elem e = elem(to_f(x[j]));
         const float w = UNC ? unc_weight(e.p, a.ug, a.ugmin) : 1.0f;
         const float t = !matched ? 0.0f
                         : codes_b ? cell_count_coded(codes_b, mix_b, tb, j, a.W, a.Wt, a.s, ga, gcol, N2)
@@ -200,14 +200,14 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(LossArgs a) {
 // matched (or forced) rows read logits and labels and write the gradient of
 // src/cuda/mask_matching_backward.cu:169-215.
 // ---------------------------------------------------------------------------
-template <bool UNC, bool FOC, bool VEC>
+template <bool UNC, bool FOC, bool VEC, typename LT>
 __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
     const int64_t qi = blockIdx.x;
     const int lb = (int)(qi / a.Q), l = lb / a.B, b = lb % a.B;
     const int HW = a.H * a.W;
     const int c0 = blockIdx.y * a.chunk_cells;
     const int nc = min(a.chunk_cells, HW - c0);
-    float* gout = a.grad_mask_logits + qi * HW + c0;
+    LT* gout = reinterpret_cast<LT*>(a.grad_mask_logits) + qi * HW + c0;
     const float mcoef = a.coef[l * 3 + 0], dcoef = a.coef[l * 3 + 1];
     const int64_t og = a.pred_to_gt[qi];
     const int64_t ga = og + (og >= a.bg ? 1 : 0);
@@ -216,14 +216,13 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
     if (!active) {
         if (VEC) {
             const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4)
-                __stcs(reinterpret_cast<float4*>(gout + k), z);
+            for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4) st4cs(gout + k, z);
         } else {
-            for (int k = threadIdx.x; k < nc; k += blockDim.x) gout[k] = 0.0f;
+            for (int k = threadIdx.x; k < nc; k += blockDim.x) gout[k] = from_f<LT>(0.0f);
         }
         return;
     }
-    const float* xin = a.mask_logits + qi * HW + c0;
+    const LT* xin = reinterpret_cast<const LT*>(a.mask_logits) + qi * HW + c0;
     const int64_t* tb = a.targets + (int64_t)b * a.Ht * a.Wt;
     const int s = a.s;
     const float N2 = (float)(s * s);
@@ -279,33 +278,33 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
         // float4 are two 16-byte loads, issued with the logits
         const bool lab2 = s == 1 && matched && !a.masks && ((reinterpret_cast<uintptr_t>(tb + c0) & 15) == 0);
         if (lab2) {
-            const float* __restrict__ xr = xin;
+            const LT* __restrict__ xr = xin;
             const longlong2* __restrict__ lr = reinterpret_cast<const longlong2*>(tb + c0);
-            float* __restrict__ gr = gout;
+            LT* __restrict__ gr = gout;
 #pragma unroll 4
             for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4) {
-                const float4 xv = __ldcs(reinterpret_cast<const float4*>(xr + k));
+                const float4 xv = ld4cs(xr + k);
                 const longlong2 l01 = lr[k >> 1], l23 = lr[(k >> 1) + 1];
                 float4 r;
                 r.x = g1(xv.x, l01.x == ga ? 1.0f : 0.0f);
                 r.y = g1(xv.y, l01.y == ga ? 1.0f : 0.0f);
                 r.z = g1(xv.z, l23.x == ga ? 1.0f : 0.0f);
                 r.w = g1(xv.w, l23.y == ga ? 1.0f : 0.0f);
-                __stcs(reinterpret_cast<float4*>(gr + k), r);
+                st4cs(gr + k, r);
             }
             return;
         }
         for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4) {
-            const float4 xv = __ldcs(reinterpret_cast<const float4*>(xin + k));
+            const float4 xv = ld4cs(xin + k);
             float4 r;
             r.x = g1(xv.x, count(k));
             r.y = g1(xv.y, count(k + 1));
             r.z = g1(xv.z, count(k + 2));
             r.w = g1(xv.w, count(k + 3));
-            __stcs(reinterpret_cast<float4*>(gout + k), r);
+            st4cs(gout + k, r);
         }
     } else {
-        for (int k = threadIdx.x; k < nc; k += blockDim.x) gout[k] = g1(xin[k], count(k));
+        for (int k = threadIdx.x; k < nc; k += blockDim.x) gout[k] = from_f<LT>(g1(to_f(xin[k]), count(k)));
     }
 }
 
@@ -414,15 +413,35 @@ __global__ void __launch_bounds__(256) bwd_cls_kernel(LossArgs a) {
     cls_grad_row(a, qi, threadIdx.x & 31, scoef[(int)(qi / n) - l0][2]);
 }
 
-template __global__ void bwd_stats_kernel<false>(LossArgs);
-template __global__ void bwd_stats_kernel<true>(LossArgs);
-template __global__ void mask_grad_kernel<false, false, false>(LossArgs);
-template __global__ void mask_grad_kernel<false, false, true>(LossArgs);
-template __global__ void mask_grad_kernel<false, true, false>(LossArgs);
-template __global__ void mask_grad_kernel<false, true, true>(LossArgs);
-template __global__ void mask_grad_kernel<true, false, false>(LossArgs);
-template __global__ void mask_grad_kernel<true, false, true>(LossArgs);
-template __global__ void mask_grad_kernel<true, true, false>(LossArgs);
-template __global__ void mask_grad_kernel<true, true, true>(LossArgs);
+template __global__ void bwd_stats_kernel<false, float>(LossArgs);
+template __global__ void bwd_stats_kernel<true, float>(LossArgs);
+template __global__ void mask_grad_kernel<false, false, false, float>(LossArgs);
+template __global__ void mask_grad_kernel<false, false, true, float>(LossArgs);
+template __global__ void mask_grad_kernel<false, true, false, float>(LossArgs);
+template __global__ void mask_grad_kernel<false, true, true, float>(LossArgs);
+template __global__ void mask_grad_kernel<true, false, false, float>(LossArgs);
+template __global__ void mask_grad_kernel<true, false, true, float>(LossArgs);
+template __global__ void mask_grad_kernel<true, true, false, float>(LossArgs);
+template __global__ void mask_grad_kernel<true, true, true, float>(LossArgs);
+template __global__ void bwd_stats_kernel<false, __nv_bfloat16>(LossArgs);
+template __global__ void bwd_stats_kernel<true, __nv_bfloat16>(LossArgs);
+template __global__ void mask_grad_kernel<false, false, false, __nv_bfloat16>(LossArgs);
+template __global__ void mask_grad_kernel<false, false, true, __nv_bfloat16>(LossArgs);
+template __global__ void mask_grad_kernel<false, true, false, __nv_bfloat16>(LossArgs);
+template __global__ void mask_grad_kernel<false, true, true, __nv_bfloat16>(LossArgs);
+template __global__ void mask_grad_kernel<true, false, false, __nv_bfloat16>(LossArgs);
+template __global__ void mask_grad_kernel<true, false, true, __nv_bfloat16>(LossArgs);
+template __global__ void mask_grad_kernel<true, true, false, __nv_bfloat16>(LossArgs);
+template __global__ void mask_grad_kernel<true, true, true, __nv_bfloat16>(LossArgs);
+template __global__ void bwd_stats_kernel<false, __half>(LossArgs);
+template __global__ void bwd_stats_kernel<true, __half>(LossArgs);
+template __global__ void mask_grad_kernel<false, false, false, __half>(LossArgs);
+template __global__ void mask_grad_kernel<false, false, true, __half>(LossArgs);
+template __global__ void mask_grad_kernel<false, true, false, __half>(LossArgs);
+template __global__ void mask_grad_kernel<false, true, true, __half>(LossArgs);
+template __global__ void mask_grad_kernel<true, false, false, __half>(LossArgs);
+template __global__ void mask_grad_kernel<true, false, true, __half>(LossArgs);
+template __global__ void mask_grad_kernel<true, true, false, __half>(LossArgs);
+template __global__ void mask_grad_kernel<true, true, true, __half>(LossArgs);
 
 }  // namespace mlb

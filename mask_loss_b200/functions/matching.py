@@ -105,6 +105,15 @@ def resolve_args(mask_logits, mask_targets, cls_logits, cls_targets, smooth, sig
     return args, nm_dev
 
 
+def logits_for_kernels(mask_logits: torch.Tensor, mask_targets: torch.Tensor) -> torch.Tensor:
+    """mask_logits as the kernels take them: bf16/fp16 kept with label-map
+    targets, otherwise fp32 (functions/mask/matching.py:109 upcasts always)."""
+    x = mask_logits.contiguous()
+    if x.dtype in (torch.bfloat16, torch.float16) and not ops.is_dense(mask_targets):
+        return x
+    return x.float()
+
+
 class MaskMatchingFunction(Function):
     """Matching + matched losses; see functions/mask/matching.py:34-252."""
 
@@ -115,7 +124,10 @@ class MaskMatchingFunction(Function):
                 force_unmatched_masks_to_empty, K, assignment_strategy, mask_focal_gamma,
                 mask_focal_alpha, cls_focal_gamma, cls_focal_alpha, void_class_index=None,
                 label_loss="sigmoid"):
-        mask_logits = mask_logits.contiguous().float()
+        # bf16/fp16 mask logits stay in their type with label-map targets (the
+        # kernels widen them; the gradient comes back in the same type);
+        # anything else is upcast as the reference does
+        mask_logits = logits_for_kernels(mask_logits, mask_targets)
         mask_targets = mask_targets.contiguous()
         cls_logits = cls_logits.contiguous().float()
         cls_targets = cls_targets.contiguous()

@@ -11,6 +11,7 @@ from __future__ import annotations
 from torch.autograd import Function
 
 from .. import ops
+from .matching import logits_for_kernels
 
 
 def _gamma(v, default=0.0):
@@ -57,7 +58,7 @@ class PairwiseMaskLossFunction(Function):
         if kind not in {"sigmoid", "softmax"}:
             raise ValueError("label_loss must be either 'sigmoid' or 'softmax'")
         return ops.pairwise_mask_loss_forward(
-            mask_logits.contiguous().float(), mask_targets.contiguous(),
+            logits_for_kernels(mask_logits, mask_targets), mask_targets.contiguous(),
             cls_logits.contiguous().float(), cls_targets.contiguous(),
             smooth if smooth is not None else 1.0,
             sigmoid_scale if sigmoid_scale is not None else 1.0,

@@ -129,10 +129,10 @@ class MatchingLossStep:
                 args[4], args[6], args[7], args[10], args[11], args[12], args[13], args[14],
                 args[15], args[16], num_masks_dev=nm_dev, forward_workspace=fws)
         else:
-            if ml.dtype != torch.float32:
-                raise RuntimeError("mask_logits must be float32")
-            args, nm_dev = resolve_args(ml, mt, cl, ct, *a)
             dense = ops.is_dense(mt)
+            if ml.dtype != torch.float32 and (dense or ml.dtype not in (torch.bfloat16, torch.float16)):
+                raise RuntimeError("mask_logits must be float32 (bfloat16/float16 with label-map targets)")
+            args, nm_dev = resolve_args(ml, mt, cl, ct, *a)
             out = ops.mask_matching_ex(
                 ml, mt, cl, ct, *args, num_masks_dev=nm_dev, want_saved=True,
                 check_void_targets=True, loss_wait_event=ev, want_workspace=not dense)

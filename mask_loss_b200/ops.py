@@ -144,6 +144,15 @@ def _dims(mask_logits, mask_targets, cls_logits, cls_targets) -> _lib.Dims:
     return _lib.Dims(L, B, Q, H, W, Ht, Wt, cls_logits.shape[3], cls_targets.shape[1])
 
 
+# mask-logit element types of the label-map entries (ml_params.logits_dtype)
+_LOGIT_DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def _with_dtype(p: _lib.Params, mask_logits: torch.Tensor) -> _lib.Params:
+    p.logits_dtype = _LOGIT_DTYPES[mask_logits.dtype]
+    return p
+
+
 def _check_quad(mask_logits, mask_targets, cls_logits, cls_targets):
     for t, n in ((mask_logits, "mask_logits"), (mask_targets, "mask_targets"),
                  (cls_logits, "cls_logits"), (cls_targets, "cls_targets")):
@@ -156,7 +165,10 @@ def _check_quad(mask_logits, mask_targets, cls_logits, cls_targets):
         raise RuntimeError("cls_logits must be (L,B,Q,C)")
     if cls_targets.dim() != 2:
         raise RuntimeError("cls_targets must be (B,GT)")
-    _check_dtype(mask_logits, torch.float32, "mask_logits")
+    if is_dense(mask_targets):
+        _check_dtype(mask_logits, torch.float32, "mask_logits")
+    elif mask_logits.dtype not in _LOGIT_DTYPES:
+        raise RuntimeError("mask_logits must be float32, bfloat16 or float16")
     _check_dtype(cls_logits, torch.float32, "cls_logits")
     if is_dense(mask_targets):
         if mask_targets.dtype not in (torch.uint8, torch.bool):
@@ -196,6 +208,7 @@ def pairwise_mask_loss_forward(mask_logits, mask_targets, cls_logits, cls_target
                 cls_gamma=cls_gamma, cls_alpha=cls_alpha,
                 use_softmax_label_loss=use_softmax_label_loss,
                 normalize_uncertainty=normalize_uncertainty)
+    _with_dtype(p, mask_logits)
     L, B, Q = mask_logits.shape[:3]
     G = lib.ml_gt_out(d.GT_total, p.background_index)
     if G == 0:
@@ -257,6 +270,7 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
                 force_unmatched_masks_to_empty, topk_matches, strategy_id, mask_gamma, mask_alpha,
                 cls_gamma, cls_alpha, void_class_index, use_softmax_label_loss,
                 normalize_uncertainty, check_void_targets)
+    _with_dtype(p, mask_logits)
     L, B, Q = mask_logits.shape[:3]
     G = lib.ml_gt_out(d.GT_total, p.background_index)
     p2g = torch.empty((L, B, Q), dtype=torch.int64, device=dev)
@@ -353,6 +367,7 @@ def mask_matching_backward(grad_layer_mask_mean, grad_layer_dice_mean, grad_laye
                 uncertainty_gamma_min, 1e30, num_masks, force_unmatched_class_to_background,
                 force_unmatched_masks_to_empty, 1, 0, mask_gamma, mask_alpha, cls_gamma, cls_alpha,
                 void_class_index, use_softmax_label_loss, normalize_uncertainty)
+    _with_dtype(p, mask_logits)
     gm = torch.empty_like(mask_logits)
     gc = torch.empty_like(cls_logits)
     nbytes = lib.ml_mask_matching_backward_workspace_size(ctypes.byref(d), ctypes.byref(p))

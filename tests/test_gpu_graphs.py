@@ -46,6 +46,27 @@ def test_graph_replay_matches_eager_and_tracks_inputs():
         torch.testing.assert_close(step.grad_cls_logits, gc, rtol=1e-5, atol=1e-9)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_graph_replay_with_16bit_mask_logits(dtype):
+    # 4x label map so the backward reuses the forward's cell codes
+    cfg = synthetic.CONFIGS["cfg3"]
+    b = synthetic.make_batch(cfg, images=[0, 1], device=DEV)
+    ml, mt, cl, ct = (b[k].contiguous() for k in ("mask_logits", "mask_targets", "cls_logits",
+                                                  "cls_targets"))
+    ml = ml.to(dtype)
+    args = _args(cfg)
+    step = MatchingLossStep(ml.clone(), mt.clone(), cl.clone(), ct.clone(), *args)
+    step.replay()
+    torch.cuda.synchronize()
+    step.check()
+    p2g, losses, gm, gc = _eager(ml, mt, cl, ct, args)
+    assert step.grad_mask_logits.dtype == dtype
+    assert torch.equal(step.pred_to_gt, p2g)
+    torch.testing.assert_close(step.losses, losses, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(step.grad_mask_logits, gm, rtol=0, atol=0)
+    torch.testing.assert_close(step.grad_cls_logits, gc, rtol=1e-5, atol=1e-9)
+
+
 def test_auto_num_masks_counts_present_gts():
     cfg = synthetic.CONFIGS["cfg1"]
     b = synthetic.make_batch(cfg, device=DEV)

@@ -336,6 +336,78 @@ def test_standalone_pairwise_mask_ops_against_oracle():
     close(dice.cpu().numpy(), ref[1], what="dice")
 
 
+@pytest.mark.parametrize("dt", ["bf16", "fp16"])
+@pytest.mark.parametrize("s", [1, 4])
+def test_half_logits_equal_fp32_path_on_widened_values(dt, s):
+    # 16-bit mask logits: the kernels widen each value exactly and then run
+    # the fp32 arithmetic, so costs, assignment and losses equal the fp32 path
+    # on the widened tensor bit for bit, and the gradient equals its fp32
+    # gradient rounded to the same type; the fp32 path is pinned to the oracle
+    dtype = {"bf16": torch.bfloat16, "fp16": torch.float16}[dt]
+    torch.manual_seed(5 + s)
+    L, B, Q, H, W, C = 2, 2, 40, 24, 32, 9
+    cfg = synthetic.Config("t", 9, L, B, Q, H, W, s, C, 3.0, "ellipse", ("fixed", 6), (0.01, 0.2))
+    mt = torch.from_numpy(np.stack([synthetic.make_image_labels(cfg, b)[0] for b in range(B)]))
+    ct = torch.randint(0, C - 1, (B, 7))
+    ct[:, 0] = -1
+    x16 = (torch.randn(L, B, Q, H, W) * 3).to(dtype)
+    cl = torch.randn(L, B, Q, C)
+    for ug in (0.0, 1.0):
+        P = O.Params(background_index=0, sigmoid_scale=5.0, dice_scale=5.0, cls_scale=2.0,
+                     uncertainty_gamma=ug, void_class_index=C - 1, use_softmax_label_loss=True,
+                     force_unmatched_class_to_background=True)
+        d16 = [v.to(DEV).contiguous() for v in (x16, mt, cl, ct)]
+        d32 = [d16[0].float()] + d16[1:]
+        r16 = ops.mask_matching_ex(*d16, *op_args(P), want_saved=True, want_costs=True)
+        r32 = ops.mask_matching_ex(*d32, *op_args(P), want_saved=True, want_costs=True)
+        for a, b, what in zip(r16, r32, ("pred_to_gt", "pred_round", "means", "saved", "costs")):
+            assert torch.equal(a, b), what
+        ep2g, _, em, ed, ec, esep = O.mask_matching(x16.float().numpy(), mt.numpy(), cl.numpy(),
+                                                    ct.numpy(), P)
+        close(r32[4].cpu().numpy(), esep, what="costs")
+        np.testing.assert_array_equal(r32[0].cpu().numpy(), ep2g)
+        g = torch.tensor([[0.9, 1.1], [0.5, 1.5], [1.0, 2.0]], device=DEV)
+        for sv in (r16[3], None):
+            gm16, gc16 = ops.mask_matching_backward(g[0].contiguous(), g[1].contiguous(),
+                                                    g[2].contiguous(), *d16, r16[0], *bwd_args(P),
+                                                    saved=sv)
+            gm32, gc32 = ops.mask_matching_backward(g[0].contiguous(), g[1].contiguous(),
+                                                    g[2].contiguous(), *d32, r32[0], *bwd_args(P),
+                                                    saved=sv)
+            assert gm16.dtype == dtype
+            assert torch.equal(gm16, gm32.to(dtype))
+            assert torch.equal(gc16, gc32)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "fp16"])
+def test_half_logits_through_the_function(dt):
+    # autograd: the gradient of 16-bit mask logits arrives in their type and
+    # equals the fp32 gradient of the widened logits, rounded
+    dtype = {"bf16": torch.bfloat16, "fp16": torch.float16}[dt]
+    cfg = synthetic.CONFIGS["cfg1"]
+    batch = synthetic.make_batch(cfg)
+    kw = synthetic.parity_kwargs(cfg)
+    ml = batch["mask_logits"].to(DEV).to(dtype)
+    mt, cl, ct = (batch[k].to(DEV) for k in ("mask_targets", "cls_logits", "cls_targets"))
+    x = ml.clone().requires_grad_(True)
+    z = cl.clone().requires_grad_(True)
+    p2g, prd, m, d, c = F.MaskMatchingFunction.apply(
+        x, mt, z, ct, kw["smooth"], kw["sigmoid_scale"], kw["dice_scale"], kw["cls_scale"],
+        kw["background_index"], 0.0, 0.05, True, kw["inf_thresh"], -1.0, True, False, 1, "global",
+        0.0, None, None, None, kw["void_class_index"], "softmax")
+    (m + d + c).sum().backward()
+    assert x.grad.dtype == dtype and torch.isfinite(x.grad.float()).all()
+    x32 = ml.float().clone().requires_grad_(True)
+    z32 = cl.clone().requires_grad_(True)
+    o32 = F.MaskMatchingFunction.apply(
+        x32, mt, z32, ct, kw["smooth"], kw["sigmoid_scale"], kw["dice_scale"], kw["cls_scale"],
+        kw["background_index"], 0.0, 0.05, True, kw["inf_thresh"], -1.0, True, False, 1, "global",
+        0.0, None, None, None, kw["void_class_index"], "softmax")
+    (o32[2] + o32[3] + o32[4]).sum().backward()
+    assert torch.equal(p2g, o32[0])
+    assert torch.equal(x.grad, x32.grad.to(dtype))
+
+
 def test_deterministic_runs():
     cfg = synthetic.CONFIGS["cfg1"]
     batch = synthetic.make_batch(cfg)
