@@ -250,8 +250,6 @@ def run_ours(args, cfg):
     if half is not None and not sampled:
         # 16-bit mask logits end to end (the kernels widen them; the gradient
         # is written in the same type)
-        if dense:
-            raise SystemExit("--logits bf16/fp16 needs label-map targets")
         ml = ml.to(half)
     if sampled:  # point-sampled configuration: bf16 logits, P points per image
         ml = ml.to(torch.bfloat16)

@@ -68,13 +68,13 @@ typedef struct ml_params {
                                           functions/mask/matching.py:180-181, done on
                                           the device); 0: no check (the binding) */
     int32_t logits_dtype;              /* element type of mask_logits and
-                                          grad_mask_logits in the label-map entries
-                                          (ml_pairwise_mask_loss_forward,
-                                          ml_mask_matching[_ex],
-                                          ml_mask_matching_backward[_ex]): 0 fp32,
-                                          1 bf16, 2 fp16.  The pointers stay typed
-                                          float* and point at values of this type;
-                                          arithmetic is fp32 either way.  The dense,
+                                          grad_mask_logits in the label-map and
+                                          dense entries (ml_pairwise_mask_loss_*
+                                          forward, ml_mask_matching[_ex|_dense],
+                                          ml_mask_matching[_dense]_backward[_ex]):
+                                          0 fp32, 1 bf16, 2 fp16.  The pointers stay
+                                          typed float* and point at values of this
+                                          type; arithmetic is fp32 either way.  The
                                           no-alloc and semantic entries take fp32
                                           only; the sampled ones have their own
                                           dtype argument and ignore this field. */

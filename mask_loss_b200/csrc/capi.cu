@@ -464,7 +464,7 @@ int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigne
     if (LBQ == 0 || P.gout == 0) return ML_OK;
     {
         ProfScope prof(0, st);  // profiled as the cost stage
-        e = launch_dense_cost(a, P.unc, P.foc, cnt, st);
+        e = launch_dense_cost(a, P.unc, P.foc, cnt, st, P.ldt);
     }
     g_launches.fetch_add(1);
     if (e != cudaSuccess) return cuda_fail(e, "dense_cost_kernel");
@@ -830,8 +830,6 @@ static int mask_matching_impl(const ml_dims* d, const ml_params* p, const float*
     FwdPlan P;
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
-    if (dense_masks && p->logits_dtype != 0)
-        return fail(ML_EUNSUPPORTED, "dense mask targets take fp32 mask_logits");
     if ((rc = make_plan(d, p, &P))) return rc;
     if (P.gout == 0)
         return fail(ML_ESHAPE, "pairwise_sigmoid_dice_loss_forward must return {3,L,B,Q,GT_out}");
@@ -925,8 +923,6 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
     const int ldt = (int)p->logits_dtype;
-    if (dense_masks && ldt != 0)
-        return fail(ML_EUNSUPPORTED, "dense mask targets take fp32 mask_logits");
     if ((rc = validate_dims(d))) return rc;
     const size_t need = ml_mask_matching_backward_workspace_size(d, p);
     if ((rc = check_ws(workspace, workspace_bytes, need))) return rc;
@@ -1067,7 +1063,6 @@ int ml_pairwise_mask_loss_dense_forward(const ml_dims* d, const ml_params* p, co
     FwdPlan P;
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
-    if (p->logits_dtype != 0) return fail(ML_EUNSUPPORTED, "dense mask targets take fp32 mask_logits");
     if ((rc = make_plan(d, p, &P))) return rc;
     if ((rc = check_ws(workspace, workspace_bytes, P.bytes + dense_count_bytes(P)))) return rc;
     if (P.gout == 0) return ML_OK;

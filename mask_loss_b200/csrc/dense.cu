@@ -22,6 +22,8 @@
 //                       accumulator has one owner thread.
 #include <algorithm>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -78,7 +80,7 @@ dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int 
 
 // grid = (nchunk * 2 halves * ngc, nqt, L*B), block = QP threads (query row t of the tile).
 // Dynamic shared memory: see dense_cost_smem.
-template <bool UNC, bool FOC>
+template <bool UNC, bool FOC, typename T>
 __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_t* cnt, int GC) {
     constexpr int NACC = UNC ? 3 : 2;
     constexpr int NROW = UNC ? 5 : 3;
@@ -146,25 +148,31 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
     };
     // logits tile in registers: thread t holds float4 (t + m*QP), m < 8 --
     // row i >> 3, cells 4*(i & 7) .. +3 -- so the next tile's loads are in
-    // flight while the current one is computed.  Rows and cells are
-    // 16-byte aligned when vec (H*W % 4 == 0, aligned logits).
-    const bool vec = (HW % 4 == 0) && ((reinterpret_cast<uintptr_t>(a.logits) & 15) == 0);
-    float4 pre[8];
+    // flight while the current one is computed.  Four elements are one
+    // 16-byte (fp32) or 8-byte (16-bit) access when vec (H*W % 4 == 0 and an
+    // aligned base); T is the logit type, widened on load.
+    // The registers keep the raw words (float4, or uint2 of four 16-bit
+    // values) and are widened only when the tile goes to shared memory, so
+    // the loads stay in flight through the current tile's compute.
+    const T* xlog = reinterpret_cast<const T*>(a.logits);
+    const bool vec = (HW % 4 == 0) && ((reinterpret_cast<uintptr_t>(xlog) & (4 * sizeof(T) - 1)) == 0);
+    using Raw = typename std::conditional<sizeof(T) == 4, float4, uint2>::type;
+    Raw pre[8];
     auto load_tile = [&](int c0n) {
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
             const int i = t + m * QP, r = i >> 3, c = (i & 7) * 4;
             const int qq = qt * a.qrows + r;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            Raw v{};  // zeros (also +0.0 in 16 bits)
             if (r < a.qrows && qq < a.Q) {
-                const float* src = a.logits + (int64_t)(row0 + r) * HW + c0n + c;
+                const T* src = xlog + (int64_t)(row0 + r) * HW + c0n + c;
                 if (vec) {
-                    if (c0n + c < cell_end) v = __ldcs(reinterpret_cast<const float4*>(src));
+                    if (c0n + c < cell_end) v = __ldcs(reinterpret_cast<const Raw*>(src));
                 } else {
-                    v.x = c0n + c < cell_end ? src[0] : 0.0f;
-                    v.y = c0n + c + 1 < cell_end ? src[1] : 0.0f;
-                    v.z = c0n + c + 2 < cell_end ? src[2] : 0.0f;
-                    v.w = c0n + c + 3 < cell_end ? src[3] : 0.0f;
+                    alignas(8) T e[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) e[u] = c0n + c + u < cell_end ? src[u] : from_f<T>(0.0f);
+                    v = *reinterpret_cast<const Raw*>(e);
                 }
             }
             pre[m] = v;
@@ -178,7 +186,12 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
         for (int m = 0; m < 8; ++m) {
             const int i = t + m * QP, r = i >> 3, c = (i & 7) * 4;
             float* d = xs + r * (kDenseTile + 1) + c;
-            d[0] = pre[m].x; d[1] = pre[m].y; d[2] = pre[m].z; d[3] = pre[m].w;
+            if constexpr (sizeof(T) == 4) {
+                d[0] = pre[m].x; d[1] = pre[m].y; d[2] = pre[m].z; d[3] = pre[m].w;
+            } else {
+                widen2(pre[m].x, d[0], d[1], xlog);
+                widen2(pre[m].y, d[2], d[3], xlog);
+            }
         }
         // the tile's counts, coalesced per GT plane
         for (int i = t; i < gn * kDenseTile; i += blockDim.x) {
@@ -276,17 +289,21 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
     }
 }
 
+template <typename T>
 __global__ void __launch_bounds__(128) dense_cost_kernel(CostArgs a, const uint16_t* cnt, int GC) {
-    dense_cost_body<false, false>(a, cnt, GC);
+    dense_cost_body<false, false, T>(a, cnt, GC);
 }
+template <typename T>
 __global__ void __launch_bounds__(128) dense_cost_unc_kernel(CostArgs a, const uint16_t* cnt, int GC) {
-    dense_cost_body<true, false>(a, cnt, GC);
+    dense_cost_body<true, false, T>(a, cnt, GC);
 }
+template <typename T>
 __global__ void __launch_bounds__(128) dense_cost_foc_kernel(CostArgs a, const uint16_t* cnt, int GC) {
-    dense_cost_body<false, true>(a, cnt, GC);
+    dense_cost_body<false, true, T>(a, cnt, GC);
 }
+template <typename T>
 __global__ void __launch_bounds__(128) dense_cost_unc_foc_kernel(CostArgs a, const uint16_t* cnt, int GC) {
-    dense_cost_body<true, true>(a, cnt, GC);
+    dense_cost_body<true, true, T>(a, cnt, GC);
 }
 
 // GT columns per block: all of them up to kDenseGC (shared memory scales with it).
@@ -308,18 +325,26 @@ cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht
     return cudaGetLastError();
 }
 
-cudaError_t launch_dense_cost(const CostArgs& a, bool unc, bool foc, const uint16_t* cnt,
-                              cudaStream_t st) {
+template <typename T>
+cudaError_t launch_dense_cost_t(const CostArgs& a, bool unc, bool foc, const uint16_t* cnt,
+                                cudaStream_t st) {
     const int gc = dense_gc(a.gout);
     const size_t smem = dense_cost_smem(a.qrows_pad, unc, gc);
     const int ngc = (a.gout + gc - 1) / gc;
     dim3 g(a.nchunk * 2 * ngc, a.nqt, a.L * a.B);
-    auto k = unc ? (foc ? dense_cost_unc_foc_kernel : dense_cost_unc_kernel)
-                 : (foc ? dense_cost_foc_kernel : dense_cost_kernel);
+    auto k = unc ? (foc ? dense_cost_unc_foc_kernel<T> : dense_cost_unc_kernel<T>)
+                 : (foc ? dense_cost_foc_kernel<T> : dense_cost_kernel<T>);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     k<<<g, a.qrows_pad, smem, st>>>(a, cnt, gc);
     return cudaGetLastError();
+}
+
+cudaError_t launch_dense_cost(const CostArgs& a, bool unc, bool foc, const uint16_t* cnt,
+                              cudaStream_t st, int ldt) {
+    if (ldt == 1) return launch_dense_cost_t<__nv_bfloat16>(a, unc, foc, cnt, st);
+    if (ldt == 2) return launch_dense_cost_t<__half>(a, unc, foc, cnt, st);
+    return launch_dense_cost_t<float>(a, unc, foc, cnt, st);
 }
 
 }  // namespace mlb

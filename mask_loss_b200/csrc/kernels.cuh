@@ -199,6 +199,7 @@ size_t dense_cost_smem(int qrows_pad, bool unc, int gc);
 int dense_gc(int gout);
 cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht, int Wt, int s,
                                int gt_total, uint16_t* cnt, int32_t* totals, cudaStream_t st);
+// ldt: mask-logit type (0 fp32, 1 bf16, 2 fp16)
 cudaError_t launch_dense_cost(const CostArgs& a, bool unc, bool foc, const uint16_t* cnt,
-                              cudaStream_t st);
+                              cudaStream_t st, int ldt);
 }  // namespace mlb

@@ -106,10 +106,10 @@ def resolve_args(mask_logits, mask_targets, cls_logits, cls_targets, smooth, sig
 
 
 def logits_for_kernels(mask_logits: torch.Tensor, mask_targets: torch.Tensor) -> torch.Tensor:
-    """mask_logits as the kernels take them: bf16/fp16 kept with label-map
-    targets, otherwise fp32 (functions/mask/matching.py:109 upcasts always)."""
+    """mask_logits as the kernels take them: bf16/fp16 kept, anything else
+    fp32 (functions/mask/matching.py:109 upcasts always)."""
     x = mask_logits.contiguous()
-    if x.dtype in (torch.bfloat16, torch.float16) and not ops.is_dense(mask_targets):
+    if x.dtype in (torch.bfloat16, torch.float16):
         return x
     return x.float()
 
@@ -124,9 +124,9 @@ class MaskMatchingFunction(Function):
                 force_unmatched_masks_to_empty, K, assignment_strategy, mask_focal_gamma,
                 mask_focal_alpha, cls_focal_gamma, cls_focal_alpha, void_class_index=None,
                 label_loss="sigmoid"):
-        # bf16/fp16 mask logits stay in their type with label-map targets (the
-        # kernels widen them; the gradient comes back in the same type);
-        # anything else is upcast as the reference does
+        # bf16/fp16 mask logits stay in their type (the kernels widen them;
+        # the gradient comes back in the same type); anything else is upcast
+        # as the reference does
         mask_logits = logits_for_kernels(mask_logits, mask_targets)
         mask_targets = mask_targets.contiguous()
         cls_logits = cls_logits.contiguous().float()

@@ -130,8 +130,8 @@ class MatchingLossStep:
                 args[15], args[16], num_masks_dev=nm_dev, forward_workspace=fws)
         else:
             dense = ops.is_dense(mt)
-            if ml.dtype != torch.float32 and (dense or ml.dtype not in (torch.bfloat16, torch.float16)):
-                raise RuntimeError("mask_logits must be float32 (bfloat16/float16 with label-map targets)")
+            if ml.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+                raise RuntimeError("mask_logits must be float32, bfloat16 or float16")
             args, nm_dev = resolve_args(ml, mt, cl, ct, *a)
             out = ops.mask_matching_ex(
                 ml, mt, cl, ct, *args, num_masks_dev=nm_dev, want_saved=True,

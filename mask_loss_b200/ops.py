@@ -165,9 +165,7 @@ def _check_quad(mask_logits, mask_targets, cls_logits, cls_targets):
         raise RuntimeError("cls_logits must be (L,B,Q,C)")
     if cls_targets.dim() != 2:
         raise RuntimeError("cls_targets must be (B,GT)")
-    if is_dense(mask_targets):
-        _check_dtype(mask_logits, torch.float32, "mask_logits")
-    elif mask_logits.dtype not in _LOGIT_DTYPES:
+    if mask_logits.dtype not in _LOGIT_DTYPES:
         raise RuntimeError("mask_logits must be float32, bfloat16 or float16")
     _check_dtype(cls_logits, torch.float32, "cls_logits")
     if is_dense(mask_targets):

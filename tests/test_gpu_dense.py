@@ -142,3 +142,25 @@ def test_dense_backward_needs_saved_statistics():
     with pytest.raises(RuntimeError, match="saved"):
         ops.mask_matching_backward(g, g, g, *t, p2g, 1.0, 1.0, 1.0, 1.0, 0, 0.0, 0.05, -1.0, False,
                                    False, 0.0, -1.0, 0.0, -1.0, -1)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shp", [(2, 2, 12, 8, 12, 1, 7, 6), (1, 2, 10, 5, 7, 2, 6, 5)])
+def test_dense_half_logits_equal_fp32_path_on_widened_values(dtype, shp):
+    # 16-bit logits with overlapping masks: the dense kernel widens each value
+    # (8-byte loads when H*W % 4 == 0, scalar loads otherwise) and runs the
+    # fp32 arithmetic, so everything equals the fp32 run on the widened tensor
+    ml, masks, cl, ct = _overlap_case(7 + sum(shp), *shp)
+    P = O.Params(smooth=1.0, sigmoid_scale=5.0, dice_scale=5.0, cls_scale=2.0,
+                 background_index=0, uncertainty_gamma=1.0,
+                 force_unmatched_class_to_background=True, void_class_index=shp[6] - 1,
+                 use_softmax_label_loss=True)
+    x16 = torch.from_numpy(ml).to(DEV).to(dtype)
+    t = [torch.from_numpy(v).to(DEV) for v in (masks, cl, ct)]
+    r16 = _run(x16, *t, P)
+    r32 = _run(x16.float(), *t, P)
+    assert torch.equal(r16[0], r32[0]) and torch.equal(r16[1], r32[1])
+    assert torch.equal(r16[2], r32[2])
+    assert r16[3].dtype == dtype
+    assert torch.equal(r16[3], r32[3].to(dtype))
+    assert torch.equal(r16[4], r32[4])
