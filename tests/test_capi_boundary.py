@@ -48,6 +48,35 @@ def test_host_only_entries():
     assert b"integer multiple" in lib.ml_last_error()
 
 
+def _header_struct_fields(name):
+    src = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (name, name), src, flags=re.S).group(1)
+    fields = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if decl:
+            fields += [f.strip() for f in re.sub(r"^\w+\s+", "", decl).split(",")]
+    return fields
+
+
+def test_ctypes_structs_mirror_the_header():
+    # field names in declaration order; the C layout rules then give both
+    # sides the same offsets and size
+    assert [f[0] for f in _lib.Params._fields_] == _header_struct_fields("ml_params")
+    assert [f[0] for f in _lib.Dims._fields_] == _header_struct_fields("ml_dims")
+
+
+def test_logits_dtype_is_validated_before_any_device_work():
+    lib = _lib.load()
+    d = _lib.Dims(1, 1, 4, 8, 8, 8, 8, 5, 3)
+    p = ops._params(background_index=0, uncertainty_gamma=0.0)
+    p.logits_dtype = 3
+    rc = lib.ml_pairwise_mask_loss_forward(ctypes.byref(d), ctypes.byref(p), None, None, None,
+                                           None, None, None, 0, None)
+    assert rc == 1  # ML_EINVAL
+    assert b"logits_dtype" in lib.ml_last_error()
+
+
 def test_op_surface_names():
     # src/bindings.cpp:157-169
     for name in ["forward_sigmoid_ce_loss", "backward_sigmoid_ce_loss", "forward_pw_sigmoid_ce_loss",
