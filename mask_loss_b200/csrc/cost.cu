@@ -418,11 +418,14 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
                     const int rem = i - bx * a.qrows * (KBOX / GR);
                     const int r = rem / (KBOX / GR), c = rem - r * (KBOX / GR);
                     const T* src = lg + (int64_t)(row0 + r) * HW + c0 + bx * KBOX + c * GR;
+                    // the last query tile can extend one row past Q (qrows =
+                    // ceil(Q / nqt)): those rows read as zeros, like the TMA fill
+                    const bool row_ok = qt * a.qrows + r < a.Q;
                     alignas(16) T vv[GR];
 #pragma unroll
                     for (int u = 0; u < GR; ++u) {
                         const int k = bx * KBOX + c * GR + u;
-                        vv[u] = (k < nvalid) ? src[u] : from_f<T>(0.0f);
+                        vv[u] = (row_ok && k < nvalid) ? src[u] : from_f<T>(0.0f);
                     }
                     *reinterpret_cast<uint4*>(xs + (st * 2 + bx) * box_elems + r * KBOX +
                                               Tile<T>::gran(r, c)) = *reinterpret_cast<const uint4*>(vv);
