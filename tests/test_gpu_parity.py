@@ -408,6 +408,44 @@ def test_half_logits_through_the_function(dt):
     assert torch.equal(x.grad, x32.grad.to(dtype))
 
 
+def test_odd_query_count_with_plain_load_producer():
+    # Q = 129: two query tiles of 65 rows, the second one row past Q; H*W = 35
+    # is not a multiple of 16 bytes in either type, so the cost kernel's
+    # producer uses plain loads (rows past Q read as zeros)
+    torch.manual_seed(129)
+    L, B, Q, H, W, s, C = 1, 2, 129, 5, 7, 2, 6
+    cfg = synthetic.Config("t", 9, L, B, Q, H, W, s, C, 3.0, "ellipse", ("fixed", 5), (0.05, 0.4))
+    mt = torch.from_numpy(np.stack([synthetic.make_image_labels(cfg, b)[0] for b in range(B)]))
+    ct = torch.randint(0, C - 1, (B, 6))
+    ct[:, 0] = -1
+    ml = torch.randn(L, B, Q, H, W) * 3
+    cl = torch.randn(L, B, Q, C)
+    P = O.Params(background_index=0, sigmoid_scale=5.0, dice_scale=5.0, cls_scale=2.0,
+                 uncertainty_gamma=0.0, void_class_index=C - 1, use_softmax_label_loss=True,
+                 force_unmatched_class_to_background=True)
+    d = [v.to(DEV).contiguous() for v in (ml, mt, cl, ct)]
+    p2g, prd, means, saved, costs = ops.mask_matching_ex(*d, *op_args(P), want_saved=True,
+                                                         want_costs=True)
+    ep2g, eprd, em, ed, ec, esep = O.mask_matching(ml.numpy(), mt.numpy(), cl.numpy(), ct.numpy(), P)
+    close(costs.cpu().numpy(), esep, what="costs")
+    np.testing.assert_array_equal(p2g.cpu().numpy(), ep2g)
+    close(means.cpu().numpy(), np.stack([em, ed, ec]), what="means")
+    g = torch.tensor([[1.0], [0.6], [1.4]], device=DEV)
+    gm, gc = ops.mask_matching_backward(g[0].contiguous(), g[1].contiguous(), g[2].contiguous(),
+                                        *d, p2g, *bwd_args(P), saved=saved)
+    egm, egc = O.mask_matching_backward([1.0], [0.6], [1.4], ml.numpy(), mt.numpy(), cl.numpy(),
+                                        ct.numpy(), ep2g, P)
+    close_grad(gm.cpu().numpy(), egm, "grad mask")
+    close_grad(gc.cpu().numpy(), egc, "grad cls")
+    # the same through 16-bit logits: equal to fp32 on the widened values
+    d16 = [d[0].to(torch.bfloat16)] + d[1:]
+    d32 = [d16[0].float()] + d[1:]
+    r16 = ops.mask_matching_ex(*d16, *op_args(P), want_saved=True, want_costs=True)
+    r32 = ops.mask_matching_ex(*d32, *op_args(P), want_saved=True, want_costs=True)
+    for a, b in zip(r16, r32):
+        assert torch.equal(a, b)
+
+
 def test_deterministic_runs():
     cfg = synthetic.CONFIGS["cfg1"]
     batch = synthetic.make_batch(cfg)
