@@ -17,14 +17,15 @@
 // partial buffer (a thread's same-address reductions apply in program order,
 // so the sums are deterministic).  Tiles whose 32 cells carry one label --
 // most of an image -- take a branch-free path.  Mixed cells (s > 1 on a label
-// boundary) add their per-pixel counts directly.
+// boundary) add the (column, pixel count) pairs of their table entry.
 //
 // Data movement: a prep kernel turns the int64 label map into one int32 code
-// per low-res cell (and the per-image histogram) once; the cost kernel then
-// streams logits tiles of (qrows x 64 cells) with two cp.async.bulk.tensor
-// boxes (128-byte swizzle, conflict-free LDS.128) plus the tile's 256 bytes of
-// codes with one cp.async.bulk, all on one mbarrier, through a 3-stage
-// pipeline.  Logits are read from HBM exactly once.
+// per low-res cell, the mixed-cell table (s > 1) and the per-image histogram
+// once; the cost kernel then streams logits tiles of (qrows x 64 cells) with
+// two cp.async.bulk.tensor boxes (128-byte swizzle for fp32, 64-byte for
+// bf16/fp16; conflict-free 128-bit reads) plus the tile's 256 bytes of codes
+// with one cp.async.bulk, all on one mbarrier, through a 2-stage pipeline.
+// Logits are read from HBM exactly once.
 //
 // The HW axis is split into chunks across CTAs (grid.x) sized to whole waves
 // of the 148 SMs; two finalize kernels reduce the chunk partials in fixed
@@ -336,7 +337,7 @@ template <typename T> struct Tile {
 
 // ---------------------------------------------------------------------------
 // The streaming cost kernel.  grid = (nchunk, nqt, L*B); block = 2*qrows_pad
-// consumer threads plus one producer warp.  The producer fills a 3-stage ring
+// consumer threads plus one producer warp.  The producer fills a 2-stage ring
 // (full/empty mbarriers, no block-wide barrier in the loop); consumer thread
 // (h, t) <-> query row qt*qrows + t, cells [h*32, h*32+32) of every 64-cell
 // tile.  Inside a box the run starts are one ballot (bnd), so the element
@@ -345,6 +346,7 @@ template <typename T> struct Tile {
 //   FOC   focal gamma/alpha on the mask BCE
 //   TMA   logits rows are 16-byte strided so the bulk-tensor path is legal
 //   MIX   cells cover several target pixels (s > 1), so mixed cells occur
+//   T     mask-logit element type (float, __nv_bfloat16, __half)
 // ---------------------------------------------------------------------------
 template <bool UNC, bool FOC, bool TMA, bool MIX, typename T>
 __global__ void __launch_bounds__(kCostThreads, (MIX && !UNC && !FOC) ? 3 : 2)
