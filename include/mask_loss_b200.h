@@ -33,8 +33,9 @@ typedef enum ml_status {
     ML_EUNSUPPORTED = 6  /* a size beyond what this build supports */
 } ml_status;
 
-/* Shapes of one call.  mask_logits (L,B,Q,H,W) fp32, mask_targets (B,Ht,Wt)
- * int64, cls_logits (L,B,Q,C) fp32, cls_targets (B,GT_total) int64 (-1 pad). */
+/* Shapes of one call.  mask_logits (L,B,Q,H,W) of ml_params.logits_dtype
+ * (fp32 by default), mask_targets (B,Ht,Wt) int64, cls_logits (L,B,Q,C) fp32,
+ * cls_targets (B,GT_total) int64 (-1 pad). */
 typedef struct ml_dims {
     int64_t L, B, Q, H, W;
     int64_t Ht, Wt;
@@ -229,8 +230,9 @@ int ml_count_masks(const ml_dims* d, const ml_params* p, const int64_t* mask_tar
 /*   grad_*_mean: (L,) fp32 device upstream gradients                       */
 /*   saved (nullable): the forward's per-query statistics; when null a      */
 /*                     statistics pass re-reads the logits (reference path) */
-/*   grad_mask_logits (L,B,Q,H,W), grad_cls_logits (L,B,Q,C): fp32, fully    */
-/*                     written (zeros where the loss does not reach).       */
+/*   grad_mask_logits (L,B,Q,H,W) of ml_params.logits_dtype, grad_cls_logits */
+/*                     (L,B,Q,C) fp32: fully written (zeros where the loss  */
+/*                     does not reach).                                     */
 /* ---------------------------------------------------------------------- */
 int ml_mask_matching_backward(const ml_dims* d, const ml_params* p,
                               const float* grad_mask_mean, const float* grad_dice_mean,

@@ -9,10 +9,14 @@
 //
 // Backward: replaces mask_matching_backward (src/cuda/mask_matching_backward.cu:
 // 21-621).  With the forward's saved per-query statistics the mask gradient is
-// a single streaming pass: read logits once (128-bit loads), write the
-// gradient once, label codes staged in shared memory per cell chunk and
-// reused by every query of the image.  Without them (the standalone binding
-// call) a statistics pass re-reads the logits first, like the reference.
+// a single streaming pass: read the matched rows' logits once (four values
+// per access), write the gradient once (rows the loss does not reach are
+// pure streaming stores of zeros).  The matched label's pixel count per cell
+// comes from the label map directly for s = 1 (16-byte label loads) and from
+// the per-cell codes plus the mixed-cell table for s > 1.  Without the
+// statistics (the standalone binding call) a statistics pass re-reads the
+// logits first, like the reference.  Logits and gradient are fp32, bf16 or
+// fp16 (template T / LT); arithmetic is fp32.
 #include "common.cuh"
 #include "kernels.cuh"
 
