@@ -137,3 +137,31 @@ def test_semantic_losses_reject_cpu_tensors():
         ops.forward_sigmoid_ce_loss(torch.zeros(1, 1, 2, 4, 4), torch.zeros(1, 4, 4, dtype=torch.long), 1.0)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.forward_dice_loss(torch.zeros(1, 1, 2, 4, 4), torch.zeros(1, 4, 4, dtype=torch.long), 1.0, 1.0)
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    # a plain C99 caller: the header is valid C, the library links, the
+    # host-only entries answer, and the struct sizes equal the ctypes mirrors
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    libdir = os.path.dirname(_lib.load()._name)
+    src = tmp_path / "caller.c"
+    src.write_text(
+        '#include "mask_loss_b200.h"\n#include <stdio.h>\n'
+        "int main(void) {\n"
+        "  ml_dims d = {1, 2, 3, 8, 8, 8, 8, 5, 3};\n"
+        "  ml_params p = {0};\n"
+        "  size_t n = ml_mask_matching_workspace_size(&d, &p);\n"
+        '  printf("%d %zu %zu %zu\\n", ml_version(), n, sizeof(ml_params), sizeof(ml_dims));\n'
+        "  return 0;\n}\n")
+    exe = tmp_path / "caller"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-pedantic",
+                    "-I" + os.path.join(REPO, "include"), str(src), "-L" + libdir,
+                    "-lmask_loss_b200", "-Wl,-rpath," + libdir, "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
+    assert int(out[0]) == _lib.load().ml_version()
+    assert int(out[1]) > 0
+    assert int(out[2]) == ctypes.sizeof(_lib.Params)
+    assert int(out[3]) == ctypes.sizeof(_lib.Dims)
