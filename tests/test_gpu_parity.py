@@ -446,6 +446,48 @@ def test_odd_query_count_with_plain_load_producer():
         assert torch.equal(a, b)
 
 
+def test_reference_benchmark_shape_properties():
+    """The reference harness's mask_matching shape (benchmarks.py:550-614): ten
+    decoder layers, 8 images, Q=128, 256x256 logits against 1024x1024 label
+    maps, C=128, bg=0, num_masks=5, forced unmatched class, void = C-1,
+    softmax label loss, K=1 global.  Size-independent checks only."""
+    base = synthetic.CONFIGS["native"]
+    cfg = synthetic.Config("ref-bench", base.cfg, 10, base.B, base.Q, base.H, base.W, base.s, base.C,
+                           base.logit_std, base.shapes, base.g_law, base.area)
+    batch = synthetic.make_batch(cfg, device=DEV, logits=False)
+    mt, ct = batch["mask_targets"].contiguous(), batch["cls_targets"].contiguous()
+    g = torch.Generator(device=DEV).manual_seed(550)
+    ml = torch.randn((cfg.L, cfg.B, cfg.Q, cfg.H, cfg.W), generator=g, device=DEV)
+    cl = torch.randn((cfg.L, cfg.B, cfg.Q, cfg.C), generator=g, device=DEV)
+    kw = synthetic.parity_kwargs(cfg)
+    kw["num_masks"] = 5.0
+    P = oracle_params(kw)
+    p2g, prd, means, saved, costs = ops.mask_matching_ex(ml, mt, cl, ct, *op_args(P),
+                                                         want_saved=True, want_costs=True)
+    again = ops.mask_matching_ex(ml, mt, cl, ct, *op_args(P), want_saved=True, want_costs=True)
+    assert torch.equal(p2g, again[0]) and torch.equal(costs, again[4])
+    assert torch.isfinite(means).all()
+    G = ct.shape[1]
+    counts = torch.stack([torch.bincount(mt[b].flatten(), minlength=G)[:G] for b in range(cfg.B)])[:, 1:]
+    absent = (counts == 0)[None, :, None, :].expand(cfg.L, cfg.B, cfg.Q, -1)
+    assert torch.equal(torch.isinf(costs[0]), absent)
+    for l in range(cfg.L):
+        for b in range(cfg.B):
+            m = p2g[l, b][p2g[l, b] >= 0]
+            assert torch.equal(torch.sort(m).values, torch.nonzero(~absent[l, b, 0]).flatten())
+    tot = (costs[0] + costs[1]) + costs[2]
+    for l, b in ((0, 0), (4, 3), (9, 7)):
+        ea, _ = O.assign_slice(tot[l, b].double().cpu().numpy(), 1e30, 1, 0)
+        np.testing.assert_array_equal(p2g[l, b].cpu().numpy(), ea)
+    up = torch.ones(cfg.L, device=DEV)
+    gm, gc = ops.mask_matching_backward(up, up, up, ml, mt, cl, ct, p2g, *bwd_args(P), saved=saved)
+    assert torch.isfinite(gm).all() and torch.isfinite(gc).all()
+    # the mask gradient reaches matched rows only (no forced-empty masks)
+    rows = gm.abs().flatten(3).amax(3)
+    assert torch.equal(rows[p2g < 0], torch.zeros_like(rows[p2g < 0]))
+    assert (rows[p2g >= 0] > 0).all()
+
+
 def test_deterministic_runs():
     cfg = synthetic.CONFIGS["cfg1"]
     batch = synthetic.make_batch(cfg)
