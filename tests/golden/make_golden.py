@@ -70,6 +70,13 @@ CASES = {
         uncertainty_gamma=1.0, uncertainty_gamma_min=0.05, num_masks=None,
         force_unmatched_class_to_background=False, force_unmatched_masks_to_empty=False,
         K=2, assignment_strategy="pseudo_greedy", void_class_index=5, label_loss="softmax")),
+    # s = 4 with rectangles off the 4-pixel grid: most boundary cells hold two
+    # to four labels (mixed cells), a few more
+    "mm_s4_mixed_uncert": (2, 2, 16, 6, 8, 4, 6, 8, dict(
+        smooth=1.0, sigmoid_scale=5.0, dice_scale=5.0, cls_scale=2.0, background_index=0,
+        uncertainty_gamma=1.0, uncertainty_gamma_min=0.05, num_masks=None,
+        force_unmatched_class_to_background=True, force_unmatched_masks_to_empty=False,
+        K=1, assignment_strategy="global", void_class_index=5, label_loss="softmax")),
 }
 
 
@@ -220,11 +227,17 @@ def gen_sampled(name, seed, L, B, Q, H, W, Ht, Wt, G, P, focal_gamma=0.0, focal_
 
 
 if __name__ == "__main__":
+    # python make_golden.py [case names ...]: all fixtures, or only the named
+    # mm_* cases (each case keeps its seed, so a subset run writes the same files)
     O.build()
     if O.ref_lib() is None:
         raise SystemExit("oracle/_ref was not built: the reference sources are required")
+    only = set(sys.argv[1:])
     for i, (name, spec) in enumerate(CASES.items()):
-        gen_case(name, spec, 100 + i)
+        if not only or name in only:
+            gen_case(name, spec, 100 + i)
+    if only:
+        raise SystemExit(0)
     gen_solver()
     gen_sampled("sampled_basic", 501, 1, 3, 8, 12, 12, 24, 24, 5, 500)
     gen_sampled("sampled_focal_s4", 502, 2, 2, 6, 8, 10, 32, 40, 4, 777, focal_gamma=2.0,
