@@ -1,6 +1,7 @@
 """Benchmark: images/s of Mask2Former-style matching + loss, forward + backward.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference]
+                    [--logits fp32|bf16|fp16] [--targets labels|dense]
 
 One step = one pass of the hot path over one batch: pairwise costs, on-device
 assignment, matched losses (forward) and dL/dlogits (backward) through
@@ -14,6 +15,12 @@ N > 1: launched by torchrun, one rank per GPU, weak scaling (16 images per
 GPU); the only collectives are an NCCL all-reduce of num_masks (before the
 loss) and of the loss scalars (reporting).  Timing is device-side (CUDA
 events), max over ranks.
+
+Other workloads: --config cfg1/cfg3/cfg4/cfg5/native (the configs of
+mask_loss_b200/synthetic.py; native = the reference harness's own shape, 8 x
+Q=128 x 256^2 logits against 1024^2 label maps), --logits bf16/fp16 (16-bit
+mask logits, widened in the kernels), --targets dense (per-GT uint8 masks cut
+from the label maps, one GPU).  The default line is config 2, fp32.
 
 --impl reference times the CPU implementation of the same path on the host
 cores: the CPU restatement in oracle/ for costs and losses, and the
