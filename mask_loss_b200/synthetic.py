@@ -10,7 +10,14 @@ is (B, max_b G_b + 1) with -1 padding, classes drawn from the real classes
 [0, C'-1) so the void class C'-1 never appears as a target.
 
 Per-image seeds are ``1000 * cfg + b`` so a subset of images can be
-regenerated independently (the CPU baseline uses that).
+regenerated independently (the CPU baseline uses that).  A redrawn image
+(``redraws={b: k}``) adds ``10**6 * k`` to each of its seeds.
+
+No-near-tie filter (``tie_free_redraws``): an image is kept only when its
+assignment survives a relative perturbation of its total costs,
+``cost * (1 + eps * U[-1, 1])``; otherwise it is redrawn with the next k.
+The caller supplies the costs and the solver (the library itself has no CPU
+arithmetic), so the filter is run by the parity tests with their checker.
 """
 from __future__ import annotations
 
@@ -119,9 +126,12 @@ def _paint_polygon(lab, gid, cy, cx, r, nv, rng):
     lab[y0:y1, x0:x1][inside] = gid
 
 
-def make_image_labels(cfg: Config, b: int):
+REDRAW_SEED_STEP = 10 ** 6
+
+
+def make_image_labels(cfg: Config, b: int, redraw: int = 0):
     """(H*s, W*s) int64 label map and the number of GT ids painted for image b."""
-    rng = np.random.default_rng(1000 * cfg.cfg + b)
+    rng = np.random.default_rng(1000 * cfg.cfg + b + REDRAW_SEED_STEP * redraw)
     Ht, Wt = cfg.H * cfg.s, cfg.W * cfg.s
     G = _n_gt(cfg.g_law, rng)
     lab = np.zeros((Ht, Wt), np.int64)
@@ -157,17 +167,20 @@ def make_image_labels(cfg: Config, b: int):
     return lab, G
 
 
-def make_batch(cfg: Config, images=None, device="cpu", logits=True):
+def make_batch(cfg: Config, images=None, device="cpu", logits=True, redraws=None):
     """Inputs of one step: mask_logits (L,B,Q,H,W) f32, mask_targets (B,Ht,Wt)
     i64, cls_logits (L,B,Q,C) f32, cls_targets (B,GTmax+1) i64.
 
-    `images` selects a subset of image indices (default: all B)."""
+    `images` selects a subset of image indices (default: all B); `redraws`
+    maps an image index to its redraw count k (default 0)."""
     idx = list(range(cfg.B)) if images is None else list(images)
-    labs, gs = zip(*(make_image_labels(cfg, b) for b in idx))
+    rd = {} if redraws is None else dict(redraws)
+    ks = [int(rd.get(b, 0)) for b in idx]
+    labs, gs = zip(*(make_image_labels(cfg, b, k) for b, k in zip(idx, ks)))
     gmax = max(gs)
     cls = np.full((len(idx), gmax + 1), -1, np.int64)
     for i, b in enumerate(idx):
-        rng = np.random.default_rng(10_000_000 + 1000 * cfg.cfg + b)
+        rng = np.random.default_rng(10_000_000 + 1000 * cfg.cfg + b + REDRAW_SEED_STEP * ks[i])
         cls[i, 1:gs[i] + 1] = rng.integers(0, cfg.C - 1, gs[i])
     targets = torch.from_numpy(np.stack(labs)).to(device)
     cls_t = torch.from_numpy(cls).to(device)
@@ -175,13 +188,43 @@ def make_batch(cfg: Config, images=None, device="cpu", logits=True):
     if logits:
         # one generator per image, so any subset of images gets the same values
         ml, cl = [], []
-        for b in idx:
+        for b, k in zip(idx, ks):
+            seed = 1000 * cfg.cfg + 7 + 100003 * b + REDRAW_SEED_STEP * k
             if str(device).startswith("cuda"):
-                g = torch.Generator(device=device).manual_seed(1000 * cfg.cfg + 7 + 100003 * b)
+                g = torch.Generator(device=device).manual_seed(seed)
             else:
-                g = torch.Generator().manual_seed(1000 * cfg.cfg + 7 + 100003 * b)
+                g = torch.Generator().manual_seed(seed)
             ml.append(torch.randn((cfg.L, 1, cfg.Q, cfg.H, cfg.W), generator=g, device=device))
             cl.append(torch.randn((cfg.L, 1, cfg.Q, cfg.C), generator=g, device=device))
         out["mask_logits"] = torch.cat(ml, 1) * cfg.logit_std
         out["cls_logits"] = torch.cat(cl, 1)
+    return out
+
+
+def tie_free_redraws(cfg: Config, images, total_cost, solve, eps: float = 1e-4,
+                     max_redraws: int = 32, log=None) -> dict:
+    """Redraw counts {b: k} that make every listed image free of near-ties.
+
+    For image b and k = 0, 1, ...: ``total_cost(b, k)`` returns its (Q, G)
+    float64 total cost matrix and ``solve(cost)`` its assignment (an int
+    array).  The draw is kept when the assignment of
+    ``cost * (1 + eps * U[-1, 1])`` (U seeded by b and k) equals that of
+    ``cost``.  eps defaults to the 1e-4 relative cost tolerance of the
+    parity contract: an assignment that a perturbation of that size can
+    change is a tie under that contract.  `log(b, k)` is called with the
+    final k of each image."""
+    out = {}
+    for b in images:
+        for k in range(max_redraws + 1):
+            c = np.asarray(total_cost(b, k), np.float64)
+            rng = np.random.default_rng(7_000_000 + 1000 * cfg.cfg + b + REDRAW_SEED_STEP * k)
+            pert = c * (1.0 + eps * rng.uniform(-1.0, 1.0, c.shape))
+            pert[~np.isfinite(c)] = c[~np.isfinite(c)]
+            if np.array_equal(np.asarray(solve(c)), np.asarray(solve(pert))):
+                out[b] = k
+                break
+        else:
+            raise RuntimeError(f"image {b}: no tie-free draw in {max_redraws} redraws")
+        if log is not None:
+            log(b, out[b])
     return out
