@@ -20,3 +20,4 @@ from .sampled import (  # noqa: F401
     pairwise_dice_loss_sampling,
     pairwise_sigmoid_cross_entropy_loss_sampling,
 )
+from .losses import dice_loss, sigmoid_cross_entropy_loss  # noqa: F401

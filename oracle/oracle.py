@@ -29,9 +29,25 @@ _LIB = None
 _REF = None
 
 
+def reference_root():
+    """The reference checkout (AndyBarcia/mask_loss sources), or None.
+
+    ``MASK_LOSS_REF`` names it; otherwise a ``reference`` directory beside the
+    repository is used when it exists.  Only build steps and fixture
+    generators look for it; tests, smoke() and bench.py never do."""
+    root = os.environ.get("MASK_LOSS_REF")
+    if not root:
+        root = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference")
+    return root if os.path.isfile(os.path.join(root, "src", "cpu", "matching.cpp")) else None
+
+
 def build(quiet: bool = True) -> None:
     """Compile liboracle.so (and oracle/_ref when the reference sources exist)."""
-    out = subprocess.run(["make", "-C", _HERE], capture_output=True, text=True)
+    cmd = ["make", "-C", _HERE]
+    root = reference_root()
+    if root:
+        cmd.append("REF_SRC=" + os.path.join(root, "src"))
+    out = subprocess.run(cmd, capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout[-2000:] + out.stderr[-4000:])
     if not quiet:

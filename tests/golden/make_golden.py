@@ -1,7 +1,7 @@
 """Generate the golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container where the reference checkout exists (default
-/root/reference, override with MASK_LOSS_REF):
+Run where the reference checkout exists (MASK_LOSS_REF, or a ``reference``
+directory beside the repository):
 
     python tests/golden/make_golden.py
 
@@ -14,7 +14,7 @@ Run in a container where the reference checkout exists (default
   C++ solver (src/cpu/matching.cpp:476-571, compiled by oracle/Makefile into
   oracle/_ref/libref.so) returns for strategies 0-3 and K in {0,1,2,3}.
 
-Fixtures are small (a few hundred KB total).  Nothing under /root/reference is
+Fixtures are small (a few hundred KB total).  Nothing of the reference is
 read at test time: the tests only read these .npz files.
 """
 import contextlib
@@ -27,7 +27,12 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("MASK_LOSS_REF", "/root/reference")
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from oracle.oracle import reference_root  # noqa: E402
+
+REF = reference_root()
+if REF is None:
+    raise SystemExit("reference checkout not found: set MASK_LOSS_REF")
 sys.path.insert(0, REPO)
 sys.path.insert(0, REF)
 

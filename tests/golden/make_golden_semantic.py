@@ -1,6 +1,6 @@
 """Golden fixtures of the standalone semantic losses, made by the reference.
 
-    python tests/golden/make_golden_semantic.py      (needs /root/reference or MASK_LOSS_REF)
+    python tests/golden/make_golden_semantic.py      (needs the reference checkout: MASK_LOSS_REF)
 
 ``semantic_*.npz``: inputs, the per-layer losses of the reference's
 ``sigmoid_cross_entropy_loss_py`` (functions/sigmoid/sigmoid_ce.py:147-226) and
@@ -16,7 +16,12 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("MASK_LOSS_REF", "/root/reference")
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from oracle.oracle import reference_root  # noqa: E402
+
+REF = reference_root()
+if REF is None:
+    raise SystemExit("reference checkout not found: set MASK_LOSS_REF")
 sys.path.insert(0, REF)
 with contextlib.redirect_stdout(io.StringIO()):
     import functions as RF  # noqa: E402  (the reference's Python package)

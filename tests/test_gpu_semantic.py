@@ -93,3 +93,25 @@ def test_semantic_deterministic_and_edges():
     assert torch.equal(ops.forward_dice_loss(e, td_, 1.0, 1.0)[0], torch.zeros(2, device=DEV))
     with pytest.raises(RuntimeError, match="integer multiple"):
         ops.forward_sigmoid_ce_loss(xd_, td_[:, :23].contiguous(), 1.0)
+
+
+@pytest.mark.parametrize("four_d", [False, True])
+def test_losses_front_end_equals_the_functions(four_d):
+    # functions/losses.py:8-67 with class_mapping=None: the same values and
+    # gradients as the Functions it wraps, for (L,B,C,h,w) and (B,C,h,w) logits
+    x, t, go = _random_case(17, 2, 2, 6, 12, 12, 2, False)
+    x, t = x.to(DEV), t.to(DEV)
+    if four_d:
+        x = x[0]
+    for front, fn, extra in ((F.sigmoid_cross_entropy_loss, F.SigmoidCELossFunction, ()),
+                             (F.dice_loss, F.DiceLossFunction, (1e-6,))):
+        xa = x.clone().requires_grad_(True)
+        xb = x.clone().requires_grad_(True)
+        la = front(xa, t, *extra, num_masks=7.0, scale=1.5)
+        lb = fn.apply(xb[None] if four_d else xb, t, *extra, 7.0, 1.5)
+        lb = lb[0] if four_d else lb
+        assert la.shape == lb.shape
+        la.sum().backward()
+        lb.sum().backward()
+        assert torch.equal(la.detach(), lb.detach())
+        assert torch.equal(xa.grad, xb.grad)
