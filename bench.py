@@ -289,7 +289,7 @@ def run_ours(args, cfg):
         losses.sum().backward()
         losses = losses.detach()
         parallel.average_losses(losses, async_op=True)
-        return losses, x.grad, z.grad
+        return losses, x.grad, z.grad, p2g
 
     def barrier():
         torch.cuda.synchronize()
@@ -320,9 +320,13 @@ def run_ours(args, cfg):
     n_eager = max(3, min(args.steps, 50))
     ms_eager = timed(lambda: step(ml, mt, cl, ct), n_eager) / n_eager
     lib.ml_profile_enable(0)
-    kms = np.zeros(3, np.float32)
-    kn = np.zeros(3, np.int64)
-    lib.ml_profile_read(kms.ctypes.data, kn.ctypes.data, 3)
+    NK = 7  # profile kinds of the library (include/mask_loss_b200.h, ml_profile_enable)
+    kms = np.zeros(NK, np.float32)
+    kn = np.zeros(NK, np.int64)
+    lib.ml_profile_read(kms.ctypes.data, kn.ctypes.data, NK)
+    kstep = kms / n_eager  # ms per step of each kind
+    # matched query rows of one step (the gradient stage re-reads their logits)
+    matched = int((step(ml, mt, cl, ct)[3] >= 0).sum().item()) if not sampled else None
 
     # ---- device-resident throughput (value): the whole step as one CUDA graph ----
     from mask_loss_b200.graphs import MatchingLossStep
@@ -383,7 +387,43 @@ def run_ours(args, cfg):
     e2e_steps = max(3, min(args.steps, 20))
     ms_e2e = timed(e2e_step, e2e_steps) / e2e_steps
     e2e = ws * cfg.B * cfg.L / (ms_e2e / 1e3)
+    # the same with both logit gradients copied back to pinned host buffers
+    h_gm = torch.empty(gstep.grad_mask_logits.shape, dtype=gstep.grad_mask_logits.dtype,
+                       pin_memory=True)
+    h_gc = torch.empty(gstep.grad_cls_logits.shape, dtype=torch.float32, pin_memory=True)
+
+    def e2e_grads_step():
+        e2e_step()
+        h_gm.copy_(gstep.grad_mask_logits, non_blocking=True)
+        h_gc.copy_(gstep.grad_cls_logits, non_blocking=True)
+
+    e2e_grads_step()
+    ms_e2e_g = timed(e2e_grads_step, e2e_steps) / e2e_steps
+    d2h_g = d2h + sum(t.numel() * t.element_size() for t in (h_gm, h_gc))
     gstep.check()
+
+    # ---- N > 1: what the num_masks collective costs the step ----
+    scaling = None
+    if ws > 1 and not sampled:
+        # the same graph step with the local GT count (no collective)
+        lstep = MatchingLossStep(
+            g_ml, g_mt, g_cl, g_ct, kw["smooth"], kw["sigmoid_scale"], kw["dice_scale"],
+            kw["cls_scale"], kw["background_index"], kw["uncertainty_gamma"],
+            kw["uncertainty_gamma_min"], True, kw["inf_thresh"], "auto", True, False, 1,
+            "global", 0.0, None, None, None, kw["void_class_index"], "softmax",
+            warmup=max(1, args.warmup))
+        for _ in range(args.warmup):
+            lstep.replay()
+        ms_local = timed(lstep.replay, args.steps) / args.steps
+        lstep = None
+        # the 4-byte all-reduce alone, back to back
+        one = torch.ones(1, device=dev)
+        for _ in range(args.warmup):
+            dist.all_reduce(one)
+        ms_ar = timed(lambda: dist.all_reduce(one), args.steps) / args.steps
+        scaling = {"step_ms_allreduce_num_masks": ms_step, "step_ms_local_num_masks": ms_local,
+                   "allreduce_4B_us": 1e3 * ms_ar,
+                   "note": "max over ranks; local = the same graph step without the collective"}
     ops.check_status(block=True)
 
     def teardown():
@@ -425,6 +465,33 @@ def run_ours(args, cfg):
     traffic = read_traffic(cfg.name, cost_kernel)
     grad_ms = float(kms[1] / max(kn[1], 1))
     match_ms = float(kms[2] / max(kn[2], 1))
+    # stage roofline (per step, algorithmic bytes):
+    #   A (costs)   = label map + every logit once + class logits
+    #   C (losses)  = the gradient written + the matched rows' logits re-read
+    #                 + label map + class logits read and their gradient written
+    LBQ = cfg.L * cfg.B * cfg.Q
+    lab_bytes = cfg.B * (cfg.H * cfg.s) * (cfg.W * cfg.s) * (GT_total if dense else 8)
+    cls_bytes = LBQ * cfg.C * 4
+    stages = None
+    if not sampled:
+        HW = cfg.H * cfg.W
+        bytes_a = lab_bytes + LBQ * HW * esize + cls_bytes
+        bytes_c = LBQ * HW * esize + matched * HW * esize + lab_bytes + 2 * cls_bytes
+        ms_a = float(kstep[3] + kstep[0] + kstep[4])
+        ms_c = float(kstep[5] + kstep[6] + kstep[1])
+        stages = {
+            "A_costs": {"ms": ms_a, "bytes": bytes_a, "frac": bytes_a / (ms_a / 1e3) / 1e9 / peak,
+                        "kernels": "label_code + cost_partial (or dense_cost) + cost_rows + cost_pairs"},
+            "B_solver": {"ms": float(kstep[2]), "kernels": "match_kernel (latency-bound, no roofline)"},
+            "C_losses_grads": {"ms": ms_c, "bytes": bytes_c,
+                               "frac": bytes_c / (ms_c / 1e3) / 1e9 / peak,
+                               "kernels": "loss_fwd + bwd_cls + mask_grad"},
+            "step": {"ms": ms_step, "bytes": bytes_a + bytes_c,
+                     "frac": (bytes_a + bytes_c) / (ms_step / 1e3) / 1e9 / peak,
+                     "note": "graph-replayed step; bytes of stages A and C"},
+            "matched_rows_per_step": matched,
+            "stage_times": "eager steps with the library's event hooks, per step",
+        }
     cpu = None
     if ws == 1 and not sampled and not dense:
         threads = max(1, os.cpu_count() or 1)
@@ -452,13 +519,21 @@ def run_ours(args, cfg):
                    "l2": ("inputs larger than L2" if not flush_ms else
                           f"L2 flushed before every step (256 MB write, {flush_ms:.3f} ms, subtracted)")},
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": ms_e2e},
+                "ms_per_step": ms_e2e,
+                "note": "headline: inputs from pinned host memory, loss means back; the "
+                        "gradients stay on the device, where the model's backward reads them"},
+        "e2e_with_grads": {"value": ws * cfg.B * cfg.L / (ms_e2e_g / 1e3), "unit": UNIT,
+                           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h_g,
+                           "ms_per_step": ms_e2e_g,
+                           "note": "as e2e, plus both logit gradients copied to pinned host memory"},
         "roofline": {"bound": "hbm", "kernel": cost_kernel, "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "algorithmic_bytes_per_launch": cost_bytes, "avg_launch_ms": cost_ms,
                      "peak_source": peak_src},
         "stages_ms": {cost_kernel: cost_ms, "mask_grad_kernel": grad_ms,
                       "match_kernel": match_ms, "eager_step": ms_eager},
+        "stages": stages,
+        "multi_gpu": scaling,
         "execution": "value and e2e replay the step as one CUDA graph "
                      "(mask_loss_b200.graphs.MatchingLossStep); stage times from eager steps",
         "gpu_launches": int(launches),

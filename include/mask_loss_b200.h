@@ -94,9 +94,11 @@ int ml_version(void);
 int64_t ml_launch_count(void);
 
 /* Measurement hooks.  While enabled, the library records a CUDA event pair
- * on the launching stream around every launch of its three hot kernels
- * (kind 0: pairwise-cost streaming kernel, 1: mask-gradient kernel,
- * 2: assignment solver).  ml_profile_read waits for the recorded events,
+ * on the launching stream around every launch of its kernels, by kind:
+ * 0: pairwise-cost streaming kernel, 1: mask-gradient kernel, 2: assignment
+ * solver, 3: label preparation (cell codes + histogram), 4: cost finalize
+ * (row statistics + pair costs), 5: matched-loss forward, 6: class-logit
+ * backward.  ml_profile_read waits for the recorded events,
  * returns the summed milliseconds and launch counts per kind (arrays of
  * nkinds entries) and clears the record.  No counterpart in the reference. */
 void ml_profile_enable(int on);
@@ -135,8 +137,11 @@ int ml_pairwise_mask_loss_forward(const ml_dims* d, const ml_params* p,
  *   - Calls larger than that limit fail with ML_EUNSUPPORTED and a message
  *     (ml_last_error); use the workspace entry point for them.
  *   - It calls no cudaMalloc/cudaFree and no allocating library routine.
- *   - The first call on a device looks up the array's device address with
- *     that device current; make that first call before any stream capture.
+ *   - The array's device address is looked up (cudaGetSymbolAddress) with
+ *     the device current on every call.  Under CUDA's lazy module loading the
+ *     first call on a device also loads this library's device code there and
+ *     with it the 64 MiB array, so make that first call before device memory
+ *     is reserved up front, and before any stream capture.
  *   - Every call shares the one array: calls that can overlap on the GPU
  *     (different streams, or different host threads on one device) race
  *     and must be serialised by the caller. */
@@ -217,6 +222,20 @@ int ml_mask_matching_ex(const ml_dims* d, const ml_params* p,
                         void* workspace, size_t workspace_bytes, ml_stream_t stream,
                         ml_event_t loss_wait_event);
 
+/* ml_mask_matching_ex plus costs_done_event (nullable): recorded on `stream`
+ * once the pairwise costs are final, before the solver launches, so that
+ * work which needs only the costs (or nothing of this call, such as zeroing
+ * the gradient buffer of ml_mask_matching_backward_ex2) can run on another
+ * stream beside the solver.  No reference counterpart. */
+int ml_mask_matching_ex2(const ml_dims* d, const ml_params* p,
+                         const float* mask_logits, const int64_t* mask_targets,
+                         const float* cls_logits, const int64_t* cls_targets,
+                         const float* num_masks_dev,
+                         int64_t* pred_to_gt, int64_t* pred_round, float* layer_means,
+                         float* sep_costs, float* saved, int32_t* dev_status,
+                         void* workspace, size_t workspace_bytes, ml_stream_t stream,
+                         ml_event_t loss_wait_event, ml_event_t costs_done_event);
+
 /* Per-image GT count (present, non-background GT ids) summed over the batch,
  * written as one fp32 to num_masks_out (device).  This is the num_masks a
  * data-parallel caller all-reduces.  Needs the forward workspace. */
@@ -259,6 +278,22 @@ int ml_mask_matching_backward_ex(const ml_dims* d, const ml_params* p,
                                  float* grad_mask_logits, float* grad_cls_logits,
                                  void* workspace, size_t workspace_bytes, ml_stream_t stream,
                                  const void* forward_workspace);
+
+/* ml_mask_matching_backward_ex plus grad_rows_prezeroed: when non-zero, the
+ * caller has already filled grad_mask_logits with zeros, and only the rows
+ * that carry a gradient (matched queries, or every query with
+ * force_unmatched_masks_to_empty) are written.  The zero fill can then run
+ * beside the solver instead of after it.  No reference counterpart. */
+int ml_mask_matching_backward_ex2(const ml_dims* d, const ml_params* p,
+                                  const float* grad_mask_mean, const float* grad_dice_mean,
+                                  const float* grad_cls_mean,
+                                  const float* mask_logits, const int64_t* mask_targets,
+                                  const float* cls_logits, const int64_t* cls_targets,
+                                  const int64_t* pred_to_gt, const float* saved,
+                                  const float* num_masks_dev,
+                                  float* grad_mask_logits, float* grad_cls_logits,
+                                  void* workspace, size_t workspace_bytes, ml_stream_t stream,
+                                  const void* forward_workspace, int grad_rows_prezeroed);
 
 /* ---------------------------------------------------------------------- */
 /* Point-sampled costs and matching (config 3).  Replaces                    */

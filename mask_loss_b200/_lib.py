@@ -71,6 +71,9 @@ SIGNATURES = {
     "ml_mask_matching_ex": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_vp, c_vp,
                                            c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                            c_vp, c_sz, c_vp, c_vp]),
+    "ml_mask_matching_ex2": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_vp,
+                                            c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                            c_vp, c_vp, c_sz, c_vp, c_vp, c_vp]),
     "ml_count_masks": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_vp, c_vp,
                                       c_vp, c_sz, c_vp]),
     "ml_dense_workspace_size": (c_sz, [ctypes.POINTER(Dims), ctypes.POINTER(Params)]),
@@ -96,6 +99,10 @@ SIGNATURES = {
     "ml_mask_matching_backward_ex": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params),
                                                     c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                                     c_vp, c_vp, c_vp, c_vp, c_vp, c_sz, c_vp, c_vp]),
+    "ml_mask_matching_backward_ex2": (ctypes.c_int, [ctypes.POINTER(Dims), ctypes.POINTER(Params),
+                                                     c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                     c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_sz,
+                                                     c_vp, c_vp, ctypes.c_int]),
     "ml_sampled_workspace_size": (c_sz, [ctypes.POINTER(Dims), ctypes.POINTER(Params), c_i64]),
     "ml_sampled_backward_workspace_size": (c_sz, [ctypes.POINTER(Dims), ctypes.POINTER(Params),
                                                   c_i64, c_i32]),

@@ -78,6 +78,13 @@ struct ProfScope {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// MASK_LOSS_B200_DENSE_MMA=1 runs dense-mask costs on the tensor-core kernel
+// (dense_mma.cu); otherwise the CUDA-core kernel (dense.cu) runs them.
+const bool g_dense_mma_off = [] {
+    const char* v = getenv("MASK_LOSS_B200_DENSE_MMA");
+    return !(v && v[0] == '1');
+}();
+
 // Raise a kernel's dynamic shared-memory limit once per (kernel, device);
 // later calls with the same or a smaller size touch no CUDA API (so they are
 // safe inside stream capture).
@@ -361,6 +368,7 @@ int run_prep(const FwdPlan& P, const CostArgs& a, cudaStream_t st) {
                                     sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
     if (e != cudaSuccess) return cuda_fail(e, "memset totals");
     cudaError_t le;
+    ProfScope prof(3, st);
     if (a.codes) {
         le = launch_label_code(a.targets, P.B, P.H, P.W, P.Wt, P.s, P.gt_total, P.bg,
                                const_cast<int32_t*>(a.codes), const_cast<int32_t*>(a.totals),
@@ -375,6 +383,30 @@ int run_prep(const FwdPlan& P, const CostArgs& a, cudaStream_t st) {
 }
 
 int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaStream_t st);
+
+// 2-D tensor map over the mask logits (rows = L*B*Q, columns = H*W) with
+// boxes of 32 cells x qrows rows: 128-byte rows with the 128-byte swizzle for
+// fp32, 64-byte rows with the 64-byte swizzle for 16-bit logits.  False when
+// the rows are not 16-byte strided or aligned (the kernels then load plainly).
+bool logits_tensor_map(const FwdPlan& P, const float* mask_logits, CUtensorMap* tm) {
+    memset(tm, 0, sizeof(*tm));
+    const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
+    if (!P.tma_ok || (reinterpret_cast<uintptr_t>(mask_logits) % 16) != 0 || LBQ == 0) return false;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const CUtensorMapDataType dt = P.ldt == 1   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                   : P.ldt == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const cuuint64_t dims[2] = {(cuuint64_t)P.H * P.W, (cuuint64_t)LBQ};
+    const cuuint64_t strides[1] = {(cuuint64_t)P.H * P.W * P.esize};
+    const cuuint32_t box[2] = {(cuuint32_t)KBOX, (cuuint32_t)P.qrows};
+    const cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(tm, dt, 2, const_cast<float*>(mask_logits), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     P.esize == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
 
 int run_finalize(const FwdPlan& P, CostArgs& a, cudaStream_t st);
 
@@ -391,29 +423,7 @@ int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaS
     if (LBQ == 0 || P.gout == 0) return ML_OK;
     // the cost kernel clears its own partial slots (no memset)
     CUtensorMap tm;
-    memset(&tm, 0, sizeof(tm));
-    bool tma = P.tma_ok && (reinterpret_cast<uintptr_t>(mask_logits) % 16 == 0);
-    if (tma) {
-        EncodeTiledFn enc = encode_fn();
-        if (!enc) {
-            tma = false;
-        } else {
-            // rows of 32 cells: 128 bytes (fp32, 128-byte swizzle) or 64 bytes
-            // (16-bit, 64-byte swizzle); the kernel's Tile<T> reads either
-            const CUtensorMapDataType dt = P.ldt == 1   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                           : P.ldt == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-            const cuuint64_t dims[2] = {(cuuint64_t)P.H * P.W, (cuuint64_t)LBQ};
-            const cuuint64_t strides[1] = {(cuuint64_t)P.H * P.W * P.esize};
-            const cuuint32_t box[2] = {(cuuint32_t)KBOX, (cuuint32_t)P.qrows};
-            const cuuint32_t es[2] = {1, 1};
-            CUresult r = enc(&tm, dt, 2, const_cast<float*>(mask_logits), dims, strides, box, es,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE,
-                             P.esize == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-            if (r != CUDA_SUCCESS) tma = false;
-        }
-    }
+    const bool tma = logits_tensor_map(P, mask_logits, &tm);
     rc = with_logit_type(P.ldt, [&](auto tag) -> int {
         using T = decltype(tag);
         if (P.unc) {
@@ -431,6 +441,7 @@ int run_cost_core(const FwdPlan& P, CostArgs& a, const float* mask_logits, cudaS
 int run_finalize(const FwdPlan& P, CostArgs& a, cudaStream_t st) {
     const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
     const unsigned rb = (unsigned)((LBQ * 32 + 255) / 256);
+    ProfScope prof(4, st);
     if (P.unc) cost_rows_kernel<true, false><<<rb, 256, 0, st>>>(a);
     else if (P.foc) cost_rows_kernel<false, false><<<rb, 256, 0, st>>>(a);
     else cost_rows_kernel<false, true><<<rb, 256, 0, st>>>(a);
@@ -464,7 +475,12 @@ int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigne
     if (LBQ == 0 || P.gout == 0) return ML_OK;
     {
         ProfScope prof(0, st);  // profiled as the cost stage
-        e = launch_dense_cost(a, P.unc, P.foc, cnt, st, P.ldt);
+        CUtensorMap tm;
+        const bool tma = logits_tensor_map(P, a.logits, &tm);
+        if (dense_mma_usable(a, P.ldt, P.unc, P.foc, tma) && !g_dense_mma_off)
+            e = launch_dense_mma(tm, a, cnt, st, P.ldt);  // tensor cores (tcgen05)
+        else
+            e = launch_dense_cost(a, P.unc, P.foc, cnt, st, P.ldt);
     }
     g_launches.fetch_add(1);
     if (e != cudaSuccess) return cuda_fail(e, "dense_cost_kernel");
@@ -533,26 +549,16 @@ LossArgs loss_args(const FwdPlan& P, const ml_params* p) {
 constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;  // 64 MiB
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-unsigned char* g_noalloc_ptr[kMaxDevices] = {};
-
 // Device address of g_noalloc_scratch on the current device.  The host-side
 // symbol is only a stand-in; the real address comes from
-// cudaGetSymbolAddress, looked up once per device with that device current.
+// cudaGetSymbolAddress with the device current.  It is looked up on every
+// call (it allocates nothing and is cheap), so a device or context reset
+// between calls cannot leave a stale cached address behind.
 int noalloc_scratch(unsigned char** out) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    if (dev < 0 || dev >= kMaxDevices) return fail(ML_EUNSUPPORTED, "device ordinal %d out of range", dev);
-    std::lock_guard<std::mutex> g(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-        void* ptr = nullptr;
-        e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
-        g_noalloc_ptr[dev] = static_cast<unsigned char*>(ptr);
-    }
-    *out = g_noalloc_ptr[dev];
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    *out = static_cast<unsigned char*>(ptr);
     return ML_OK;
 }
 
@@ -826,7 +832,8 @@ static int mask_matching_impl(const ml_dims* d, const ml_params* p, const float*
                               int64_t* pred_to_gt, int64_t* pred_round, float* layer_means,
                               float* sep_costs, float* saved, int32_t* dev_status, void* workspace,
                               size_t workspace_bytes, ml_stream_t stream, cudaEvent_t loss_wait,
-                              const uint8_t* dense_masks = nullptr) {
+                              const uint8_t* dense_masks = nullptr,
+                              cudaEvent_t costs_done = nullptr) {
     FwdPlan P;
     int rc = validate_params(p, d ? d->C : 0);
     if (rc) return rc;
@@ -843,6 +850,10 @@ static int mask_matching_impl(const ml_dims* d, const ml_params* p, const float*
     if (dense_masks) rc = run_dense_costs(P, a, dense_masks, ws, st);
     else rc = run_costs(P, a, mask_logits, st);
     if (rc) return rc;
+    if (costs_done) {  // the costs are final: work that needs only them may start
+        cudaError_t e = cudaEventRecord(costs_done, st);
+        if (e != cudaSuccess) return cuda_fail(e, "record costs_done_event");
+    }
     if ((rc = launch_match<float>(a.total, (int64_t)P.L * P.B, P.Q, P.gout, p->inf_thresh,
                                   p->topk_matches, p->strategy_id, pred_to_gt, pred_round,
                                   dev_status, st)))
@@ -864,7 +875,10 @@ static int mask_matching_impl(const ml_dims* d, const ml_params* p, const float*
         cudaError_t e = cudaStreamWaitEvent(st, loss_wait, 0);
         if (e != cudaSuccess) return cuda_fail(e, "wait for loss_wait_event");
     }
-    loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
+    {
+        ProfScope prof(5, st);
+        loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
+    }
     ML_CHECK_LAUNCH("loss_fwd_kernel");
     return ML_OK;
 }
@@ -889,6 +903,19 @@ int ml_mask_matching_ex(const ml_dims* d, const ml_params* p, const float* mask_
                               pred_to_gt, pred_round, layer_means, sep_costs, saved, dev_status,
                               workspace, workspace_bytes, stream,
                               reinterpret_cast<cudaEvent_t>(loss_wait_event));
+}
+
+int ml_mask_matching_ex2(const ml_dims* d, const ml_params* p, const float* mask_logits,
+                         const int64_t* mask_targets, const float* cls_logits,
+                         const int64_t* cls_targets, const float* num_masks_dev, int64_t* pred_to_gt,
+                         int64_t* pred_round, float* layer_means, float* sep_costs, float* saved,
+                         int32_t* dev_status, void* workspace, size_t workspace_bytes,
+                         ml_stream_t stream, ml_event_t loss_wait_event, ml_event_t costs_done_event) {
+    return mask_matching_impl(d, p, mask_logits, mask_targets, cls_logits, cls_targets, num_masks_dev,
+                              pred_to_gt, pred_round, layer_means, sep_costs, saved, dev_status,
+                              workspace, workspace_bytes, stream,
+                              reinterpret_cast<cudaEvent_t>(loss_wait_event), nullptr,
+                              reinterpret_cast<cudaEvent_t>(costs_done_event));
 }
 
 int ml_count_masks(const ml_dims* d, const ml_params* p, const int64_t* mask_targets,
@@ -917,7 +944,7 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
                          const float* num_masks_dev, float* grad_mask_logits,
                          float* grad_cls_logits, void* workspace, size_t workspace_bytes,
                          ml_stream_t stream, const uint8_t* dense_masks,
-                         const void* forward_workspace = nullptr) {
+                         const void* forward_workspace = nullptr, int rows_prezeroed = 0) {
     if (dense_masks && !saved)
         return fail(ML_EINVAL, "dense mask targets need the forward's saved statistics");
     int rc = validate_params(p, d ? d->C : 0);
@@ -947,6 +974,7 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
     la.grad_mask = grad_mask_mean; la.grad_dice = grad_dice_mean; la.grad_cls = grad_cls_mean;
     la.coef = coef; la.grad_mask_logits = grad_mask_logits; la.grad_cls_logits = grad_cls_logits;
     la.masks = dense_masks;
+    la.rows_zeroed = rows_prezeroed ? 1 : 0;
     const int HW = P.H * P.W;
     if (lay.cells && !dense_masks && HW > 0) {
         // per-cell column codes + mixed-cell table: the gradient kernels read
@@ -971,7 +999,10 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
         la.mixtab = mixtab;
     }
     // coefficients + class-logit gradient first; the mask gradient reads coef
-    bwd_cls_kernel<<<(unsigned)((LBQ + 7) / 8), 256, 0, st>>>(la);
+    {
+        ProfScope prof(6, st);
+        bwd_cls_kernel<<<(unsigned)((LBQ + 7) / 8), 256, 0, st>>>(la);
+    }
     ML_CHECK_LAUNCH("bwd_cls_kernel");
     const bool unc = p->uncertainty_gamma != 0.0f;
     const bool foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
@@ -1045,6 +1076,21 @@ int ml_mask_matching_backward_ex(const ml_dims* d, const ml_params* p, const flo
                          mask_targets, cls_logits, cls_targets, pred_to_gt, saved, num_masks_dev,
                          grad_mask_logits, grad_cls_logits, workspace, workspace_bytes, stream,
                          nullptr, forward_workspace);
+}
+
+int ml_mask_matching_backward_ex2(const ml_dims* d, const ml_params* p, const float* grad_mask_mean,
+                                  const float* grad_dice_mean, const float* grad_cls_mean,
+                                  const float* mask_logits, const int64_t* mask_targets,
+                                  const float* cls_logits, const int64_t* cls_targets,
+                                  const int64_t* pred_to_gt, const float* saved,
+                                  const float* num_masks_dev, float* grad_mask_logits,
+                                  float* grad_cls_logits, void* workspace, size_t workspace_bytes,
+                                  ml_stream_t stream, const void* forward_workspace,
+                                  int grad_rows_prezeroed) {
+    return backward_impl(d, p, grad_mask_mean, grad_dice_mean, grad_cls_mean, mask_logits,
+                         mask_targets, cls_logits, cls_targets, pred_to_gt, saved, num_masks_dev,
+                         grad_mask_logits, grad_cls_logits, workspace, workspace_bytes, stream,
+                         nullptr, forward_workspace, grad_rows_prezeroed);
 }
 
 // ---------------------------------------------------------------------------
@@ -1169,7 +1215,10 @@ int ml_mask_matching_sampled(const ml_dims* d, const ml_params* p, int64_t num_p
         la.cls_targets = cls_targets;
         la.void_status = dev_status;
     }
-    loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
+    {
+        ProfScope prof(5, st);
+        loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
+    }
     ML_CHECK_LAUNCH("loss_fwd_kernel");
     return ML_OK;
 }
@@ -1218,7 +1267,10 @@ int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int6
     la.stats_in = saved; la.grad_cls_logits = grad_cls_logits;
     if (LBQ == 0) return ML_OK;
     // coefficients + class-logit gradient first; the mask gradient reads coef
-    bwd_cls_kernel<<<(unsigned)((LBQ + 7) / 8), 256, 0, st>>>(la);
+    {
+        ProfScope prof(6, st);
+        bwd_cls_kernel<<<(unsigned)((LBQ + 7) / 8), 256, 0, st>>>(la);
+    }
     ML_CHECK_LAUNCH("bwd_cls_kernel");
     const bool foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;
     float* gacc = logits_dtype == 1 ? reinterpret_cast<float*>(ws + off_gacc)

@@ -128,6 +128,23 @@ ML_INLINE float rcp_approx(float x) {
     return y;
 }
 
+// Element pieces for the default path (no entropy weight, no focal terms):
+// e = exp(-|x|), d = 1 + e (log1p(e) = log(d) is summed through a product of
+// several d's and one log2), p = sigmoid(x).
+struct Fast {
+    float d, p;
+};
+
+ML_INLINE Fast fast_elem(float x) {
+    const float e = ex2_approx(-fabsf(x) * 1.4426950408889634f);
+    const float d = 1.0f + e;
+    const float r = rcp_approx(d);
+    Fast f;
+    f.d = d;
+    f.p = x >= 0.0f ? r : e * r;
+    return f;
+}
+
 struct Elem {
     float p;      // sigmoid(x)
     float sp;     // log1p(exp(-|x|))
@@ -217,6 +234,13 @@ ML_INLINE void fence_mbar_init() {
 
 ML_INLINE void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// Raise the phase's expected transaction bytes without arriving (the arrival
+// comes later, once the producer has also written its own shared data).
+ML_INLINE void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;"
                  ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 

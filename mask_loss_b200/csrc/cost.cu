@@ -244,25 +244,7 @@ cudaError_t launch_label_code(const int64_t* targets, int B, int H, int W, int W
     return cudaGetLastError();
 }
 
-// ---------------------------------------------------------------------------
-// Element pieces for the default path (no entropy weight, no focal terms):
-// e = exp(-|x|), d = 1 + e (log1p(e) = log(d) is summed through a product of
-// eight d's and one log2), p = sigmoid(x).
-// ---------------------------------------------------------------------------
-struct Fast {
-    float d, p;
-};
-
-
-ML_INLINE Fast fast_elem(float x) {
-    const float e = ex2_approx(-fabsf(x) * 1.4426950408889634f);
-    const float d = 1.0f + e;
-    const float r = rcp_approx(d);
-    Fast f;
-    f.d = d;
-    f.p = x >= 0.0f ? r : e * r;
-    return f;
-}
+// Element pieces for the default path: fast_elem (common.cuh).
 
 // red.add into the partial buffer (program order per address -> deterministic).
 ML_INLINE void red_add(float* p, float v) {

@@ -1,0 +1,410 @@
+// dense_mma.cu -- dense per-GT mask costs on the 5th-generation tensor cores.
+//
+// With dense (B, GT_total, H_t, W_t) masks (overlap allowed; no reference
+// counterpart, the reference API takes a label map) the contractions of the
+// pairwise costs (src/cuda/pw_mask.cu:52-308)
+//     D[q,g] = sum_j x_qj k_gj          (sigmoid-CE, before the sign)
+//     I[q,g] = sum_j sigmoid(x_qj) k_gj (dice intersection)
+// are real GEMMs: k_gj is the pixel count of GT g in cell j, and a cell may
+// be covered by several GTs.  This kernel runs them on tcgen05 UMMA with the
+// fp32 accumulators in tensor memory (TMEM):
+//   * per CTA: one image, one query tile (M = 128 rows, rows >= qrows unused)
+//     and half a cell chunk, all GT columns (N = gout rounded up to 16, <= 64);
+//   * K blocks of 32 cells.  A TMA box brings the block's logits into shared
+//     memory (the cost kernel's tensor map: fp32 rows with the 128-byte
+//     swizzle, bf16/fp16 rows with the 64-byte one, widened exactly);
+//   * eight producer warps (warp w: rows 32*(w%4).., cells 16*(w/4)..) compute
+//     sigmoid and the row sums on CUDA cores and write the A operands to TMEM
+//     as bf16 hi/lo pairs (x = xh + xl and p = ph + pl, each part rounded to
+//     nearest, so |x - xh - xl| <= 2^-18 |x|): four K-major 128 x 32 bf16
+//     operands, 16 TMEM columns each.  They also stage the block's counts as
+//     the bf16 B operand (N x 32, exact for counts <= 256) in shared memory in
+//     the no-swizzle K-major layout (8-row x 16-byte core matrices);
+//   * one thread of the control warp issues the TMA loads and the MMAs
+//     (kind::f16, A from TMEM, B from shared memory, 128 x N x 16 each):
+//     D += xh k + xl k, I += ph k + pl k, and signals completion with
+//     tcgen05.commit on an mbarrier;
+//   * a two-stage ring: while the tensor core works on block kb the producers
+//     fill stage (kb+1)%2;
+//   * epilogue: the producer warps read D and I from TMEM (tcgen05.ld) and
+//     write the label path's chunk-partial slot, so cost_rows / cost_pairs,
+//     the solver and the matched loss run unchanged.
+// TMEM: 2N accumulator columns + 2 stages x 4 operands x 16 columns <= 256,
+// so two CTAs share an SM.  Every wait is bounded (2 s) and reports through
+// the status word instead of hanging; TMEM is released on every path.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace mlb {
+
+namespace {
+
+constexpr int kMmaK = 32;          // cells per K block
+constexpr int kMmaStages = 2;
+constexpr int kMmaProducers = 8;   // warps
+constexpr int kMmaThreads = (kMmaProducers + 1) * 32;
+constexpr int kMmaTmemCols = 256;
+
+// --- tcgen05 / TMEM wrappers (PTX ISA 8.7, sm_100a) -------------------------
+ML_INLINE void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+ML_INLINE void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+ML_INLINE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+ML_INLINE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+ML_INLINE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+ML_INLINE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// eight 32-bit columns of this warp's 32 lanes
+ML_INLINE void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};"
+                 ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]),
+                   "r"(v[6]), "r"(v[7]) : "memory");
+}
+ML_INLINE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+ML_INLINE void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, "
+                 "%10, %11, %12, %13, %14, %15}, [%16];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                   "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+                   "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                 : "r"(taddr) : "memory");
+}
+ML_INLINE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] x B[smem]^T, kind::f16 (bf16 in, fp32 accumulate).
+ML_INLINE void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                       bool accumulate) {
+    const uint32_t acc = accumulate ? 1u : 0u;
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc) : "memory");
+}
+// Arrive once on `bar` when every MMA this thread issued before has completed.
+ML_INLINE void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major without swizzle: core matrices of
+// 8 rows x 16 bytes stored contiguously; `lbo` = byte distance between the
+// two 16-byte K halves of one K=16 step, `sbo` = between 8-row groups.
+// Fields: start address >> 4 [0,14), LBO >> 4 [16,30), SBO >> 4 [32,46),
+// descriptor version 1 [46,48), base offset 0, layout type 0 (no swizzle).
+ML_INLINE uint64_t smem_desc_noswizzle(const void* p, uint32_t lbo, uint32_t sbo) {
+    const uint64_t a = (uint64_t)((smem_u32(p) >> 4) & 0x3FFFu);
+    return a | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) |
+           (1ull << 46);
+}
+
+// Instruction descriptor of kind::f16: bf16 A and B (K-major), fp32 D,
+// M = 128, N = n (multiple of 16, <= 256).
+ML_INLINE uint32_t idesc_bf16_f32(int n) {
+    return (1u << 4)             // D format: f32
+           | (1u << 7)           // A format: bf16
+           | (1u << 10)          // B format: bf16
+           | ((uint32_t)(n >> 3) << 17)
+           | ((uint32_t)(128 >> 4) << 24);
+}
+
+ML_INLINE uint32_t pack_bf16(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&v);
+}
+ML_INLINE float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+ML_INLINE float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+struct MmaShared {
+    uint64_t full[kMmaStages];    // logits tile landed (TMA)
+    uint64_t aready[kMmaStages];  // A (TMEM) and B (smem) of the stage written
+    uint64_t mdone[kMmaStages];   // the stage's MMAs completed
+    uint64_t accf;                // all MMAs completed
+    uint32_t tmem_base;
+    int32_t err;
+    float rows[4][32][3];         // row sums of the second cell half (warps 4..7)
+};
+
+}  // namespace
+
+// Four logits [4*u, 4*u + 4) of cells 16*kh.. of row r from the swizzled TMA
+// tile: fp32 rows of 128 bytes (16-byte granule g at g ^ (r & 7)), 16-bit
+// rows of 64 bytes (granule g at g ^ ((r >> 1) & 3)), widened exactly.
+template <typename T>
+ML_INLINE float4 tile_quad(const T* row, int r, int kh, int u) {
+    if constexpr (sizeof(T) == 4) {
+        const int g = 4 * kh + u;
+        return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(row) + ((g ^ (r & 7)) << 2));
+    } else {
+        const int k = 16 * kh + 4 * u;           // first of the four cells
+        const int g = k >> 3;                     // 8 cells per granule
+        const uint2 w = *reinterpret_cast<const uint2*>(row + ((g ^ ((r >> 1) & 3)) << 3) + (k & 7));
+        float4 v;
+        widen2(w.x, v.x, v.y, row);
+        widen2(w.y, v.z, v.w, row);
+        return v;
+    }
+}
+
+// grid = (nchunk * 2, nqt, L*B); block = kMmaThreads.
+// Dynamic shared memory: per stage the logits tile [qrows_smem][32] of T
+// (1024-aligned), then per stage the B tile [4][N][8] bf16, then MmaShared.
+template <typename T>
+__global__ void __launch_bounds__(kMmaThreads, 2)
+dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a, const uint16_t* cnt, int N) {
+    extern __shared__ __align__(1024) unsigned char dsm_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+    const int QS = (a.qrows + 7) / 8 * 8;
+    T* xs = reinterpret_cast<T*>(base);                                // [stage][QS][32]
+    __nv_bfloat16* bs = reinterpret_cast<__nv_bfloat16*>(xs + kMmaStages * QS * kMmaK);  // [stage][4][N][8]
+    MmaShared* sh = reinterpret_cast<MmaShared*>(bs + kMmaStages * 4 * N * 8);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int slot = blockIdx.x, chunk = slot >> 1, half = slot & 1;
+    const int qt = blockIdx.y, lb = blockIdx.z, b = lb % a.B;
+    const int HW = a.H * a.W, G = a.gout;
+    const int half_cells = a.chunk_cells / 2;
+    const int cb = min(HW, chunk * a.chunk_cells + half * half_cells);
+    const int ce = min(HW, cb + half_cells);
+    const int nkb = (ce - cb + kMmaK - 1) / kMmaK;
+    const int row0 = lb * a.Q + qt * a.qrows;
+    const uint32_t cols_acc = 2u * N;
+
+    if (tid == 0) {
+        for (int i = 0; i < kMmaStages; ++i) {
+            mbar_init(&sh->full[i], 1);
+            mbar_init(&sh->aready[i], kMmaProducers);
+            mbar_init(&sh->mdone[i], 1);
+        }
+        mbar_init(&sh->accf, 1);
+        sh->err = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaProducers) {  // the control warp owns the TMEM allocation
+        tmem_alloc(&sh->tmem_base, kMmaTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = sh->tmem_base;
+    // TMEM columns: D [0, N), I [N, 2N), then stage s operand o at 2N + (4s + o) * 16
+    auto a_col = [&](int s, int o) { return tbase + cols_acc + (uint32_t)((4 * s + o) * 16); };
+
+    if (warp == kMmaProducers) {
+        // ------------------------------ control warp ------------------------------
+        if (lane == 0) {
+            bool ok = true;
+            const uint32_t idesc = idesc_bf16_f32(N);
+            auto issue_tma = [&](int kb) {
+                const int s = kb % kMmaStages;
+                mbar_arrive_expect_tx(&sh->full[s], (uint32_t)a.qrows * kMmaK * (uint32_t)sizeof(T));
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+                    " [%0], [%1, {%2, %3}], [%4];"
+                    ::"r"(smem_u32(xs + s * QS * kMmaK)), "l"(&tmap), "r"(cb + kb * kMmaK), "r"(row0),
+                      "r"(smem_u32(&sh->full[s])) : "memory");
+            };
+            for (int kb = 0; kb < min(nkb, kMmaStages); ++kb) issue_tma(kb);
+            for (int kb = 0; kb < nkb && ok; ++kb) {
+                const int s = kb % kMmaStages;
+                if (!mbar_wait(&sh->aready[s], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
+                tc_fence_after();
+                // the producers have read this stage's logits: refill it
+                if (kb + kMmaStages < nkb) issue_tma(kb + kMmaStages);
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {  // K = 16 cells per MMA
+                    const uint64_t bd = smem_desc_noswizzle(bs + ((s * 4 + 2 * kk) * N) * 8,
+                                                            (uint32_t)N * 16u, 128u);
+                    const bool acc = kb > 0 || kk > 0;
+                    umma_ts(tbase, a_col(s, 0) + 8 * kk, bd, idesc, acc);          // D += xh k
+                    umma_ts(tbase, a_col(s, 1) + 8 * kk, bd, idesc, true);         // D += xl k
+                    umma_ts(tbase + N, a_col(s, 2) + 8 * kk, bd, idesc, acc);      // I += ph k
+                    umma_ts(tbase + N, a_col(s, 3) + 8 * kk, bd, idesc, true);     // I += pl k
+                }
+                umma_commit(&sh->mdone[s]);
+            }
+            if (ok && nkb > 0) umma_commit(&sh->accf);
+            if (!ok) {
+                sh->err = 1;
+                if (a.status) atomicOr(a.status, 2);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------ producer warps ------------------------------
+        const int r = 32 * (warp & 3) + lane;      // query row of the tile (TMEM lane)
+        const int kh = warp >> 2;                  // cells [16 kh, 16 kh + 16) of each block
+        const bool rvalid = r < a.qrows && qt * a.qrows + r < a.Q;
+        const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+        float rsum[3] = {0.0f, 0.0f, 0.0f};        // sum max(x,0), sum p, sum log2(1+e)
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int s = kb % kMmaStages;
+            const int c0 = cb + kb * kMmaK;
+            const int nv = min(kMmaK, ce - c0);
+            // the stage's A and B are free once its previous MMAs completed
+            if (kb >= kMmaStages &&
+                !mbar_wait(&sh->mdone[s], (uint32_t)(((kb / kMmaStages) - 1) & 1))) { ok = false; break; }
+            // B: counts of this block (rows g < N, cells k < 32) as bf16, core-matrix layout
+            __nv_bfloat16* bt = bs + s * 4 * N * 8;
+            for (int i = tid; i < N * 4; i += kMmaProducers * 32) {
+                const int g = i >> 2, kc = i & 3;          // row g, 8 cells starting at 8 kc
+                uint32_t w[4] = {0u, 0u, 0u, 0u};
+                if (g < G) {
+                    const int ga = g + (g >= a.bg ? 1 : 0);
+                    const uint16_t* src = cnt + ((int64_t)b * a.gt_total + ga) * HW + c0 + 8 * kc;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int k0 = 8 * kc + 2 * u;
+                        const float lo = k0 < nv ? (float)src[2 * u] : 0.0f;
+                        const float hi = k0 + 1 < nv ? (float)src[2 * u + 1] : 0.0f;
+                        w[u] = pack_bf16(lo, hi);
+                    }
+                }
+                *reinterpret_cast<uint4*>(bt + (kc * N + g) * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            if (!mbar_wait(&sh->full[s], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
+            // A: this thread's 16 cells of row r
+            const T* xr = xs + (s * QS + r) * kMmaK;
+            uint32_t xh[8], xl[8], ph[8], pl[8];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {  // four 16-byte granules = 16 cells
+                const float4 v = rvalid ? tile_quad<T>(xr, r, kh, u) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float xv[4] = {v.x, v.y, v.z, v.w};
+                float pv[4];
+                float prod = 1.0f;
+#pragma unroll
+                for (int e4 = 0; e4 < 4; ++e4) {
+                    const int k = 16 * kh + 4 * u + e4;
+                    const float x = k < nv ? xv[e4] : 0.0f;
+                    const Fast f = fast_elem(x);
+                    pv[e4] = k < nv ? f.p : 0.0f;
+                    if (k < nv && rvalid) {
+                        rsum[0] += fmaxf(x, 0.0f);
+                        rsum[1] += f.p;
+                        prod *= f.d;
+                    }
+                }
+                rsum[2] += lg2_approx(prod);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const float x0 = (16 * kh + 4 * u + 2 * j < nv) ? xv[2 * j] : 0.0f;
+                    const float x1 = (16 * kh + 4 * u + 2 * j + 1 < nv) ? xv[2 * j + 1] : 0.0f;
+                    const uint32_t hx = pack_bf16(x0, x1);
+                    xh[2 * u + j] = hx;
+                    xl[2 * u + j] = pack_bf16(x0 - bf16_lo(hx), x1 - bf16_hi(hx));
+                    const uint32_t hp = pack_bf16(pv[2 * j], pv[2 * j + 1]);
+                    ph[2 * u + j] = hp;
+                    pl[2 * u + j] = pack_bf16(pv[2 * j] - bf16_lo(hp), pv[2 * j + 1] - bf16_hi(hp));
+                }
+            }
+            const uint32_t colk = (uint32_t)(8 * kh);  // 16 bf16 cells = 8 columns
+            tmem_st8(a_col(s, 0) + lane_off + colk, xh);
+            tmem_st8(a_col(s, 1) + lane_off + colk, xl);
+            tmem_st8(a_col(s, 2) + lane_off + colk, ph);
+            tmem_st8(a_col(s, 3) + lane_off + colk, pl);
+            tmem_wait_st();
+            fence_proxy_async_smem();  // the B tile is read by the tensor core
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh->aready[s]);
+        }
+        if (!ok) {
+            sh->err = 1;
+            if (lane == 0 && a.status) atomicOr(a.status, 2);
+        }
+        // ---- epilogue: row sums of the two cell halves, then D and I from TMEM ----
+        if (kh == 1) {
+#pragma unroll
+            for (int i = 0; i < 3; ++i) sh->rows[warp & 3][lane][i] = rsum[i];
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kMmaProducers * 32) : "memory");
+        const bool have_acc = ok && nkb > 0 && mbar_wait(&sh->accf, 0u);
+        tc_fence_after();
+        float* part = a.part + ((((int64_t)lb * a.nqt + qt) * a.nchunk + chunk) * 2 + half) *
+                                   (int64_t)a.part_stride;
+        const int QP = a.qrows_pad;
+        // warps 0-3 write D (as -D: the partial holds sum(-x k)) and the row
+        // sums, warps 4-7 write I
+        const uint32_t acc_base = tbase + lane_off + (kh ? (uint32_t)N : 0u);
+        for (int g0 = 0; g0 < N; g0 += 16) {
+            uint32_t v[16];
+            if (have_acc) {
+                tmem_ld16(acc_base + (uint32_t)g0, v);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = 0u;
+            }
+            if (rvalid) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int g = g0 + j;
+                    if (g < G) {
+                        const float val = __uint_as_float(v[j]);
+                        part[((int64_t)kh * G + g) * QP + r] = kh ? val : -val;
+                    }
+                }
+            }
+        }
+        if (kh == 0 && rvalid) {
+#pragma unroll
+            for (int i = 0; i < 3; ++i)
+                part[(int64_t)2 * G * QP + (int64_t)i * QP + r] = rsum[i] + sh->rows[warp & 3][lane][i];
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == kMmaProducers) {
+        tc_fence_after();
+        tmem_dealloc(tbase, kMmaTmemCols);
+    }
+}
+
+int dense_mma_n(int gout) { return (gout + 15) / 16 * 16; }
+
+bool dense_mma_usable(const CostArgs& a, int ldt, bool unc, bool foc, bool tma) {
+    (void)ldt;
+    const int N = dense_mma_n(a.gout);
+    return !unc && !foc && tma && a.gout > 0 && N <= 64 && a.qrows <= 128 &&
+           a.chunk_cells % (2 * kMmaK) == 0;
+}
+
+size_t dense_mma_smem(const CostArgs& a, int esize) {
+    const int N = dense_mma_n(a.gout);
+    const int QS = (a.qrows + 7) / 8 * 8;
+    return 1024 + (size_t)kMmaStages * QS * kMmaK * esize + (size_t)kMmaStages * 4 * N * 8 * 2 +
+           sizeof(MmaShared);
+}
+
+template <typename T>
+cudaError_t launch_dense_mma_t(const CUtensorMap& tm, const CostArgs& a, const uint16_t* cnt,
+                               cudaStream_t st) {
+    const int N = dense_mma_n(a.gout);
+    const size_t smem = dense_mma_smem(a, (int)sizeof(T));
+    cudaError_t e = cudaFuncSetAttribute(dense_mma_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 g(a.nchunk * 2, a.nqt, a.L * a.B);
+    dense_mma_kernel<T><<<g, kMmaThreads, smem, st>>>(tm, a, cnt, N);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dense_mma(const CUtensorMap& tm, const CostArgs& a, const uint16_t* cnt,
+                             cudaStream_t st, int ldt) {
+    if (ldt == 1) return launch_dense_mma_t<__nv_bfloat16>(tm, a, cnt, st);
+    if (ldt == 2) return launch_dense_mma_t<__half>(tm, a, cnt, st);
+    return launch_dense_mma_t<float>(tm, a, cnt, st);
+}
+
+}  // namespace mlb

@@ -132,6 +132,7 @@ struct LossArgs {
     const uint8_t* masks;    // dense (B,GT_total,Ht,Wt) targets instead of the label map, or null
     const int32_t* codes;    // (B, H*W) per-cell column codes (s > 1 label map), or null
     const uint4* mixtab;     // (B, H*W) mixed-cell table beside `codes`, or null
+    int rows_zeroed;         // backward: rows without a gradient already hold zeros
 };
 
 __global__ void loss_fwd_kernel(LossArgs a);
@@ -202,4 +203,10 @@ cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht
 // ldt: mask-logit type (0 fp32, 1 bf16, 2 fp16)
 cudaError_t launch_dense_cost(const CostArgs& a, bool unc, bool foc, const uint16_t* cnt,
                               cudaStream_t st, int ldt);
+// The same partials on tcgen05 tensor cores (dense_mma.cu): no entropy
+// weights or focal terms, GT_out <= 64, TMA-aligned logits (ldt: 0 fp32,
+// 1 bf16, 2 fp16).
+bool dense_mma_usable(const CostArgs& a, int ldt, bool unc, bool foc, bool tma);
+cudaError_t launch_dense_mma(const CUtensorMap& tm, const CostArgs& a, const uint16_t* cnt,
+                             cudaStream_t st, int ldt);
 }  // namespace mlb

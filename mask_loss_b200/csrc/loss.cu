@@ -218,6 +218,7 @@ __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
     const bool matched = og >= 0 && ga < a.gt_total;
     const bool active = (matched || a.force_masks) && !(mcoef == 0.0f && dcoef == 0.0f);
     if (!active) {
+        if (a.rows_zeroed) return;  // the caller zeroed the gradient beforehand
         if (VEC) {
             const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int k = threadIdx.x * 4; k < nc; k += blockDim.x * 4) st4cs(gout + k, z);

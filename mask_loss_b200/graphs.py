@@ -62,6 +62,7 @@ class MatchingLossStep:
         self._wts = None
         self._side = None
         self._ev = None
+        self._zs = None
         self.graph = None
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -133,18 +134,41 @@ class MatchingLossStep:
             if ml.dtype not in (torch.float32, torch.bfloat16, torch.float16):
                 raise RuntimeError("mask_logits must be float32, bfloat16 or float16")
             args, nm_dev = resolve_args(ml, mt, cl, ct, *a)
+            # label maps: the mask gradient is zero-filled on a side stream
+            # while the solver runs (it needs nothing but the costs' end), and
+            # the backward writes only the rows that carry a gradient
+            prezero = not dense
+            gm_buf = None
+            if prezero:
+                if self._zs is None:
+                    self._zs = torch.cuda.Stream(device=ml.device)
+                    self._costs_ev = torch.cuda.Event()
+                    self._zero_ev = torch.cuda.Event()
+                    # torch creates an event's handle on its first record; the
+                    # library records costs_ev itself, so create both now
+                    self._costs_ev.record(main)
+                    self._zero_ev.record(main)
+                gm_buf = torch.empty_like(ml)
             out = ops.mask_matching_ex(
                 ml, mt, cl, ct, *args, num_masks_dev=nm_dev, want_saved=True,
-                check_void_targets=True, loss_wait_event=ev, want_workspace=not dense)
+                check_void_targets=True, loss_wait_event=ev, want_workspace=not dense,
+                costs_done_event=self._costs_ev if prezero else None)
             p2g, prd, means, saved = out[:4]
             fws = None if dense else out[5]
+            if prezero:
+                self._zs.wait_event(self._costs_ev)
+                with torch.cuda.stream(self._zs):
+                    gm_buf.zero_()
+                    self._zero_ev.record(self._zs)
+                gm_buf.record_stream(self._zs)
+                main.wait_event(self._zero_ev)
             if ev is not None:
                 main.wait_stream(self._side)  # join the side branch
             gm, gc = ops.mask_matching_backward(
                 wm, wd, wc, ml, mt, cl, ct, p2g, args[0], args[1], args[2], args[3], args[4],
                 args[5], args[6], args[8], args[9], args[10], args[13], args[14], args[15],
                 args[16], args[17], args[18], args[19], saved=saved, num_masks_dev=nm_dev,
-                forward_workspace=fws)
+                forward_workspace=fws, grad_mask_out=gm_buf, grad_rows_prezeroed=prezero)
         return p2g, prd, means, gm, gc
 
     def replay(self) -> None:

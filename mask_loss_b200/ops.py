@@ -54,6 +54,8 @@ def check_status(block: bool = False) -> None:
     """Raise if an earlier on-device assignment solve reported failure."""
     if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
         return  # no event queries inside stream capture
+    for st in list(_sticky.values()):
+        st.check(block)
     keep = []
     err = None
     for ev, host, msg in _pending:
@@ -114,6 +116,90 @@ def _status_message(v: int) -> str:
 
 def _track_status(status: torch.Tensor) -> None:
     _defer(status, _status_message)
+
+
+# ---------------------------------------------------------------------------
+# Per-stream state of the two hot ops (outside CUDA-graph capture): a sticky
+# device status word that the kernels OR their error bits into, read back
+# every _STATUS_EVERY calls (and by check_status); and the scratch workspace,
+# reused by every call on the same stream (stream order keeps calls apart).
+# ---------------------------------------------------------------------------
+_STATUS_EVERY = 8
+
+
+class _StickyStatus:
+    def __init__(self, device):
+        self.dev = torch.zeros(1, dtype=torch.int32, device=device)
+        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.ev = torch.cuda.Event()
+        self.stream = torch.cuda.current_stream(device)
+        self.inflight = False
+        self.calls = 0
+
+    def after_call(self):
+        self.calls += 1
+        if self.inflight and self.ev.query():
+            self._consume()
+        if not self.inflight and (_SYNC or self.calls % _STATUS_EVERY == 0):
+            self._issue()
+        if _SYNC:
+            self.check(block=True)
+
+    def _issue(self):
+        self.host.copy_(self.dev, non_blocking=True)
+        self.ev.record(self.stream)
+        self.inflight = True
+
+    def _consume(self):
+        self.inflight = False
+        v = int(self.host[0])
+        if v != 0:
+            with torch.cuda.stream(self.stream):
+                self.dev.zero_()
+            self.host.zero_()
+            raise RuntimeError(_status_message(v))
+
+    def check(self, block: bool):
+        if block and not self.inflight:
+            self._issue()
+        if self.inflight:
+            if block:
+                self.ev.synchronize()
+            if self.ev.query():
+                self._consume()
+
+
+_sticky: dict = {}
+_ws_cache: dict = {}
+_fwd_plans: dict = {}  # argument key -> (ml_dims, ml_params, GT_out, workspace bytes)
+_bwd_plans: dict = {}
+
+
+def _stream_key(device):
+    return (device.index, torch.cuda.current_stream(device).cuda_stream)
+
+
+def _sticky_status(device) -> Optional[_StickyStatus]:
+    """The stream's sticky status word, or None inside stream capture."""
+    if torch.cuda.is_current_stream_capturing():
+        return None
+    k = _stream_key(device)
+    st = _sticky.get(k)
+    if st is None:
+        st = _sticky[k] = _StickyStatus(device)
+    return st
+
+
+def _cached_workspace(nbytes: int, device, tag: str) -> torch.Tensor:
+    """A workspace of at least nbytes reused by every call on this stream;
+    a fresh one inside stream capture."""
+    if torch.cuda.is_current_stream_capturing():
+        return _workspace(nbytes, device)
+    k = _stream_key(device) + (tag,)
+    ws = _ws_cache.get(k)
+    if ws is None or ws.numel() < nbytes:
+        ws = _ws_cache[k] = _workspace(nbytes, device)
+    return ws
 
 
 def _params(smooth=1.0, sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0, background_index=-1,
@@ -238,6 +324,7 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
                      *, num_masks_dev: Optional[torch.Tensor] = None, want_saved: bool = False,
                      want_costs: bool = False, check_void_targets: bool = False,
                      loss_wait_event: Optional[torch.cuda.Event] = None,
+                     costs_done_event: Optional[torch.cuda.Event] = None,
                      want_workspace: bool = False):
     """``mask_matching`` plus the extras this implementation offers: a device
     ``num_masks_dev`` (fp32 scalar, e.g. after an all-reduce), the per-query
@@ -248,6 +335,8 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
     device.  ``loss_wait_event``: the matched-loss kernel (the only reader
     of ``num_masks_dev``) waits for it, so an all-reduce producing that count
     on another stream overlaps the cost and solver kernels.
+    ``costs_done_event``: recorded once the costs are final, before the solver
+    (work on another stream may wait for it and run beside the solver).
 
     ``want_workspace``: also return the forward workspace, which
     mask_matching_backward(forward_workspace=) reuses (label-map targets).
@@ -262,39 +351,66 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
         raise RuntimeError("Invalid matching strategy id")
     lib = _lib_handle()
     dev = mask_logits.device
-    d = _dims(mask_logits, mask_targets, cls_logits, cls_targets)
-    p = _params(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, uncertainty_gamma,
-                uncertainty_gamma_min, inf_thresh, num_masks, force_unmatched_class_to_background,
-                force_unmatched_masks_to_empty, topk_matches, strategy_id, mask_gamma, mask_alpha,
-                cls_gamma, cls_alpha, void_class_index, use_softmax_label_loss,
-                normalize_uncertainty, check_void_targets)
-    _with_dtype(p, mask_logits)
+    dense = is_dense(mask_targets)
+    key = (mask_logits.shape, mask_logits.dtype, mask_targets.shape, cls_logits.shape,
+           cls_targets.shape, smooth, sigmoid_scale, dice_scale, cls_scale, background_index,
+           uncertainty_gamma, uncertainty_gamma_min, inf_thresh, num_masks,
+           force_unmatched_class_to_background, force_unmatched_masks_to_empty, topk_matches,
+           strategy_id, mask_gamma, mask_alpha, cls_gamma, cls_alpha, void_class_index,
+           use_softmax_label_loss, normalize_uncertainty, check_void_targets)
+    plan = _fwd_plans.get(key)
+    if plan is None:
+        d = _dims(mask_logits, mask_targets, cls_logits, cls_targets)
+        p = _params(smooth, sigmoid_scale, dice_scale, cls_scale, background_index,
+                    uncertainty_gamma, uncertainty_gamma_min, inf_thresh, num_masks,
+                    force_unmatched_class_to_background, force_unmatched_masks_to_empty,
+                    topk_matches, strategy_id, mask_gamma, mask_alpha, cls_gamma, cls_alpha,
+                    void_class_index, use_softmax_label_loss, normalize_uncertainty,
+                    check_void_targets)
+        _with_dtype(p, mask_logits)
+        size_fn = lib.ml_dense_workspace_size if dense else lib.ml_mask_matching_workspace_size
+        nb = size_fn(ctypes.byref(d), ctypes.byref(p))
+        if nb == 0:
+            raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
+        plan = (d, p, lib.ml_gt_out(d.GT_total, p.background_index), nb)
+        if len(_fwd_plans) > 256:
+            _fwd_plans.clear()
+        _fwd_plans[key] = plan
+    d, p, G, nbytes = plan
     L, B, Q = mask_logits.shape[:3]
-    G = lib.ml_gt_out(d.GT_total, p.background_index)
-    p2g = torch.empty((L, B, Q), dtype=torch.int64, device=dev)
-    prd = torch.empty((L, B, Q), dtype=torch.int64, device=dev)
-    means = torch.empty((3, L), dtype=torch.float32, device=dev)
-    saved = torch.empty((L, B, Q, 4), dtype=torch.float32, device=dev) if want_saved else None
+    LBQ = L * B * Q
+    idx = torch.empty((2, L, B, Q), dtype=torch.int64, device=dev)
+    p2g, prd = idx[0], idx[1]
+    fl = torch.empty(3 * L + (4 * LBQ if want_saved else 0), dtype=torch.float32, device=dev)
+    means = fl[:3 * L].view(3, L)
+    saved = fl[3 * L:].view(L, B, Q, 4) if want_saved else None
     costs = (torch.empty((3, L, B, Q, G), dtype=torch.float32, device=dev)
              if want_costs and G > 0 else None)
-    status = torch.zeros(1, dtype=torch.int32, device=dev)
-    dense = is_dense(mask_targets)
-    size_fn = lib.ml_dense_workspace_size if dense else lib.ml_mask_matching_workspace_size
-    nbytes = size_fn(ctypes.byref(d), ctypes.byref(p))
-    if nbytes == 0:
-        raise RuntimeError(lib.ml_last_error().decode() or "invalid shapes")
-    ws = _workspace(nbytes, dev)
+    sticky = _sticky_status(dev)
+    status = sticky.dev if sticky is not None else torch.zeros(1, dtype=torch.int32, device=dev)
+    # the forward workspace is handed out when asked for (its codes feed the
+    # backward), otherwise the stream's cached one is used
+    ws = _workspace(nbytes, dev) if want_workspace else _cached_workspace(nbytes, dev, "fwd")
     if num_masks_dev is not None:
         _check_input(num_masks_dev, "num_masks_dev")
         _check_dtype(num_masks_dev, torch.float32, "num_masks_dev")
     if dense:
-        if loss_wait_event is not None:
-            raise RuntimeError("loss_wait_event is not supported with dense mask targets")
+        if loss_wait_event is not None or costs_done_event is not None:
+            raise RuntimeError("stream events are not supported with dense mask targets")
         _lib.check(lib.ml_mask_matching_dense(
             ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets),
             _ptr(cls_logits), _ptr(cls_targets), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd),
             _ptr(means), _ptr(costs), _ptr(saved), _ptr(status), _ptr(ws), ws.numel(),
             _stream(dev)))
+    elif costs_done_event is not None:
+        if not costs_done_event.cuda_event:
+            raise RuntimeError("costs_done_event has no CUDA event yet: record it once first")
+        _lib.check(lib.ml_mask_matching_ex2(
+            ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets),
+            _ptr(cls_logits), _ptr(cls_targets), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd),
+            _ptr(means), _ptr(costs), _ptr(saved), _ptr(status), _ptr(ws), ws.numel(),
+            _stream(dev), ctypes.c_void_p(loss_wait_event.cuda_event if loss_wait_event else 0),
+            ctypes.c_void_p(costs_done_event.cuda_event)))
     elif loss_wait_event is not None:
         _lib.check(lib.ml_mask_matching_ex(
             ctypes.byref(d), ctypes.byref(p), _ptr(mask_logits), _ptr(mask_targets),
@@ -307,7 +423,10 @@ def mask_matching_ex(mask_logits, mask_targets, cls_logits, cls_targets, smooth,
             _ptr(cls_logits), _ptr(cls_targets), _ptr(num_masks_dev), _ptr(p2g), _ptr(prd),
             _ptr(means), _ptr(costs), _ptr(saved), _ptr(status), _ptr(ws), ws.numel(),
             _stream(dev)))
-    _track_status(status)
+    if sticky is not None:
+        sticky.after_call()
+    else:
+        _track_status(status)
     if want_workspace:
         return p2g, prd, means, saved, costs, ws
     return p2g, prd, means, saved, costs
@@ -343,11 +462,16 @@ def mask_matching_backward(grad_layer_mask_mean, grad_layer_dice_mean, grad_laye
                            use_softmax_label_loss=False, normalize_uncertainty=True, *,
                            saved: Optional[torch.Tensor] = None,
                            num_masks_dev: Optional[torch.Tensor] = None,
-                           forward_workspace: Optional[torch.Tensor] = None) -> List[torch.Tensor]:
+                           forward_workspace: Optional[torch.Tensor] = None,
+                           grad_mask_out: Optional[torch.Tensor] = None,
+                           grad_rows_prezeroed: bool = False) -> List[torch.Tensor]:
     """[grad_mask_logits, grad_cls_logits] (src/cuda/mask_matching_backward.cu:378-621).
 
     ``forward_workspace``: the workspace returned by mask_matching_ex(want_workspace=True)
-    for the same inputs and arguments; its per-cell label codes are reused."""
+    for the same inputs and arguments; its per-cell label codes are reused.
+    ``grad_mask_out``: the buffer to write the mask gradient into (like
+    mask_logits); with ``grad_rows_prezeroed`` the caller has filled it with
+    zeros and only the rows that carry a gradient are written."""
     check_status()
     for t, n in ((grad_layer_mask_mean, "grad_layer_mask_mean"),
                  (grad_layer_dice_mean, "grad_layer_dice_mean"),
@@ -360,16 +484,38 @@ def mask_matching_backward(grad_layer_mask_mean, grad_layer_dice_mean, grad_laye
     _check_dtype(pred_to_gt, torch.int64, "pred_to_gt")
     lib = _lib_handle()
     dev = mask_logits.device
-    d = _dims(mask_logits, mask_targets, cls_logits, cls_targets)
-    p = _params(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, uncertainty_gamma,
-                uncertainty_gamma_min, 1e30, num_masks, force_unmatched_class_to_background,
-                force_unmatched_masks_to_empty, 1, 0, mask_gamma, mask_alpha, cls_gamma, cls_alpha,
-                void_class_index, use_softmax_label_loss, normalize_uncertainty)
-    _with_dtype(p, mask_logits)
-    gm = torch.empty_like(mask_logits)
+    key = (mask_logits.shape, mask_logits.dtype, mask_targets.shape, cls_logits.shape,
+           cls_targets.shape, smooth, sigmoid_scale, dice_scale, cls_scale, background_index,
+           uncertainty_gamma, uncertainty_gamma_min, num_masks,
+           force_unmatched_class_to_background, force_unmatched_masks_to_empty, mask_gamma,
+           mask_alpha, cls_gamma, cls_alpha, void_class_index, use_softmax_label_loss,
+           normalize_uncertainty)
+    plan = _bwd_plans.get(key)
+    if plan is None:
+        d = _dims(mask_logits, mask_targets, cls_logits, cls_targets)
+        p = _params(smooth, sigmoid_scale, dice_scale, cls_scale, background_index,
+                    uncertainty_gamma, uncertainty_gamma_min, 1e30, num_masks,
+                    force_unmatched_class_to_background, force_unmatched_masks_to_empty, 1, 0,
+                    mask_gamma, mask_alpha, cls_gamma, cls_alpha, void_class_index,
+                    use_softmax_label_loss, normalize_uncertainty)
+        _with_dtype(p, mask_logits)
+        plan = (d, p, lib.ml_mask_matching_backward_workspace_size(ctypes.byref(d),
+                                                                   ctypes.byref(p)))
+        if len(_bwd_plans) > 256:
+            _bwd_plans.clear()
+        _bwd_plans[key] = plan
+    d, p, nbytes = plan
+    if grad_mask_out is not None:
+        _check_input(grad_mask_out, "grad_mask_out")
+        if grad_mask_out.shape != mask_logits.shape or grad_mask_out.dtype != mask_logits.dtype:
+            raise RuntimeError("grad_mask_out must match mask_logits in shape and dtype")
+        gm = grad_mask_out
+    else:
+        if grad_rows_prezeroed:
+            raise RuntimeError("grad_rows_prezeroed needs grad_mask_out")
+        gm = torch.empty_like(mask_logits)
     gc = torch.empty_like(cls_logits)
-    nbytes = lib.ml_mask_matching_backward_workspace_size(ctypes.byref(d), ctypes.byref(p))
-    ws = _workspace(nbytes, dev)
+    ws = _cached_workspace(nbytes, dev, "bwd")
     if saved is not None:
         _check_input(saved, "saved")
     if is_dense(mask_targets) and saved is None:
@@ -380,7 +526,13 @@ def mask_matching_backward(grad_layer_mask_mean, grad_layer_dice_mean, grad_laye
             _ptr(saved), _ptr(num_masks_dev), _ptr(gm), _ptr(gc), _ptr(ws), ws.numel(),
             _stream(dev))
     if is_dense(mask_targets):
+        if grad_rows_prezeroed:
+            raise RuntimeError("grad_rows_prezeroed is not supported with dense mask targets")
         _lib.check(lib.ml_mask_matching_dense_backward(*args))
+    elif grad_rows_prezeroed:
+        if forward_workspace is not None:
+            _check_input(forward_workspace, "forward_workspace")
+        _lib.check(lib.ml_mask_matching_backward_ex2(*args, _ptr(forward_workspace), 1))
     elif forward_workspace is not None:
         _check_input(forward_workspace, "forward_workspace")
         _lib.check(lib.ml_mask_matching_backward_ex(*args, _ptr(forward_workspace)))

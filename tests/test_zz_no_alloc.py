@@ -76,6 +76,46 @@ def test_noalloc_matches_workspace_entry_on_two_calls():
         _close(got, ref)
 
 
+def test_noalloc_odd_plane_and_no_device_allocation():
+    # 33 x 35 cells: H*W is not a multiple of 4, so the cost kernel's producer
+    # takes the plain-load path through the shared array; and repeated calls
+    # must not take device memory (the driver's free-memory figure stays put;
+    # torch's caching allocator is not involved either way)
+    torch.manual_seed(7)
+    L, B, Q, H, W, C, G = 1, 2, 30, 33, 35, 9, 6
+    cfg = synthetic.Config("odd", 9, L, B, Q, H, W, 1, C, 3.0, "ellipse", ("fixed", G - 1),
+                           (0.02, 0.3))
+    mt = torch.from_numpy(np.stack([synthetic.make_image_labels(cfg, b)[0]
+                                    for b in range(B)])).to(DEV)
+    ml = (torch.randn(L, B, Q, H, W) * 3).to(DEV)
+    cl = torch.randn(L, B, Q, C).to(DEV)
+    ct = torch.randint(0, C - 1, (B, G)).to(DEV)
+    ct[:, 0] = -1
+    kw = dict(smooth=1.0, sigmoid_scale=5.0, dice_scale=5.0, cls_scale=2.0, background_index=0,
+              uncertainty_gamma=1.0, uncertainty_gamma_min=0.05, mask_gamma=0.0, mask_alpha=-1.0,
+              cls_gamma=0.0, cls_alpha=-1.0, use_softmax_label_loss=True,
+              normalize_uncertainty=True)
+    ref = _with_workspace(ml, mt, cl, ct, kw)
+    rc, got = _noalloc(ml, mt, cl, ct, kw)  # first call: any lazy loading happens here
+    assert rc == 0, _lib.load().ml_last_error()
+    torch.cuda.synchronize()
+    _close(got, ref)
+    out = torch.empty_like(got)
+    lib = _lib.load()
+    d = ops._dims(ml, mt, cl, ct)
+    p = ops._params(**kw)
+    free0 = torch.cuda.mem_get_info(DEV)[0]
+    for _ in range(5):
+        rc = lib.ml_pairwise_mask_loss_forward_noalloc(
+            ctypes.byref(d), ctypes.byref(p), ops._ptr(ml), ops._ptr(mt), ops._ptr(cl),
+            ops._ptr(ct), ops._ptr(out), ops._stream(ml.device))
+        assert rc == 0
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info(DEV)[0]
+    assert free1 >= free0, f"device memory dropped by {free0 - free1} bytes"
+    _close(out, ref)
+
+
 def test_noalloc_rejects_calls_beyond_its_scratch():
     lib = _lib.load()
     limit = lib.ml_noalloc_scratch_limit()
