@@ -78,11 +78,12 @@ struct ProfScope {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// MASK_LOSS_B200_DENSE_MMA=1 runs dense-mask costs on the tensor-core kernel
-// (dense_mma.cu); otherwise the CUDA-core kernel (dense.cu) runs them.
+// Dense-mask costs run on the tensor-core kernel (dense_mma.cu) where it
+// applies; MASK_LOSS_B200_DENSE_MMA=0 keeps them on the CUDA-core kernel
+// (dense.cu), which also covers entropy weights, focal terms and GT_out > 64.
 const bool g_dense_mma_off = [] {
     const char* v = getenv("MASK_LOSS_B200_DENSE_MMA");
-    return !(v && v[0] == '1');
+    return v && v[0] == '0';
 }();
 
 // Raise a kernel's dynamic shared-memory limit once per (kernel, device);

@@ -38,10 +38,13 @@ def _multi_rank() -> bool:
 class MatchingLossStep:
     """With ``point_coords`` (B,P,2) the step runs the point-sampled op
     (MaskMatchingSampledFunction) and ``args`` are its 17 scalar arguments;
-    otherwise MaskMatchingFunction's 20."""
+    otherwise MaskMatchingFunction's 20.  ``zero_fill_beside_solver``: with
+    label-map targets, zero the mask gradient on a side stream while the
+    solver runs and let the backward write only the rows with a gradient."""
 
     def __init__(self, mask_logits, mask_targets, cls_logits, cls_targets, *args,
-                 point_coords=None, warmup: int = 2, loss_weights=(1.0, 1.0, 1.0)):
+                 point_coords=None, warmup: int = 2, loss_weights=(1.0, 1.0, 1.0),
+                 zero_fill_beside_solver: bool = True):
         self.sampled = point_coords is not None
         nargs = 17 if self.sampled else 20
         if len(args) != nargs:
@@ -63,6 +66,7 @@ class MatchingLossStep:
         self._side = None
         self._ev = None
         self._zs = None
+        self.prezero = bool(zero_fill_beside_solver)
         self.graph = None
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -137,7 +141,7 @@ class MatchingLossStep:
             # label maps: the mask gradient is zero-filled on a side stream
             # while the solver runs (it needs nothing but the costs' end), and
             # the backward writes only the rows that carry a gradient
-            prezero = not dense
+            prezero = self.prezero and not dense
             gm_buf = None
             if prezero:
                 if self._zs is None:

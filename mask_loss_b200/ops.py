@@ -31,11 +31,22 @@ def _lib_handle():
 
 
 def _ptr(t: Optional[torch.Tensor]):
-    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+    # a plain int (or None for NULL): ctypes converts it for the c_void_p
+    # arguments the bindings declare
+    return t.data_ptr() if t is not None else None
 
 
-def _stream(device) -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream_handle(device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _stream(device) -> int:
+    return _stream_handle(device)
 
 
 def _check_input(t: torch.Tensor, name: str) -> None:
@@ -176,7 +187,7 @@ _bwd_plans: dict = {}
 
 
 def _stream_key(device):
-    return (device.index, torch.cuda.current_stream(device).cuda_stream)
+    return (device.index, _stream_handle(device))
 
 
 def _sticky_status(device) -> Optional[_StickyStatus]:
