@@ -460,6 +460,25 @@ size_t dense_count_bytes(const FwdPlan& P) {
     return align256(sizeof(uint16_t) * (size_t)P.B * P.H * P.W * std::max(P.gt_total, 1));
 }
 
+// 2-D tensor map over the dense counts (bf16 bit patterns, rows = B*GT_total
+// GT planes, columns = H*W cells): boxes of 32 cells x the MMA's N rows, the
+// 64-byte swizzle the tensor-core kernel's B descriptor expects.
+bool counts_tensor_map(const FwdPlan& P, const uint16_t* cnt, CUtensorMap* km) {
+    memset(km, 0, sizeof(*km));
+    const int HW = P.H * P.W;
+    if (HW % 8 != 0 || (reinterpret_cast<uintptr_t>(cnt) % 16) != 0) return false;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)HW, (cuuint64_t)P.B * P.gt_total};
+    const cuuint64_t strides[1] = {(cuuint64_t)HW * 2};
+    const cuuint32_t box[2] = {32u, (cuuint32_t)dense_mma_n(P.gt_total)};
+    const cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(km, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(cnt), dims,
+                     strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigned char* ws,
                     cudaStream_t st) {
     cudaError_t e = cudaMemsetAsync(const_cast<int32_t*>(a.totals), 0,
@@ -476,10 +495,12 @@ int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigne
     if (LBQ == 0 || P.gout == 0) return ML_OK;
     {
         ProfScope prof(0, st);  // profiled as the cost stage
-        CUtensorMap tm;
-        const bool tma = logits_tensor_map(P, a.logits, &tm);
-        if (dense_mma_usable(a, P.ldt, P.unc, P.foc, tma) && !g_dense_mma_off)
-            e = launch_dense_mma(tm, a, cnt, st, P.ldt);  // tensor cores (tcgen05)
+        CUtensorMap tm, km;
+        bool mma = !g_dense_mma_off && logits_tensor_map(P, a.logits, &tm) &&
+                   dense_mma_usable(a, P.ldt, P.unc, P.foc, true) &&
+                   counts_tensor_map(P, cnt, &km);
+        if (mma)
+            e = launch_dense_mma(tm, km, a, st, P.ldt);  // tensor cores (tcgen05)
         else
             e = launch_dense_cost(a, P.unc, P.foc, cnt, st, P.ldt);
     }

@@ -128,6 +128,12 @@ ML_INLINE float rcp_approx(float x) {
     return y;
 }
 
+// Dense-mask pixel counts are kept as bf16 bit patterns (exact up to 256,
+// i.e. s <= 16): the CUDA-core kernel widens them, the tensor-core kernel
+// feeds them to the MMA as they are.
+ML_INLINE uint16_t count_bits(float n) { return __bfloat16_as_ushort(__float2bfloat16_rn(n)); }
+ML_INLINE float count_value(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+
 // Element pieces for the default path (no entropy weight, no focal terms):
 // e = exp(-|x|), d = 1 + e (log1p(e) = log(d) is summed through a product of
 // several d's and one log2), p = sigmoid(x).

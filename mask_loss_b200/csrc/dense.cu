@@ -10,7 +10,8 @@
 // Two kernels feed the label path's finalize (cost_rows / cost_pairs), the
 // solver and the matched loss unchanged:
 //   dense_count_kernel  per (image, cell) the pixel count of every GT
-//                       (uint16, [b][GT_total][cell]) and per (image, GT) the
+//                       (bf16 bit patterns, exact for counts <= 256,
+//                       [b][GT_total][cell]) and per (image, GT) the
 //                       mask area (the histogram the label path builds);
 //   dense_cost_kernel   per (layer*image, query tile, cell chunk, GT chunk of up to 64)
 //                       the chunk partials in the label path's layout: row
@@ -68,8 +69,55 @@ dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int 
         for (int u = 0; u < 8; ++u) {
             const int g = g0 + u;
             if (g >= gt_total) break;
-            if (valid) cnt[((int64_t)b * gt_total + g) * HW + cell] = (uint16_t)n[u];
+            if (valid) cnt[((int64_t)b * gt_total + g) * HW + cell] = count_bits((float)n[u]);
             const int sum = (int)__reduce_add_sync(0xffffffffu, (unsigned)n[u]);
+            if ((threadIdx.x & 31) == 0 && sum) atomicAdd(&area[g], sum);
+        }
+    }
+    __syncthreads();
+    for (int g = threadIdx.x; g < gt_total; g += blockDim.x)
+        if (area[g]) atomicAdd(&totals[(int64_t)b * gt_total + g], area[g]);
+}
+
+// s = 1 (one mask pixel per cell), H*W a multiple of 8: eight cells per
+// thread, one 8-byte mask load and one 16-byte count store per GT plane,
+// four planes in flight.  grid = (ceil(H*W / 2048), B), block 256.
+__global__ void __launch_bounds__(256)
+dense_count_s1_kernel(const uint8_t* __restrict__ masks, int HW, int gt_total,
+                      uint16_t* __restrict__ cnt, int32_t* __restrict__ totals) {
+    extern __shared__ int32_t area[];  // [gt_total]
+    const int b = blockIdx.y;
+    for (int g = threadIdx.x; g < gt_total; g += blockDim.x) area[g] = 0;
+    __syncthreads();
+    const int cell0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    const bool valid = cell0 < HW;
+    const uint32_t one = count_bits(1.0f);
+    for (int g0 = 0; g0 < gt_total; g0 += 4) {
+        uint2 m[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int g = g0 + u;
+            m[u] = (valid && g < gt_total)
+                       ? *reinterpret_cast<const uint2*>(masks + ((int64_t)b * gt_total + g) * HW + cell0)
+                       : make_uint2(0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int g = g0 + u;
+            if (g >= gt_total) break;
+            // 0xFF in every byte that is non-zero, then one bit per cell
+            const uint32_t nz0 = __vcmpne4(m[u].x, 0u), nz1 = __vcmpne4(m[u].y, 0u);
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                w[k] = ((nz0 >> (16 * k)) & 1u ? one : 0u) | ((nz0 >> (16 * k + 8)) & 1u ? one << 16 : 0u);
+                w[2 + k] = ((nz1 >> (16 * k)) & 1u ? one : 0u) | ((nz1 >> (16 * k + 8)) & 1u ? one << 16 : 0u);
+            }
+            if (valid)
+                *reinterpret_cast<uint4*>(cnt + ((int64_t)b * gt_total + g) * HW + cell0) =
+                    make_uint4(w[0], w[1], w[2], w[3]);
+            const int n = (__popc(nz0) + __popc(nz1)) >> 3;
+            const int sum = (int)__reduce_add_sync(0xffffffffu, (unsigned)n);
             if ((threadIdx.x & 31) == 0 && sum) atomicAdd(&area[g], sum);
         }
     }
@@ -197,7 +245,7 @@ __device__ __forceinline__ void dense_cost_body(const CostArgs& a, const uint16_
         for (int i = t; i < gn * kDenseTile; i += blockDim.x) {
             const int j = i / kDenseTile, k = i - j * kDenseTile;
             const int g = g0 + j;
-            ct[i] = k < nv ? (float)cnt[((int64_t)b * a.gt_total + g + (g >= a.bg ? 1 : 0)) * HW + c0 + k]
+            ct[i] = k < nv ? count_value(cnt[((int64_t)b * a.gt_total + g + (g >= a.bg ? 1 : 0)) * HW + c0 + k])
                            : 0.0f;
         }
         __syncthreads();
@@ -319,6 +367,13 @@ size_t dense_cost_smem(int qrows_pad, bool unc, int gc) {
 cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht, int Wt, int s,
                                int gt_total, uint16_t* cnt, int32_t* totals, cudaStream_t st) {
     const int HW = H * W;
+    if (s == 1 && HW % 8 == 0 && (reinterpret_cast<uintptr_t>(masks) & 7) == 0 &&
+        (reinterpret_cast<uintptr_t>(cnt) & 15) == 0) {
+        dim3 g((HW / 8 + 255) / 256, B);
+        dense_count_s1_kernel<<<g, 256, sizeof(int32_t) * (size_t)std::max(gt_total, 1), st>>>(
+            masks, HW, gt_total, cnt, totals);
+        return cudaGetLastError();
+    }
     dim3 g((HW + 255) / 256, B);
     dense_count_kernel<<<g, 256, sizeof(int32_t) * (size_t)std::max(gt_total, 1), st>>>(
         masks, H, W, Ht, Wt, s, gt_total, cnt, totals);

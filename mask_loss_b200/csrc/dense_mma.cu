@@ -9,7 +9,8 @@
 // be covered by several GTs.  This kernel runs them on tcgen05 UMMA with the
 // fp32 accumulators in tensor memory (TMEM):
 //   * per CTA: one image, one query tile (M = 128 rows, rows >= qrows unused)
-//     and half a cell chunk, all GT columns (N = gout rounded up to 16, <= 64);
+//     and half a cell chunk, all GT columns (N = GT_total rounded up to 16,
+//     <= 64; the background column is computed and dropped on output);
 //   * K blocks of 32 cells.  A TMA box brings the block's logits into shared
 //     memory (the cost kernel's tensor map: fp32 rows with the 128-byte
 //     swizzle, bf16/fp16 rows with the 64-byte one, widened exactly);
@@ -17,9 +18,10 @@
 //     sigmoid and the row sums on CUDA cores and write the A operands to TMEM
 //     as bf16 hi/lo pairs (x = xh + xl and p = ph + pl, each part rounded to
 //     nearest, so |x - xh - xl| <= 2^-18 |x|): four K-major 128 x 32 bf16
-//     operands, 16 TMEM columns each.  They also stage the block's counts as
-//     the bf16 B operand (N x 32, exact for counts <= 256) in shared memory in
-//     the no-swizzle K-major layout (8-row x 16-byte core matrices);
+//     operands, 16 TMEM columns each;
+//   * the B operand -- the block's pixel counts, kept as bf16 by the count
+//     kernel (exact for counts <= 256) -- arrives by TMA with the logits:
+//     N rows of 64 bytes in the 64-byte swizzled K-major layout the MMA reads;
 //   * one thread of the control warp issues the TMA loads and the MMAs
 //     (kind::f16, A from TMEM, B from shared memory, 128 x N x 16 each):
 //     D += xh k + xl k, I += ph k + pl k, and signals completion with
@@ -95,15 +97,12 @@ ML_INLINE void umma_commit(uint64_t* bar) {
                  ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Shared-memory matrix descriptor, K-major without swizzle: core matrices of
-// 8 rows x 16 bytes stored contiguously; `lbo` = byte distance between the
-// two 16-byte K halves of one K=16 step, `sbo` = between 8-row groups.
-// Fields: start address >> 4 [0,14), LBO >> 4 [16,30), SBO >> 4 [32,46),
-// descriptor version 1 [46,48), base offset 0, layout type 0 (no swizzle).
-ML_INLINE uint64_t smem_desc_noswizzle(const void* p, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor, K-major with the 64-byte swizzle (rows of
+// 32 bf16; 8-row atoms of 512 bytes, so SBO = 512; LBO unused, 1): the layout
+// a TMA box with CU_TENSOR_MAP_SWIZZLE_64B writes.  Layout type 4 [61,64).
+ML_INLINE uint64_t smem_desc_sw64(const void* p) {
     const uint64_t a = (uint64_t)((smem_u32(p) >> 4) & 0x3FFFu);
-    return a | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) |
-           (1ull << 46);
+    return a | (1ull << 16) | ((uint64_t)(512u >> 4) << 32) | (1ull << 46) | (4ull << 61);
 }
 
 // Instruction descriptor of kind::f16: bf16 A and B (K-major), fp32 D,
@@ -159,19 +158,22 @@ ML_INLINE float4 tile_quad(const T* row, int r, int kh, int u) {
 // (1024-aligned), then per stage the B tile [4][N][8] bf16, then MmaShared.
 template <typename T>
 __global__ void __launch_bounds__(kMmaThreads, 2)
-dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a, const uint16_t* cnt, int N) {
+dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap kmap,
+                 CostArgs a, int N) {
     extern __shared__ __align__(1024) unsigned char dsm_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
     const int QS = (a.qrows + 7) / 8 * 8;
-    T* xs = reinterpret_cast<T*>(base);                                // [stage][QS][32]
-    __nv_bfloat16* bs = reinterpret_cast<__nv_bfloat16*>(xs + kMmaStages * QS * kMmaK);  // [stage][4][N][8]
-    MmaShared* sh = reinterpret_cast<MmaShared*>(bs + kMmaStages * 4 * N * 8);
+    // per stage: counts [N][32] bf16 (64-byte rows, 1024-aligned), logits [QS][32] of T
+    const int bstage = (N * 64 + 1023) / 1024 * 1024;
+    __nv_bfloat16* bs = reinterpret_cast<__nv_bfloat16*>(base);                 // [stage][N][32]
+    T* xs = reinterpret_cast<T*>(base + kMmaStages * bstage);                    // [stage][QS][32]
+    MmaShared* sh = reinterpret_cast<MmaShared*>(xs + kMmaStages * QS * kMmaK);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int slot = blockIdx.x, chunk = slot >> 1, half = slot & 1;
     const int qt = blockIdx.y, lb = blockIdx.z, b = lb % a.B;
-    const int HW = a.H * a.W, G = a.gout;
+    const int HW = a.H * a.W, G = a.gout, NG = a.gt_total;
     const int half_cells = a.chunk_cells / 2;
     const int cb = min(HW, chunk * a.chunk_cells + half * half_cells);
     const int ce = min(HW, cb + half_cells);
@@ -207,24 +209,31 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a, const uin
             const uint32_t idesc = idesc_bf16_f32(N);
             auto issue_tma = [&](int kb) {
                 const int s = kb % kMmaStages;
-                mbar_arrive_expect_tx(&sh->full[s], (uint32_t)a.qrows * kMmaK * (uint32_t)sizeof(T));
+                mbar_arrive_expect_tx(&sh->full[s], (uint32_t)a.qrows * kMmaK * (uint32_t)sizeof(T) +
+                                                        (uint32_t)N * kMmaK * 2u);
+                const int c0 = cb + kb * kMmaK;
                 asm volatile(
                     "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
                     " [%0], [%1, {%2, %3}], [%4];"
-                    ::"r"(smem_u32(xs + s * QS * kMmaK)), "l"(&tmap), "r"(cb + kb * kMmaK), "r"(row0),
+                    ::"r"(smem_u32(xs + s * QS * kMmaK)), "l"(&tmap), "r"(c0), "r"(row0),
                       "r"(smem_u32(&sh->full[s])) : "memory");
+                // counts of GT rows [b*NG, b*NG + N) (rows past the image's own
+                // are other images' or zeros: their accumulators are never read)
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+                    " [%0], [%1, {%2, %3}], [%4];"
+                    ::"r"(smem_u32(reinterpret_cast<unsigned char*>(bs) + s * bstage)), "l"(&kmap),
+                      "r"(c0), "r"(b * NG), "r"(smem_u32(&sh->full[s])) : "memory");
             };
             for (int kb = 0; kb < min(nkb, kMmaStages); ++kb) issue_tma(kb);
             for (int kb = 0; kb < nkb && ok; ++kb) {
                 const int s = kb % kMmaStages;
                 if (!mbar_wait(&sh->aready[s], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
                 tc_fence_after();
-                // the producers have read this stage's logits: refill it
-                if (kb + kMmaStages < nkb) issue_tma(kb + kMmaStages);
 #pragma unroll
-                for (int kk = 0; kk < 2; ++kk) {  // K = 16 cells per MMA
-                    const uint64_t bd = smem_desc_noswizzle(bs + ((s * 4 + 2 * kk) * N) * 8,
-                                                            (uint32_t)N * 16u, 128u);
+                for (int kk = 0; kk < 2; ++kk) {  // K = 16 cells (32 bytes of a row) per MMA
+                    const uint64_t bd =
+                        smem_desc_sw64(reinterpret_cast<unsigned char*>(bs) + s * bstage + 32 * kk);
                     const bool acc = kb > 0 || kk > 0;
                     umma_ts(tbase, a_col(s, 0) + 8 * kk, bd, idesc, acc);          // D += xh k
                     umma_ts(tbase, a_col(s, 1) + 8 * kk, bd, idesc, true);         // D += xl k
@@ -232,6 +241,11 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a, const uin
                     umma_ts(tbase + N, a_col(s, 3) + 8 * kk, bd, idesc, true);     // I += pl k
                 }
                 umma_commit(&sh->mdone[s]);
+                // the stage's counts feed these MMAs: refill it once they are done
+                if (kb + kMmaStages < nkb) {
+                    if (!mbar_wait(&sh->mdone[s], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
+                    issue_tma(kb + kMmaStages);
+                }
             }
             if (ok && nkb > 0) umma_commit(&sh->accf);
             if (!ok) {
@@ -255,66 +269,57 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a, const uin
             // the stage's A and B are free once its previous MMAs completed
             if (kb >= kMmaStages &&
                 !mbar_wait(&sh->mdone[s], (uint32_t)(((kb / kMmaStages) - 1) & 1))) { ok = false; break; }
-            // B: counts of this block (rows g < N, cells k < 32) as bf16, core-matrix layout
-            __nv_bfloat16* bt = bs + s * 4 * N * 8;
-            for (int i = tid; i < N * 4; i += kMmaProducers * 32) {
-                const int g = i >> 2, kc = i & 3;          // row g, 8 cells starting at 8 kc
-                uint32_t w[4] = {0u, 0u, 0u, 0u};
-                if (g < G) {
-                    const int ga = g + (g >= a.bg ? 1 : 0);
-                    const uint16_t* src = cnt + ((int64_t)b * a.gt_total + ga) * HW + c0 + 8 * kc;
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int k0 = 8 * kc + 2 * u;
-                        const float lo = k0 < nv ? (float)src[2 * u] : 0.0f;
-                        const float hi = k0 + 1 < nv ? (float)src[2 * u + 1] : 0.0f;
-                        w[u] = pack_bf16(lo, hi);
-                    }
-                }
-                *reinterpret_cast<uint4*>(bt + (kc * N + g) * 8) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
             if (!mbar_wait(&sh->full[s], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
             // A: this thread's 16 cells of row r
             const T* xr = xs + (s * QS + r) * kMmaK;
             uint32_t xh[8], xl[8], ph[8], pl[8];
+            const bool full = nv == kMmaK && rvalid;
+            float prod = 1.0f;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {  // four 16-byte granules = 16 cells
                 const float4 v = rvalid ? tile_quad<T>(xr, r, kh, u) : make_float4(0.f, 0.f, 0.f, 0.f);
-                const float xv[4] = {v.x, v.y, v.z, v.w};
+                float xv[4] = {v.x, v.y, v.z, v.w};
                 float pv[4];
-                float prod = 1.0f;
+                if (full) {
 #pragma unroll
-                for (int e4 = 0; e4 < 4; ++e4) {
-                    const int k = 16 * kh + 4 * u + e4;
-                    const float x = k < nv ? xv[e4] : 0.0f;
-                    const Fast f = fast_elem(x);
-                    pv[e4] = k < nv ? f.p : 0.0f;
-                    if (k < nv && rvalid) {
-                        rsum[0] += fmaxf(x, 0.0f);
+                    for (int e4 = 0; e4 < 4; ++e4) {
+                        const Fast f = fast_elem(xv[e4]);
+                        pv[e4] = f.p;
+                        rsum[0] += fmaxf(xv[e4], 0.0f);
                         rsum[1] += f.p;
                         prod *= f.d;
                     }
+                } else {
+#pragma unroll
+                    for (int e4 = 0; e4 < 4; ++e4) {
+                        const bool in = rvalid && 16 * kh + 4 * u + e4 < nv;
+                        xv[e4] = in ? xv[e4] : 0.0f;
+                        const Fast f = fast_elem(xv[e4]);
+                        pv[e4] = in ? f.p : 0.0f;
+                        if (in) {
+                            rsum[0] += fmaxf(xv[e4], 0.0f);
+                            rsum[1] += f.p;
+                            prod *= f.d;
+                        }
+                    }
                 }
-                rsum[2] += lg2_approx(prod);
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
-                    const float x0 = (16 * kh + 4 * u + 2 * j < nv) ? xv[2 * j] : 0.0f;
-                    const float x1 = (16 * kh + 4 * u + 2 * j + 1 < nv) ? xv[2 * j + 1] : 0.0f;
-                    const uint32_t hx = pack_bf16(x0, x1);
+                    const uint32_t hx = pack_bf16(xv[2 * j], xv[2 * j + 1]);
                     xh[2 * u + j] = hx;
-                    xl[2 * u + j] = pack_bf16(x0 - bf16_lo(hx), x1 - bf16_hi(hx));
+                    xl[2 * u + j] = pack_bf16(xv[2 * j] - bf16_lo(hx), xv[2 * j + 1] - bf16_hi(hx));
                     const uint32_t hp = pack_bf16(pv[2 * j], pv[2 * j + 1]);
                     ph[2 * u + j] = hp;
                     pl[2 * u + j] = pack_bf16(pv[2 * j] - bf16_lo(hp), pv[2 * j + 1] - bf16_hi(hp));
                 }
             }
+            rsum[2] += lg2_approx(prod);  // 16 factors in [1, 2]
             const uint32_t colk = (uint32_t)(8 * kh);  // 16 bf16 cells = 8 columns
             tmem_st8(a_col(s, 0) + lane_off + colk, xh);
             tmem_st8(a_col(s, 1) + lane_off + colk, xl);
             tmem_st8(a_col(s, 2) + lane_off + colk, ph);
             tmem_st8(a_col(s, 3) + lane_off + colk, pl);
             tmem_wait_st();
-            fence_proxy_async_smem();  // the B tile is read by the tensor core
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh->aready[s]);
@@ -337,10 +342,10 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a, const uin
         // warps 0-3 write D (as -D: the partial holds sum(-x k)) and the row
         // sums, warps 4-7 write I
         const uint32_t acc_base = tbase + lane_off + (kh ? (uint32_t)N : 0u);
-        for (int g0 = 0; g0 < N; g0 += 16) {
+        for (int c0a = 0; c0a < N; c0a += 16) {  // accumulator columns = GT ids
             uint32_t v[16];
             if (have_acc) {
-                tmem_ld16(acc_base + (uint32_t)g0, v);
+                tmem_ld16(acc_base + (uint32_t)c0a, v);
                 tmem_wait_ld();
             } else {
 #pragma unroll
@@ -349,8 +354,9 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a, const uin
             if (rvalid) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const int g = g0 + j;
-                    if (g < G) {
+                    const int ga = c0a + j;
+                    if (ga < NG && ga != a.bg) {
+                        const int g = ga - (ga > a.bg ? 1 : 0);  // output column
                         const float val = __uint_as_float(v[j]);
                         part[((int64_t)kh * G + g) * QP + r] = kh ? val : -val;
                     }
@@ -371,40 +377,40 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a, const uin
     }
 }
 
-int dense_mma_n(int gout) { return (gout + 15) / 16 * 16; }
+int dense_mma_n(int gt_total) { return (gt_total + 15) / 16 * 16; }
 
 bool dense_mma_usable(const CostArgs& a, int ldt, bool unc, bool foc, bool tma) {
     (void)ldt;
-    const int N = dense_mma_n(a.gout);
-    return !unc && !foc && tma && a.gout > 0 && N <= 64 && a.qrows <= 128 &&
-           a.chunk_cells % (2 * kMmaK) == 0;
+    const int HW = a.H * a.W;
+    return !unc && !foc && tma && a.gout > 0 && dense_mma_n(a.gt_total) <= 64 && a.qrows <= 128 &&
+           a.chunk_cells % (2 * kMmaK) == 0 && HW % 8 == 0;  // counts rows: 16-byte pitch
 }
 
 size_t dense_mma_smem(const CostArgs& a, int esize) {
-    const int N = dense_mma_n(a.gout);
+    const int N = dense_mma_n(a.gt_total);
     const int QS = (a.qrows + 7) / 8 * 8;
-    return 1024 + (size_t)kMmaStages * QS * kMmaK * esize + (size_t)kMmaStages * 4 * N * 8 * 2 +
-           sizeof(MmaShared);
+    const size_t bstage = ((size_t)N * 64 + 1023) / 1024 * 1024;
+    return 1024 + kMmaStages * bstage + (size_t)kMmaStages * QS * kMmaK * esize + sizeof(MmaShared);
 }
 
 template <typename T>
-cudaError_t launch_dense_mma_t(const CUtensorMap& tm, const CostArgs& a, const uint16_t* cnt,
+cudaError_t launch_dense_mma_t(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
                                cudaStream_t st) {
-    const int N = dense_mma_n(a.gout);
+    const int N = dense_mma_n(a.gt_total);
     const size_t smem = dense_mma_smem(a, (int)sizeof(T));
     cudaError_t e = cudaFuncSetAttribute(dense_mma_kernel<T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 g(a.nchunk * 2, a.nqt, a.L * a.B);
-    dense_mma_kernel<T><<<g, kMmaThreads, smem, st>>>(tm, a, cnt, N);
+    dense_mma_kernel<T><<<g, kMmaThreads, smem, st>>>(tm, km, a, N);
     return cudaGetLastError();
 }
 
-cudaError_t launch_dense_mma(const CUtensorMap& tm, const CostArgs& a, const uint16_t* cnt,
+cudaError_t launch_dense_mma(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
                              cudaStream_t st, int ldt) {
-    if (ldt == 1) return launch_dense_mma_t<__nv_bfloat16>(tm, a, cnt, st);
-    if (ldt == 2) return launch_dense_mma_t<__half>(tm, a, cnt, st);
-    return launch_dense_mma_t<float>(tm, a, cnt, st);
+    if (ldt == 1) return launch_dense_mma_t<__nv_bfloat16>(tm, km, a, st);
+    if (ldt == 2) return launch_dense_mma_t<__half>(tm, km, a, st);
+    return launch_dense_mma_t<float>(tm, km, a, st);
 }
 
 }  // namespace mlb

@@ -207,6 +207,9 @@ cudaError_t launch_dense_cost(const CostArgs& a, bool unc, bool foc, const uint1
 // weights or focal terms, GT_out <= 64, TMA-aligned logits (ldt: 0 fp32,
 // 1 bf16, 2 fp16).
 bool dense_mma_usable(const CostArgs& a, int ldt, bool unc, bool foc, bool tma);
-cudaError_t launch_dense_mma(const CUtensorMap& tm, const CostArgs& a, const uint16_t* cnt,
+int dense_mma_n(int gt_total);  // MMA N: GT_total rounded up to 16
+// tm: the logits map (logits_tensor_map); km: the counts, bf16 [B*GT_total][H*W]
+// with boxes of 32 cells x dense_mma_n(GT_total) rows and the 64-byte swizzle.
+cudaError_t launch_dense_mma(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
                              cudaStream_t st, int ldt);
 }  // namespace mlb
