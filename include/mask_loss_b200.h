@@ -153,6 +153,14 @@ int ml_pairwise_mask_loss_forward_noalloc(const ml_dims* d, const ml_params* p,
 /* Scratch capacity (bytes) of ml_pairwise_mask_loss_forward_noalloc. */
 size_t ml_noalloc_scratch_limit(void);
 
+/* The cost-only entries (ml_pairwise_mask_loss_forward, its dense, sampled
+ * and no-alloc forms) have no dev_status argument: their kernels OR bit 2
+ * into a library-wide device word when a bounded pipeline wait runs out.
+ * ml_cost_status copies that word to *out and clears it.  It synchronises
+ * with the device (a plain cudaMemcpyFromSymbol); call it when checking
+ * results, not on a hot path.  No reference counterpart. */
+int ml_cost_status(int32_t* out);
+
 /* Pairwise label cost alone.  Replaces forward_pw_sigmoid_label_loss /     */
 /* forward_pw_softmax_label_loss (src/bindings.cpp:141-155,                 */
 /* src/cuda/pw_sigmoid_label_loss.cu:108-187, pw_softmax_label_loss.cu:105-174). */

@@ -58,6 +58,7 @@ SIGNATURES = {
                                                              ctypes.POINTER(Params), c_vp, c_vp,
                                                              c_vp, c_vp, c_vp, c_vp]),
     "ml_noalloc_scratch_limit": (c_sz, []),
+    "ml_cost_status": (ctypes.c_int, [ctypes.POINTER(c_i32)]),
     "ml_pairwise_label_loss_forward": (ctypes.c_int, [c_i64, c_i64, c_i64, c_i64, c_i64, c_i64,
                                                       c_f32, c_f32, c_f32, c_i32, c_vp, c_vp, c_vp,
                                                       c_vp]),
@@ -139,6 +140,10 @@ def load() -> ctypes.CDLL:
             fn.argtypes = args
         _LIB = lib
     return _LIB
+
+
+def loaded() -> bool:
+    return _LIB is not None
 
 
 def check(rc: int) -> None:

@@ -750,6 +750,20 @@ size_t ml_mask_matching_backward_workspace_size(const ml_dims* d, const ml_param
     return bwd_layout(d, p).bytes;
 }
 
+// Status word of the cost-only entries (which have no dev_status argument):
+// the cost kernels OR bit 2 into it when a bounded pipeline wait runs out.
+// Read (and cleared) by ml_cost_status.  Its address is looked up per call.
+static __device__ int32_t g_cost_status;
+
+int32_t* cost_status_ptr() {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_cost_status) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;  // the kernels then report nothing (as before)
+    }
+    return static_cast<int32_t*>(ptr);
+}
+
 int ml_pairwise_mask_loss_forward(const ml_dims* d, const ml_params* p, const float* mask_logits,
                                   const int64_t* mask_targets, const float* cls_logits,
                                   const int64_t* cls_targets, float* out, void* workspace,
@@ -761,9 +775,24 @@ int ml_pairwise_mask_loss_forward(const ml_dims* d, const ml_params* p, const fl
     if ((rc = check_ws(workspace, workspace_bytes, P.bytes))) return rc;
     if (P.gout == 0) return ML_OK;
     unsigned char* ws = ws_base(workspace);
-    CostArgs a = cost_args(P, p, mask_logits, mask_targets, cls_logits, cls_targets, ws, nullptr);
+    CostArgs a = cost_args(P, p, mask_logits, mask_targets, cls_logits, cls_targets, ws,
+                           cost_status_ptr());
     a.sep = out; a.total = nullptr; a.rawI = nullptr; a.rawT = nullptr;
     return run_costs(P, a, mask_logits, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ml_cost_status(int32_t* out) {
+    if (!out) return fail(ML_EINVAL, "out is null");
+    int32_t v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_cost_status, sizeof(v));
+    if (e != cudaSuccess) return cuda_fail(e, "read the cost status word");
+    if (v != 0) {
+        const int32_t zero = 0;
+        e = cudaMemcpyToSymbol(g_cost_status, &zero, sizeof(zero));
+        if (e != cudaSuccess) return cuda_fail(e, "clear the cost status word");
+    }
+    *out = v;
+    return ML_OK;
 }
 
 int ml_pairwise_mask_loss_forward_noalloc(const ml_dims* d, const ml_params* p,
@@ -793,7 +822,8 @@ int ml_pairwise_mask_loss_forward_noalloc(const ml_dims* d, const ml_params* p,
     if (P.gout == 0) return ML_OK;
     unsigned char* scratch = nullptr;
     if ((rc = noalloc_scratch(&scratch))) return rc;
-    CostArgs a = cost_args(P, p, mask_logits, mask_targets, cls_logits, cls_targets, scratch, nullptr);
+    CostArgs a = cost_args(P, p, mask_logits, mask_targets, cls_logits, cls_targets, scratch,
+                           cost_status_ptr());
     a.totals = reinterpret_cast<int32_t*>(scratch);
     a.codes = reinterpret_cast<int32_t*>(scratch + n_tot);
     a.part = reinterpret_cast<float*>(scratch + n_tot + n_codes);
@@ -1135,7 +1165,8 @@ int ml_pairwise_mask_loss_dense_forward(const ml_dims* d, const ml_params* p, co
     if ((rc = check_ws(workspace, workspace_bytes, P.bytes + dense_count_bytes(P)))) return rc;
     if (P.gout == 0) return ML_OK;
     unsigned char* ws = ws_base(workspace);
-    CostArgs a = cost_args(P, p, mask_logits, nullptr, cls_logits, cls_targets, ws, nullptr);
+    CostArgs a = cost_args(P, p, mask_logits, nullptr, cls_logits, cls_targets, ws,
+                           cost_status_ptr());
     a.sep = out; a.total = nullptr; a.rawI = nullptr; a.rawT = nullptr;
     return run_dense_costs(P, a, mask_masks, ws, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -1188,7 +1219,8 @@ int ml_pairwise_mask_loss_sampled_forward(const ml_dims* d, const ml_params* p, 
     if (S.cp.gout == 0) return ML_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned char* ws = ws_base(workspace);
-    CostArgs a = cost_args(S.cp, p, nullptr, mask_targets, cls_logits, cls_targets, ws, nullptr);
+    CostArgs a = cost_args(S.cp, p, nullptr, mask_targets, cls_logits, cls_targets, ws,
+                           cost_status_ptr());
     if ((rc = run_sampled_prep(S, p, mask_logits, logits_dtype, mask_targets, point_coords,
                                align_corners, ws, a, st)))
         return rc;

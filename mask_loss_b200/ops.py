@@ -67,6 +67,12 @@ def check_status(block: bool = False) -> None:
         return  # no event queries inside stream capture
     for st in list(_sticky.values()):
         st.check(block)
+    if block and torch.cuda.is_available() and _lib.loaded():
+        # the cost-only ops' word (they have no per-call status argument)
+        v = ctypes.c_int32(0)
+        _lib.check(_lib.load().ml_cost_status(ctypes.byref(v)))
+        if v.value:
+            raise RuntimeError(_status_message(v.value))
     keep = []
     err = None
     for ev, host, msg in _pending:
