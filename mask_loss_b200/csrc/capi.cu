@@ -591,7 +591,7 @@ int noalloc_scratch(unsigned char** out) {
 struct SampledPlan {
     FwdPlan cp;          // cost-stage plan over the sampled values
     int H, W, Ht, Wt, P;
-    size_t off_present, off_perm, off_scoords, off_zs, bytes;
+    size_t off_present, off_perm, off_scoords, off_zs, off_sort, bytes;
 };
 
 int make_sampled_plan(const ml_dims* d, const ml_params* p, int64_t P, SampledPlan* S) {
@@ -617,6 +617,7 @@ int make_sampled_plan(const ml_dims* d, const ml_params* p, int64_t P, SampledPl
     S->off_perm = off; off += align256(sizeof(int32_t) * (size_t)d->B * P);
     S->off_scoords = off; off += align256(sizeof(float) * 2 * (size_t)d->B * P);
     S->off_zs = off; off += align256(sizeof(float) * LBQ * P);
+    S->off_sort = off; off += align256(point_sort_scratch_bytes((int)d->B, (int)P, S->cp.gout));
     S->bytes = off + 256;
     return ML_OK;
 }
@@ -642,7 +643,8 @@ int run_sampled_prep(const SampledPlan& S, const ml_params* p, const void* mask_
         if (he != cudaSuccess) return cuda_fail(he, "label_hist_kernel");
         cudaError_t le = launch_point_sort(mask_targets, coords, P.B, S.Ht, S.Wt, S.P, P.gt_total, P.bg,
                                            P.gout, perm, const_cast<int32_t*>(a.codes), scoords,
-                                           const_cast<int32_t*>(a.totals), st);
+                                           const_cast<int32_t*>(a.totals), st,
+                                           reinterpret_cast<int32_t*>(ws + S.off_sort));
         g_launches.fetch_add(1);
         if (le != cudaSuccess) return cuda_fail(le, "point_sort_kernel");
     }

@@ -156,9 +156,14 @@ constexpr int kPointRowThreads = 512;  // block of the per-row point sample / gr
 constexpr size_t kRowMapMaxBytes = 96 * 1024;  // per-row maps staged in shared memory up to this
 constexpr int kMaxSortPoints = 40960;          // points per image (sort keys live in shared memory)
 size_t point_sort_smem(int P, int gout);
+constexpr int kSortBlockPts = 1024;            // points per block of the multi-block sort
+// scratch (point_sort_scratch_bytes) selects the multi-block sort; null the
+// one-block-per-image form.
+size_t point_sort_scratch_bytes(int B, int P, int gout);
 cudaError_t launch_point_sort(const int64_t* targets, const float* coords, int B, int Ht, int Wt,
                               int P, int gt_total, int bg, int gout, int32_t* perm, int32_t* scodes,
-                              float* scoords, int32_t* ptotals, cudaStream_t st);
+                              float* scoords, int32_t* ptotals, cudaStream_t st,
+                              int32_t* scratch = nullptr);
 cudaError_t launch_point_sample(int dtype, const void* logits, const float* scoords, int B, int L,
                                 int Q, int H, int W, int P, int align, float* zs, cudaStream_t st);
 cudaError_t launch_point_grad(bool foc, int dtype, const LossArgs& la, const float* zs,

@@ -127,6 +127,125 @@ point_sort_kernel(const int64_t* __restrict__ targets, const float* __restrict__
     }
 }
 
+// ---------------------------------------------------------------------------
+// The same stable counting sort spread over kSortBlockPts-point blocks of
+// every image (the single-block form leaves most SMs idle: one CTA per image).
+//   point_keys_kernel     grid (nblk, B): each point's key (column + 1, 0 =
+//                         no column) and the block's bucket counts; the
+//                         per-label point totals.
+//   point_scatter_kernel  grid (nblk, B): the block's bucket offsets (all
+//                         buckets before, then earlier blocks of the same
+//                         bucket -- a fixed order), then the single-block
+//                         kernel's warp-ordered scatter within the block.
+// Same result as point_sort_kernel, bit for bit.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+point_keys_kernel(const int64_t* __restrict__ targets, const float* __restrict__ coords, int Ht,
+                  int Wt, int P, int gt_total, int bg, int gout, int32_t* __restrict__ keys,
+                  int32_t* __restrict__ bhist, int32_t* __restrict__ ptotals) {
+    extern __shared__ int32_t hsm[];  // [NB]
+    const int NB = gout + 1;
+    const int b = blockIdx.y, j = blockIdx.x, nblk = gridDim.x;
+    for (int k = threadIdx.x; k < NB; k += blockDim.x) hsm[k] = 0;
+    __syncthreads();
+    const int64_t* tb = targets + (int64_t)b * Ht * Wt;
+    const float2* cb = reinterpret_cast<const float2*>(coords + (int64_t)b * P * 2);
+    int32_t* pt = ptotals + (int64_t)b * gt_total;
+    const int p0 = j * kSortBlockPts, p1 = min(P, p0 + kSortBlockPts);
+    constexpr int U = kSortBlockPts / 256;
+    float2 c[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int p = p0 + u * 256 + (int)threadIdx.x;
+        c[u] = p < p1 ? cb[p] : make_float2(0.0f, 0.0f);
+    }
+    int64_t lab[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+        lab[u] = p0 + u * 256 + (int)threadIdx.x < p1 ? point_label(tb, Ht, Wt, c[u].x, c[u].y) : -1;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int p = p0 + u * 256 + (int)threadIdx.x;
+        if (p >= p1) continue;
+        if (lab[u] >= 0 && lab[u] < gt_total) atomicAdd(&pt[lab[u]], 1);
+        const int key = label_to_col(lab[u], gt_total, bg) + 1;
+        keys[(int64_t)b * P + p] = key;
+        atomicAdd(&hsm[key], 1);
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < NB; k += blockDim.x) bhist[((int64_t)b * nblk + j) * NB + k] = hsm[k];
+}
+
+__global__ void __launch_bounds__(256)
+point_scatter_kernel(const int32_t* __restrict__ keys, const int32_t* __restrict__ bhist,
+                     const float* __restrict__ coords, int P, int gout, int32_t* __restrict__ perm,
+                     int32_t* __restrict__ scodes, float* __restrict__ scoords) {
+    extern __shared__ int32_t ssm[];
+    constexpr int NW = 8;
+    const int NB = gout + 1;
+    int32_t* base = ssm;             // [NB] this block's first position per bucket
+    int32_t* wcnt = base + NB;       // [NW][NB]
+    const int b = blockIdx.y, j = blockIdx.x, nblk = gridDim.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int32_t* bh = bhist + (int64_t)b * nblk * NB;
+    for (int k = tid; k < NB; k += blockDim.x) {
+        int all = 0, before = 0;
+        for (int jj = 0; jj < nblk; ++jj) {
+            const int c = bh[(int64_t)jj * NB + k];
+            all += c;
+            if (jj < j) before += c;
+        }
+        base[k] = all;      // bucket total for now
+        wcnt[k] = before;   // scratch: earlier blocks' share of bucket k
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int k = 0; k < NB; ++k) {
+            const int c = base[k];
+            base[k] = run + wcnt[k];
+            run += c;
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < NW * NB; i += blockDim.x) wcnt[i] = 0;
+    __syncthreads();
+    const int p0 = j * kSortBlockPts, p1 = min(P, p0 + kSortBlockPts);
+    const int seg = kSortBlockPts / NW;
+    const int s0 = min(p1, p0 + warp * seg), s1 = min(p1, s0 + seg);
+    const int32_t* kb = keys + (int64_t)b * P;
+    for (int p = s0 + lane; p < s1; p += 32) atomicAdd(&wcnt[warp * NB + kb[p]], 1);
+    __syncthreads();
+    for (int k = tid; k < NB; k += blockDim.x) {
+        int run = base[k];
+        for (int w = 0; w < NW; ++w) {
+            const int c = wcnt[w * NB + k];
+            wcnt[w * NB + k] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    int32_t* off = wcnt + warp * NB;
+    const float* cb = coords + (int64_t)b * P * 2;
+    for (int q0 = s0; q0 < s1; q0 += 32) {
+        const int p = q0 + lane;
+        const int key = p < s1 ? kb[p] : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, key);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        const int pos = p < s1 ? off[key] + rank : 0;
+        __syncwarp();
+        if (p < s1 && rank == 0) off[key] += __popc(peers);
+        __syncwarp();
+        if (p < s1) {
+            const int64_t o = (int64_t)b * P + pos;
+            perm[o] = p;
+            scodes[o] = key - 1;
+            scoords[2 * o] = cb[2 * p];
+            scoords[2 * o + 1] = cb[2 * p + 1];
+        }
+    }
+}
+
 // Bilinear taps of a point (grid_sample semantics, zero padding).
 struct Taps {
     int idx[4];
@@ -406,9 +525,33 @@ size_t point_sort_smem(int P, int gout) {
     return sizeof(int32_t) * ((size_t)P + (size_t)(kSortWarps + 1) * (gout + 1));
 }
 
+size_t point_sort_scratch_bytes(int B, int P, int gout) {
+    const int nblk = (P + kSortBlockPts - 1) / kSortBlockPts;
+    return sizeof(int32_t) * ((size_t)B * P + (size_t)B * nblk * (gout + 1));
+}
+
 cudaError_t launch_point_sort(const int64_t* targets, const float* coords, int B, int Ht, int Wt,
                               int P, int gt_total, int bg, int gout, int32_t* perm, int32_t* scodes,
-                              float* scoords, int32_t* ptotals, cudaStream_t st) {
+                              float* scoords, int32_t* ptotals, cudaStream_t st, int32_t* scratch) {
+    if (scratch) {  // blocks of kSortBlockPts points: keys + block histograms, then the scatter
+        const int nblk = (P + kSortBlockPts - 1) / kSortBlockPts;
+        const int NB = gout + 1;
+        int32_t* keys = scratch;
+        int32_t* bhist = scratch + (size_t)B * P;
+        const size_t ks = sizeof(int32_t) * (size_t)NB;
+        const size_t ss = sizeof(int32_t) * (size_t)NB * 9;
+        cudaError_t e = cudaFuncSetAttribute(point_keys_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ks);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(point_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)ss);
+        if (e != cudaSuccess) return e;
+        point_keys_kernel<<<dim3(nblk, B), 256, ks, st>>>(targets, coords, Ht, Wt, P, gt_total, bg,
+                                                          gout, keys, bhist, ptotals);
+        point_scatter_kernel<<<dim3(nblk, B), 256, ss, st>>>(keys, bhist, coords, P, gout, perm,
+                                                             scodes, scoords);
+        return cudaGetLastError();
+    }
     const size_t smem = point_sort_smem(P, gout);
     cudaError_t e = cudaFuncSetAttribute(point_sort_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
