@@ -508,7 +508,11 @@ def run_ours(args, cfg):
     # roofline of the dominant kernel: the streaming cost kernel reads every
     # logit once plus one int32 code per cell and image
     cells = synthetic.CFG3_POINTS if sampled else cfg.H * cfg.W  # sampled values are fp32
-    cost_kernel = "dense_cost_kernel" if dense else "cost_partial_kernel"
+    # dense targets run on the tensor-core kernel unless MASK_LOSS_B200_DENSE_MMA=0
+    # (the bench's settings have no entropy weights or focal terms, GT_out <= 64)
+    dense_kernel = ("dense_cost_kernel" if os.environ.get("MASK_LOSS_B200_DENSE_MMA", "1")[:1] == "0"
+                    else "dense_mma_kernel")
+    cost_kernel = dense_kernel if dense else "cost_partial_kernel"
     # dense: every logit plus each GT's uint16 count per cell
     esize = 2 if (half is not None and not sampled) else 4
     cost_bytes = (cfg.L * cfg.B * cfg.Q * cells * esize +
@@ -535,7 +539,7 @@ def run_ours(args, cfg):
         ms_c = max(ms_step - ms_a - ms_b, 1e-6)
         stages = {
             "A_costs": {"ms": ms_a, "bytes": bytes_a, "frac": bytes_a / (ms_a / 1e3) / 1e9 / peak,
-                        "kernels": "label_code + cost_partial (or dense_cost) + cost_rows + "
+                        "kernels": f"label_code + {cost_kernel} + cost_rows + "
                                    "cost_pairs, timed as their own CUDA graph"},
             "B_solver": {"ms": ms_b, "kernels": "match_kernel, event-timed (latency-bound, "
                                                 "no roofline)"},

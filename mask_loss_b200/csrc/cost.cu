@@ -227,11 +227,73 @@ cudaError_t launch_label_hist(const int64_t* targets, int B, int64_t npix, int g
     return cudaGetLastError();
 }
 
+// s = 1 with H*W a multiple of 8 and 16-byte aligned maps: eight cells per
+// thread (four 16-byte label loads issued together, two 16-byte code
+// stores); the histogram counts the thread's runs in registers and adds the
+// warp's last runs with one atomic per label, like label_hist_kernel.
+__global__ void __launch_bounds__(256)
+label_code_s1_kernel(const int64_t* __restrict__ targets, int HW, int gt_total, int bg,
+                     int32_t* __restrict__ codes, int32_t* __restrict__ totals) {
+    extern __shared__ int32_t hist[];
+    const int b = blockIdx.y;
+    const bool use_sh = totals && gt_total <= kHistSmemMax;
+    if (use_sh)
+        for (int i = threadIdx.x; i < gt_total; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    int32_t* hc = use_sh ? hist : (totals ? totals + (int64_t)b * gt_total : nullptr);
+    const int64_t* tb = targets + (int64_t)b * HW;
+    int32_t* cb = codes + (int64_t)b * HW;
+    for (int base = blockIdx.x * blockDim.x * 8; base < HW; base += gridDim.x * blockDim.x * 8) {
+        const int c0 = base + (int)threadIdx.x * 8;
+        int run = -1, rc = 0;
+        if (c0 < HW) {
+            int64_t v[8];
+            const longlong2* q = reinterpret_cast<const longlong2*>(tb + c0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const longlong2 t2 = q[i];
+                v[2 * i] = t2.x;
+                v[2 * i + 1] = t2.y;
+            }
+            int c[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                c[i] = label_to_col(v[i], gt_total, bg);
+                const int key = (v[i] >= 0 && v[i] < gt_total) ? (int)v[i] : -1;
+                if (key != run) {
+                    if (run >= 0 && hc) atomicAdd(&hc[run], rc);
+                    run = key;
+                    rc = 0;
+                }
+                ++rc;
+            }
+            reinterpret_cast<int4*>(cb + c0)[0] = make_int4(c[0], c[1], c[2], c[3]);
+            reinterpret_cast<int4*>(cb + c0)[1] = make_int4(c[4], c[5], c[6], c[7]);
+        }
+        if (hc) {
+            const unsigned peers = __match_any_sync(0xffffffffu, run);
+            const int n = (int)__reduce_add_sync(peers, (unsigned)rc);
+            if (run >= 0 && (int)(threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hc[run], n);
+        }
+    }
+    __syncthreads();
+    if (use_sh && totals)
+        for (int i = threadIdx.x; i < gt_total; i += blockDim.x)
+            if (hist[i]) atomicAdd(&totals[(int64_t)b * gt_total + i], hist[i]);
+}
+
 cudaError_t launch_label_code(const int64_t* targets, int B, int H, int W, int Wt, int s,
                               int gt_total, int bg, int32_t* codes, int32_t* totals, uint4* mixtab,
                               cudaStream_t st) {
     const int HW = H * W;
     if (B <= 0 || HW <= 0) return cudaSuccess;
+    if (s == 1 && codes && HW % 8 == 0 && (reinterpret_cast<uintptr_t>(targets) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(codes) & 15) == 0) {
+        const int bx = std::max(1, std::min((HW / 8 + 255) / 256, 65535));
+        const size_t hs = (totals && gt_total <= kHistSmemMax) ? sizeof(int32_t) * gt_total : 0;
+        label_code_s1_kernel<<<dim3(bx, B), 256, hs, st>>>(targets, HW, gt_total, bg, codes, totals);
+        return cudaGetLastError();
+    }
     const int bx = std::max(1, std::min((HW + 255) / 256, 65535));
     const size_t hs = (totals && gt_total <= kHistSmemMax) ? sizeof(int32_t) * gt_total : 0;
     const dim3 grid(bx, B);
