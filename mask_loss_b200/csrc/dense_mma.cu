@@ -26,8 +26,10 @@
 //     (kind::f16, A from TMEM, B from shared memory, 128 x N x 16 each):
 //     D += xh k + xl k, I += ph k + pl k, and signals completion with
 //     tcgen05.commit on an mbarrier;
-//   * a two-stage ring: while the tensor core works on block kb the producers
-//     fill stage (kb+1)%2;
+//   * two rings: four shared-memory stages of logits + counts, refilled as
+//     soon as the MMAs that read a stage's counts completed (loads run up to
+//     three blocks ahead), and two TMEM stages of A operands: while the
+//     tensor core works on block kb the producers write block kb+1;
 //   * epilogue: the producer warps read D and I from TMEM (tcgen05.ld) and
 //     write the label path's chunk-partial slot, so cost_rows / cost_pairs,
 //     the solver and the matched loss run unchanged.
@@ -44,7 +46,8 @@ namespace mlb {
 namespace {
 
 constexpr int kMmaK = 32;          // cells per K block
-constexpr int kMmaStages = 2;
+constexpr int kMmaStages = 2;     // A operand stages in TMEM
+constexpr int kTmaStages = 4;     // logits + counts stages in shared memory
 constexpr int kMmaProducers = 8;   // warps
 constexpr int kMmaThreads = (kMmaProducers + 1) * 32;
 constexpr int kMmaTmemCols = 256;
@@ -123,9 +126,9 @@ ML_INLINE float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 ML_INLINE float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 struct MmaShared {
-    uint64_t full[kMmaStages];    // logits tile landed (TMA)
-    uint64_t aready[kMmaStages];  // A (TMEM) and B (smem) of the stage written
-    uint64_t mdone[kMmaStages];   // the stage's MMAs completed
+    uint64_t full[kTmaStages];    // logits and counts of the stage landed (TMA)
+    uint64_t aready[kMmaStages];  // A operands of the TMEM stage written
+    uint64_t mdone[kTmaStages];   // the MMAs of the block held in the stage completed
     uint64_t accf;                // all MMAs completed
     uint32_t tmem_base;
     int32_t err;
@@ -167,8 +170,8 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
     // per stage: counts [N][32] bf16 (64-byte rows, 1024-aligned), logits [QS][32] of T
     const int bstage = (N * 64 + 1023) / 1024 * 1024;
     __nv_bfloat16* bs = reinterpret_cast<__nv_bfloat16*>(base);                 // [stage][N][32]
-    T* xs = reinterpret_cast<T*>(base + kMmaStages * bstage);                    // [stage][QS][32]
-    MmaShared* sh = reinterpret_cast<MmaShared*>(xs + kMmaStages * QS * kMmaK);
+    T* xs = reinterpret_cast<T*>(base + kTmaStages * bstage);                    // [stage][QS][32]
+    MmaShared* sh = reinterpret_cast<MmaShared*>(xs + kTmaStages * QS * kMmaK);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int slot = blockIdx.x, chunk = slot >> 1, half = slot & 1;
@@ -182,11 +185,11 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
     const uint32_t cols_acc = 2u * N;
 
     if (tid == 0) {
-        for (int i = 0; i < kMmaStages; ++i) {
+        for (int i = 0; i < kTmaStages; ++i) {
             mbar_init(&sh->full[i], 1);
-            mbar_init(&sh->aready[i], kMmaProducers);
             mbar_init(&sh->mdone[i], 1);
         }
+        for (int i = 0; i < kMmaStages; ++i) mbar_init(&sh->aready[i], kMmaProducers);
         mbar_init(&sh->accf, 1);
         sh->err = 0;
         fence_mbar_init();
@@ -208,7 +211,7 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
             bool ok = true;
             const uint32_t idesc = idesc_bf16_f32(N);
             auto issue_tma = [&](int kb) {
-                const int s = kb % kMmaStages;
+                const int s = kb % kTmaStages;
                 mbar_arrive_expect_tx(&sh->full[s], (uint32_t)a.qrows * kMmaK * (uint32_t)sizeof(T) +
                                                         (uint32_t)N * kMmaK * 2u);
                 const int c0 = cb + kb * kMmaK;
@@ -225,26 +228,33 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
                     ::"r"(smem_u32(reinterpret_cast<unsigned char*>(bs) + s * bstage)), "l"(&kmap),
                       "r"(c0), "r"(b * NG), "r"(smem_u32(&sh->full[s])) : "memory");
             };
-            for (int kb = 0; kb < min(nkb, kMmaStages); ++kb) issue_tma(kb);
+            for (int kb = 0; kb < min(nkb, kTmaStages); ++kb) issue_tma(kb);
             for (int kb = 0; kb < nkb && ok; ++kb) {
-                const int s = kb % kMmaStages;
-                if (!mbar_wait(&sh->aready[s], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
+                const int s = kb % kTmaStages;   // shared-memory stage (counts)
+                const int ts = kb % kMmaStages;  // TMEM stage (A operands)
+                if (!mbar_wait(&sh->aready[ts], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < 2; ++kk) {  // K = 16 cells (32 bytes of a row) per MMA
                     const uint64_t bd =
                         smem_desc_sw64(reinterpret_cast<unsigned char*>(bs) + s * bstage + 32 * kk);
                     const bool acc = kb > 0 || kk > 0;
-                    umma_ts(tbase, a_col(s, 0) + 8 * kk, bd, idesc, acc);          // D += xh k
-                    umma_ts(tbase, a_col(s, 1) + 8 * kk, bd, idesc, true);         // D += xl k
-                    umma_ts(tbase + N, a_col(s, 2) + 8 * kk, bd, idesc, acc);      // I += ph k
-                    umma_ts(tbase + N, a_col(s, 3) + 8 * kk, bd, idesc, true);     // I += pl k
+                    umma_ts(tbase, a_col(ts, 0) + 8 * kk, bd, idesc, acc);          // D += xh k
+                    umma_ts(tbase, a_col(ts, 1) + 8 * kk, bd, idesc, true);         // D += xl k
+                    umma_ts(tbase + N, a_col(ts, 2) + 8 * kk, bd, idesc, acc);      // I += ph k
+                    umma_ts(tbase + N, a_col(ts, 3) + 8 * kk, bd, idesc, true);     // I += pl k
                 }
                 umma_commit(&sh->mdone[s]);
-                // the stage's counts feed these MMAs: refill it once they are done
-                if (kb + kMmaStages < nkb) {
-                    if (!mbar_wait(&sh->mdone[s], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
-                    issue_tma(kb + kMmaStages);
+                // refill the stage of the previous block (its MMAs, issued one
+                // block ago, read its counts) with the block kTmaStages later,
+                // so loads run up to three blocks ahead of the producers
+                const int kp = kb - 1;
+                if (kp >= 0 && kp + kTmaStages < nkb) {
+                    if (!mbar_wait(&sh->mdone[kp % kTmaStages], (uint32_t)((kp / kTmaStages) & 1))) {
+                        ok = false;
+                        break;
+                    }
+                    issue_tma(kp + kTmaStages);
                 }
             }
             if (ok && nkb > 0) umma_commit(&sh->accf);
@@ -263,13 +273,19 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
         float rsum[3] = {0.0f, 0.0f, 0.0f};        // sum max(x,0), sum p, sum log2(1+e)
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % kMmaStages;
+            const int s = kb % kTmaStages;   // shared-memory stage
+            const int ts = kb % kMmaStages;  // TMEM stage
             const int c0 = cb + kb * kMmaK;
             const int nv = min(kMmaK, ce - c0);
-            // the stage's A and B are free once its previous MMAs completed
-            if (kb >= kMmaStages &&
-                !mbar_wait(&sh->mdone[s], (uint32_t)(((kb / kMmaStages) - 1) & 1))) { ok = false; break; }
-            if (!mbar_wait(&sh->full[s], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
+            // the TMEM stage is free once the MMAs of block kb - kMmaStages completed
+            if (kb >= kMmaStages) {
+                const int kq = kb - kMmaStages;
+                if (!mbar_wait(&sh->mdone[kq % kTmaStages], (uint32_t)((kq / kTmaStages) & 1))) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (!mbar_wait(&sh->full[s], (uint32_t)((kb / kTmaStages) & 1))) { ok = false; break; }
             // A: this thread's 16 cells of row r
             const T* xr = xs + (s * QS + r) * kMmaK;
             uint32_t xh[8], xl[8], ph[8], pl[8];
@@ -315,14 +331,14 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
             }
             rsum[2] += lg2_approx(prod);  // 16 factors in [1, 2]
             const uint32_t colk = (uint32_t)(8 * kh);  // 16 bf16 cells = 8 columns
-            tmem_st8(a_col(s, 0) + lane_off + colk, xh);
-            tmem_st8(a_col(s, 1) + lane_off + colk, xl);
-            tmem_st8(a_col(s, 2) + lane_off + colk, ph);
-            tmem_st8(a_col(s, 3) + lane_off + colk, pl);
+            tmem_st8(a_col(ts, 0) + lane_off + colk, xh);
+            tmem_st8(a_col(ts, 1) + lane_off + colk, xl);
+            tmem_st8(a_col(ts, 2) + lane_off + colk, ph);
+            tmem_st8(a_col(ts, 3) + lane_off + colk, pl);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sh->aready[s]);
+            if (lane == 0) mbar_arrive(&sh->aready[ts]);
         }
         if (!ok) {
             sh->err = 1;
@@ -390,7 +406,7 @@ size_t dense_mma_smem(const CostArgs& a, int esize) {
     const int N = dense_mma_n(a.gt_total);
     const int QS = (a.qrows + 7) / 8 * 8;
     const size_t bstage = ((size_t)N * 64 + 1023) / 1024 * 1024;
-    return 1024 + kMmaStages * bstage + (size_t)kMmaStages * QS * kMmaK * esize + sizeof(MmaShared);
+    return 1024 + kTmaStages * bstage + (size_t)kTmaStages * QS * kMmaK * esize + sizeof(MmaShared);
 }
 
 template <typename T>
