@@ -143,10 +143,11 @@ __global__ void __launch_bounds__(256)
 point_keys_kernel(const int64_t* __restrict__ targets, const float* __restrict__ coords, int Ht,
                   int Wt, int P, int gt_total, int bg, int gout, int32_t* __restrict__ keys,
                   int32_t* __restrict__ bhist, int32_t* __restrict__ ptotals) {
-    extern __shared__ int32_t hsm[];  // [NB]
+    extern __shared__ int32_t hsm[];  // [NB] bucket counts, then [gt_total] label counts
     const int NB = gout + 1;
+    int32_t* hl = hsm + NB;
     const int b = blockIdx.y, j = blockIdx.x, nblk = gridDim.x;
-    for (int k = threadIdx.x; k < NB; k += blockDim.x) hsm[k] = 0;
+    for (int k = threadIdx.x; k < NB + gt_total; k += blockDim.x) hsm[k] = 0;
     __syncthreads();
     const int64_t* tb = targets + (int64_t)b * Ht * Wt;
     const float2* cb = reinterpret_cast<const float2*>(coords + (int64_t)b * P * 2);
@@ -167,13 +168,16 @@ point_keys_kernel(const int64_t* __restrict__ targets, const float* __restrict__
     for (int u = 0; u < U; ++u) {
         const int p = p0 + u * 256 + (int)threadIdx.x;
         if (p >= p1) continue;
-        if (lab[u] >= 0 && lab[u] < gt_total) atomicAdd(&pt[lab[u]], 1);
+        if (lab[u] >= 0 && lab[u] < gt_total) atomicAdd(&hl[lab[u]], 1);
         const int key = label_to_col(lab[u], gt_total, bg) + 1;
         keys[(int64_t)b * P + p] = key;
         atomicAdd(&hsm[key], 1);
     }
     __syncthreads();
     for (int k = threadIdx.x; k < NB; k += blockDim.x) bhist[((int64_t)b * nblk + j) * NB + k] = hsm[k];
+    // one global atomic per label present in the block (integer: order-free)
+    for (int k = threadIdx.x; k < gt_total; k += blockDim.x)
+        if (hl[k]) atomicAdd(&pt[k], hl[k]);
 }
 
 __global__ void __launch_bounds__(256)
@@ -455,6 +459,39 @@ point_grad_global_focal_kernel(LossArgs a, const float* zs, const float* scoords
     point_grad_global_body<true>(a, zs, scoords, scodes, P, align, gacc);
 }
 
+// One row of HW values in the logits' dtype, from a shared-memory fp32 map
+// (or zeros when map is null): 16-byte stores where the row allows them.
+template <typename TO>
+ML_INLINE void write_grad_row(TO* out, const float* map, int HW) {
+    constexpr int V = 16 / (int)sizeof(TO);
+    if (HW % V == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+        uint4* o = reinterpret_cast<uint4*>(out);
+        for (int i = threadIdx.x; i < HW / V; i += blockDim.x) {
+            float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (map) {
+                const float4* m = reinterpret_cast<const float4*>(map + i * V);
+                const float4 a = m[0];
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+                if (V == 8) {
+                    const float4 b = m[1];
+                    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+                }
+            }
+            uint4 w;
+            if constexpr (sizeof(TO) == 4) {
+                w = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                               __float_as_uint(v[3]));
+            } else {
+                w = make_uint4(narrow2(v[0], v[1], out), narrow2(v[2], v[3], out),
+                               narrow2(v[4], v[5], out), narrow2(v[6], v[7], out));
+            }
+            o[i] = w;
+        }
+    } else {
+        for (int i = threadIdx.x; i < HW; i += blockDim.x) out[i] = from_f32<TO>(map ? map[i] : 0.0f);
+    }
+}
+
 // Block per (l,b,q) row: the gradient map is accumulated in shared memory
 // and written once in the logits' dtype (zeros for rows the loss does not
 // reach), so no memset, no global atomics and no conversion pass.
@@ -468,10 +505,12 @@ __device__ __forceinline__ void point_grad_row_body(const LossArgs& a, const flo
     TO* out = grad + qi * (int64_t)HW;
     const RowGrad r = row_grad_setup(a, qi);
     if (!r.active) {
-        for (int i = threadIdx.x; i < HW; i += blockDim.x) out[i] = from_f32<TO>(0.0f);
+        write_grad_row<TO>(out, nullptr, HW);
         return;
     }
-    for (int i = threadIdx.x; i < HW; i += blockDim.x) gmap[i] = 0.0f;
+    for (int i = threadIdx.x; i < HW / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(gmap)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = (HW / 4) * 4 + threadIdx.x; i < HW; i += blockDim.x) gmap[i] = 0.0f;
     __syncthreads();
     const int b = (int)((qi / a.Q) % a.B);
     const float* cb = scoords + (int64_t)b * P * 2;
@@ -487,7 +526,7 @@ __device__ __forceinline__ void point_grad_row_body(const LossArgs& a, const flo
             if (tp.w[k] != 0.0f) atomicAdd(&gmap[tp.idx[k]], g * tp.w[k]);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < HW; i += blockDim.x) out[i] = from_f32<TO>(gmap[i]);
+    write_grad_row<TO>(out, gmap, HW);
 }
 
 __global__ void __launch_bounds__(kPointRowThreads)
@@ -538,7 +577,7 @@ cudaError_t launch_point_sort(const int64_t* targets, const float* coords, int B
         const int NB = gout + 1;
         int32_t* keys = scratch;
         int32_t* bhist = scratch + (size_t)B * P;
-        const size_t ks = sizeof(int32_t) * (size_t)NB;
+        const size_t ks = sizeof(int32_t) * ((size_t)NB + (size_t)gt_total);
         const size_t ss = sizeof(int32_t) * (size_t)NB * 9;
         cudaError_t e = cudaFuncSetAttribute(point_keys_kernel,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ks);
