@@ -931,7 +931,7 @@ static int mask_matching_impl(const ml_dims* d, const ml_params* p, const float*
     }
     {
         ProfScope prof(5, st);
-        loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
+        loss_fwd_kernel<<<P.L, 1024, 0, st>>>(la);
     }
     ML_CHECK_LAUNCH("loss_fwd_kernel");
     return ML_OK;
@@ -1273,7 +1273,7 @@ int ml_mask_matching_sampled(const ml_dims* d, const ml_params* p, int64_t num_p
     }
     {
         ProfScope prof(5, st);
-        loss_fwd_kernel<<<P.L, 512, 0, st>>>(la);
+        loss_fwd_kernel<<<P.L, 1024, 0, st>>>(la);
     }
     ML_CHECK_LAUNCH("loss_fwd_kernel");
     return ML_OK;

@@ -65,9 +65,9 @@ ML_INLINE void denominators(const LossArgs& a, float matched, float* md, float* 
 }
 
 // ---------------------------------------------------------------------------
-// Forward: grid = L, block = 512.
+// Forward: grid = L, block = 1024.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) loss_fwd_kernel(LossArgs a) {
+__global__ void __launch_bounds__(1024) loss_fwd_kernel(LossArgs a) {
     __shared__ float sh[32 * 4];
     const int l = blockIdx.x;
     if (a.void_status && l == 0) {  // functions/mask/matching.py:180-181
@@ -92,9 +92,9 @@ __global__ void __launch_bounds__(512) loss_fwd_kernel(LossArgs a) {
     const int64_t slice = (int64_t)a.L * a.B * a.Q * G;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};  // mask, dice, cls, matched
     const bool need_cls = a.force_cls || a.has_void;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const int64_t qi = (int64_t)l * n + i;
-        const int64_t g = a.pred_to_gt[qi];
+    // rows in pairs: both assignments load before either row's gathers, so
+    // each thread has two dependent load chains in flight
+    auto row = [&](int64_t qi, int64_t g) {
         const float* qs = a.qstat + qi * kQStat;
         float sv[kSaved] = {qs[0], 0.0f, 0.0f, qs[1]};
         if (g >= 0) {
@@ -112,6 +112,14 @@ __global__ void __launch_bounds__(512) loss_fwd_kernel(LossArgs a) {
         if (a.saved)
 #pragma unroll
             for (int k = 0; k < kSaved; ++k) a.saved[qi * kSaved + k] = sv[k];
+    };
+    for (int i = threadIdx.x; i < n; i += 2 * blockDim.x) {
+        const int i2 = i + blockDim.x;
+        const int64_t q1 = (int64_t)l * n + i, q2 = (int64_t)l * n + i2;
+        const int64_t g1 = a.pred_to_gt[q1];
+        const int64_t g2 = i2 < n ? a.pred_to_gt[q2] : -1;
+        row(q1, g1);
+        if (i2 < n) row(q2, g2);
     }
     block_sum<4>(acc, sh);
     if (threadIdx.x == 0) {
