@@ -26,9 +26,14 @@ def _bg(background_index):
 
 
 def _sampled_costs(logits, targets, background_index, num_points, align_corners, point_coords,
-                   which, smooth=1.0, scale=1.0, focal_gamma=0.0, focal_alpha=None):
+                   which, smooth=1.0, scale=1.0, focal_gamma=0.0, focal_alpha=None, num_gts=None):
     bg = _bg(background_index)
-    gt_total = int(targets.max().item()) + 1 if targets.numel() else 0
+    # GT_total sets the output's width: read from the targets on the host
+    # unless the caller passes it (num_gts)
+    if num_gts is not None:
+        gt_total = int(num_gts)
+    else:
+        gt_total = int(targets.max().item()) + 1 if targets.numel() else 0
     L, B, Q = logits.shape[:3]
     if point_coords is None:
         point_coords = ops.reference_point_coords(targets, num_points, bg)
@@ -45,16 +50,19 @@ def _sampled_costs(logits, targets, background_index, num_points, align_corners,
 def pairwise_sigmoid_cross_entropy_loss_sampling(logits, targets, background_index=None, scale=1.0,
                                                  num_points=5000, align_corners=False,
                                                  focal_gamma=0.0, focal_alpha=None,
-                                                 point_coords=None):
+                                                 point_coords=None, *, num_gts=None):
+    """num_gts (keyword): targets.max() + 1 when known, to skip the host read."""
     return _sampled_costs(logits, targets, background_index, num_points, align_corners,
                           point_coords, 0, scale=scale, focal_gamma=focal_gamma,
-                          focal_alpha=focal_alpha)
+                          focal_alpha=focal_alpha, num_gts=num_gts)
 
 
 def pairwise_dice_loss_sampling(logits, targets, smooth=1.0, background_index=None, scale=1.0,
-                                num_points=5000, align_corners=False, point_coords=None):
+                                num_points=5000, align_corners=False, point_coords=None, *,
+                                num_gts=None):
+    """num_gts (keyword): targets.max() + 1 when known, to skip the host read."""
     return _sampled_costs(logits, targets, background_index, num_points, align_corners,
-                          point_coords, 1, smooth=smooth, scale=scale)
+                          point_coords, 1, smooth=smooth, scale=scale, num_gts=num_gts)
 
 
 def resolve_sampled_args(smooth, sigmoid_scale, dice_scale, cls_scale, background_index, inf_thresh,

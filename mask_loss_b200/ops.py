@@ -562,13 +562,17 @@ def mask_matching_backward(grad_layer_mask_mean, grad_layer_dice_mean, grad_laye
 # Standalone pairwise ops (src/bindings.cpp:22-31, 51-62, 141-155)
 # ---------------------------------------------------------------------------
 def _pairwise_mask_only(logits, targets, background_index, which, smooth=1.0, scale=1.0, gamma=0.0,
-                        alpha=-1.0, ug=1.0, ugmin=0.05, normalize=True):
+                        alpha=-1.0, ug=1.0, ugmin=0.05, normalize=True, num_gts=None):
     _check_input(logits, "logits")
     _check_input(targets, "targets")
     if logits.dim() != 5:
         raise RuntimeError("logits must be (L,B,C,H,W)")
-    # GT_total = targets.max() + 1 (src/cuda/pw_sigmoid_ce.cu:221-224): a host read, as in the reference
-    gt_total = int(targets.max().item()) + 1 if targets.numel() else 0
+    # GT_total = targets.max() + 1 (src/cuda/pw_sigmoid_ce.cu:221-224): the output's
+    # width, so a host read as in the reference, unless the caller passes it
+    if num_gts is not None:
+        gt_total = int(num_gts)
+    else:
+        gt_total = int(targets.max().item()) + 1 if targets.numel() else 0
     L, B, Q = logits.shape[:3]
     dev = logits.device
     cls_logits = torch.zeros((L, B, Q, 1), dtype=torch.float32, device=dev)
@@ -583,17 +587,22 @@ def _pairwise_mask_only(logits, targets, background_index, which, smooth=1.0, sc
 
 def forward_pw_sigmoid_ce_loss(logits, targets, background_index=-1, scale=1.0, gamma=0.0,
                                alpha=-1.0, uncertainty_gamma=1.0, uncertainty_gamma_min=0.05,
-                               normalize_uncertainty=True):
-    """(L,B,C,GT_out) pairwise sigmoid-CE (src/cuda/pw_sigmoid_ce.cu:199-316)."""
+                               normalize_uncertainty=True, *, num_gts=None):
+    """(L,B,C,GT_out) pairwise sigmoid-CE (src/cuda/pw_sigmoid_ce.cu:199-316).
+
+    num_gts (keyword, not in the reference): GT_total = targets.max() + 1 when
+    the caller knows it; the op then makes no host read of the targets."""
     return _pairwise_mask_only(logits, targets, background_index, 0, 1.0, scale, gamma, alpha,
-                               uncertainty_gamma, uncertainty_gamma_min, normalize_uncertainty)
+                               uncertainty_gamma, uncertainty_gamma_min, normalize_uncertainty,
+                               num_gts)
 
 
 def forward_pw_dice_loss(logits, targets, smooth, background_index=-1, scale=1.0,
-                         uncertainty_gamma=1.0, uncertainty_gamma_min=0.05):
-    """(L,B,C,GT_out) pairwise dice (src/cuda/pw_dice_loss.cu:111-220)."""
+                         uncertainty_gamma=1.0, uncertainty_gamma_min=0.05, *, num_gts=None):
+    """(L,B,C,GT_out) pairwise dice (src/cuda/pw_dice_loss.cu:111-220); num_gts as
+    in forward_pw_sigmoid_ce_loss."""
     return _pairwise_mask_only(logits, targets, background_index, 1, smooth, scale, 0.0, -1.0,
-                               uncertainty_gamma, uncertainty_gamma_min, True)
+                               uncertainty_gamma, uncertainty_gamma_min, True, num_gts)
 
 
 def _label_cost(logits, targets, background_index, scale, gamma, alpha, softmax, name):

@@ -334,6 +334,11 @@ def test_standalone_pairwise_mask_ops_against_oracle():
     dice = ops.forward_pw_dice_loss(x.to(DEV), t.to(DEV), 1.0, 0, 3.0, 1.0, 0.05)
     close(sce.cpu().numpy(), ref[0], what="sigmoid-ce")
     close(dice.cpu().numpy(), ref[1], what="dice")
+    # with the GT count passed in (no host read of the targets): the same values
+    sce2 = ops.forward_pw_sigmoid_ce_loss(x.to(DEV), t.to(DEV), 0, 3.0, 0.0, -1.0, 1.0, 0.05, True,
+                                          num_gts=gt_total)
+    dice2 = ops.forward_pw_dice_loss(x.to(DEV), t.to(DEV), 1.0, 0, 3.0, 1.0, 0.05, num_gts=gt_total)
+    assert torch.equal(sce2, sce) and torch.equal(dice2, dice)
 
 
 @pytest.mark.parametrize("dt", ["bf16", "fp16"])
