@@ -357,7 +357,7 @@ int launch_cost_t(const FwdPlan& P, const CUtensorMap& tm, const CostArgs& a, cu
     if (e != cudaSuccess) return cuda_fail(e, "cost_partial_kernel attributes");
     dim3 grid(P.nchunk, P.nqt, P.L * P.B);
     ProfScope prof(0, st);
-    k<<<grid, 2 * P.qrows_pad + 32, P.cost_smem, st>>>(tm, a);
+    launch_pdl(k, grid, dim3(2 * P.qrows_pad + 32), P.cost_smem, st, tm, a);
     ML_CHECK_LAUNCH("cost_partial_kernel");
     return ML_OK;
 }
@@ -443,13 +443,13 @@ int run_finalize(const FwdPlan& P, CostArgs& a, cudaStream_t st) {
     const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
     const unsigned rb = (unsigned)((LBQ * 32 + 255) / 256);
     ProfScope prof(4, st);
-    if (P.unc) cost_rows_kernel<true, false><<<rb, 256, 0, st>>>(a);
-    else if (P.foc) cost_rows_kernel<false, false><<<rb, 256, 0, st>>>(a);
-    else cost_rows_kernel<false, true><<<rb, 256, 0, st>>>(a);
+    if (P.unc) launch_pdl(cost_rows_kernel<true, false>, dim3(rb), dim3(256), 0, st, a);
+    else if (P.foc) launch_pdl(cost_rows_kernel<false, false>, dim3(rb), dim3(256), 0, st, a);
+    else launch_pdl(cost_rows_kernel<false, true>, dim3(rb), dim3(256), 0, st, a);
     ML_CHECK_LAUNCH("cost_rows_kernel");
     dim3 pg((unsigned)((P.qrows * P.gout + 31) / 32), P.nqt, P.L * P.B);
-    if (P.unc) cost_pairs_kernel<true><<<pg, 256, 0, st>>>(a);
-    else cost_pairs_kernel<false><<<pg, 256, 0, st>>>(a);
+    if (P.unc) launch_pdl(cost_pairs_kernel<true>, dim3(pg), dim3(256), 0, st, a);
+    else launch_pdl(cost_pairs_kernel<false>, dim3(pg), dim3(256), 0, st, a);
     ML_CHECK_LAUNCH("cost_pairs_kernel");
     return ML_OK;
 }
@@ -538,7 +538,7 @@ int launch_match(const CT* costs, int64_t N, int64_t Q, int64_t G, double thr, i
     if (e != cudaSuccess) return cuda_fail(e, "match_kernel attributes");
     {
         ProfScope prof(2, st);
-        k<<<(unsigned)N, threads, smem, st>>>(a);
+        launch_pdl(k, dim3((unsigned)N), dim3(threads), smem, st, a);
     }
     ML_CHECK_LAUNCH("match_kernel");
     return ML_OK;
@@ -931,7 +931,7 @@ static int mask_matching_impl(const ml_dims* d, const ml_params* p, const float*
     }
     {
         ProfScope prof(5, st);
-        loss_fwd_kernel<<<P.L, 1024, 0, st>>>(la);
+        launch_pdl(loss_fwd_kernel, dim3(P.L), dim3(1024), 0, st, la);
     }
     ML_CHECK_LAUNCH("loss_fwd_kernel");
     return ML_OK;
@@ -1055,7 +1055,7 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
     // coefficients + class-logit gradient first; the mask gradient reads coef
     {
         ProfScope prof(6, st);
-        bwd_cls_kernel<<<(unsigned)((LBQ + 7) / 8), 256, 0, st>>>(la);
+        launch_pdl(bwd_cls_kernel, dim3((unsigned)((LBQ + 7) / 8)), dim3(256), 0, st, la);
     }
     ML_CHECK_LAUNCH("bwd_cls_kernel");
     const bool unc = p->uncertainty_gamma != 0.0f;
@@ -1084,7 +1084,7 @@ static int backward_impl(const ml_dims* d, const ml_params* p, const float* grad
     const int nchunk = (int)((HW + ck - 1) / ck);
     dim3 gg((unsigned)LBQ, nchunk);
     const size_t gs = 0;
-#define ML_MG(U, F, V) mask_grad_kernel<U, F, V, T><<<gg, 256, gs, st>>>(la)
+#define ML_MG(U, F, V) launch_pdl(mask_grad_kernel<U, F, V, T>, dim3(gg), dim3(256), gs, st, la)
     {
     ProfScope prof(1, st);
     with_logit_type(ldt, [&](auto tag) -> int {
@@ -1273,7 +1273,7 @@ int ml_mask_matching_sampled(const ml_dims* d, const ml_params* p, int64_t num_p
     }
     {
         ProfScope prof(5, st);
-        loss_fwd_kernel<<<P.L, 1024, 0, st>>>(la);
+        launch_pdl(loss_fwd_kernel, dim3(P.L), dim3(1024), 0, st, la);
     }
     ML_CHECK_LAUNCH("loss_fwd_kernel");
     return ML_OK;
@@ -1325,7 +1325,7 @@ int ml_mask_matching_sampled_backward(const ml_dims* d, const ml_params* p, int6
     // coefficients + class-logit gradient first; the mask gradient reads coef
     {
         ProfScope prof(6, st);
-        bwd_cls_kernel<<<(unsigned)((LBQ + 7) / 8), 256, 0, st>>>(la);
+        launch_pdl(bwd_cls_kernel, dim3((unsigned)((LBQ + 7) / 8)), dim3(256), 0, st, la);
     }
     ML_CHECK_LAUNCH("bwd_cls_kernel");
     const bool foc = p->mask_gamma > 0.0f || p->mask_alpha >= 0.0f;

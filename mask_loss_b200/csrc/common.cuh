@@ -289,4 +289,27 @@ ML_INLINE void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes, ui
         ::"r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+// Programmatic dependent launch.  Kernels of the forward/backward chain are
+// launched with launch_pdl, so a kernel's blocks can be scheduled while the
+// previous kernel drains; pdl_enter, each such kernel's first statement,
+// waits until the previous grid has completed and its writes are visible
+// (a no-op when the kernel was launched without the attribute).  No kernel
+// triggers its dependents early: measured on B200, an early trigger made
+// the cfg2 step slower (0.2346 -> 0.2371 ms), the implicit trigger at block
+// exit faster (0.2344 -> 0.2316 ms).
+ML_INLINE void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t c = {};
+    c.gridDim = g; c.blockDim = b; c.dynamicSmemBytes = smem; c.stream = st;
+    c.attrs = at; c.numAttrs = 1;
+    return cudaLaunchKernelEx(&c, k, static_cast<KArgs>(args)...);
+}
+
 }  // namespace mlb

@@ -395,6 +395,7 @@ template <typename T> struct Tile {
 template <bool UNC, bool FOC, bool TMA, bool MIX, typename T>
 __global__ void __launch_bounds__(kCostThreads, (MIX && !UNC && !FOC) ? 3 : 2)
 cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
+    pdl_enter();
     constexpr int NACC = UNC ? 3 : 2;
     constexpr int NROW = UNC ? 5 : 3;
     constexpr bool FAST = !UNC && !FOC;
@@ -697,6 +698,7 @@ cost_partial_kernel(const __grid_constant__ CUtensorMap tmap, CostArgs a) {
 // ---------------------------------------------------------------------------
 template <bool UNC, bool FAST>
 __global__ void __launch_bounds__(256) cost_rows_kernel(CostArgs a) {
+    pdl_enter();
     constexpr int NACC = UNC ? 3 : 2;
     constexpr int NROW = UNC ? 5 : 3;
     const int64_t qi = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -784,6 +786,7 @@ __global__ void __launch_bounds__(256) cost_rows_kernel(CostArgs a) {
 // ---------------------------------------------------------------------------
 template <bool UNC>
 __global__ void __launch_bounds__(256) cost_pairs_kernel(CostArgs a) {
+    pdl_enter();
     constexpr int NACC = UNC ? 3 : 2;
     __shared__ float red[8][NACC][32];
     const int qt = blockIdx.y, lb = blockIdx.z, b = lb % a.B;

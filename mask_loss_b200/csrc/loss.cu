@@ -68,6 +68,7 @@ ML_INLINE void denominators(const LossArgs& a, float matched, float* md, float* 
 // Forward: grid = L, block = 1024.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) loss_fwd_kernel(LossArgs a) {
+    pdl_enter();
     __shared__ float sh[32 * 4];
     const int l = blockIdx.x;
     if (a.void_status && l == 0) {  // functions/mask/matching.py:180-181
@@ -214,6 +215,7 @@ __global__ void __launch_bounds__(256) bwd_stats_kernel(LossArgs a) {
 // ---------------------------------------------------------------------------
 template <bool UNC, bool FOC, bool VEC, typename LT>
 __global__ void __launch_bounds__(256) mask_grad_kernel(LossArgs a) {
+    pdl_enter();
     const int64_t qi = blockIdx.x;
     const int lb = (int)(qi / a.Q), l = lb / a.B, b = lb % a.B;
     const int HW = a.H * a.W;
@@ -397,6 +399,7 @@ ML_INLINE void cls_grad_row(const LossArgs& a, int64_t qi, int lane, float base)
 // coef[l] for mask_grad_kernel, which runs after it.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) bwd_cls_kernel(LossArgs a) {
+    pdl_enter();
     __shared__ float sh[32];
     __shared__ float scoef[8][3];
     const int64_t rows = (int64_t)a.L * a.B * a.Q;

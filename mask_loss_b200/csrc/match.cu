@@ -394,6 +394,7 @@ ML_INLINE int warp_compact(int n, F flag, int* out, const int* in) {
 // copy in double for the solver.
 template <typename CT>
 __global__ void __launch_bounds__(kMatchMaxThreads) match_kernel(MatchArgs<CT> a) {
+    pdl_enter();
     extern __shared__ __align__(16) unsigned char msh[];
     __shared__ BlkShared sh;
     __shared__ int sh_n, failed;
