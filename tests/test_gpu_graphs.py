@@ -111,3 +111,31 @@ def test_void_class_in_targets_raises_deferred():
     step.replay()
     with pytest.raises(RuntimeError, match="void class index"):
         step.check()
+
+
+@pytest.mark.parametrize("opt", ["zero_fill_beside_solver"])
+@pytest.mark.parametrize("cname,dtype", [("cfg1", torch.float32), ("cfg3", torch.bfloat16)])
+def test_graph_step_with_the_gradient_zeroed_early(opt, cname, dtype):
+    # the mask gradient zeroed on a side stream beside the solver and then
+    # written only on the rows the loss reaches: the
+    # same results as the default step, bit for bit, over replays whose
+    # matched rows change (the buffer keeps no stale rows)
+    cfg = synthetic.CONFIGS[cname]
+    b = synthetic.make_batch(cfg, images=[0, 1], device=DEV)
+    ml, mt, cl, ct = (b[k].contiguous() for k in ("mask_logits", "mask_targets", "cls_logits",
+                                                  "cls_targets"))
+    ml = ml.to(dtype)
+    args = _args(cfg)
+    ref = MatchingLossStep(ml.clone(), mt.clone(), cl.clone(), ct.clone(), *args)
+    alt = MatchingLossStep(ml.clone(), mt.clone(), cl.clone(), ct.clone(), *args, **{opt: True})
+    for scale in (1.0, -0.7):
+        for s in (ref, alt):
+            s.inputs["mask_logits"].copy_(ml * scale)
+            s.replay()
+        torch.cuda.synchronize()
+        ref.check()
+        alt.check()
+        assert torch.equal(alt.pred_to_gt, ref.pred_to_gt)
+        assert torch.equal(alt.losses, ref.losses)
+        assert torch.equal(alt.grad_mask_logits, ref.grad_mask_logits)
+        assert torch.equal(alt.grad_cls_logits, ref.grad_cls_logits)
