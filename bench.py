@@ -508,15 +508,23 @@ def run_ours(args, cfg):
     # roofline of the dominant kernel: the streaming cost kernel reads every
     # logit once plus one int32 code per cell and image
     cells = synthetic.CFG3_POINTS if sampled else cfg.H * cfg.W  # sampled values are fp32
-    # dense targets run on the tensor-core kernel unless MASK_LOSS_B200_DENSE_MMA=0
-    # (the bench's settings have no entropy weights or focal terms, GT_out <= 64)
-    dense_kernel = ("dense_cost_kernel" if os.environ.get("MASK_LOSS_B200_DENSE_MMA", "1")[:1] == "0"
-                    else "dense_mma_kernel")
+    # dense targets run on the tensor-core kernels unless MASK_LOSS_B200_DENSE_MMA=0
+    # (the bench's settings have no entropy weights or focal terms, GT_out <= 64):
+    # fp32 logits with GT_total <= 32 on the kind::tf32 one (fp32 counts, unless
+    # MASK_LOSS_B200_DENSE_TF32=0), else the bf16 one (bf16 counts)
+    count_bytes = 2
+    if os.environ.get("MASK_LOSS_B200_DENSE_MMA", "1")[:1] == "0":
+        dense_kernel = "dense_cost_kernel"
+    elif (half is None and (GT_total + 15) // 16 * 16 <= 32 and
+          os.environ.get("MASK_LOSS_B200_DENSE_TF32", "1")[:1] != "0"):
+        dense_kernel, count_bytes = "dense_mma_tf32_kernel", 4
+    else:
+        dense_kernel = "dense_mma_kernel"
     cost_kernel = dense_kernel if dense else "cost_partial_kernel"
-    # dense: every logit plus each GT's uint16 count per cell
+    # dense: every logit plus each GT's count per cell
     esize = 2 if (half is not None and not sampled) else 4
     cost_bytes = (cfg.L * cfg.B * cfg.Q * cells * esize +
-                  (cfg.B * cells * (GT_total - 1) * 2 if dense else cfg.B * cells * 4))
+                  (cfg.B * cells * (GT_total - 1) * count_bytes if dense else cfg.B * cells * 4))
     cost_ms = float(kms[0] / max(kn[0], 1))
     achieved = cost_bytes / (cost_ms / 1e3) / 1e9
     traffic = read_traffic(cfg.name, cost_kernel)

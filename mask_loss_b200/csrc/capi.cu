@@ -85,6 +85,12 @@ const bool g_dense_mma_off = [] {
     const char* v = getenv("MASK_LOSS_B200_DENSE_MMA");
     return v && v[0] == '0';
 }();
+// fp32 logits run on the kind::tf32 kernel (GT_total <= 32);
+// MASK_LOSS_B200_DENSE_TF32=0 keeps them on the bf16 hi/lo one.
+const bool g_dense_tf32_off = [] {
+    const char* v = getenv("MASK_LOSS_B200_DENSE_TF32");
+    return v && v[0] == '0';
+}();
 
 // Raise a kernel's dynamic shared-memory limit once per (kernel, device);
 // later calls with the same or a smaller size touch no CUDA API (so they are
@@ -456,25 +462,29 @@ int run_finalize(const FwdPlan& P, CostArgs& a, cudaStream_t st) {
 
 // Dense per-GT masks: counts + areas, then the dense cost kernel, then the
 // same finalize.  The counts live after the plan's workspace.
+// Counts take 4 bytes a cell and GT (fp32 for the tf32 kernel; the bf16
+// forms use the first half).
 size_t dense_count_bytes(const FwdPlan& P) {
-    return align256(sizeof(uint16_t) * (size_t)P.B * P.H * P.W * std::max(P.gt_total, 1));
+    return align256(sizeof(float) * (size_t)P.B * P.H * P.W * std::max(P.gt_total, 1));
 }
 
-// 2-D tensor map over the dense counts (bf16 bit patterns, rows = B*GT_total
-// GT planes, columns = H*W cells): boxes of 32 cells x the MMA's N rows, the
-// 64-byte swizzle the tensor-core kernel's B descriptor expects.
-bool counts_tensor_map(const FwdPlan& P, const uint16_t* cnt, CUtensorMap* km) {
+// 2-D tensor map over the dense counts (rows = B*GT_total GT planes, columns
+// = H*W cells): boxes of 32 cells x the MMA's N rows; bf16 bit patterns with
+// the 64-byte swizzle (bf16 tensor-core kernel) or fp32 with the 128-byte
+// one (tf32 kernel), the layouts their B descriptors expect.
+bool counts_tensor_map(const FwdPlan& P, const void* cnt, CUtensorMap* km, bool f32) {
     memset(km, 0, sizeof(*km));
     const int HW = P.H * P.W;
     if (HW % 8 != 0 || (reinterpret_cast<uintptr_t>(cnt) % 16) != 0) return false;
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)HW, (cuuint64_t)P.B * P.gt_total};
-    const cuuint64_t strides[1] = {(cuuint64_t)HW * 2};
+    const cuuint64_t strides[1] = {(cuuint64_t)HW * (f32 ? 4 : 2)};
     const cuuint32_t box[2] = {32u, (cuuint32_t)dense_mma_n(P.gt_total)};
     const cuuint32_t es[2] = {1, 1};
-    CUresult r = enc(km, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(cnt), dims,
-                     strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+    CUresult r = enc(km, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                     const_cast<void*>(cnt), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -485,22 +495,27 @@ int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigne
                                     sizeof(int32_t) * (size_t)P.B * P.gt_total, st);
     if (e != cudaSuccess) return cuda_fail(e, "memset mask areas");
     uint16_t* cnt = reinterpret_cast<uint16_t*>(ws + (P.bytes - 256));
+    const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
+    // which cost kernel, before the counts are written in its format
+    CUtensorMap tm, km;
+    const bool mma = LBQ > 0 && P.gout > 0 && !g_dense_mma_off && logits_tensor_map(P, a.logits, &tm) &&
+                     dense_mma_usable(a, P.ldt, P.unc, P.foc, true);
+    const bool tf32 = mma && !g_dense_tf32_off && dense_mma_tf32_usable(a, P.ldt);
     if (P.B > 0 && P.gt_total > 0) {
         e = launch_dense_count(masks, P.B, P.H, P.W, P.Ht, P.Wt, P.s, P.gt_total, cnt,
-                               const_cast<int32_t*>(a.totals), st);
+                               const_cast<int32_t*>(a.totals), st, tf32);
         g_launches.fetch_add(1);
         if (e != cudaSuccess) return cuda_fail(e, "dense_count_kernel");
     }
-    const int64_t LBQ = (int64_t)P.L * P.B * P.Q;
     if (LBQ == 0 || P.gout == 0) return ML_OK;
     {
         ProfScope prof(0, st);  // profiled as the cost stage
-        CUtensorMap tm, km;
-        bool mma = !g_dense_mma_off && logits_tensor_map(P, a.logits, &tm) &&
-                   dense_mma_usable(a, P.ldt, P.unc, P.foc, true) &&
-                   counts_tensor_map(P, cnt, &km);
-        if (mma)
-            e = launch_dense_mma(tm, km, a, st, P.ldt);  // tensor cores (tcgen05)
+        if (tf32 && counts_tensor_map(P, cnt, &km, true))
+            e = launch_dense_mma_tf32(tm, km, a, st);   // tensor cores, kind::tf32
+        else if (mma && !tf32 && counts_tensor_map(P, cnt, &km, false))
+            e = launch_dense_mma(tm, km, a, st, P.ldt);  // tensor cores, kind::f16
+        else if (tf32)
+            return fail(ML_EINVAL, "dense counts tensor map could not be encoded");
         else
             e = launch_dense_cost(a, P.unc, P.foc, cnt, st, P.ldt);
     }

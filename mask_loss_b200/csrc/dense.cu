@@ -37,9 +37,11 @@ constexpr int kDenseGC = 64;     // GT columns per block (grid chunk)
 
 // grid = (ceil(HW / 256), B), block 256: thread per cell; eight GT planes'
 // loads in flight per thread, areas summed per warp.
+// F32: counts as fp32 (the tf32 tensor-core kernel's B operand), else bf16 bits.
+template <bool F32>
 __global__ void __launch_bounds__(256)
 dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int Wt, int s,
-                   int gt_total, uint16_t* __restrict__ cnt, int32_t* __restrict__ totals) {
+                   int gt_total, void* __restrict__ cnt_out, int32_t* __restrict__ totals) {
     extern __shared__ int32_t area[];  // [gt_total]
     const int b = blockIdx.y;
     const int HW = H * W;
@@ -69,7 +71,11 @@ dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int 
         for (int u = 0; u < 8; ++u) {
             const int g = g0 + u;
             if (g >= gt_total) break;
-            if (valid) cnt[((int64_t)b * gt_total + g) * HW + cell] = count_bits((float)n[u]);
+            if (valid) {
+                const int64_t o = ((int64_t)b * gt_total + g) * HW + cell;
+                if (F32) static_cast<float*>(cnt_out)[o] = (float)n[u];
+                else static_cast<uint16_t*>(cnt_out)[o] = count_bits((float)n[u]);
+            }
             const int sum = (int)__reduce_add_sync(0xffffffffu, (unsigned)n[u]);
             if ((threadIdx.x & 31) == 0 && sum) atomicAdd(&area[g], sum);
         }
@@ -82,9 +88,10 @@ dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int 
 // s = 1 (one mask pixel per cell), H*W a multiple of 8: eight cells per
 // thread, one 8-byte mask load and one 16-byte count store per GT plane,
 // four planes in flight.  grid = (ceil(H*W / 2048), B), block 256.
+template <bool F32>
 __global__ void __launch_bounds__(256)
 dense_count_s1_kernel(const uint8_t* __restrict__ masks, int HW, int gt_total,
-                      uint16_t* __restrict__ cnt, int32_t* __restrict__ totals) {
+                      void* __restrict__ cnt_out, int32_t* __restrict__ totals) {
     extern __shared__ int32_t area[];  // [gt_total]
     const int b = blockIdx.y;
     for (int g = threadIdx.x; g < gt_total; g += blockDim.x) area[g] = 0;
@@ -113,9 +120,23 @@ dense_count_s1_kernel(const uint8_t* __restrict__ masks, int HW, int gt_total,
                 w[k] = ((nz0 >> (16 * k)) & 1u ? one : 0u) | ((nz0 >> (16 * k + 8)) & 1u ? one << 16 : 0u);
                 w[2 + k] = ((nz1 >> (16 * k)) & 1u ? one : 0u) | ((nz1 >> (16 * k + 8)) & 1u ? one << 16 : 0u);
             }
-            if (valid)
-                *reinterpret_cast<uint4*>(cnt + ((int64_t)b * gt_total + g) * HW + cell0) =
-                    make_uint4(w[0], w[1], w[2], w[3]);
+            if (valid) {
+                const int64_t o = ((int64_t)b * gt_total + g) * HW + cell0;
+                if (F32) {
+                    float c8[8];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        c8[k] = (nz0 >> (8 * k)) & 1u ? 1.0f : 0.0f;
+                        c8[4 + k] = (nz1 >> (8 * k)) & 1u ? 1.0f : 0.0f;
+                    }
+                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(cnt_out) + o);
+                    dst[0] = make_float4(c8[0], c8[1], c8[2], c8[3]);
+                    dst[1] = make_float4(c8[4], c8[5], c8[6], c8[7]);
+                } else {
+                    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(cnt_out) + o) =
+                        make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
             const int n = (__popc(nz0) + __popc(nz1)) >> 3;
             const int sum = (int)__reduce_add_sync(0xffffffffu, (unsigned)n);
             if ((threadIdx.x & 31) == 0 && sum) atomicAdd(&area[g], sum);
@@ -365,18 +386,19 @@ size_t dense_cost_smem(int qrows_pad, bool unc, int gc) {
 }
 
 cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht, int Wt, int s,
-                               int gt_total, uint16_t* cnt, int32_t* totals, cudaStream_t st) {
+                               int gt_total, void* cnt, int32_t* totals, cudaStream_t st, bool f32) {
     const int HW = H * W;
+    const size_t hs = sizeof(int32_t) * (size_t)std::max(gt_total, 1);
     if (s == 1 && HW % 8 == 0 && (reinterpret_cast<uintptr_t>(masks) & 7) == 0 &&
         (reinterpret_cast<uintptr_t>(cnt) & 15) == 0) {
         dim3 g((HW / 8 + 255) / 256, B);
-        dense_count_s1_kernel<<<g, 256, sizeof(int32_t) * (size_t)std::max(gt_total, 1), st>>>(
-            masks, HW, gt_total, cnt, totals);
+        if (f32) dense_count_s1_kernel<true><<<g, 256, hs, st>>>(masks, HW, gt_total, cnt, totals);
+        else dense_count_s1_kernel<false><<<g, 256, hs, st>>>(masks, HW, gt_total, cnt, totals);
         return cudaGetLastError();
     }
     dim3 g((HW + 255) / 256, B);
-    dense_count_kernel<<<g, 256, sizeof(int32_t) * (size_t)std::max(gt_total, 1), st>>>(
-        masks, H, W, Ht, Wt, s, gt_total, cnt, totals);
+    if (f32) dense_count_kernel<true><<<g, 256, hs, st>>>(masks, H, W, Ht, Wt, s, gt_total, cnt, totals);
+    else dense_count_kernel<false><<<g, 256, hs, st>>>(masks, H, W, Ht, Wt, s, gt_total, cnt, totals);
     return cudaGetLastError();
 }
 

@@ -125,6 +125,51 @@ ML_INLINE uint32_t pack_bf16(float lo, float hi) {
 ML_INLINE float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 ML_INLINE float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// The kind::tf32 forms (fp32 logits): D[tmem] (+)= A x B^T with A from TMEM
+// (ts) or shared memory (ss), B from shared memory, 32-bit operands of
+// which the tensor core uses the tf32 part.
+ML_INLINE void umma_ts_tf32(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                            bool accumulate) {
+    const uint32_t acc = accumulate ? 1u : 0u;
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc) : "memory");
+}
+ML_INLINE void umma_ss_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                            bool accumulate) {
+    const uint32_t acc = accumulate ? 1u : 0u;
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc) : "memory");
+}
+// K-major, 128-byte swizzle (rows of 32 fp32; 8-row atoms of 1024 bytes, so
+// SBO = 1024; LBO unused, 1): the layout a TMA box with
+// CU_TENSOR_MAP_SWIZZLE_128B writes.  Layout type 2 [61,64).
+ML_INLINE uint64_t smem_desc_sw128(const void* p) {
+    const uint64_t a = (uint64_t)((smem_u32(p) >> 4) & 0x3FFFu);
+    return a | (1ull << 16) | ((uint64_t)(1024u >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+// kind::tf32 instruction descriptor: tf32 A and B (K-major), fp32 D, M = 128.
+ML_INLINE uint32_t idesc_tf32_f32(int n) {
+    return (1u << 4)             // D format: f32
+           | (2u << 7)           // A format: tf32
+           | (2u << 10)          // B format: tf32
+           | ((uint32_t)(n >> 3) << 17)
+           | ((uint32_t)(128 >> 4) << 24);
+}
+// sixteen 32-bit columns of this warp's 32 lanes
+ML_INLINE void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, "
+                 "%9, %10, %11, %12, %13, %14, %15, %16};"
+                 ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]),
+                   "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]),
+                   "r"(v[13]), "r"(v[14]), "r"(v[15]) : "memory");
+}
+// the tf32 part of x (the low 13 mantissa bits cleared) and its remainder
+ML_INLINE float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+
 struct MmaShared {
     uint64_t full[kTmaStages];    // logits and counts of the stage landed (TMA)
     uint64_t aready[kMmaStages];  // A operands of the TMEM stage written
@@ -393,6 +438,226 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
     }
 }
 
+// fp32 logits on kind::tf32.  The same tiling, rings and epilogue as
+// dense_mma_kernel, with the operands split the tf32 way:
+//   * D += x_hi k + x_lo k: x_hi is the logits tile itself -- the producers
+//     clear the low 13 mantissa bits of each value in place (so the tensor
+//     core's tf32 read is exact whatever its rounding) and the MMA takes it
+//     straight from shared memory; x_lo = x - x_hi goes to TMEM;
+//   * I += p_hi k + p_lo k, both from TMEM (p_hi with the low bits cleared);
+//   * B: the counts as fp32 (exact), N rows of 128 bytes, 128-byte swizzle.
+// Per logit the producers thus do a sigmoid, two splits and the row sums;
+// the bf16 kernel's four operand conversions become one in-place mask.
+// |x - x_hi - tf32(x_lo)| <= 2^-21 |x|, likewise for p.
+// TMEM: 2N accumulator columns + 2 stages x 3 operands x 32 columns <= 256
+// (N <= 32), so two CTAs share an SM.
+__global__ void __launch_bounds__(kMmaThreads, 2)
+dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap kmap,
+                      CostArgs a, int N) {
+    extern __shared__ __align__(1024) unsigned char dsm_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+    constexpr uint32_t kXStage = 128u * kMmaK * 4u;   // logits [128][32] fp32 per stage
+    const uint32_t bstage = ((uint32_t)N * 128u + 1023u) / 1024u * 1024u;
+    float* xs = reinterpret_cast<float*>(base);                               // [stage][128][32]
+    unsigned char* bs = base + kTmaStages * kXStage;                          // [stage][N][32] fp32
+    MmaShared* sh = reinterpret_cast<MmaShared*>(bs + kTmaStages * bstage);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int slot = blockIdx.x, chunk = slot >> 1, half = slot & 1;
+    const int qt = blockIdx.y, lb = blockIdx.z, b = lb % a.B;
+    const int HW = a.H * a.W, G = a.gout, NG = a.gt_total;
+    const int half_cells = a.chunk_cells / 2;
+    const int cb = min(HW, chunk * a.chunk_cells + half * half_cells);
+    const int ce = min(HW, cb + half_cells);
+    const int nkb = (ce - cb + kMmaK - 1) / kMmaK;
+    const int row0 = lb * a.Q + qt * a.qrows;
+    const uint32_t cols_acc = 2u * N;
+
+    if (tid == 0) {
+        for (int i = 0; i < kTmaStages; ++i) {
+            mbar_init(&sh->full[i], 1);
+            mbar_init(&sh->mdone[i], 1);
+        }
+        for (int i = 0; i < kMmaStages; ++i) mbar_init(&sh->aready[i], kMmaProducers);
+        mbar_init(&sh->accf, 1);
+        sh->err = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaProducers) {
+        tmem_alloc(&sh->tmem_base, kMmaTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = sh->tmem_base;
+    // TMEM columns: D [0, N), I [N, 2N), then stage s operand o at 2N + (3s + o) * 32
+    auto a_col = [&](int s, int o) { return tbase + cols_acc + (uint32_t)((3 * s + o) * 32); };
+
+    if (warp == kMmaProducers) {
+        // ------------------------------ control warp ------------------------------
+        if (lane == 0) {
+            bool ok = true;
+            const uint32_t idesc = idesc_tf32_f32(N);
+            auto issue_tma = [&](int kb) {
+                const int s = kb % kTmaStages;
+                mbar_arrive_expect_tx(&sh->full[s], (uint32_t)a.qrows * kMmaK * 4u + (uint32_t)N * kMmaK * 4u);
+                const int c0 = cb + kb * kMmaK;
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+                    " [%0], [%1, {%2, %3}], [%4];"
+                    ::"r"(smem_u32(reinterpret_cast<unsigned char*>(xs) + s * kXStage)), "l"(&tmap),
+                      "r"(c0), "r"(row0), "r"(smem_u32(&sh->full[s])) : "memory");
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+                    " [%0], [%1, {%2, %3}], [%4];"
+                    ::"r"(smem_u32(bs + s * bstage)), "l"(&kmap), "r"(c0), "r"(b * NG),
+                      "r"(smem_u32(&sh->full[s])) : "memory");
+            };
+            for (int kb = 0; kb < min(nkb, kTmaStages); ++kb) issue_tma(kb);
+            for (int kb = 0; kb < nkb && ok; ++kb) {
+                const int s = kb % kTmaStages;
+                const int ts = kb % kMmaStages;
+                if (!mbar_wait(&sh->aready[ts], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {  // K = 8 cells (32 bytes of a row) per MMA
+                    const uint64_t ad =
+                        smem_desc_sw128(reinterpret_cast<unsigned char*>(xs) + s * kXStage + 32 * kk);
+                    const uint64_t bd = smem_desc_sw128(bs + s * bstage + 32 * kk);
+                    const bool acc = kb > 0 || kk > 0;
+                    umma_ss_tf32(tbase, ad, bd, idesc, acc);                      // D += x_hi k
+                    umma_ts_tf32(tbase, a_col(ts, 0) + 8 * kk, bd, idesc, true);  // D += x_lo k
+                    umma_ts_tf32(tbase + N, a_col(ts, 1) + 8 * kk, bd, idesc, acc);  // I += p_hi k
+                    umma_ts_tf32(tbase + N, a_col(ts, 2) + 8 * kk, bd, idesc, true); // I += p_lo k
+                }
+                umma_commit(&sh->mdone[s]);
+                const int kp = kb - 1;
+                if (kp >= 0 && kp + kTmaStages < nkb) {
+                    if (!mbar_wait(&sh->mdone[kp % kTmaStages], (uint32_t)((kp / kTmaStages) & 1))) {
+                        ok = false;
+                        break;
+                    }
+                    issue_tma(kp + kTmaStages);
+                }
+            }
+            if (ok && nkb > 0) umma_commit(&sh->accf);
+            if (!ok) {
+                sh->err = 1;
+                if (a.status) atomicOr(a.status, 2);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------ producer warps ------------------------------
+        const int r = 32 * (warp & 3) + lane;      // query row of the tile (TMEM lane)
+        const int kh = warp >> 2;                  // cells [16 kh, 16 kh + 16) of each block
+        const bool rvalid = r < a.qrows && qt * a.qrows + r < a.Q;
+        const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
+        float rsum[3] = {0.0f, 0.0f, 0.0f};        // sum max(x,0), sum p, sum log2(1+e)
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+            const int s = kb % kTmaStages;
+            const int ts = kb % kMmaStages;
+            const int c0 = cb + kb * kMmaK;
+            const int nv = min(kMmaK, ce - c0);
+            if (kb >= kMmaStages) {
+                const int kq = kb - kMmaStages;
+                if (!mbar_wait(&sh->mdone[kq % kTmaStages], (uint32_t)((kq / kTmaStages) & 1))) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (!mbar_wait(&sh->full[s], (uint32_t)((kb / kTmaStages) & 1))) { ok = false; break; }
+            float* xr = xs + (size_t)s * (kXStage / 4) + r * kMmaK;   // row r: 128 swizzled bytes
+            uint32_t xl[16], ph[16], pl[16];
+            float prod = 1.0f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {  // four 16-byte granules = 16 cells
+                float4* gp = reinterpret_cast<float4*>(xr + (((4 * kh + u) ^ (r & 7)) << 2));
+                const float4 v = *gp;
+                const float xv[4] = {v.x, v.y, v.z, v.w};
+                float xt[4];
+#pragma unroll
+                for (int e4 = 0; e4 < 4; ++e4) {
+                    const float x = xv[e4];
+                    xt[e4] = tf32_hi(x);
+                    const Fast f = fast_elem(x);
+                    const float pt = tf32_hi(f.p);
+                    xl[4 * u + e4] = __float_as_uint(x - xt[e4]);
+                    ph[4 * u + e4] = __float_as_uint(pt);
+                    pl[4 * u + e4] = __float_as_uint(f.p - pt);
+                    if (rvalid && 16 * kh + 4 * u + e4 < nv) {
+                        rsum[0] += fmaxf(x, 0.0f);
+                        rsum[1] += f.p;
+                        prod *= f.d;
+                    }
+                }
+                *gp = make_float4(xt[0], xt[1], xt[2], xt[3]);  // the MMA reads x_hi here
+            }
+            rsum[2] += lg2_approx(prod);  // 16 factors in [1, 2]
+            const uint32_t colk = (uint32_t)(16 * kh);  // 16 fp32 cells = 16 columns
+            tmem_st16(a_col(ts, 0) + lane_off + colk, xl);
+            tmem_st16(a_col(ts, 1) + lane_off + colk, ph);
+            tmem_st16(a_col(ts, 2) + lane_off + colk, pl);
+            tmem_wait_st();
+            fence_proxy_async_smem();  // the in-place x_hi is read by the tensor core
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh->aready[ts]);
+        }
+        if (!ok) {
+            sh->err = 1;
+            if (lane == 0 && a.status) atomicOr(a.status, 2);
+        }
+        // ---- epilogue (as dense_mma_kernel): row sums, then D and I from TMEM ----
+        if (kh == 1) {
+#pragma unroll
+            for (int i = 0; i < 3; ++i) sh->rows[warp & 3][lane][i] = rsum[i];
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kMmaProducers * 32) : "memory");
+        const bool have_acc = ok && nkb > 0 && mbar_wait(&sh->accf, 0u);
+        tc_fence_after();
+        float* part = a.part + ((((int64_t)lb * a.nqt + qt) * a.nchunk + chunk) * 2 + half) *
+                                   (int64_t)a.part_stride;
+        const int QP = a.qrows_pad;
+        const uint32_t acc_base = tbase + lane_off + (kh ? (uint32_t)N : 0u);
+        for (int c0a = 0; c0a < N; c0a += 16) {
+            uint32_t v[16];
+            if (have_acc) {
+                tmem_ld16(acc_base + (uint32_t)c0a, v);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = 0u;
+            }
+            if (rvalid) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int ga = c0a + j;
+                    if (ga < NG && ga != a.bg) {
+                        const int g = ga - (ga > a.bg ? 1 : 0);
+                        const float val = __uint_as_float(v[j]);
+                        part[((int64_t)kh * G + g) * QP + r] = kh ? val : -val;
+                    }
+                }
+            }
+        }
+        if (kh == 0 && rvalid) {
+#pragma unroll
+            for (int i = 0; i < 3; ++i)
+                part[(int64_t)2 * G * QP + (int64_t)i * QP + r] = rsum[i] + sh->rows[warp & 3][lane][i];
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == kMmaProducers) {
+        tc_fence_after();
+        tmem_dealloc(tbase, kMmaTmemCols);
+    }
+}
+
 int dense_mma_n(int gt_total) { return (gt_total + 15) / 16 * 16; }
 
 bool dense_mma_usable(const CostArgs& a, int ldt, bool unc, bool foc, bool tma) {
@@ -419,6 +684,23 @@ cudaError_t launch_dense_mma_t(const CUtensorMap& tm, const CUtensorMap& km, con
     if (e != cudaSuccess) return e;
     dim3 g(a.nchunk * 2, a.nqt, a.L * a.B);
     dense_mma_kernel<T><<<g, kMmaThreads, smem, st>>>(tm, km, a, N);
+    return cudaGetLastError();
+}
+
+bool dense_mma_tf32_usable(const CostArgs& a, int ldt) {
+    return ldt == 0 && dense_mma_n(a.gt_total) <= 32;
+}
+
+cudaError_t launch_dense_mma_tf32(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
+                                  cudaStream_t st) {
+    const int N = dense_mma_n(a.gt_total);
+    const size_t bstage = ((size_t)N * 128 + 1023) / 1024 * 1024;
+    const size_t smem = 1024 + kTmaStages * ((size_t)128 * kMmaK * 4 + bstage) + sizeof(MmaShared);
+    cudaError_t e = cudaFuncSetAttribute(dense_mma_tf32_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 g(a.nchunk * 2, a.nqt, a.L * a.B);
+    dense_mma_tf32_kernel<<<g, kMmaThreads, smem, st>>>(tm, km, a, N);
     return cudaGetLastError();
 }
 

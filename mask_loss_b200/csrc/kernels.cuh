@@ -203,8 +203,9 @@ namespace mlb {
 // Dense per-GT mask targets (dense.cu).
 size_t dense_cost_smem(int qrows_pad, bool unc, int gc);
 int dense_gc(int gout);
+// cnt: [B][GT_total][H*W] counts, bf16 bits (f32 false) or fp32 (f32 true).
 cudaError_t launch_dense_count(const uint8_t* masks, int B, int H, int W, int Ht, int Wt, int s,
-                               int gt_total, uint16_t* cnt, int32_t* totals, cudaStream_t st);
+                               int gt_total, void* cnt, int32_t* totals, cudaStream_t st, bool f32);
 // ldt: mask-logit type (0 fp32, 1 bf16, 2 fp16)
 cudaError_t launch_dense_cost(const CostArgs& a, bool unc, bool foc, const uint16_t* cnt,
                               cudaStream_t st, int ldt);
@@ -217,4 +218,10 @@ int dense_mma_n(int gt_total);  // MMA N: GT_total rounded up to 16
 // with boxes of 32 cells x dense_mma_n(GT_total) rows and the 64-byte swizzle.
 cudaError_t launch_dense_mma(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
                              cudaStream_t st, int ldt);
+// fp32 logits with GT_total <= 32 (and dense_mma_usable): the kind::tf32
+// kernel; km: the counts as fp32 [B*GT_total][H*W], boxes of 32 cells x
+// dense_mma_n(GT_total) rows with the 128-byte swizzle.
+bool dense_mma_tf32_usable(const CostArgs& a, int ldt);
+cudaError_t launch_dense_mma_tf32(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
+                                  cudaStream_t st);
 }  // namespace mlb
