@@ -510,14 +510,17 @@ def run_ours(args, cfg):
     cells = synthetic.CFG3_POINTS if sampled else cfg.H * cfg.W  # sampled values are fp32
     # dense targets run on the tensor-core kernels unless MASK_LOSS_B200_DENSE_MMA=0
     # (the bench's settings have no entropy weights or focal terms, GT_out <= 64):
-    # fp32 logits with GT_total <= 32 on the kind::tf32 one (fp32 counts, unless
+    # fp32 logits with GT_total <= 32 on the kind::tf32 one (unless
     # MASK_LOSS_B200_DENSE_TF32=0), else the bf16 one (bf16 counts)
     count_bytes = 2
     if os.environ.get("MASK_LOSS_B200_DENSE_MMA", "1")[:1] == "0":
         dense_kernel = "dense_cost_kernel"
     elif (half is None and (GT_total + 15) // 16 * 16 <= 32 and
           os.environ.get("MASK_LOSS_B200_DENSE_TF32", "1")[:1] != "0"):
-        dense_kernel, count_bytes = "dense_mma_tf32_kernel", 4
+        # unscaled masks (16-cell rows) are its B source directly: one byte a
+        # cell and GT; else fp32 counts
+        dense_kernel = "dense_mma_tf32_kernel"
+        count_bytes = 1 if (cfg.s == 1 and (cfg.H * cfg.W) % 16 == 0) else 4
     else:
         dense_kernel = "dense_mma_kernel"
     cost_kernel = dense_kernel if dense else "cost_partial_kernel"

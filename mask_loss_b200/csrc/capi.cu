@@ -489,6 +489,25 @@ bool counts_tensor_map(const FwdPlan& P, const void* cnt, CUtensorMap* km, bool 
     return r == CUDA_SUCCESS;
 }
 
+// 2-D tensor map over the uint8 masks themselves (s = 1; rows = B*GT_total
+// planes, columns = H*W cells): boxes of 32 cells x the MMA's N rows, no
+// swizzle -- the tf32 kernel turns them into its fp32 B tile.
+bool masks_tensor_map(const FwdPlan& P, const uint8_t* masks, CUtensorMap* km) {
+    memset(km, 0, sizeof(*km));
+    const int HW = P.H * P.W;
+    if (P.s != 1 || HW % 16 != 0 || (reinterpret_cast<uintptr_t>(masks) % 16) != 0) return false;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)HW, (cuuint64_t)P.B * P.gt_total};
+    const cuuint64_t strides[1] = {(cuuint64_t)HW};
+    const cuuint32_t box[2] = {32u, (cuuint32_t)dense_mma_n(P.gt_total)};
+    const cuuint32_t es[2] = {1, 1};
+    CUresult r = enc(km, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(masks), dims, strides,
+                     box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigned char* ws,
                     cudaStream_t st) {
     cudaError_t e = cudaMemsetAsync(const_cast<int32_t*>(a.totals), 0,
@@ -501,17 +520,22 @@ int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigne
     const bool mma = LBQ > 0 && P.gout > 0 && !g_dense_mma_off && logits_tensor_map(P, a.logits, &tm) &&
                      dense_mma_usable(a, P.ldt, P.unc, P.foc, true);
     const bool tf32 = mma && !g_dense_tf32_off && dense_mma_tf32_usable(a, P.ldt);
+    // s = 1: the tf32 kernel reads the masks themselves; the count pass then
+    // only sums the mask areas
+    const bool masks_b = tf32 && masks_tensor_map(P, masks, &km);
     if (P.B > 0 && P.gt_total > 0) {
-        e = launch_dense_count(masks, P.B, P.H, P.W, P.Ht, P.Wt, P.s, P.gt_total, cnt,
-                               const_cast<int32_t*>(a.totals), st, tf32);
+        e = launch_dense_count(masks, P.B, P.H, P.W, P.Ht, P.Wt, P.s, P.gt_total,
+                               masks_b ? nullptr : cnt, const_cast<int32_t*>(a.totals), st, tf32);
         g_launches.fetch_add(1);
         if (e != cudaSuccess) return cuda_fail(e, "dense_count_kernel");
     }
     if (LBQ == 0 || P.gout == 0) return ML_OK;
     {
         ProfScope prof(0, st);  // profiled as the cost stage
-        if (tf32 && counts_tensor_map(P, cnt, &km, true))
-            e = launch_dense_mma_tf32(tm, km, a, st);   // tensor cores, kind::tf32
+        if (masks_b)
+            e = launch_dense_mma_tf32(tm, km, a, st, true);   // kind::tf32, B from the masks
+        else if (tf32 && counts_tensor_map(P, cnt, &km, true))
+            e = launch_dense_mma_tf32(tm, km, a, st, false);  // kind::tf32, B from fp32 counts
         else if (mma && !tf32 && counts_tensor_map(P, cnt, &km, false))
             e = launch_dense_mma(tm, km, a, st, P.ldt);  // tensor cores, kind::f16
         else if (tf32)

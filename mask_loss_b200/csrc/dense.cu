@@ -71,7 +71,7 @@ dense_count_kernel(const uint8_t* __restrict__ masks, int H, int W, int Ht, int 
         for (int u = 0; u < 8; ++u) {
             const int g = g0 + u;
             if (g >= gt_total) break;
-            if (valid) {
+            if (valid && cnt_out) {  // null: areas only
                 const int64_t o = ((int64_t)b * gt_total + g) * HW + cell;
                 if (F32) static_cast<float*>(cnt_out)[o] = (float)n[u];
                 else static_cast<uint16_t*>(cnt_out)[o] = count_bits((float)n[u]);
@@ -120,7 +120,7 @@ dense_count_s1_kernel(const uint8_t* __restrict__ masks, int HW, int gt_total,
                 w[k] = ((nz0 >> (16 * k)) & 1u ? one : 0u) | ((nz0 >> (16 * k + 8)) & 1u ? one << 16 : 0u);
                 w[2 + k] = ((nz1 >> (16 * k)) & 1u ? one : 0u) | ((nz1 >> (16 * k + 8)) & 1u ? one << 16 : 0u);
             }
-            if (valid) {
+            if (valid && cnt_out) {  // null: areas only
                 const int64_t o = ((int64_t)b * gt_total + g) * HW + cell0;
                 if (F32) {
                     float c8[8];

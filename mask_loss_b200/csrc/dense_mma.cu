@@ -451,6 +451,11 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
 // |x - x_hi - tf32(x_lo)| <= 2^-21 |x|, likewise for p.
 // TMEM: 2N accumulator columns + 2 stages x 3 operands x 32 columns <= 256
 // (N <= 32), so two CTAs share an SM.
+// MASKB (s = 1): kmap covers the uint8 masks themselves ([B*GT_total][H*W],
+// boxes of 32 cells x N rows, no swizzle); the producers turn each block's
+// mask bytes into the fp32 B tile (1.0 where non-zero), so no count planes
+// are written or read.
+template <bool MASKB>
 __global__ void __launch_bounds__(kMmaThreads, 2)
 dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap kmap,
                       CostArgs a, int N) {
@@ -461,7 +466,10 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
     const uint32_t bstage = ((uint32_t)N * 128u + 1023u) / 1024u * 1024u;
     float* xs = reinterpret_cast<float*>(base);                               // [stage][128][32]
     unsigned char* bs = base + kTmaStages * kXStage;                          // [stage][N][32] fp32
-    MmaShared* sh = reinterpret_cast<MmaShared*>(bs + kTmaStages * bstage);
+    // MASKB: the TMA'd mask bytes, [stage][N][32] uint8
+    unsigned char* ms = bs + kTmaStages * bstage;
+    const uint32_t mstage = MASKB ? ((uint32_t)N * 32u + 127u) / 128u * 128u : 0u;
+    MmaShared* sh = reinterpret_cast<MmaShared*>(ms + kTmaStages * mstage);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int slot = blockIdx.x, chunk = slot >> 1, half = slot & 1;
@@ -502,7 +510,8 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
             const uint32_t idesc = idesc_tf32_f32(N);
             auto issue_tma = [&](int kb) {
                 const int s = kb % kTmaStages;
-                mbar_arrive_expect_tx(&sh->full[s], (uint32_t)a.qrows * kMmaK * 4u + (uint32_t)N * kMmaK * 4u);
+                mbar_arrive_expect_tx(&sh->full[s], (uint32_t)a.qrows * kMmaK * 4u +
+                                                        (uint32_t)N * kMmaK * (MASKB ? 1u : 4u));
                 const int c0 = cb + kb * kMmaK;
                 asm volatile(
                     "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
@@ -512,8 +521,8 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
                 asm volatile(
                     "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
                     " [%0], [%1, {%2, %3}], [%4];"
-                    ::"r"(smem_u32(bs + s * bstage)), "l"(&kmap), "r"(c0), "r"(b * NG),
-                      "r"(smem_u32(&sh->full[s])) : "memory");
+                    ::"r"(smem_u32(MASKB ? ms + s * mstage : bs + s * bstage)), "l"(&kmap), "r"(c0),
+                      "r"(b * NG), "r"(smem_u32(&sh->full[s])) : "memory");
             };
             for (int kb = 0; kb < min(nkb, kTmaStages); ++kb) issue_tma(kb);
             for (int kb = 0; kb < nkb && ok; ++kb) {
@@ -596,13 +605,23 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
                 }
                 *gp = make_float4(xt[0], xt[1], xt[2], xt[3]);  // the MMA reads x_hi here
             }
+            if (MASKB) {  // mask bytes -> the fp32 B tile, 4 cells per thread
+                const int pt = warp * 32 + lane;
+                if (pt < N * 8) {
+                    const int n = pt >> 3, g = pt & 7;
+                    const uint32_t m = *reinterpret_cast<const uint32_t*>(ms + s * mstage + n * 32 + g * 4);
+                    *reinterpret_cast<float4*>(bs + s * bstage + n * 128 + ((g ^ (n & 7)) << 4)) =
+                        make_float4((m & 0xFFu) ? 1.0f : 0.0f, (m & 0xFF00u) ? 1.0f : 0.0f,
+                                    (m & 0xFF0000u) ? 1.0f : 0.0f, (m & 0xFF000000u) ? 1.0f : 0.0f);
+                }
+            }
             rsum[2] += lg2_approx(prod);  // 16 factors in [1, 2]
             const uint32_t colk = (uint32_t)(16 * kh);  // 16 fp32 cells = 16 columns
             tmem_st16(a_col(ts, 0) + lane_off + colk, xl);
             tmem_st16(a_col(ts, 1) + lane_off + colk, ph);
             tmem_st16(a_col(ts, 2) + lane_off + colk, pl);
             tmem_wait_st();
-            fence_proxy_async_smem();  // the in-place x_hi is read by the tensor core
+            fence_proxy_async_smem();  // the in-place x_hi (and B tile) are read by the tensor core
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh->aready[ts]);
@@ -692,15 +711,16 @@ bool dense_mma_tf32_usable(const CostArgs& a, int ldt) {
 }
 
 cudaError_t launch_dense_mma_tf32(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
-                                  cudaStream_t st) {
+                                  cudaStream_t st, bool masks_b) {
     const int N = dense_mma_n(a.gt_total);
     const size_t bstage = ((size_t)N * 128 + 1023) / 1024 * 1024;
-    const size_t smem = 1024 + kTmaStages * ((size_t)128 * kMmaK * 4 + bstage) + sizeof(MmaShared);
-    cudaError_t e = cudaFuncSetAttribute(dense_mma_tf32_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t mstage = masks_b ? ((size_t)N * 32 + 127) / 128 * 128 : 0;
+    const size_t smem = 1024 + kTmaStages * ((size_t)128 * kMmaK * 4 + bstage + mstage) + sizeof(MmaShared);
+    auto k = masks_b ? dense_mma_tf32_kernel<true> : dense_mma_tf32_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 g(a.nchunk * 2, a.nqt, a.L * a.B);
-    dense_mma_tf32_kernel<<<g, kMmaThreads, smem, st>>>(tm, km, a, N);
+    k<<<g, kMmaThreads, smem, st>>>(tm, km, a, N);
     return cudaGetLastError();
 }
 

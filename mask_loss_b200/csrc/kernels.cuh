@@ -220,8 +220,9 @@ cudaError_t launch_dense_mma(const CUtensorMap& tm, const CUtensorMap& km, const
                              cudaStream_t st, int ldt);
 // fp32 logits with GT_total <= 32 (and dense_mma_usable): the kind::tf32
 // kernel; km: the counts as fp32 [B*GT_total][H*W], boxes of 32 cells x
-// dense_mma_n(GT_total) rows with the 128-byte swizzle.
+// dense_mma_n(GT_total) rows with the 128-byte swizzle, or (masks_b, s = 1)
+// the uint8 masks themselves with the same boxes and no swizzle.
 bool dense_mma_tf32_usable(const CostArgs& a, int ldt);
 cudaError_t launch_dense_mma_tf32(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
-                                  cudaStream_t st);
+                                  cudaStream_t st, bool masks_b);
 }  // namespace mlb
