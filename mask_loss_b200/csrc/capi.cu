@@ -520,10 +520,10 @@ int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigne
     const bool mma = LBQ > 0 && P.gout > 0 && !g_dense_mma_off && logits_tensor_map(P, a.logits, &tm) &&
                      dense_mma_usable(a, P.ldt, P.unc, P.foc, true);
     const bool tf32 = mma && !g_dense_tf32_off && dense_mma_tf32_usable(a, P.ldt);
-    // s = 1: the tf32 kernel reads the masks themselves; the count pass then
-    // only sums the mask areas
+    // s = 1: the tf32 kernel reads the masks themselves and sums the mask
+    // areas as it goes, so no count pass runs
     const bool masks_b = tf32 && masks_tensor_map(P, masks, &km);
-    if (P.B > 0 && P.gt_total > 0) {
+    if (P.B > 0 && P.gt_total > 0 && !masks_b) {
         e = launch_dense_count(masks, P.B, P.H, P.W, P.Ht, P.Wt, P.s, P.gt_total,
                                masks_b ? nullptr : cnt, const_cast<int32_t*>(a.totals), st, tf32);
         g_launches.fetch_add(1);

@@ -565,6 +565,7 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
         const bool rvalid = r < a.qrows && qt * a.qrows + r < a.Q;
         const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
         float rsum[3] = {0.0f, 0.0f, 0.0f};        // sum max(x,0), sum p, sum log2(1+e)
+        int area = 0;  // MASKB: non-zero mask bytes this thread converted (its GT row)
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
             const int s = kb % kTmaStages;
@@ -613,6 +614,7 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
                     *reinterpret_cast<float4*>(bs + s * bstage + n * 128 + ((g ^ (n & 7)) << 4)) =
                         make_float4((m & 0xFFu) ? 1.0f : 0.0f, (m & 0xFF00u) ? 1.0f : 0.0f,
                                     (m & 0xFF0000u) ? 1.0f : 0.0f, (m & 0xFF000000u) ? 1.0f : 0.0f);
+                    area += __popc(__vcmpne4(m, 0u)) >> 3;  // cells past H*W read as zeros
                 }
             }
             rsum[2] += lg2_approx(prod);  // 16 factors in [1, 2]
@@ -629,6 +631,16 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
         if (!ok) {
             sh->err = 1;
             if (lane == 0 && a.status) atomicOr(a.status, 2);
+        }
+        if (MASKB && qt == 0 && lb < a.B) {  // first query tile of the first layer
+            // mask areas (the count pass's other output): the eight lanes of a
+            // GT row sum their bytes, one atomic per row, the image's own rows
+            // only (the box's rows past GT_total are the next image's)
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) area += __shfl_down_sync(0xffffffffu, area, o);
+            const int n = (warp * 32 + lane) >> 3;
+            if ((lane & 7) == 0 && n < NG && area > 0)
+                atomicAdd(const_cast<int32_t*>(a.totals) + (int64_t)b * NG + n, area);
         }
         // ---- epilogue (as dense_mma_kernel): row sums, then D and I from TMEM ----
         if (kh == 1) {

@@ -89,7 +89,8 @@ def _overlap_case(seed, L, B, Q, H, W, s, C, GT):
     return ml, masks, cl, ct
 
 
-@pytest.mark.parametrize("variant", ["softmax", "unc_sigmoid_focal", "s2_forced_k2", "s3_unc_nobg"])
+@pytest.mark.parametrize("variant", ["softmax", "unc_sigmoid_focal", "s2_forced_k2", "s3_unc_nobg",
+                                     "masks_b_two_layers", "masks_b_two_query_tiles"])
 def test_dense_overlapping_against_oracle(variant):
     if variant == "softmax":
         shp = (2, 2, 12, 8, 9, 1, 7, 6)
@@ -101,6 +102,14 @@ def test_dense_overlapping_against_oracle(variant):
         P = O.Params(smooth=1.0, sigmoid_scale=2.0, dice_scale=3.0, cls_scale=1.5,
                      background_index=0, uncertainty_gamma=1.0, num_masks=4.0, mask_gamma=2.0,
                      mask_alpha=0.25, cls_gamma=1.5, cls_alpha=0.3)
+    elif variant.startswith("masks_b"):
+        # fp32 logits, s = 1, 16-cell rows, few GTs: the tf32 kernel with the
+        # masks as its B operand, which also sums the mask areas -- once per
+        # image over two layers, and over two query tiles
+        shp = (2, 2, 12, 8, 8, 1, 7, 6) if variant.endswith("layers") else (1, 1, 130, 8, 8, 1, 7, 6)
+        P = O.Params(smooth=1.0, sigmoid_scale=5.0, dice_scale=5.0, cls_scale=2.0,
+                     background_index=0, uncertainty_gamma=0.0, force_unmatched_class_to_background=True,
+                     void_class_index=6, use_softmax_label_loss=True)
     elif variant == "s3_unc_nobg":
         shp = (2, 2, 9, 5, 7, 3, 4, 6)
         P = O.Params(smooth=0.5, sigmoid_scale=1.0, dice_scale=1.0, cls_scale=1.0,
