@@ -38,6 +38,8 @@
 // the status word instead of hanging; TMEM is released on every path.
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -93,6 +95,15 @@ ML_INLINE void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
         ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc) : "memory");
+}
+// D[tmem] (+)= A[smem] x B[smem]^T, kind::f16 (bf16 in, fp32 accumulate).
+ML_INLINE void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                       bool accumulate) {
+    const uint32_t acc = accumulate ? 1u : 0u;
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc) : "memory");
 }
 // Arrive once on `bar` when every MMA this thread issued before has completed.
 ML_INLINE void umma_commit(uint64_t* bar) {
@@ -211,7 +222,12 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
     extern __shared__ __align__(1024) unsigned char dsm_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
-    const int QS = (a.qrows + 7) / 8 * 8;
+    // bf16 logits are exact bf16 A operands: the MMA reads x straight from the
+    // TMA'd tile (128 rows per stage, so the M = 128 read stays in the stage)
+    // and only p is split; fp32 and fp16 logits are split into bf16 hi/lo
+    constexpr bool AX = std::is_same<T, __nv_bfloat16>::value;
+    constexpr int NOP = AX ? 2 : 4;  // TMEM operands per stage
+    const int QS = AX ? 128 : (a.qrows + 7) / 8 * 8;
     // per stage: counts [N][32] bf16 (64-byte rows, 1024-aligned), logits [QS][32] of T
     const int bstage = (N * 64 + 1023) / 1024 * 1024;
     __nv_bfloat16* bs = reinterpret_cast<__nv_bfloat16*>(base);                 // [stage][N][32]
@@ -247,8 +263,8 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = sh->tmem_base;
-    // TMEM columns: D [0, N), I [N, 2N), then stage s operand o at 2N + (4s + o) * 16
-    auto a_col = [&](int s, int o) { return tbase + cols_acc + (uint32_t)((4 * s + o) * 16); };
+    // TMEM columns: D [0, N), I [N, 2N), then stage s operand o at 2N + (NOP s + o) * 16
+    auto a_col = [&](int s, int o) { return tbase + cols_acc + (uint32_t)((NOP * s + o) * 16); };
 
     if (warp == kMmaProducers) {
         // ------------------------------ control warp ------------------------------
@@ -284,10 +300,18 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
                     const uint64_t bd =
                         smem_desc_sw64(reinterpret_cast<unsigned char*>(bs) + s * bstage + 32 * kk);
                     const bool acc = kb > 0 || kk > 0;
-                    umma_ts(tbase, a_col(ts, 0) + 8 * kk, bd, idesc, acc);          // D += xh k
-                    umma_ts(tbase, a_col(ts, 1) + 8 * kk, bd, idesc, true);         // D += xl k
-                    umma_ts(tbase + N, a_col(ts, 2) + 8 * kk, bd, idesc, acc);      // I += ph k
-                    umma_ts(tbase + N, a_col(ts, 3) + 8 * kk, bd, idesc, true);     // I += pl k
+                    if constexpr (AX) {
+                        const uint64_t ad = smem_desc_sw64(
+                            reinterpret_cast<const unsigned char*>(xs + s * QS * kMmaK) + 32 * kk);
+                        umma_ss(tbase, ad, bd, idesc, acc);                             // D += x k
+                        umma_ts(tbase + N, a_col(ts, 0) + 8 * kk, bd, idesc, acc);      // I += ph k
+                        umma_ts(tbase + N, a_col(ts, 1) + 8 * kk, bd, idesc, true);     // I += pl k
+                    } else {
+                        umma_ts(tbase, a_col(ts, 0) + 8 * kk, bd, idesc, acc);          // D += xh k
+                        umma_ts(tbase, a_col(ts, 1) + 8 * kk, bd, idesc, true);         // D += xl k
+                        umma_ts(tbase + N, a_col(ts, 2) + 8 * kk, bd, idesc, acc);      // I += ph k
+                        umma_ts(tbase + N, a_col(ts, 3) + 8 * kk, bd, idesc, true);     // I += pl k
+                    }
                 }
                 umma_commit(&sh->mdone[s]);
                 // refill the stage of the previous block (its MMAs, issued one
@@ -366,9 +390,11 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
                 }
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
-                    const uint32_t hx = pack_bf16(xv[2 * j], xv[2 * j + 1]);
-                    xh[2 * u + j] = hx;
-                    xl[2 * u + j] = pack_bf16(xv[2 * j] - bf16_lo(hx), xv[2 * j + 1] - bf16_hi(hx));
+                    if constexpr (!AX) {
+                        const uint32_t hx = pack_bf16(xv[2 * j], xv[2 * j + 1]);
+                        xh[2 * u + j] = hx;
+                        xl[2 * u + j] = pack_bf16(xv[2 * j] - bf16_lo(hx), xv[2 * j + 1] - bf16_hi(hx));
+                    }
                     const uint32_t hp = pack_bf16(pv[2 * j], pv[2 * j + 1]);
                     ph[2 * u + j] = hp;
                     pl[2 * u + j] = pack_bf16(pv[2 * j] - bf16_lo(hp), pv[2 * j + 1] - bf16_hi(hp));
@@ -376,10 +402,15 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
             }
             rsum[2] += lg2_approx(prod);  // 16 factors in [1, 2]
             const uint32_t colk = (uint32_t)(8 * kh);  // 16 bf16 cells = 8 columns
-            tmem_st8(a_col(ts, 0) + lane_off + colk, xh);
-            tmem_st8(a_col(ts, 1) + lane_off + colk, xl);
-            tmem_st8(a_col(ts, 2) + lane_off + colk, ph);
-            tmem_st8(a_col(ts, 3) + lane_off + colk, pl);
+            if constexpr (AX) {
+                tmem_st8(a_col(ts, 0) + lane_off + colk, ph);
+                tmem_st8(a_col(ts, 1) + lane_off + colk, pl);
+            } else {
+                tmem_st8(a_col(ts, 0) + lane_off + colk, xh);
+                tmem_st8(a_col(ts, 1) + lane_off + colk, xl);
+                tmem_st8(a_col(ts, 2) + lane_off + colk, ph);
+                tmem_st8(a_col(ts, 3) + lane_off + colk, pl);
+            }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -698,9 +729,9 @@ bool dense_mma_usable(const CostArgs& a, int ldt, bool unc, bool foc, bool tma) 
            a.chunk_cells % (2 * kMmaK) == 0 && HW % 8 == 0;  // counts rows: 16-byte pitch
 }
 
-size_t dense_mma_smem(const CostArgs& a, int esize) {
+size_t dense_mma_smem(const CostArgs& a, int esize, bool ax) {
     const int N = dense_mma_n(a.gt_total);
-    const int QS = (a.qrows + 7) / 8 * 8;
+    const int QS = ax ? 128 : (a.qrows + 7) / 8 * 8;
     const size_t bstage = ((size_t)N * 64 + 1023) / 1024 * 1024;
     return 1024 + kTmaStages * bstage + (size_t)kTmaStages * QS * kMmaK * esize + sizeof(MmaShared);
 }
@@ -709,7 +740,7 @@ template <typename T>
 cudaError_t launch_dense_mma_t(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
                                cudaStream_t st) {
     const int N = dense_mma_n(a.gt_total);
-    const size_t smem = dense_mma_smem(a, (int)sizeof(T));
+    const size_t smem = dense_mma_smem(a, (int)sizeof(T), std::is_same<T, __nv_bfloat16>::value);
     cudaError_t e = cudaFuncSetAttribute(dense_mma_kernel<T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;

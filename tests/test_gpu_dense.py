@@ -173,3 +173,36 @@ def test_dense_half_logits_equal_fp32_path_on_widened_values(dtype, shp):
     assert r16[3].dtype == dtype
     assert torch.equal(r16[3], r32[3].to(dtype))
     assert torch.equal(r16[4], r32[4])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_dense_tensor_core_path_with_half_logits_against_oracle(dtype):
+    # no entropy weights or focal terms: the tensor-core kernel runs (bf16
+    # logits: the MMA reads the logits tile itself as its A operand; fp16:
+    # bf16 hi/lo split).  Against the oracle on the widened logits: costs,
+    # means and the class gradient at the usual tolerance, indices equal, the
+    # mask gradient (stored in the logits' 16-bit type) within its rounding
+    shp = (2, 2, 12, 8, 8, 1, 7, 6)
+    ml, masks, cl, ct = _overlap_case(41, *shp)
+    P = O.Params(smooth=1.0, sigmoid_scale=5.0, dice_scale=5.0, cls_scale=2.0,
+                 background_index=0, uncertainty_gamma=0.0, force_unmatched_class_to_background=True,
+                 void_class_index=shp[6] - 1, use_softmax_label_loss=True)
+    x16 = torch.from_numpy(ml).to(DEV).to(dtype)
+    wide = x16.float().cpu().numpy()
+    ep2g, eprd, em, ed, ec, esep = D.mask_matching(wide, masks, cl, ct, P)
+    L = ml.shape[0]
+    up = (1.0, 0.7, 1.3)
+    egx, egz = D.mask_matching_backward(np.full(L, up[0]), np.full(L, up[1]), np.full(L, up[2]),
+                                        wide, masks, cl, ct, ep2g, P)
+    t = [torch.from_numpy(v).to(DEV) for v in (masks, cl, ct)]
+    kw = (P.smooth, P.sigmoid_scale, P.dice_scale, P.cls_scale, P.background_index,
+          P.uncertainty_gamma, P.uncertainty_gamma_min)
+    sep = ops.pairwise_mask_loss_forward(x16, *t, *kw, use_softmax_label_loss=True)
+    close(sep.cpu().numpy(), esep)
+    p2g, prd, means, gx, gz = _run(x16, *t, P, up)
+    np.testing.assert_array_equal(p2g.cpu().numpy(), ep2g)
+    close(means.cpu().numpy(), np.stack([em, ed, ec]))
+    assert gx.dtype == dtype
+    ref = np.asarray(egx, np.float64)
+    np.testing.assert_allclose(gx.float().cpu().numpy(), ref, rtol=1e-2, atol=1e-2 * np.abs(ref).max())
+    close_grad(gz.cpu().numpy(), egz)
