@@ -523,6 +523,9 @@ def run_ours(args, cfg):
         count_bytes = 1 if (cfg.s == 1 and (cfg.H * cfg.W) % 16 == 0) else 4
     else:
         dense_kernel = "dense_mma_kernel"
+        # bf16 logits with unscaled masks: the masks are its B source too
+        if half is torch.bfloat16 and cfg.s == 1 and (cfg.H * cfg.W) % 16 == 0:
+            count_bytes = 1
     cost_kernel = dense_kernel if dense else "cost_partial_kernel"
     # dense: every logit plus each GT's count per cell
     esize = 2 if (half is not None and not sampled) else 4

@@ -522,7 +522,7 @@ int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigne
     const bool tf32 = mma && !g_dense_tf32_off && dense_mma_tf32_usable(a, P.ldt);
     // s = 1: the tf32 kernel reads the masks themselves and sums the mask
     // areas as it goes, so no count pass runs
-    const bool masks_b = tf32 && masks_tensor_map(P, masks, &km);
+    const bool masks_b = (tf32 || (mma && P.ldt == 1)) && masks_tensor_map(P, masks, &km);
     if (P.B > 0 && P.gt_total > 0 && !masks_b) {
         e = launch_dense_count(masks, P.B, P.H, P.W, P.Ht, P.Wt, P.s, P.gt_total,
                                masks_b ? nullptr : cnt, const_cast<int32_t*>(a.totals), st, tf32);
@@ -532,12 +532,14 @@ int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigne
     if (LBQ == 0 || P.gout == 0) return ML_OK;
     {
         ProfScope prof(0, st);  // profiled as the cost stage
-        if (masks_b)
+        if (masks_b && tf32)
             e = launch_dense_mma_tf32(tm, km, a, st, true);   // kind::tf32, B from the masks
+        else if (masks_b)
+            e = launch_dense_mma(tm, km, a, st, P.ldt, true);  // kind::f16 (bf16 logits), B from the masks
         else if (tf32 && counts_tensor_map(P, cnt, &km, true))
             e = launch_dense_mma_tf32(tm, km, a, st, false);  // kind::tf32, B from fp32 counts
         else if (mma && !tf32 && counts_tensor_map(P, cnt, &km, false))
-            e = launch_dense_mma(tm, km, a, st, P.ldt);  // tensor cores, kind::f16
+            e = launch_dense_mma(tm, km, a, st, P.ldt, false);  // tensor cores, kind::f16
         else if (tf32)
             return fail(ML_EINVAL, "dense counts tensor map could not be encoded");
         else

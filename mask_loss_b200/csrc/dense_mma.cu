@@ -215,7 +215,10 @@ ML_INLINE float4 tile_quad(const T* row, int r, int kh, int u) {
 // grid = (nchunk * 2, nqt, L*B); block = kMmaThreads.
 // Dynamic shared memory: per stage the logits tile [qrows_smem][32] of T
 // (1024-aligned), then per stage the B tile [4][N][8] bf16, then MmaShared.
-template <typename T>
+// MASKB (bf16 logits, s = 1): kmap covers the uint8 masks; the producers
+// build the bf16 B tile from the mask bytes and sum the mask areas, as in
+// dense_mma_tf32_kernel.
+template <typename T, bool MASKB>
 __global__ void __launch_bounds__(kMmaThreads, 2)
 dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap kmap,
                  CostArgs a, int N) {
@@ -232,7 +235,9 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
     const int bstage = (N * 64 + 1023) / 1024 * 1024;
     __nv_bfloat16* bs = reinterpret_cast<__nv_bfloat16*>(base);                 // [stage][N][32]
     T* xs = reinterpret_cast<T*>(base + kTmaStages * bstage);                    // [stage][QS][32]
-    MmaShared* sh = reinterpret_cast<MmaShared*>(xs + kTmaStages * QS * kMmaK);
+    unsigned char* ms = reinterpret_cast<unsigned char*>(xs + kTmaStages * QS * kMmaK);  // MASKB bytes
+    const uint32_t mstage = MASKB ? ((uint32_t)N * 32u + 127u) / 128u * 128u : 0u;
+    MmaShared* sh = reinterpret_cast<MmaShared*>(ms + kTmaStages * mstage);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int slot = blockIdx.x, chunk = slot >> 1, half = slot & 1;
@@ -274,7 +279,7 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
             auto issue_tma = [&](int kb) {
                 const int s = kb % kTmaStages;
                 mbar_arrive_expect_tx(&sh->full[s], (uint32_t)a.qrows * kMmaK * (uint32_t)sizeof(T) +
-                                                        (uint32_t)N * kMmaK * 2u);
+                                                        (uint32_t)N * kMmaK * (MASKB ? 1u : 2u));
                 const int c0 = cb + kb * kMmaK;
                 asm volatile(
                     "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
@@ -286,8 +291,9 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
                 asm volatile(
                     "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
                     " [%0], [%1, {%2, %3}], [%4];"
-                    ::"r"(smem_u32(reinterpret_cast<unsigned char*>(bs) + s * bstage)), "l"(&kmap),
-                      "r"(c0), "r"(b * NG), "r"(smem_u32(&sh->full[s])) : "memory");
+                    ::"r"(smem_u32(MASKB ? ms + s * mstage
+                                         : reinterpret_cast<unsigned char*>(bs) + s * bstage)),
+                      "l"(&kmap), "r"(c0), "r"(b * NG), "r"(smem_u32(&sh->full[s])) : "memory");
             };
             for (int kb = 0; kb < min(nkb, kTmaStages); ++kb) issue_tma(kb);
             for (int kb = 0; kb < nkb && ok; ++kb) {
@@ -340,6 +346,7 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
         const bool rvalid = r < a.qrows && qt * a.qrows + r < a.Q;
         const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
         float rsum[3] = {0.0f, 0.0f, 0.0f};        // sum max(x,0), sum p, sum log2(1+e)
+        int area = 0;  // MASKB: non-zero mask bytes this thread converted (its GT row)
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
             const int s = kb % kTmaStages;   // shared-memory stage
@@ -401,6 +408,20 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
                 }
             }
             rsum[2] += lg2_approx(prod);  // 16 factors in [1, 2]
+            if constexpr (MASKB) {  // mask bytes -> the bf16 B tile (64-byte swizzle), 4 cells a thread
+                const int pt = warp * 32 + lane;
+                if (pt < N * 8) {
+                    const int n = pt >> 3, q = pt & 7;
+                    const uint32_t m = *reinterpret_cast<const uint32_t*>(ms + s * mstage + n * 32 + q * 4);
+                    const uint32_t one = 0x3F80u;  // bf16 1.0
+                    const uint2 w = make_uint2(((m & 0xFFu) ? one : 0u) | ((m & 0xFF00u) ? one << 16 : 0u),
+                                               ((m & 0xFF0000u) ? one : 0u) | ((m & 0xFF000000u) ? one << 16 : 0u));
+                    *reinterpret_cast<uint2*>(reinterpret_cast<unsigned char*>(bs) + s * bstage + n * 64 +
+                                              ((((q >> 1) ^ ((n >> 1) & 3))) << 4) + (q & 1) * 8) = w;
+                    area += __popc(__vcmpne4(m, 0u)) >> 3;  // cells past H*W read as zeros
+                }
+                fence_proxy_async_smem();  // the B tile is read by the tensor core
+            }
             const uint32_t colk = (uint32_t)(8 * kh);  // 16 bf16 cells = 8 columns
             if constexpr (AX) {
                 tmem_st8(a_col(ts, 0) + lane_off + colk, ph);
@@ -419,6 +440,13 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
         if (!ok) {
             sh->err = 1;
             if (lane == 0 && a.status) atomicOr(a.status, 2);
+        }
+        if (MASKB && qt == 0 && lb < a.B) {  // mask areas: first query tile of the first layer
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) area += __shfl_down_sync(0xffffffffu, area, o);
+            const int n = (warp * 32 + lane) >> 3;
+            if ((lane & 7) == 0 && n < NG && area > 0)
+                atomicAdd(const_cast<int32_t*>(a.totals) + (int64_t)b * NG + n, area);
         }
         // ---- epilogue: row sums of the two cell halves, then D and I from TMEM ----
         if (kh == 1) {
@@ -729,23 +757,25 @@ bool dense_mma_usable(const CostArgs& a, int ldt, bool unc, bool foc, bool tma) 
            a.chunk_cells % (2 * kMmaK) == 0 && HW % 8 == 0;  // counts rows: 16-byte pitch
 }
 
-size_t dense_mma_smem(const CostArgs& a, int esize, bool ax) {
+size_t dense_mma_smem(const CostArgs& a, int esize, bool ax, bool masks_b) {
     const int N = dense_mma_n(a.gt_total);
     const int QS = ax ? 128 : (a.qrows + 7) / 8 * 8;
     const size_t bstage = ((size_t)N * 64 + 1023) / 1024 * 1024;
-    return 1024 + kTmaStages * bstage + (size_t)kTmaStages * QS * kMmaK * esize + sizeof(MmaShared);
+    const size_t mstage = masks_b ? ((size_t)N * 32 + 127) / 128 * 128 : 0;
+    return 1024 + kTmaStages * bstage + (size_t)kTmaStages * QS * kMmaK * esize + kTmaStages * mstage +
+           sizeof(MmaShared);
 }
 
-template <typename T>
+template <typename T, bool MASKB>
 cudaError_t launch_dense_mma_t(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
                                cudaStream_t st) {
     const int N = dense_mma_n(a.gt_total);
-    const size_t smem = dense_mma_smem(a, (int)sizeof(T), std::is_same<T, __nv_bfloat16>::value);
-    cudaError_t e = cudaFuncSetAttribute(dense_mma_kernel<T>,
+    const size_t smem = dense_mma_smem(a, (int)sizeof(T), std::is_same<T, __nv_bfloat16>::value, MASKB);
+    cudaError_t e = cudaFuncSetAttribute(dense_mma_kernel<T, MASKB>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 g(a.nchunk * 2, a.nqt, a.L * a.B);
-    dense_mma_kernel<T><<<g, kMmaThreads, smem, st>>>(tm, km, a, N);
+    dense_mma_kernel<T, MASKB><<<g, kMmaThreads, smem, st>>>(tm, km, a, N);
     return cudaGetLastError();
 }
 
@@ -768,10 +798,13 @@ cudaError_t launch_dense_mma_tf32(const CUtensorMap& tm, const CUtensorMap& km, 
 }
 
 cudaError_t launch_dense_mma(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
-                             cudaStream_t st, int ldt) {
-    if (ldt == 1) return launch_dense_mma_t<__nv_bfloat16>(tm, km, a, st);
-    if (ldt == 2) return launch_dense_mma_t<__half>(tm, km, a, st);
-    return launch_dense_mma_t<float>(tm, km, a, st);
+                             cudaStream_t st, int ldt, bool masks_b) {
+    if (ldt == 1)
+        return masks_b ? launch_dense_mma_t<__nv_bfloat16, true>(tm, km, a, st)
+                       : launch_dense_mma_t<__nv_bfloat16, false>(tm, km, a, st);
+    if (masks_b) return cudaErrorInvalidValue;  // bf16 logits only
+    if (ldt == 2) return launch_dense_mma_t<__half, false>(tm, km, a, st);
+    return launch_dense_mma_t<float, false>(tm, km, a, st);
 }
 
 }  // namespace mlb

@@ -216,8 +216,10 @@ bool dense_mma_usable(const CostArgs& a, int ldt, bool unc, bool foc, bool tma);
 int dense_mma_n(int gt_total);  // MMA N: GT_total rounded up to 16
 // tm: the logits map (logits_tensor_map); km: the counts, bf16 [B*GT_total][H*W]
 // with boxes of 32 cells x dense_mma_n(GT_total) rows and the 64-byte swizzle.
+// masks_b (bf16 logits, s = 1): km covers the uint8 masks (boxes of 32 cells
+// x N rows, no swizzle); the kernel builds its B tile and the mask areas.
 cudaError_t launch_dense_mma(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
-                             cudaStream_t st, int ldt);
+                             cudaStream_t st, int ldt, bool masks_b);
 // fp32 logits with GT_total <= 32 (and dense_mma_usable): the kind::tf32
 // kernel; km: the counts as fp32 [B*GT_total][H*W], boxes of 32 cells x
 // dense_mma_n(GT_total) rows with the 128-byte swizzle, or (masks_b, s = 1)
