@@ -522,7 +522,10 @@ int run_dense_costs(const FwdPlan& P, CostArgs& a, const uint8_t* masks, unsigne
     const bool tf32 = mma && !g_dense_tf32_off && dense_mma_tf32_usable(a, P.ldt);
     // s = 1: the tf32 kernel reads the masks themselves and sums the mask
     // areas as it goes, so no count pass runs
-    const bool masks_b = (tf32 || (mma && P.ldt == 1)) && masks_tensor_map(P, masks, &km);
+    // (the producers' 256 threads convert N x 32 mask bytes a block, 4 each:
+    // N <= 32)
+    const bool masks_b = (tf32 || (mma && P.ldt == 1 && dense_mma_n(P.gt_total) <= 32)) &&
+                         masks_tensor_map(P, masks, &km);
     if (P.B > 0 && P.gt_total > 0 && !masks_b) {
         e = launch_dense_count(masks, P.B, P.H, P.W, P.Ht, P.Wt, P.s, P.gt_total,
                                masks_b ? nullptr : cnt, const_cast<int32_t*>(a.totals), st, tf32);

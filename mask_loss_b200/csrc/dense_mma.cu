@@ -215,9 +215,9 @@ ML_INLINE float4 tile_quad(const T* row, int r, int kh, int u) {
 // grid = (nchunk * 2, nqt, L*B); block = kMmaThreads.
 // Dynamic shared memory: per stage the logits tile [qrows_smem][32] of T
 // (1024-aligned), then per stage the B tile [4][N][8] bf16, then MmaShared.
-// MASKB (bf16 logits, s = 1): kmap covers the uint8 masks; the producers
-// build the bf16 B tile from the mask bytes and sum the mask areas, as in
-// dense_mma_tf32_kernel.
+// MASKB (bf16 logits, s = 1, N <= 32): kmap covers the uint8 masks; the
+// producers build the bf16 B tile from the mask bytes (one thread per GT row
+// and 4 cells) and sum the mask areas, as in dense_mma_tf32_kernel.
 template <typename T, bool MASKB>
 __global__ void __launch_bounds__(kMmaThreads, 2)
 dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap kmap,

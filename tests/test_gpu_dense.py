@@ -175,14 +175,17 @@ def test_dense_half_logits_equal_fp32_path_on_widened_values(dtype, shp):
     assert torch.equal(r16[4], r32[4])
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_dense_tensor_core_path_with_half_logits_against_oracle(dtype):
+@pytest.mark.parametrize("gt", [6, 40])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_dense_tensor_core_path_with_half_logits_against_oracle(dtype, gt):
     # no entropy weights or focal terms: the tensor-core kernel runs (bf16
     # logits: the MMA reads the logits tile itself as its A operand; fp16:
     # bf16 hi/lo split).  Against the oracle on the widened logits: costs,
     # means and the class gradient at the usual tolerance, indices equal, the
-    # mask gradient (stored in the logits' 16-bit type) within its rounding
-    shp = (2, 2, 12, 8, 8, 1, 7, 6)
+    # mask gradient (stored in the logits' 16-bit type) within its rounding.
+    # gt 6: the mask bytes are the B operand (bf16; tf32 for fp32 logits);
+    # gt 40 (N = 48): counts as B, and fp32 logits on the bf16 hi/lo kernel
+    shp = (2, 2, 12, 8, 8, 1, 7, gt)
     ml, masks, cl, ct = _overlap_case(41, *shp)
     P = O.Params(smooth=1.0, sigmoid_scale=5.0, dice_scale=5.0, cls_scale=2.0,
                  background_index=0, uncertainty_gamma=0.0, force_unmatched_class_to_background=True,
@@ -204,5 +207,9 @@ def test_dense_tensor_core_path_with_half_logits_against_oracle(dtype):
     close(means.cpu().numpy(), np.stack([em, ed, ec]))
     assert gx.dtype == dtype
     ref = np.asarray(egx, np.float64)
-    np.testing.assert_allclose(gx.float().cpu().numpy(), ref, rtol=1e-2, atol=1e-2 * np.abs(ref).max())
+    if dtype == torch.float32:
+        close_grad(gx.cpu().numpy(), ref)
+    else:
+        np.testing.assert_allclose(gx.float().cpu().numpy(), ref, rtol=1e-2,
+                                   atol=1e-2 * np.abs(ref).max())
     close_grad(gz.cpu().numpy(), egz)
