@@ -732,12 +732,20 @@ __global__ void __launch_bounds__(256) cost_rows_kernel(CostArgs a) {
     for (int c = lane; c < a.C; c += 32) m = fmaxf(m, z[c]);
     m = warp_max(m);
     float se = 0.0f, sn = 0.0f, snu = 0.0f;
-    for (int c = lane; c < a.C; c += 32) {
-        const float zc = z[c];
-        se += __expf(zc - m);
-        const Elem e = elem(zc);
-        sn += focal_neg(cf, e);
-        snu += focal_neg(uf, e);
+    // the sigmoid sums only where a term below reads them (softmax with forced
+    // unmatched classes and a void class, the Mask2Former setting, needs none)
+    const bool need_sn = !a.use_softmax;
+    const bool need_snu = a.force_cls && (!a.has_void || !a.use_softmax);
+    if (need_sn || need_snu) {
+        for (int c = lane; c < a.C; c += 32) {
+            const float zc = z[c];
+            se += __expf(zc - m);
+            const Elem e = elem(zc);
+            sn += focal_neg(cf, e);
+            snu += focal_neg(uf, e);
+        }
+    } else {
+        for (int c = lane; c < a.C; c += 32) se += __expf(z[c] - m);
     }
     se = warp_sum(se); sn = warp_sum(sn); snu = warp_sum(snu);
     if (lane != 0) return;
