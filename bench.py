@@ -510,12 +510,12 @@ def run_ours(args, cfg):
     cells = synthetic.CFG3_POINTS if sampled else cfg.H * cfg.W  # sampled values are fp32
     # dense targets run on the tensor-core kernels unless MASK_LOSS_B200_DENSE_MMA=0
     # (the bench's settings have no entropy weights or focal terms, GT_out <= 64):
-    # fp32 logits with GT_total <= 32 on the kind::tf32 one (unless
+    # fp32 logits with GT_total <= 64 on the kind::tf32 one (unless
     # MASK_LOSS_B200_DENSE_TF32=0), else the bf16 one (bf16 counts)
     count_bytes = 2
     if os.environ.get("MASK_LOSS_B200_DENSE_MMA", "1")[:1] == "0":
         dense_kernel = "dense_cost_kernel"
-    elif (half is None and (GT_total + 15) // 16 * 16 <= 32 and
+    elif (half is None and (GT_total + 15) // 16 * 16 <= 64 and
           os.environ.get("MASK_LOSS_B200_DENSE_TF32", "1")[:1] != "0"):
         # unscaled masks (16-cell rows) are its B source directly: one byte a
         # cell and GT; else fp32 counts

@@ -85,7 +85,7 @@ const bool g_dense_mma_off = [] {
     const char* v = getenv("MASK_LOSS_B200_DENSE_MMA");
     return v && v[0] == '0';
 }();
-// fp32 logits run on the kind::tf32 kernel (GT_total <= 32);
+// fp32 logits run on the kind::tf32 kernel (GT_total <= 64);
 // MASK_LOSS_B200_DENSE_TF32=0 keeps them on the bf16 hi/lo one.
 const bool g_dense_tf32_off = [] {
     const char* v = getenv("MASK_LOSS_B200_DENSE_TF32");

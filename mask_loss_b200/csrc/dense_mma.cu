@@ -508,13 +508,13 @@ dense_mma_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant
 // Per logit the producers thus do a sigmoid, two splits and the row sums;
 // the bf16 kernel's four operand conversions become one in-place mask.
 // |x - x_hi - tf32(x_lo)| <= 2^-21 |x|, likewise for p.
-// TMEM: 2N accumulator columns + 2 stages x 3 operands x 32 columns <= 256
-// (N <= 32), so two CTAs share an SM.
+// TMEM: 2N accumulator columns + TS stages x 3 operands x 32 columns <= 256
+// (TS = 2 for N <= 32, 1 for N <= 64), so two CTAs share an SM.
 // MASKB (s = 1): kmap covers the uint8 masks themselves ([B*GT_total][H*W],
 // boxes of 32 cells x N rows, no swizzle); the producers turn each block's
 // mask bytes into the fp32 B tile (1.0 where non-zero), so no count planes
 // are written or read.
-template <bool MASKB>
+template <bool MASKB, int TS>
 __global__ void __launch_bounds__(kMmaThreads, 2)
 dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap kmap,
                       CostArgs a, int N) {
@@ -546,7 +546,7 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
             mbar_init(&sh->full[i], 1);
             mbar_init(&sh->mdone[i], 1);
         }
-        for (int i = 0; i < kMmaStages; ++i) mbar_init(&sh->aready[i], kMmaProducers);
+        for (int i = 0; i < TS; ++i) mbar_init(&sh->aready[i], kMmaProducers);
         mbar_init(&sh->accf, 1);
         sh->err = 0;
         fence_mbar_init();
@@ -586,8 +586,8 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
             for (int kb = 0; kb < min(nkb, kTmaStages); ++kb) issue_tma(kb);
             for (int kb = 0; kb < nkb && ok; ++kb) {
                 const int s = kb % kTmaStages;
-                const int ts = kb % kMmaStages;
-                if (!mbar_wait(&sh->aready[ts], (uint32_t)((kb / kMmaStages) & 1))) { ok = false; break; }
+                const int ts = kb % TS;
+                if (!mbar_wait(&sh->aready[ts], (uint32_t)((kb / TS) & 1))) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {  // K = 8 cells (32 bytes of a row) per MMA
@@ -624,15 +624,15 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
         const bool rvalid = r < a.qrows && qt * a.qrows + r < a.Q;
         const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
         float rsum[3] = {0.0f, 0.0f, 0.0f};        // sum max(x,0), sum p, sum log2(1+e)
-        int area = 0;  // MASKB: non-zero mask bytes this thread converted (its GT row)
+        int area[2] = {0, 0};  // MASKB: non-zero mask bytes converted, GT rows n and n + 32
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
             const int s = kb % kTmaStages;
-            const int ts = kb % kMmaStages;
+            const int ts = kb % TS;
             const int c0 = cb + kb * kMmaK;
             const int nv = min(kMmaK, ce - c0);
-            if (kb >= kMmaStages) {
-                const int kq = kb - kMmaStages;
+            if (kb >= TS) {
+                const int kq = kb - TS;
                 if (!mbar_wait(&sh->mdone[kq % kTmaStages], (uint32_t)((kq / kTmaStages) & 1))) {
                     ok = false;
                     break;
@@ -667,13 +667,16 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
             }
             if (MASKB) {  // mask bytes -> the fp32 B tile, 4 cells per thread
                 const int pt = warp * 32 + lane;
-                if (pt < N * 8) {
-                    const int n = pt >> 3, g = pt & 7;
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {  // rows n and n + 32 (N <= 64)
+                    const int t2 = pt + 256 * h2;
+                    if (t2 >= N * 8) break;
+                    const int n = t2 >> 3, g = t2 & 7;
                     const uint32_t m = *reinterpret_cast<const uint32_t*>(ms + s * mstage + n * 32 + g * 4);
                     *reinterpret_cast<float4*>(bs + s * bstage + n * 128 + ((g ^ (n & 7)) << 4)) =
                         make_float4((m & 0xFFu) ? 1.0f : 0.0f, (m & 0xFF00u) ? 1.0f : 0.0f,
                                     (m & 0xFF0000u) ? 1.0f : 0.0f, (m & 0xFF000000u) ? 1.0f : 0.0f);
-                    area += __popc(__vcmpne4(m, 0u)) >> 3;  // cells past H*W read as zeros
+                    area[h2] += __popc(__vcmpne4(m, 0u)) >> 3;  // cells past H*W read as zeros
                 }
             }
             rsum[2] += lg2_approx(prod);  // 16 factors in [1, 2]
@@ -696,10 +699,14 @@ dense_mma_tf32_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
             // GT row sum their bytes, one atomic per row, the image's own rows
             // only (the box's rows past GT_total are the next image's)
 #pragma unroll
-            for (int o = 4; o > 0; o >>= 1) area += __shfl_down_sync(0xffffffffu, area, o);
-            const int n = (warp * 32 + lane) >> 3;
-            if ((lane & 7) == 0 && n < NG && area > 0)
-                atomicAdd(const_cast<int32_t*>(a.totals) + (int64_t)b * NG + n, area);
+            for (int h2 = 0; h2 < 2; ++h2) {
+                int v = area[h2];
+#pragma unroll
+                for (int o = 4; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+                const int n = ((warp * 32 + lane) >> 3) + 32 * h2;
+                if ((lane & 7) == 0 && n < NG && v > 0)
+                    atomicAdd(const_cast<int32_t*>(a.totals) + (int64_t)b * NG + n, v);
+            }
         }
         // ---- epilogue (as dense_mma_kernel): row sums, then D and I from TMEM ----
         if (kh == 1) {
@@ -780,7 +787,7 @@ cudaError_t launch_dense_mma_t(const CUtensorMap& tm, const CUtensorMap& km, con
 }
 
 bool dense_mma_tf32_usable(const CostArgs& a, int ldt) {
-    return ldt == 0 && dense_mma_n(a.gt_total) <= 32;
+    return ldt == 0 && dense_mma_n(a.gt_total) <= 64;
 }
 
 cudaError_t launch_dense_mma_tf32(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
@@ -789,7 +796,10 @@ cudaError_t launch_dense_mma_tf32(const CUtensorMap& tm, const CUtensorMap& km, 
     const size_t bstage = ((size_t)N * 128 + 1023) / 1024 * 1024;
     const size_t mstage = masks_b ? ((size_t)N * 32 + 127) / 128 * 128 : 0;
     const size_t smem = 1024 + kTmaStages * ((size_t)128 * kMmaK * 4 + bstage + mstage) + sizeof(MmaShared);
-    auto k = masks_b ? dense_mma_tf32_kernel<true> : dense_mma_tf32_kernel<false>;
+    // two TMEM operand stages while 2N + 2 x 96 columns fit in 256 (N <= 32),
+    // else one (the producers then wait for the previous block's MMAs)
+    auto k = N <= 32 ? (masks_b ? dense_mma_tf32_kernel<true, 2> : dense_mma_tf32_kernel<false, 2>)
+                     : (masks_b ? dense_mma_tf32_kernel<true, 1> : dense_mma_tf32_kernel<false, 1>);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 g(a.nchunk * 2, a.nqt, a.L * a.B);

@@ -220,7 +220,7 @@ int dense_mma_n(int gt_total);  // MMA N: GT_total rounded up to 16
 // x N rows, no swizzle); the kernel builds its B tile and the mask areas.
 cudaError_t launch_dense_mma(const CUtensorMap& tm, const CUtensorMap& km, const CostArgs& a,
                              cudaStream_t st, int ldt, bool masks_b);
-// fp32 logits with GT_total <= 32 (and dense_mma_usable): the kind::tf32
+// fp32 logits with GT_total <= 64 (and dense_mma_usable): the kind::tf32
 // kernel; km: the counts as fp32 [B*GT_total][H*W], boxes of 32 cells x
 // dense_mma_n(GT_total) rows with the 128-byte swizzle, or (masks_b, s = 1)
 // the uint8 masks themselves with the same boxes and no swizzle.
