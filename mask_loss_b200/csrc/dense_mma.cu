@@ -6,8 +6,10 @@
 //     D[q,g] = sum_j x_qj k_gj          (sigmoid-CE, before the sign)
 //     I[q,g] = sum_j sigmoid(x_qj) k_gj (dice intersection)
 // are real GEMMs: k_gj is the pixel count of GT g in cell j, and a cell may
-// be covered by several GTs.  This kernel runs them on tcgen05 UMMA with the
-// fp32 accumulators in tensor memory (TMEM):
+// be covered by several GTs.  Two kernels run them on tcgen05 UMMA with the
+// fp32 accumulators in tensor memory (TMEM): dense_mma_tf32_kernel (fp32
+// logits, kind::tf32, below) and dense_mma_kernel (16-bit logits, and fp32
+// logits when the tf32 one is switched off; kind::f16), described here:
 //   * per CTA: one image, one query tile (M = 128 rows, rows >= qrows unused)
 //     and half a cell chunk, all GT columns (N = GT_total rounded up to 16,
 //     <= 64; the background column is computed and dropped on output);
@@ -34,8 +36,13 @@
 //     write the label path's chunk-partial slot, so cost_rows / cost_pairs,
 //     the solver and the matched loss run unchanged.
 // TMEM: 2N accumulator columns + 2 stages x 4 operands x 16 columns <= 256,
-// so two CTAs share an SM.  Every wait is bounded (2 s) and reports through
-// the status word instead of hanging; TMEM is released on every path.
+// so two CTAs share an SM.  With bf16 logits x is already an exact bf16
+// operand: the MMA reads it from the TMA'd tile and only p is split (two
+// TMEM operands a stage).  With unscaled masks (and bf16 logits, N <= 32)
+// the B tile is built by the producers from the mask bytes themselves, and
+// the mask areas are summed on the way, so no count pass runs.  Every wait
+// is bounded (2 s) and reports through the status word instead of hanging;
+// TMEM is released on every path.
 #include <cuda.h>
 
 #include <type_traits>
